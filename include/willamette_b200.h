@@ -1,0 +1,209 @@
+/*
+ * willamette_b200.h -- C ABI of the B200 (sm_100a) BitLinear hot-path library.
+ *
+ * A drop-in for project-willamette's BitLinear / lm-head call surface
+ * (Rust crate project-willamette v0.14.0).  Each entry point names the
+ * reference function it replaces.  The ABI uses plain pointers and sizes
+ * only: no CUDA, torch or C++ types cross it (a cudaStream_t is passed as
+ * `void *`).
+ *
+ * Two families of entry points:
+ *   wl_*      synchronous, HOST buffers in and out -- the same contract as the
+ *             reference functions (inputs borrowed, output caller-allocated
+ *             and fully overwritten on success, never written with fake
+ *             values on error).  Weights are uploaded to the GPU on first use
+ *             and cached, keyed by (data pointer, length, type, shape); the
+ *             reference's weights are an immutable mmap for the life of the
+ *             process, which is what makes that cache valid.
+ *   wl_dev_*  asynchronous on a caller stream, DEVICE pointers, no host sync.
+ *
+ * Every entry point returns a wl_status; on failure wl_last_error() (thread
+ * local) holds the message.  No entry point ever falls back to a CPU
+ * implementation: without a usable sm_100 device they return WL_ERR_CUDA or
+ * WL_ERR_NO_DEVICE.
+ */
+#ifndef WILLAMETTE_B200_H
+#define WILLAMETTE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status
+ * Mirrors the variants of WillametteError (src/error.rs:9-57) that the hot
+ * path can produce, plus the device-side failures a GPU adds. */
+typedef enum wl_status {
+    WL_OK = 0,
+    WL_ERR_UNSUPPORTED_TENSOR_TYPE = 1, /* UnsupportedTensorType(u32), error.rs:29 */
+    WL_ERR_GGUF_PARSE = 2,              /* GgufParse(String), error.rs:14: shape/length/scale */
+    WL_ERR_NOT_IMPLEMENTED = 3,         /* NotImplemented(String), error.rs:35: arms left to the CPU */
+    WL_ERR_INVALID_ARGUMENT = 4,        /* NULL / misaligned pointer, size beyond a stated limit */
+    WL_ERR_CUDA = 5,                    /* CUDA runtime error */
+    WL_ERR_NO_DEVICE = 6,               /* no sm_100 device visible */
+    WL_ERR_DEVICE_TIMEOUT = 7,          /* a bounded device-side wait gave up */
+    WL_ERR_COMM = 8                     /* multi-GPU peer setup / exchange failure */
+} wl_status;
+
+/* GGML type ids (src/gguf/types.rs:66-99). */
+#define WL_GGML_F32 0u
+#define WL_GGML_F16 1u
+#define WL_GGML_Q4_0 2u
+#define WL_GGML_Q8_0 8u
+#define WL_GGML_Q4_K 12u
+#define WL_GGML_Q6_K 14u
+#define WL_GGML_I2_S 36u
+
+/* Layout constants (src/gguf/tensor.rs:86-105, :141-175). */
+#define WL_I2S_ELEMENTS_PER_BLOCK 128u
+#define WL_I2S_PACKED_BYTES_PER_BLOCK 32u
+#define WL_Q6K_ELEMENTS_PER_BLOCK 256u
+#define WL_Q6K_BYTES_PER_BLOCK 210u
+#define WL_Q8_0_ELEMENTS_PER_BLOCK 32u
+#define WL_Q8_0_BYTES_PER_BLOCK 34u
+
+/* Largest in_dim the I2_S kernels accept (its int32 partial sums stay exact
+ * far beyond this; the bound keeps activations register-resident). */
+#define WL_I2S_MAX_IN_DIM 65536u
+
+/* TensorView (src/gguf/tensor.rs:21-54) as plain C.  shape is GGUF order,
+ * innermost first: [in_dim, out_dim] for a 2-D weight.  For I2_S, data is
+ * the packed-codes area only and scale_data the 32-byte trailing block whose
+ * first 4 bytes are the little-endian f32 per-tensor scale. */
+typedef struct wl_tensor_view {
+    const char *name;          /* may be NULL; used in error messages */
+    const uint64_t *shape;
+    uint32_t n_dims;
+    uint32_t ggml_type;        /* raw GGML type id */
+    const uint8_t *data;
+    size_t data_len;
+    const uint8_t *scale_data; /* I2_S only, else NULL */
+    size_t scale_len;
+} wl_tensor_view;
+
+/* ------------------------------------------------------------------ library */
+const char *wl_version(void);
+/* Message of the last failure on this thread ("" if none). */
+const char *wl_last_error(void);
+/* Raw GGML type carried by the last WL_ERR_UNSUPPORTED_TENSOR_TYPE. */
+uint32_t wl_last_error_tensor_type(void);
+/* Select the CUDA device for this process (default: 0 on first use).
+ * Fails with WL_ERR_NO_DEVICE unless the device is compute capability 10.x. */
+int wl_init(int device);
+/* Free every cached device copy of host weights. */
+int wl_release_weights(void);
+/* Device-side error word (bit 0: a bounded wait timed out).  Reading
+ * clears it. */
+int wl_device_status(uint32_t *flags);
+
+/* ------------------------------------------------- host-buffer entry points */
+
+/* bitlinear_i2s_matvec_f32 (src/model/bitlinear.rs:67), x86 dispatch
+ * target bitlinear_i2s_matvec_f32_sse2_i8 (src/model/bitlinear_sse2.rs:313):
+ * per-vector absmax int8 quantisation of input, exact int32 ternary dot per
+ * row, output[j] = (w_scale * act_scale) * (float)acc[j].  Validation as
+ * bitlinear_sse2.rs:129-177 (data_len >= in_dim/4*out_dim) and
+ * tensor.rs:278-309 (finite scale). */
+int wl_bitlinear_i2s_matvec_f32(const wl_tensor_view *weight, const float *input,
+                                size_t input_len, float *output, size_t output_len);
+
+/* As wl_bitlinear_i2s_matvec_f32, also returning the parity intermediates:
+ * acc_out[out_dim] int32 row dots, act_scale_out[1], act_q_out[in_dim]
+ * (each may be NULL). */
+int wl_bitlinear_i2s_matvec_f32_dbg(const wl_tensor_view *weight, const float *input,
+                                    size_t input_len, float *output, size_t output_len,
+                                    int32_t *acc_out, float *act_scale_out, int8_t *act_q_out);
+
+/* Prefill over m tokens: the reference runs bitlinear_i2s_matvec_f32 once
+ * per token (src/model/generate.rs:241-250, src/model/multi_forward.rs:106-110),
+ * i.e. per-token absmax quantisation; here one int8 tensor-core GEMM.
+ * input is m x in_dim, output m x out_dim, row-major.  acc_out optional. */
+int wl_bitlinear_i2s_gemm_f32(const wl_tensor_view *weight, const float *input, size_t m,
+                              float *output, int32_t *acc_out);
+
+/* linear_matvec_f32 (src/model/linear.rs:11): I2_S, Q8_0 (linear.rs:171,
+ * AVX2 row order q8_0_simd.rs:72) and Q6_K (linear.rs:43, SSE2 row order
+ * q6_k_sse2.rs:46) arms.  F16 / Q4_0 / Q4_K return WL_ERR_NOT_IMPLEMENTED;
+ * other types WL_ERR_UNSUPPORTED_TENSOR_TYPE (linear.rs:23). */
+int wl_linear_matvec_f32(const wl_tensor_view *weight, const float *input, size_t input_len,
+                         float *output, size_t output_len);
+
+/* compute_logits (src/model/lm_head.rs:29) for Q6_K and Q8_0 tables:
+ * logits[v] = dot_row(row_v, final_hidden), bit-identical to the
+ * reference's x86 row dot.  F16 / Q4_0 / Q4_K tables return
+ * WL_ERR_NOT_IMPLEMENTED. */
+int wl_compute_logits(const float *final_hidden, size_t hidden_len,
+                      const wl_tensor_view *token_embd, uint32_t embedding_length,
+                      uint32_t vocab_size, float *logits, size_t logits_len);
+
+/* argmax (src/model/lm_head.rs:161): first index of the maximum, strict
+ * '>' scan (ties -> lowest id; NaN never wins unless at index 0).  *out_id
+ * = -1 for an empty slice (the reference's None). */
+int wl_argmax(const float *logits, size_t len, int64_t *out_id);
+
+/* Greedy next token for a batch of hidden rows: compute_logits + argmax
+ * fused (sampler.rs:133-136 greedy short-circuit, generate.rs:166-169).
+ * hidden is batch x embedding_length; token_ids[batch]; logits (optional,
+ * batch x vocab_size) receives the full logit rows. */
+int wl_lm_head_greedy(const float *hidden, size_t batch, const wl_tensor_view *token_embd,
+                      uint32_t embedding_length, uint32_t vocab_size, uint32_t *token_ids,
+                      float *logits);
+
+/* ------------------------------------------------ device-pointer entry points
+ * All asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ * stream).  Device buffers must be 16-byte aligned. */
+
+/* Per-row absmax int8 quantisation (bitlinear_sse2.rs:285-304) of an
+ * m x n f32 matrix: q (m x n int8), act_scale (m f32). */
+int wl_dev_quantize_absmax_i8(const float *x, uint32_t n, uint32_t m, int8_t *q,
+                              float *act_scale, void *stream);
+
+/* Up to WL_I2S_MAX_FUSED weights of equal in_dim sharing one quantised
+ * input (e.g. Q/K/V or gate/up), one launch: y_i[out_dim_i] =
+ * (w_scale_i * act_scale[0]) * acc.  acc_i may be NULL. */
+#define WL_I2S_MAX_FUSED 4
+typedef struct wl_i2s_dev_weight {
+    const uint8_t *packed; /* out_dim x in_dim/4 bytes, device */
+    float w_scale;
+    uint32_t out_dim;
+    float *y;              /* device, out_dim f32 */
+    int32_t *acc;          /* device, out_dim i32, or NULL */
+} wl_i2s_dev_weight;
+int wl_dev_i2s_matvec(const wl_i2s_dev_weight *weights, uint32_t n_weights, uint32_t in_dim,
+                      const int8_t *q, const float *act_scale, void *stream);
+
+/* Quantise x then matvec (the two kernels chained with programmatic
+ * dependent launch).  q_scratch: in_dim int8, scale_scratch: 1 f32. */
+int wl_dev_i2s_matvec_f32(const uint8_t *packed, float w_scale, uint32_t in_dim,
+                          uint32_t out_dim, const float *x, float *y, int8_t *q_scratch,
+                          float *scale_scratch, void *stream);
+
+/* Q6_K lm-head.  The raw GGUF rows (vocab x n_embd/256 x 210 bytes) are
+ * repacked once into the device layout (wl_q6k_packed_bytes bytes). */
+size_t wl_q6k_packed_bytes(uint32_t n_embd, uint32_t vocab);
+int wl_dev_q6k_repack(const uint8_t *raw, uint32_t n_embd, uint32_t vocab, uint8_t *packed,
+                      void *stream);
+/* Logits (optional, batch x vocab) and greedy ids (batch) for batch hidden
+ * rows.  scratch: wl_q6k_scratch_bytes(batch) bytes, zero before the first
+ * call; every call leaves it zero again. */
+size_t wl_q6k_scratch_bytes(uint32_t batch);
+int wl_dev_q6k_lm_head(const uint8_t *packed, uint32_t n_embd, uint32_t vocab,
+                       const float *hidden, uint32_t batch, float *logits, uint32_t *ids,
+                       void *scratch, void *stream);
+
+/* Q8_0 matvec / lm-head rows (q8_0_simd.rs:72-104 order), after a one-time
+ * repack (wl_q8_0_packed_bytes).  Non-finite block scales are rejected by
+ * the host entry points before upload (q8_0.rs:25-33). */
+size_t wl_q8_0_packed_bytes(uint32_t in_dim, uint32_t out_dim);
+int wl_dev_q8_0_repack(const uint8_t *raw, uint32_t in_dim, uint32_t out_dim, uint8_t *packed,
+                       void *stream);
+int wl_dev_q8_0_matvec(const uint8_t *packed, uint32_t in_dim, uint32_t out_dim,
+                       const float *x, float *y, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WILLAMETTE_B200_H */

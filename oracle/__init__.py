@@ -1,0 +1,243 @@
+"""ctypes binding for the CPU oracle (test infrastructure only).
+
+The oracle is a C restatement of project-willamette's x86 BitLinear /
+lm-head path (see ``willamette_oracle.h``).  It is the parity checker for
+the CUDA library and the timed CPU baseline.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline and
+``--impl reference`` legs import this module; the product package never
+does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libwillamette_oracle.so")
+
+_u8p = C.POINTER(C.c_uint8)
+_i8p = C.POINTER(C.c_int8)
+_i32p = C.POINTER(C.c_int32)
+_f32p = C.POINTER(C.c_float)
+_sz = C.c_size_t
+_u32 = C.c_uint32
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (no-op when up to date)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.or_f16_to_f32.argtypes = [C.c_uint16]
+        L.or_f16_to_f32.restype = C.c_float
+        L.or_f32_to_f16.argtypes = [C.c_float]
+        L.or_f32_to_f16.restype = C.c_uint16
+        L.or_ternary_from_code.argtypes = [C.c_uint8]
+        L.or_ternary_from_code.restype = C.c_int8
+        L.or_i2s_matvec_scalar.argtypes = [_u8p, _sz, C.c_float, _u32, _u32, _f32p, _f32p]
+        L.or_quantize_absmax_i8.argtypes = [_f32p, _sz, _i8p]
+        L.or_quantize_absmax_i8.restype = C.c_float
+        L.or_i2s_matvec_sse2_i8.argtypes = [_u8p, _sz, C.c_float, _u32, _u32, _f32p, _f32p,
+                                            _i32p, _f32p, _i8p]
+        L.or_i2s_gemm_rows.argtypes = [_u8p, _sz, C.c_float, _u32, _u32, _u32, _f32p, _f32p,
+                                       _i32p, _f32p, C.c_int]
+        L.or_i2s_matvec_sse2_f32.argtypes = [_u8p, _sz, C.c_float, _u32, _u32, _f32p, _f32p]
+        L.or_i2s_matvec_lut.argtypes = [_u8p, _sz, C.c_float, _u32, _u32, _f32p, _f32p]
+        L.or_i2s_unpack_row.argtypes = [_u8p, _sz, _u32, _u32, _u32, _i8p]
+        for name in ("or_q6k_dot_row_scalar", "or_q6k_dot_row_sse2", "or_q8_0_dot_row_scalar",
+                     "or_q8_0_dot_row_avx2", "or_q8_0_dot_row_sse2"):
+            getattr(L, name).argtypes = [_u8p, _sz, _f32p, _sz, _f32p]
+        L.or_q6k_dequantize_row.argtypes = [_u8p, _sz, _f32p, _sz]
+        L.or_q8_0_dequantize_row.argtypes = [_u8p, _sz, _f32p, _sz]
+        L.or_q6k_quantize_row.argtypes = [_f32p, _sz, _u8p, _sz]
+        L.or_q8_0_matvec.argtypes = [_u8p, _sz, _u32, _u32, _f32p, _f32p, C.c_int]
+        L.or_compute_logits.argtypes = [_f32p, _u32, _u8p, _sz, _u32, _u32, _f32p, C.c_int]
+        L.or_argmax.argtypes = [_f32p, _sz]
+        L.or_argmax.restype = C.c_int64
+        _lib = L
+    return _lib
+
+
+class OracleError(RuntimeError):
+    """The reference would have returned Err(..) for these inputs."""
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(t)
+
+
+def _u8(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise OracleError(f"{what}: reference rejects these inputs (rc={rc})")
+
+
+def f16_to_f32(bits: int) -> float:
+    return float(lib().or_f16_to_f32(bits))
+
+
+def f32_to_f16(value: float) -> int:
+    return int(lib().or_f32_to_f16(value))
+
+
+def ternary_from_code(code: int) -> int:
+    return int(lib().or_ternary_from_code(code))
+
+
+def quantize_absmax_i8(x) -> tuple[np.ndarray, float]:
+    x = _f32(x)
+    q = np.zeros(x.size, np.int8)
+    s = lib().or_quantize_absmax_i8(_p(x, _f32p), x.size, _p(q, _i8p))
+    return q, float(s)
+
+
+def i2s_matvec_scalar(packed, scale: float, in_dim: int, out_dim: int, x) -> np.ndarray:
+    packed, x = _u8(packed), _f32(x)
+    y = np.zeros(out_dim, np.float32)
+    _check(lib().or_i2s_matvec_scalar(_p(packed, _u8p), packed.size, scale, in_dim, out_dim,
+                                      _p(x, _f32p), _p(y, _f32p)), "i2s_matvec_scalar")
+    return y
+
+
+def i2s_matvec_sse2_i8(packed, scale: float, in_dim: int, out_dim: int, x):
+    """Returns (y f32[out_dim], acc i32[out_dim], act_scale, act_q i8[in_dim])."""
+    packed, x = _u8(packed), _f32(x)
+    y = np.zeros(out_dim, np.float32)
+    acc = np.zeros(out_dim, np.int32)
+    q = np.zeros(in_dim, np.int8)
+    s = C.c_float(0.0)
+    _check(lib().or_i2s_matvec_sse2_i8(_p(packed, _u8p), packed.size, scale, in_dim, out_dim,
+                                       _p(x, _f32p), _p(y, _f32p), _p(acc, _i32p), C.byref(s),
+                                       _p(q, _i8p)), "i2s_matvec_sse2_i8")
+    return y, acc, float(s.value), q
+
+
+def i2s_gemm_rows(packed, scale: float, in_dim: int, out_dim: int, X, n_threads: int = 1):
+    """Per-token SSE2-i8 matvec over the rows of X (how the reference prefills)."""
+    packed, X = _u8(packed), _f32(X)
+    m = X.shape[0]
+    Y = np.zeros((m, out_dim), np.float32)
+    acc = np.zeros((m, out_dim), np.int32)
+    sc = np.zeros(m, np.float32)
+    _check(lib().or_i2s_gemm_rows(_p(packed, _u8p), packed.size, scale, in_dim, out_dim, m,
+                                  _p(X, _f32p), _p(Y, _f32p), _p(acc, _i32p), _p(sc, _f32p),
+                                  n_threads), "i2s_gemm_rows")
+    return Y, acc, sc
+
+
+def i2s_matvec_sse2_f32(packed, scale: float, in_dim: int, out_dim: int, x) -> np.ndarray:
+    packed, x = _u8(packed), _f32(x)
+    y = np.zeros(out_dim, np.float32)
+    _check(lib().or_i2s_matvec_sse2_f32(_p(packed, _u8p), packed.size, scale, in_dim, out_dim,
+                                        _p(x, _f32p), _p(y, _f32p)), "i2s_matvec_sse2_f32")
+    return y
+
+
+def i2s_matvec_lut(packed, scale: float, in_dim: int, out_dim: int, x) -> np.ndarray:
+    packed, x = _u8(packed), _f32(x)
+    y = np.zeros(out_dim, np.float32)
+    _check(lib().or_i2s_matvec_lut(_p(packed, _u8p), packed.size, scale, in_dim, out_dim,
+                                   _p(x, _f32p), _p(y, _f32p)), "i2s_matvec_lut")
+    return y
+
+
+def i2s_unpack_row(packed, in_dim: int, out_dim: int, row: int) -> np.ndarray:
+    packed = _u8(packed)
+    out = np.zeros(in_dim, np.int8)
+    _check(lib().or_i2s_unpack_row(_p(packed, _u8p), packed.size, in_dim, out_dim, row,
+                                   _p(out, _i8p)), "i2s_unpack_row")
+    return out
+
+
+def _row_fn(name: str, row, x) -> float:
+    row, x = _u8(row), _f32(x)
+    out = C.c_float(0.0)
+    _check(getattr(lib(), name)(_p(row, _u8p), row.size, _p(x, _f32p), x.size, C.byref(out)), name)
+    return float(out.value)
+
+
+def q6k_dot_row_scalar(row, x) -> float:
+    return _row_fn("or_q6k_dot_row_scalar", row, x)
+
+
+def q6k_dot_row_sse2(row, x) -> float:
+    return _row_fn("or_q6k_dot_row_sse2", row, x)
+
+
+def q8_0_dot_row_scalar(row, x) -> float:
+    return _row_fn("or_q8_0_dot_row_scalar", row, x)
+
+
+def q8_0_dot_row_avx2(row, x) -> float:
+    return _row_fn("or_q8_0_dot_row_avx2", row, x)
+
+
+def q8_0_dot_row_sse2(row, x) -> float:
+    return _row_fn("or_q8_0_dot_row_sse2", row, x)
+
+
+def q6k_dequantize_row(row, n: int) -> np.ndarray:
+    row = _u8(row)
+    out = np.zeros(n, np.float32)
+    _check(lib().or_q6k_dequantize_row(_p(row, _u8p), row.size, _p(out, _f32p), n),
+           "q6k_dequantize_row")
+    return out
+
+
+def q8_0_dequantize_row(row, n: int) -> np.ndarray:
+    row = _u8(row)
+    out = np.zeros(n, np.float32)
+    _check(lib().or_q8_0_dequantize_row(_p(row, _u8p), row.size, _p(out, _f32p), n),
+           "q8_0_dequantize_row")
+    return out
+
+
+def q6k_quantize_row(x) -> np.ndarray:
+    x = _f32(x)
+    out = np.zeros(x.size // 256 * 210, np.uint8)
+    _check(lib().or_q6k_quantize_row(_p(x, _f32p), x.size, _p(out, _u8p), out.size),
+           "q6k_quantize_row")
+    return out
+
+
+def q8_0_matvec(w, in_dim: int, out_dim: int, x, n_threads: int = 0) -> np.ndarray:
+    w, x = _u8(w), _f32(x)
+    y = np.zeros(out_dim, np.float32)
+    _check(lib().or_q8_0_matvec(_p(w, _u8p), w.size, in_dim, out_dim, _p(x, _f32p),
+                                _p(y, _f32p), n_threads), "q8_0_matvec")
+    return y
+
+
+def compute_logits(hidden, w, ggml_type: int, n_embd: int, vocab: int,
+                   n_threads: int = 0) -> np.ndarray:
+    hidden, w = _f32(hidden), _u8(w)
+    logits = np.zeros(vocab, np.float32)
+    _check(lib().or_compute_logits(_p(hidden, _f32p), n_embd, _p(w, _u8p), w.size, ggml_type,
+                                   vocab, _p(logits, _f32p), n_threads), "compute_logits")
+    return logits
+
+
+def argmax(logits):
+    logits = _f32(logits)
+    r = lib().or_argmax(_p(logits, _f32p), logits.size)
+    return None if r < 0 else int(r)

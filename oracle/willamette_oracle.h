@@ -1,0 +1,126 @@
+/*
+ * willamette_oracle.h -- CPU oracle for the BitLinear hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This is a plain-C restatement of the
+ * reference's x86 code path (Rust crate project-willamette v0.14.0), used
+ * as the parity checker for the CUDA library and as the timed CPU
+ * baseline.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline / --impl reference leg may load it.  The product library
+ * never links or calls it.
+ *
+ * Parity pin: the reference is Rust and no Rust toolchain exists on the
+ * build or GPU machines, so it cannot be executed.  The restatement is
+ * pinned by the reference's own known-answer unit tests (transcribed from
+ * its test sources into tests/test_oracle_kats.py).
+ *
+ * Every function names the reference file:line it follows.  All f32
+ * arithmetic is compiled with -ffp-contract=off (Rust never contracts a*b+c
+ * into an FMA) and uses the same SSE2/AVX2 intrinsics, in the same
+ * reduction order, as the reference's x86 kernels.
+ *
+ * Status codes: 0 = ok, negative = the reference would return Err(..).
+ */
+#ifndef WILLAMETTE_ORACLE_H
+#define WILLAMETTE_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* src/model/primitives.rs:61-88 */
+float or_f16_to_f32(uint16_t bits);
+/* IEEE binary32 -> binary16, round-to-nearest-even (half 2.7.1 f16::from_f32). */
+uint16_t or_f32_to_f16(float value);
+
+/* src/model/bitlinear.rs:43-50 */
+int8_t or_ternary_from_code(uint8_t code);
+
+/* src/model/bitlinear.rs:146-242 (scalar two-accumulator f32 reference). */
+int or_i2s_matvec_scalar(const uint8_t *packed, size_t packed_len, float scale,
+                         uint32_t in_dim, uint32_t out_dim, const float *x,
+                         float *y);
+
+/* src/model/bitlinear_sse2.rs:285-304 (per-vector absmax int8 quantiser).
+ * Returns the activation scale (max_abs / 127, or 1.0 for an all-zero x). */
+float or_quantize_absmax_i8(const float *x, size_t n, int8_t *q);
+
+/* src/model/bitlinear_sse2.rs:313-342 (x86 default: int8 activations).
+ * acc_out (out_dim i32), act_scale_out (1 f32) and act_q_out (in_dim i8)
+ * are optional debug outputs (NULL to skip). */
+int or_i2s_matvec_sse2_i8(const uint8_t *packed, size_t packed_len,
+                          float w_scale, uint32_t in_dim, uint32_t out_dim,
+                          const float *x, float *y, int32_t *acc_out,
+                          float *act_scale_out, int8_t *act_q_out);
+
+/* Prefill "GEMM" as the reference runs it: one sse2_i8 matvec per token
+ * (src/model/generate.rs:241-250, src/model/multi_forward.rs:106-110).
+ * X is m x in_dim row-major, Y is m x out_dim, acc_out optional m x out_dim,
+ * act_scale_out optional m. */
+int or_i2s_gemm_rows(const uint8_t *packed, size_t packed_len, float w_scale,
+                     uint32_t in_dim, uint32_t out_dim, uint32_t m,
+                     const float *x, float *y, int32_t *acc_out,
+                     float *act_scale_out, int n_threads);
+
+/* src/model/bitlinear_sse2.rs:89-124 + :206-255 (f32 mask-add kernel). */
+int or_i2s_matvec_sse2_f32(const uint8_t *packed, size_t packed_len,
+                           float scale, uint32_t in_dim, uint32_t out_dim,
+                           const float *x, float *y);
+
+/* src/model/bitlinear_lut.rs:59-131 (scalar 256-entry LUT kernel). */
+int or_i2s_matvec_lut(const uint8_t *packed, size_t packed_len, float scale,
+                      uint32_t in_dim, uint32_t out_dim, const float *x,
+                      float *y);
+
+/* src/model/bitlinear.rs:247-299 */
+int or_i2s_unpack_row(const uint8_t *packed, size_t packed_len,
+                      uint32_t in_dim, uint32_t out_dim, uint32_t row,
+                      int8_t *out);
+
+/* src/model/q6_k.rs:59-69 (for_each_weight :25-57). n = values. */
+int or_q6k_dequantize_row(const uint8_t *row, size_t row_len, float *out,
+                          size_t n);
+/* src/model/q6_k.rs:84-96 */
+int or_q6k_dot_row_scalar(const uint8_t *row, size_t row_len, const float *x,
+                          size_t n, float *out);
+/* src/model/q6_k_sse2.rs:46-116 (the x86 dispatch target, q6_k.rs:71-82) */
+int or_q6k_dot_row_sse2(const uint8_t *row, size_t row_len, const float *x,
+                        size_t n, float *out);
+/* src/model/q6_k.rs:232-238 (offline quantiser; used only to rebuild the
+ * reference's Q6_K unit-test fixtures). */
+int or_q6k_quantize_row(const float *in, size_t n, uint8_t *out,
+                        size_t out_len);
+
+/* src/model/q8_0.rs:35-48 */
+int or_q8_0_dequantize_row(const uint8_t *row, size_t row_len, float *out,
+                           size_t n);
+/* src/model/q8_0.rs:72-85 */
+int or_q8_0_dot_row_scalar(const uint8_t *row, size_t row_len, const float *x,
+                           size_t n, float *out);
+/* src/model/q8_0_simd.rs:72-104 (x86 hosts with AVX2, q8_0.rs:59-62) */
+int or_q8_0_dot_row_avx2(const uint8_t *row, size_t row_len, const float *x,
+                         size_t n, float *out);
+/* src/model/q8_0_simd.rs:108-141 */
+int or_q8_0_dot_row_sse2(const uint8_t *row, size_t row_len, const float *x,
+                         size_t n, float *out);
+
+/* src/model/linear.rs:171-224 (rayon over rows -> OpenMP over rows). */
+int or_q8_0_matvec(const uint8_t *w, size_t w_len, uint32_t in_dim,
+                   uint32_t out_dim, const float *x, float *y, int n_threads);
+
+/* src/model/lm_head.rs:29-108.  ggml_type: 1 = F16, 8 = Q8_0, 14 = Q6_K.
+ * Rows are independent (rayon); n_threads <= 0 uses all cores. */
+int or_compute_logits(const float *hidden, uint32_t n_embd,
+                      const uint8_t *w, size_t w_len, uint32_t ggml_type,
+                      uint32_t vocab, float *logits, int n_threads);
+
+/* src/model/lm_head.rs:161-174.  Returns -1 for an empty slice. */
+int64_t or_argmax(const float *logits, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WILLAMETTE_ORACLE_H */

@@ -1,0 +1,111 @@
+"""ctypes prototypes for include/willamette_b200.h.
+
+Loads project_willamette_b200/_lib/libwillamette_b200.so (built in-tree by
+``python -m project_willamette_b200.build``).  A missing library is an
+error: there is no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_lib", "libwillamette_b200.so")
+HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "willamette_b200.h")
+
+
+class WLStatus(enum.IntEnum):
+    OK = 0
+    UNSUPPORTED_TENSOR_TYPE = 1
+    GGUF_PARSE = 2
+    NOT_IMPLEMENTED = 3
+    INVALID_ARGUMENT = 4
+    CUDA = 5
+    NO_DEVICE = 6
+    DEVICE_TIMEOUT = 7
+    COMM = 8
+
+
+class WlTensorView(C.Structure):
+    _fields_ = [
+        ("name", C.c_char_p),
+        ("shape", C.POINTER(C.c_uint64)),
+        ("n_dims", C.c_uint32),
+        ("ggml_type", C.c_uint32),
+        ("data", C.POINTER(C.c_uint8)),
+        ("data_len", C.c_size_t),
+        ("scale_data", C.POINTER(C.c_uint8)),
+        ("scale_len", C.c_size_t),
+    ]
+
+
+class WlI2sDevWeight(C.Structure):
+    _fields_ = [
+        ("packed", C.c_void_p),
+        ("w_scale", C.c_float),
+        ("out_dim", C.c_uint32),
+        ("y", C.c_void_p),
+        ("acc", C.c_void_p),
+    ]
+
+
+_vp = C.c_void_p
+_sz = C.c_size_t
+_u32 = C.c_uint32
+_i = C.c_int
+_fp = C.POINTER(C.c_float)
+_tv = C.POINTER(WlTensorView)
+
+PROTOTYPES = {
+    "wl_version": ([], C.c_char_p),
+    "wl_last_error": ([], C.c_char_p),
+    "wl_last_error_tensor_type": ([], _u32),
+    "wl_init": ([_i], _i),
+    "wl_release_weights": ([], _i),
+    "wl_device_status": ([C.POINTER(_u32)], _i),
+    "wl_bitlinear_i2s_matvec_f32": ([_tv, _fp, _sz, _fp, _sz], _i),
+    "wl_bitlinear_i2s_matvec_f32_dbg": ([_tv, _fp, _sz, _fp, _sz, C.POINTER(C.c_int32), _fp,
+                                         C.POINTER(C.c_int8)], _i),
+    "wl_bitlinear_i2s_gemm_f32": ([_tv, _fp, _sz, _fp, C.POINTER(C.c_int32)], _i),
+    "wl_linear_matvec_f32": ([_tv, _fp, _sz, _fp, _sz], _i),
+    "wl_compute_logits": ([_fp, _sz, _tv, _u32, _u32, _fp, _sz], _i),
+    "wl_argmax": ([_fp, _sz, C.POINTER(C.c_int64)], _i),
+    "wl_lm_head_greedy": ([_fp, _sz, _tv, _u32, _u32, C.POINTER(_u32), _fp], _i),
+    "wl_dev_quantize_absmax_i8": ([_vp, _u32, _u32, _vp, _vp, _vp], _i),
+    "wl_dev_i2s_matvec": ([C.POINTER(WlI2sDevWeight), _u32, _u32, _vp, _vp, _vp], _i),
+    "wl_dev_i2s_matvec_f32": ([_vp, C.c_float, _u32, _u32, _vp, _vp, _vp, _vp, _vp], _i),
+    "wl_q6k_packed_bytes": ([_u32, _u32], _sz),
+    "wl_dev_q6k_repack": ([_vp, _u32, _u32, _vp, _vp], _i),
+    "wl_q6k_scratch_bytes": ([_u32], _sz),
+    "wl_dev_q6k_lm_head": ([_vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp, _vp], _i),
+    "wl_q8_0_packed_bytes": ([_u32, _u32], _sz),
+    "wl_dev_q8_0_repack": ([_vp, _u32, _u32, _vp, _vp], _i),
+    "wl_dev_q8_0_matvec": ([_vp, _u32, _u32, _vp, _vp, _vp], _i),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m project_willamette_b200.build` "
+                "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (args, res) in PROTOTYPES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def header_functions() -> list[str]:
+    """Names of the functions include/willamette_b200.h declares."""
+    import re
+    src = open(HEADER_PATH).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(wl_[a-z0-9_]+)\s*\(", src)))

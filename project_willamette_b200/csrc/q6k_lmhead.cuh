@@ -1,0 +1,306 @@
+// q6k_lmhead.cuh -- Q6_K tied lm-head (logits + greedy argmax) for sm_100a.
+//
+// Reference: compute_logits (src/model/lm_head.rs:29-108) -> q6_k::dot_row
+// (src/model/q6_k.rs:71-82) -> dot_row_sse2_validated
+// (src/model/q6_k_sse2.rs:46-116); argmax (src/model/lm_head.rs:161-174).
+//
+// Bit-exact logits.  The reference's SSE2 row dot keeps 16 independent f32
+// accumulation chains: 4 vector accumulators (one per quarter a = q1..q4 of
+// each 128-value half) x 4 lanes k.  Chain (a, k) visits, in order, blocks
+// b, halves h, and l = k, k+4, ..., k+28 of
+//     acc += (q * (d * sc)) * x          (two roundings, never an FMA)
+// with q = 6-bit value - 32, then reduces
+//     v_k = (acc_0k + acc_1k) + (acc_2k + acc_3k),
+//     logit = (v_0 + v_3) + (v_1 + v_2).
+// Here one thread owns quarter a of one row and runs that quarter's four
+// chains with the same IEEE round-to-nearest operations (__fmul_rn /
+// __fadd_rn: no contraction), then the four threads of a row combine their
+// chains with the same tree.  The int->float conversion of q uses the
+// 2^23 magic-number construction, which is exact.
+//
+// Device layout (one-time repack, q6k_repack_kernel): each row becomes
+//   [ql: nb x 128][qh: nb x 64][sc: nb x 16][d: nb x 2][pad to 16 B]
+// (nb = n_embd / 256; 2112 bytes per row at n_embd 2560, 0.57 % above the
+// GGUF 2100) so rows and sections are 16-byte aligned for bulk copies.
+//
+// Streaming: 148 persistent CTAs each own a contiguous row range; a producer
+// warp streams 32-row chunks into a 3-stage shared-memory ring with 1-D bulk
+// copies; two consumer groups of 4 warps take alternate chunks.
+//
+// Argmax: key = (orderable(logit) << 32) | (0xFFFFFFFF - row); the maximum
+// key is the reference's answer (ties -> lowest row, -0.0 == +0.0, NaN never
+// wins, except a NaN at row 0, which the strict '>' scan keeps).  CTAs
+// atomicMax into a per-batch-row slot; the last CTA to finish writes the ids
+// and re-zeroes the slots and its counter.
+#pragma once
+
+#include <cstdint>
+
+#include "wl_ptx.cuh"
+
+namespace wl {
+
+constexpr int Q6K_CONSUMER_WARPS = 8;
+constexpr int Q6K_THREADS = (Q6K_CONSUMER_WARPS + 1) * 32;
+constexpr int Q6K_GROUP_THREADS = 128;  // 4 warps per consumer group
+constexpr int Q6K_ROWS_PER_CHUNK = Q6K_GROUP_THREADS / 4;  // 4 threads per row
+constexpr int Q6K_STAGES = 3;
+
+__host__ __device__ constexpr uint32_t q6k_row_stride(uint32_t nb) {
+    return (nb * 208u + ((nb * 2u + 15u) & ~15u));
+}
+
+// x index -> padded shared-memory index (4 floats of padding per 32 so the
+// four quarters of a row read distinct banks).
+__device__ __forceinline__ uint32_t q6k_xpad(uint32_t i) { return i + (i >> 5) * 4u; }
+
+struct Q6kParams {
+    const uint8_t *packed;   // vocab x row_stride bytes, device layout
+    uint32_t n_embd, vocab, nb, row_stride;
+    uint32_t rows_per_cta;
+    uint32_t nstages;        // 2 or 3 (<= Q6K_STAGES), whatever fits in shared memory
+    const float *hidden;     // BG x n_embd (this launch's batch rows)
+    float *logits;           // BG x vocab or null
+    uint32_t *ids;           // BG or null
+    unsigned long long *slots;  // BG argmax slots (zero on entry)
+    uint32_t *counter;          // CTA completion counter (zero on entry)
+    uint32_t *status;
+};
+
+__device__ __forceinline__ uint32_t f32_order_key(float v, uint32_t row) {
+    if (isnan(v)) return row == 0 ? 0xFFFFFFFFu : 0u;
+    if (v == 0.0f) v = 0.0f;  // -0.0 ties with +0.0
+    const uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+    // primitives.rs:61-88, exact (incl. subnormals, inf, NaN payload).
+    const uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    if (exp == 0) {
+        if (man == 0) return __uint_as_float(sign << 31);
+        const float val = __fmul_rn((float)man, 5.9604644775390625e-8f);  // 2^-24
+        return sign ? -val : val;
+    }
+    if (exp == 0x1F) return __uint_as_float((sign << 31) | (0xFFu << 23) | (man << 13));
+    return __uint_as_float((sign << 31) | ((exp + 112u) << 23) | (man << 13));
+}
+
+// Repack GGUF Q6_K rows (210-byte super-blocks) into the device layout.
+__global__ void q6k_repack_kernel(const uint8_t *__restrict__ raw, uint32_t nb, uint32_t vocab,
+                                  uint8_t *__restrict__ out) {
+    const uint32_t stride = q6k_row_stride(nb);
+    const size_t total = (size_t)vocab * nb;
+    for (size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t row = (uint32_t)(t / nb), b = (uint32_t)(t % nb);
+        const uint8_t *src = raw + ((size_t)row * nb + b) * 210u;
+        uint8_t *dst = out + (size_t)row * stride;
+        for (int i = 0; i < 128; ++i) dst[b * 128u + i] = src[i];
+        for (int i = 0; i < 64; ++i) dst[nb * 128u + b * 64u + i] = src[128 + i];
+        for (int i = 0; i < 16; ++i) dst[nb * 192u + b * 16u + i] = src[192 + i];
+        dst[nb * 208u + b * 2u] = src[208];
+        dst[nb * 208u + b * 2u + 1] = src[209];
+        if (b == 0)
+            for (uint32_t i = nb * 210u; i < stride; ++i) dst[i] = 0;
+    }
+}
+
+template <int BG>
+__global__ void __launch_bounds__(Q6K_THREADS, 1)
+    q6k_lmhead_kernel(const __grid_constant__ Q6kParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bar[Q6K_STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[Q6K_STAGES];
+    __shared__ unsigned long long cta_best[BG];
+    __shared__ uint32_t s_timeout;
+    __shared__ uint32_t s_last;
+
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t chunk_bytes = Q6K_ROWS_PER_CHUNK * p.row_stride;
+    const uint32_t nst = p.nstages;
+    float *xs = reinterpret_cast<float *>(smem + nst * chunk_bytes);
+    const uint32_t xs_len = p.n_embd + p.n_embd / 8;  // padded floats per batch row
+
+    const uint32_t r0 = blockIdx.x * p.rows_per_cta;
+    const uint32_t r1 = min(r0 + p.rows_per_cta, p.vocab);
+    const uint32_t nchunks = r0 < r1 ? (r1 - r0 + Q6K_ROWS_PER_CHUNK - 1) / Q6K_ROWS_PER_CHUNK : 0;
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < nst; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], Q6K_GROUP_THREADS / 32);
+        }
+        fence_mbar_init();
+        s_timeout = 0;
+    }
+    if (tid < BG) cta_best[tid] = 0ull;
+    __syncthreads();
+
+    pdl_launch_dependents();
+
+    if (warp == Q6K_CONSUMER_WARPS) {
+        // Producer warp: one elected lane streams the chunks.  The weights do
+        // not depend on the previous kernel, so streaming starts before the
+        // programmatic-dependency wait.
+        if (lane == 0) {
+            const uint64_t policy = l2_policy_evict_first();
+            for (uint32_t c = 0; c < nchunks; ++c) {
+                const uint32_t st = c % nst;
+                if (c >= nst) {
+                    if (!mbar_wait(&empty_bar[st], ((c / nst) - 1u) & 1u)) {
+                        atomicOr(&s_timeout, 1u);
+                        break;
+                    }
+                }
+                const uint32_t a = r0 + c * Q6K_ROWS_PER_CHUNK;
+                const uint32_t b = min(a + Q6K_ROWS_PER_CHUNK, r1);
+                const uint32_t bytes = (b - a) * p.row_stride;
+                mbar_arrive_expect_tx(&full_bar[st], bytes);
+                bulk_g2s_evict_first(smem + st * chunk_bytes, p.packed + (size_t)a * p.row_stride,
+                                     bytes, &full_bar[st], policy);
+            }
+        }
+    } else {
+        // Consumers: wait for the previous kernel (the hidden rows, and the
+        // argmax scratch of a previous call), then stage the hidden rows
+        // (padded) in shared memory.
+        pdl_wait();
+        for (uint32_t i = tid; i < BG * p.n_embd; i += Q6K_CONSUMER_WARPS * 32) {
+            const uint32_t bg = i / p.n_embd, e = i % p.n_embd;
+            xs[bg * xs_len + q6k_xpad(e)] = p.hidden[(size_t)bg * p.n_embd + e];
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(Q6K_CONSUMER_WARPS * 32));
+
+        const uint32_t group = warp / 4;
+        const uint32_t gtid = tid - group * Q6K_GROUP_THREADS;
+        const uint32_t row_local = gtid >> 2;
+        const uint32_t a = gtid & 3u;
+        const uint32_t nb = p.nb;
+        unsigned long long best[BG];
+#pragma unroll
+        for (int g = 0; g < BG; ++g) best[g] = 0ull;
+
+        for (uint32_t c = group; c < nchunks; c += 2) {
+            const uint32_t st = c % nst;
+            if (!mbar_wait(&full_bar[st], (c / nst) & 1u)) {
+                atomicOr(&s_timeout, 1u);
+                break;
+            }
+            const uint32_t row = r0 + c * Q6K_ROWS_PER_CHUNK + row_local;
+            const uint8_t *rp = smem + st * chunk_bytes + row_local * p.row_stride;
+            float acc[BG][4];
+#pragma unroll
+            for (int g = 0; g < BG; ++g)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[g][k] = 0.0f;
+
+            if (row < r1) {
+                const uint8_t *ql_sec = rp, *qh_sec = rp + nb * 128u, *sc_sec = rp + nb * 192u;
+                const uint16_t *d_sec = reinterpret_cast<const uint16_t *>(rp + nb * 208u);
+                const uint32_t ql_shift = (a >> 1) * 4u, qh_shift = a * 2u;
+                for (uint32_t b = 0; b < nb; ++b) {
+                    const float d = f16_bits_to_f32(d_sec[b]);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int8_t *sc = reinterpret_cast<const int8_t *>(sc_sec + b * 16u + h * 8);
+                        const float s0 = __fmul_rn(d, (float)sc[a * 2]);
+                        const float s1 = __fmul_rn(d, (float)sc[a * 2 + 1]);
+                        const uint4 qlv0 = *reinterpret_cast<const uint4 *>(
+                            ql_sec + b * 128u + h * 64 + (a & 1u) * 32u);
+                        const uint4 qlv1 = *reinterpret_cast<const uint4 *>(
+                            ql_sec + b * 128u + h * 64 + (a & 1u) * 32u + 16u);
+                        const uint4 qhv0 =
+                            *reinterpret_cast<const uint4 *>(qh_sec + b * 64u + h * 32);
+                        const uint4 qhv1 =
+                            *reinterpret_cast<const uint4 *>(qh_sec + b * 64u + h * 32 + 16);
+                        const uint32_t qlw[8] = {qlv0.x, qlv0.y, qlv0.z, qlv0.w,
+                                                 qlv1.x, qlv1.y, qlv1.z, qlv1.w};
+                        const uint32_t qhw[8] = {qhv0.x, qhv0.y, qhv0.z, qhv0.w,
+                                                 qhv1.x, qhv1.y, qhv1.z, qhv1.w};
+                        const uint32_t xbase = b * 256u + h * 128u + a * 32u;
+#pragma unroll
+                        for (int m = 0; m < 8; ++m) {
+                            const uint32_t u4 = ((qlw[m] >> ql_shift) & 0x0F0F0F0Fu) |
+                                                (((qhw[m] >> qh_shift) & 0x03030303u) << 4);
+                            const float sc_f = m < 4 ? s0 : s1;
+                            float w[4];
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const float qf = __fadd_rn(
+                                    __uint_as_float(__byte_perm(u4, 0x4B000000u, 0x7440 + k)),
+                                    -8388640.0f);  // (2^23 + u) - (2^23 + 32) = u - 32, exact
+                                w[k] = __fmul_rn(qf, sc_f);
+                            }
+#pragma unroll
+                            for (int g = 0; g < BG; ++g) {
+                                const float4 xv = *reinterpret_cast<const float4 *>(
+                                    xs + g * xs_len + q6k_xpad(xbase + 4u * m));
+                                acc[g][0] = __fadd_rn(acc[g][0], __fmul_rn(w[0], xv.x));
+                                acc[g][1] = __fadd_rn(acc[g][1], __fmul_rn(w[1], xv.y));
+                                acc[g][2] = __fadd_rn(acc[g][2], __fmul_rn(w[2], xv.z));
+                                acc[g][3] = __fadd_rn(acc[g][3], __fmul_rn(w[3], xv.w));
+                            }
+                        }
+                    }
+                }
+            }
+            // Release the stage (all loads of this chunk are done).
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[st]);
+
+            // Combine the 16 chains exactly as _mm_add_ps / hsum do.
+#pragma unroll
+            for (int g = 0; g < BG; ++g) {
+                float v[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float other = __shfl_down_sync(0xffffffffu, acc[g][k], 1);
+                    const float pair = __fadd_rn(acc[g][k], other);  // lanes a=0: q1+q2, a=2: q3+q4
+                    const float hi = __shfl_down_sync(0xffffffffu, pair, 2);
+                    v[k] = __fadd_rn(pair, hi);                      // lane a=0
+                }
+                const float logit = __fadd_rn(__fadd_rn(v[0], v[3]), __fadd_rn(v[1], v[2]));
+                if (a == 0 && row < r1) {
+                    if (p.logits) p.logits[(size_t)g * p.vocab + row] = logit;
+                    const unsigned long long key =
+                        ((unsigned long long)f32_order_key(logit, row) << 32) |
+                        (unsigned long long)(0xFFFFFFFFu - row);
+                    best[g] = best[g] > key ? best[g] : key;
+                }
+            }
+        }
+        if (p.ids) {
+#pragma unroll
+            for (int g = 0; g < BG; ++g) {
+                unsigned long long k = best[g];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
+                    k = k > o ? k : o;
+                }
+                if (lane == 0) atomicMax(&cta_best[g], k);
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        if (s_timeout) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
+        if (p.ids) {
+            for (int g = 0; g < BG; ++g) atomicMax(&p.slots[g], cta_best[g]);
+            __threadfence();
+            s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
+        } else {
+            s_last = 0;
+        }
+    }
+    __syncthreads();
+    if (s_last && tid < BG) {
+        __threadfence();
+        const unsigned long long k = atomicExch(&p.slots[tid], 0ull);
+        p.ids[tid] = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+        if (tid == 0) *p.counter = 0u;
+    }
+}
+
+}  // namespace wl

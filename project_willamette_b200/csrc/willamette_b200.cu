@@ -1,0 +1,882 @@
+// willamette_b200.cu -- the C ABI (include/willamette_b200.h) and its host
+// logic: validation that mirrors the reference's error behaviour, the device
+// cache of host weights, staging buffers, and kernel launches.
+//
+// Built as one translation unit with the kernel headers so the whole library
+// is a single sm_100a object (see project_willamette_b200/build.py).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/willamette_b200.h"
+#include "argmax.cuh"
+#include "i2s_matvec.cuh"
+#include "q6k_lmhead.cuh"
+#include "q8_0.cuh"
+
+namespace {
+
+using namespace wl;
+
+// ------------------------------------------------------------------ errors
+thread_local std::string g_last_error;
+thread_local uint32_t g_last_type = 0;
+
+int fail(int status, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int fail_type(uint32_t raw) {
+    g_last_type = raw;
+    return fail(WL_ERR_UNSUPPORTED_TENSOR_TYPE, "Unsupported GGML tensor type: %u", raw);
+}
+
+#define WL_CUDA(call)                                                                   \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return fail(WL_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));   \
+    } while (0)
+
+const char *tname(const wl_tensor_view *t) { return t && t->name ? t->name : "<unnamed>"; }
+
+// ------------------------------------------------------------------ state
+struct DevBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+};
+
+struct CachedWeight {
+    void *dptr = nullptr;
+    size_t bytes = 0;
+    bool bad_scale = false;  // Q8_0: some block scale is not finite
+};
+
+using CacheKey = std::tuple<const void *, size_t, uint32_t, uint64_t, uint64_t>;
+
+struct Ctx {
+    std::mutex mu;
+    bool inited = false;
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t *d_status = nullptr;
+    uint32_t *h_status = nullptr;  // pinned
+    void *pinned = nullptr;
+    size_t pinned_cap = 0;
+    DevBuf x, y, q, scale, acc, ids, scratch;
+    std::map<CacheKey, CachedWeight> cache;
+};
+
+Ctx &ctx() {
+    static Ctx c;
+    return c;
+}
+
+constexpr int WL_MAX_DYN_SMEM = 227 * 1024 - 1024;
+
+// Raise the dynamic shared-memory limit of every kernel once, at init, so
+// launches never call cudaFuncSetAttribute (they can be captured in graphs).
+int configure_kernels() {
+    const void *kernels[] = {
+        (const void *)i2s_matvec_kernel<8, 1>,  (const void *)i2s_matvec_kernel<8, 2>,
+        (const void *)i2s_matvec_kernel<8, 3>,  (const void *)i2s_matvec_kernel<8, 4>,
+        (const void *)i2s_matvec_kernel<8, 5>,  (const void *)i2s_matvec_kernel<32, 0>,
+        (const void *)i2s_matvec_kernel<32, 2>, (const void *)i2s_matvec_kernel<32, 3>,
+        (const void *)i2s_matvec_kernel<32, 4>, (const void *)i2s_matvec_kernel<32, 5>,
+        (const void *)i2s_matvec_kernel<32, 6>, (const void *)i2s_matvec_kernel<32, 7>,
+        (const void *)i2s_matvec_kernel<32, 8>, (const void *)q6k_lmhead_kernel<1>,
+        (const void *)q6k_lmhead_kernel<4>,     (const void *)q8_0_matvec_kernel,
+    };
+    for (const void *k : kernels)
+        WL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     WL_MAX_DYN_SMEM));
+    return WL_OK;
+}
+
+int init_locked(Ctx &c, int device) {
+    if (c.inited) return WL_OK;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+        return fail(WL_ERR_NO_DEVICE, "no CUDA device visible");
+    if (device < 0 || device >= n) return fail(WL_ERR_NO_DEVICE, "device %d out of range", device);
+    cudaDeviceProp prop;
+    WL_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(WL_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+    WL_CUDA(cudaSetDevice(device));
+    c.device = device;
+    c.sm_count = prop.multiProcessorCount;
+    WL_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    WL_CUDA(cudaMalloc(&c.d_status, 64));
+    WL_CUDA(cudaMemset(c.d_status, 0, 64));
+    WL_CUDA(cudaMallocHost(&c.h_status, 64));
+    int rc = configure_kernels();
+    if (rc) return rc;
+    c.inited = true;
+    return WL_OK;
+}
+
+int ensure_init(Ctx &c) {
+    if (c.inited) {
+        cudaSetDevice(c.device);
+        return WL_OK;
+    }
+    return init_locked(c, 0);
+}
+
+int grow(DevBuf &b, size_t bytes) {
+    if (b.cap >= bytes) return WL_OK;
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.cap = 0;
+    size_t cap = bytes < 4096 ? 4096 : bytes;
+    WL_CUDA(cudaMalloc(&b.p, cap));
+    WL_CUDA(cudaMemset(b.p, 0, cap));
+    b.cap = cap;
+    return WL_OK;
+}
+
+int grow_pinned(Ctx &c, size_t bytes) {
+    if (c.pinned_cap >= bytes) return WL_OK;
+    if (c.pinned) cudaFreeHost(c.pinned);
+    c.pinned = nullptr;
+    c.pinned_cap = 0;
+    size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
+    WL_CUDA(cudaMallocHost(&c.pinned, cap));
+    c.pinned_cap = cap;
+    return WL_OK;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ launches
+template <typename Kern, typename... Args>
+cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                   Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+int sm_count_for_launch() {
+    Ctx &c = ctx();
+    if (c.inited) return c.sm_count;
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        n = 148;
+    return n;
+}
+
+uint32_t *status_ptr() {
+    Ctx &c = ctx();
+    if (!c.inited) {
+        std::lock_guard<std::mutex> g(c.mu);
+        if (init_locked(c, 0) != WL_OK) return nullptr;
+    }
+    return c.d_status;
+}
+
+using I2sKernel = void (*)(I2sMatvecParams);
+
+I2sKernel pick_i2s_kernel(uint32_t K, int *lpr) {
+    const uint32_t P = K / 64u;
+    if (P <= 40) {
+        *lpr = 8;
+        switch ((P + 7) / 8) {
+        case 1: return i2s_matvec_kernel<8, 1>;
+        case 2: return i2s_matvec_kernel<8, 2>;
+        case 3: return i2s_matvec_kernel<8, 3>;
+        case 4: return i2s_matvec_kernel<8, 4>;
+        default: return i2s_matvec_kernel<8, 5>;
+        }
+    }
+    *lpr = 32;
+    switch ((P + 31) / 32) {
+    case 2: return i2s_matvec_kernel<32, 2>;
+    case 3: return i2s_matvec_kernel<32, 3>;
+    case 4: return i2s_matvec_kernel<32, 4>;
+    case 5: return i2s_matvec_kernel<32, 5>;
+    case 6: return i2s_matvec_kernel<32, 6>;
+    case 7: return i2s_matvec_kernel<32, 7>;
+    case 8: return i2s_matvec_kernel<32, 8>;
+    default: return i2s_matvec_kernel<32, 0>;
+    }
+}
+
+int launch_quantize(const float *x, uint32_t n, uint32_t m, int8_t *q, float *scale,
+                    cudaStream_t s, bool pdl) {
+    if (m == 0 || n == 0) return WL_OK;
+    WL_CUDA(launch(quantize_absmax_kernel, dim3(m), dim3(QUANT_THREADS), 0, s, pdl, x, n, q,
+                   scale));
+    return WL_OK;
+}
+
+int launch_i2s(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K, const int8_t *q,
+               const float *act_scale, cudaStream_t s, bool pdl) {
+    I2sMatvecParams p = {};
+    uint32_t rows = 0;
+    for (uint32_t j = 0; j < nw; ++j) {
+        p.jobs[j].w = w[j].packed;
+        p.jobs[j].w_scale = w[j].w_scale;
+        p.jobs[j].out_dim = w[j].out_dim;
+        p.jobs[j].row_begin = rows;
+        p.jobs[j].y = w[j].y;
+        p.jobs[j].acc = w[j].acc;
+        rows += w[j].out_dim;
+    }
+    if (rows == 0) return WL_OK;
+    p.njobs = (int)nw;
+    p.K = K;
+    p.total_rows = rows;
+    p.q = q;
+    p.act_scale = act_scale;
+    p.status = status_ptr();
+    if (!p.status) return WL_ERR_NO_DEVICE;
+    int lpr = 32;
+    I2sKernel k = pick_i2s_kernel(K, &lpr);
+    const uint32_t rpi = (uint32_t)I2S_WARPS * (32u / (uint32_t)lpr);
+    const uint32_t G = std::min<uint32_t>((uint32_t)sm_count_for_launch(), rows);
+    p.rows_per_cta = (rows + G - 1) / G;
+    const uint32_t stage_bytes = rpi * (K / 4u);
+    const uint32_t nchunks = (p.rows_per_cta + rpi - 1) / rpi;
+    uint32_t nst = std::max<uint32_t>(1u, I2S_STAGE_BUDGET / stage_bytes);
+    nst = std::min<uint32_t>(nst, (uint32_t)I2S_MAX_STAGES);
+    nst = std::min<uint32_t>(nst, nchunks);
+    p.nstages = nst;
+    const size_t smem = (size_t)nst * stage_bytes;
+    if (smem > (size_t)WL_MAX_DYN_SMEM)
+        return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for one shared-memory stage", K);
+    const uint32_t grid = (rows + p.rows_per_cta - 1) / p.rows_per_cta;
+    WL_CUDA(launch(k, dim3(grid), dim3(I2S_THREADS), smem, s, pdl, p));
+    return WL_OK;
+}
+
+int q6k_launch_cfg(uint32_t n_embd, int bg, uint32_t *nst, size_t *smem) {
+    const uint32_t stride = q6k_row_stride(n_embd / 256u);
+    const size_t chunk = (size_t)Q6K_ROWS_PER_CHUNK * stride;
+    const size_t xs = (size_t)bg * (n_embd + n_embd / 8u) * sizeof(float);
+    const size_t cap = (size_t)WL_MAX_DYN_SMEM;
+    for (uint32_t n = Q6K_STAGES; n >= 2; --n) {
+        if (n * chunk + xs <= cap) {
+            *nst = n;
+            *smem = n * chunk + xs;
+            return WL_OK;
+        }
+    }
+    return fail(WL_ERR_INVALID_ARGUMENT, "embedding_length %u too large for the Q6_K lm-head",
+                n_embd);
+}
+
+int launch_q6k(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, const float *hidden,
+               uint32_t batch, float *logits, uint32_t *ids, void *scratch, cudaStream_t s,
+               bool pdl) {
+    if (batch == 0 || vocab == 0) return WL_OK;
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    unsigned long long *slots = reinterpret_cast<unsigned long long *>(scratch);
+    uint32_t *counter = reinterpret_cast<uint32_t *>(slots + batch);
+    const uint32_t G = std::min<uint32_t>((uint32_t)sm_count_for_launch(), vocab);
+    Q6kParams p = {};
+    p.packed = packed;
+    p.n_embd = n_embd;
+    p.vocab = vocab;
+    p.nb = n_embd / 256u;
+    p.row_stride = q6k_row_stride(p.nb);
+    p.rows_per_cta = (vocab + G - 1) / G;
+    p.counter = counter;
+    p.status = status;
+    const uint32_t grid = (vocab + p.rows_per_cta - 1) / p.rows_per_cta;
+    for (uint32_t b0 = 0; b0 < batch;) {
+        const int bg = (batch - b0 >= 4) ? 4 : 1;
+        uint32_t nst;
+        size_t smem;
+        int rc = q6k_launch_cfg(n_embd, bg, &nst, &smem);
+        if (rc) return rc;
+        p.nstages = nst;
+        p.hidden = hidden + (size_t)b0 * n_embd;
+        p.logits = logits ? logits + (size_t)b0 * vocab : nullptr;
+        p.ids = ids ? ids + b0 : nullptr;
+        p.slots = slots + b0;
+        if (bg == 4) {
+            WL_CUDA(launch(q6k_lmhead_kernel<4>, dim3(grid), dim3(Q6K_THREADS), smem, s, pdl, p));
+        } else {
+            WL_CUDA(launch(q6k_lmhead_kernel<1>, dim3(grid), dim3(Q6K_THREADS), smem, s, pdl, p));
+        }
+        b0 += (uint32_t)bg;
+    }
+    return WL_OK;
+}
+
+int launch_q8(const uint8_t *packed, uint32_t K, uint32_t N, const float *x, float *y,
+              cudaStream_t s, bool pdl) {
+    if (N == 0) return WL_OK;
+    const uint32_t nb = K / 32u;
+    const uint32_t R = nb >= (uint32_t)Q8_THREADS ? 1u : (uint32_t)Q8_THREADS / nb;
+    const size_t smem = ((size_t)K + K / 8u + (size_t)R * nb) * sizeof(float);
+    if (smem > (size_t)WL_MAX_DYN_SMEM)
+        return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for the Q8_0 kernel", K);
+    const uint32_t tiles = (N + R - 1) / R;
+    const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)sm_count_for_launch() * 4u);
+    WL_CUDA(launch(q8_0_matvec_kernel, dim3(grid), dim3(Q8_THREADS), smem, s, pdl, packed, K, N, x,
+                   y));
+    return WL_OK;
+}
+
+// ------------------------------------------------------------------ validation
+// bitlinear_sse2.rs:129-177 + tensor.rs:278-309 (the x86 dispatch target).
+int validate_i2s(const wl_tensor_view *w, size_t input_len, size_t output_len, bool check_io,
+                 uint32_t *in_dim, uint32_t *out_dim, float *scale) {
+    if (!w) return fail(WL_ERR_INVALID_ARGUMENT, "weight is NULL");
+    if (w->ggml_type != WL_GGML_I2_S) return fail_type(w->ggml_type);
+    if (w->n_dims != 2 || !w->shape)
+        return fail(WL_ERR_GGUF_PARSE, "bitlinear_i2s_matvec_f32: weight \"%s\" is not 2-D",
+                    tname(w));
+    const uint64_t K = w->shape[0], N = w->shape[1];
+    if (check_io && input_len != K)
+        return fail(WL_ERR_GGUF_PARSE, "bitlinear_i2s_matvec_f32: input.len()=%zu != in_dim=%llu",
+                    input_len, (unsigned long long)K);
+    if (check_io && output_len != N)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "bitlinear_i2s_matvec_f32: output.len()=%zu != out_dim=%llu", output_len,
+                    (unsigned long long)N);
+    if (K == 0 || K % WL_I2S_ELEMENTS_PER_BLOCK != 0)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "bitlinear_i2s_matvec_f32: in_dim %llu is not a positive multiple of 128",
+                    (unsigned long long)K);
+    if (K > WL_I2S_MAX_IN_DIM)
+        return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %llu exceeds WL_I2S_MAX_IN_DIM (%u)",
+                    (unsigned long long)K, WL_I2S_MAX_IN_DIM);
+    if (N > 0xFFFFFFFFull / 2)
+        return fail(WL_ERR_INVALID_ARGUMENT, "out_dim %llu too large", (unsigned long long)N);
+    const uint64_t expected = K / 4 * N;
+    if (!w->data && expected > 0) return fail(WL_ERR_INVALID_ARGUMENT, "weight data is NULL");
+    if (w->data_len < expected)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "bitlinear_i2s_matvec_f32: weight data.len()=%zu < %llu (in_dim/4 x out_dim)",
+                    w->data_len, (unsigned long long)expected);
+    if (!w->scale_data)
+        return fail(WL_ERR_GGUF_PARSE, "i2s_scale: tensor \"%s\" has no scale_data set", tname(w));
+    if (w->scale_len < 4)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "i2s_scale: scale_data for \"%s\" too short (%zu bytes, need >= 4)", tname(w),
+                    w->scale_len);
+    float s;
+    memcpy(&s, w->scale_data, 4);
+    if (!std::isfinite(s))
+        return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale (%g) for tensor \"%s\"", s,
+                    tname(w));
+    *in_dim = (uint32_t)K;
+    *out_dim = (uint32_t)N;
+    *scale = s;
+    return WL_OK;
+}
+
+// Row byte length for the quantized lm-head / linear arms
+// (tensor.rs q6k_expected_byte_len / q8_0_expected_byte_len).
+int row_bytes_for(uint32_t type, uint64_t row_elems, uint64_t *row_bytes) {
+    if (type == WL_GGML_Q6_K) {
+        if (row_elems % WL_Q6K_ELEMENTS_PER_BLOCK)
+            return fail(WL_ERR_GGUF_PARSE, "Q6_K row length %llu is not a multiple of QK_K=256",
+                        (unsigned long long)row_elems);
+        *row_bytes = row_elems / WL_Q6K_ELEMENTS_PER_BLOCK * WL_Q6K_BYTES_PER_BLOCK;
+        return WL_OK;
+    }
+    if (type == WL_GGML_Q8_0) {
+        if (row_elems % WL_Q8_0_ELEMENTS_PER_BLOCK)
+            return fail(WL_ERR_GGUF_PARSE, "Q8_0 row length %llu is not a multiple of QK8_0=32",
+                        (unsigned long long)row_elems);
+        *row_bytes = row_elems / WL_Q8_0_ELEMENTS_PER_BLOCK * WL_Q8_0_BYTES_PER_BLOCK;
+        return WL_OK;
+    }
+    return fail_type(type);
+}
+
+float h2f(uint16_t h) {
+    const uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0x1F) bits = (sign << 31) | (0xFFu << 23) | (man << 13);
+    else if (exp == 0) return (sign ? -1.0f : 1.0f) * (float)man * (1.0f / 16777216.0f);
+    else bits = (sign << 31) | ((exp + 112u) << 23) | (man << 13);
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+// ------------------------------------------------------------------ weight cache
+int get_weight(Ctx &c, const wl_tensor_view *w, uint64_t in_dim, uint64_t out_dim,
+               size_t used_bytes, CachedWeight **out) {
+    CacheKey key{w->data, w->data_len, w->ggml_type, in_dim, out_dim};
+    auto it = c.cache.find(key);
+    if (it != c.cache.end()) {
+        *out = &it->second;
+        return WL_OK;
+    }
+    CachedWeight cw;
+    if (w->ggml_type == WL_GGML_I2_S) {
+        cw.bytes = used_bytes;
+        WL_CUDA(cudaMalloc(&cw.dptr, std::max<size_t>(cw.bytes, 16)));
+        if (cw.bytes) WL_CUDA(cudaMemcpy(cw.dptr, w->data, cw.bytes, cudaMemcpyHostToDevice));
+    } else if (w->ggml_type == WL_GGML_Q6_K || w->ggml_type == WL_GGML_Q8_0) {
+        const bool q6 = w->ggml_type == WL_GGML_Q6_K;
+        cw.bytes = q6 ? wl_q6k_packed_bytes((uint32_t)in_dim, (uint32_t)out_dim)
+                      : wl_q8_0_packed_bytes((uint32_t)in_dim, (uint32_t)out_dim);
+        if (!q6) {
+            const size_t nblk = used_bytes / WL_Q8_0_BYTES_PER_BLOCK;
+            for (size_t b = 0; b < nblk; ++b) {
+                uint16_t h;
+                memcpy(&h, w->data + b * WL_Q8_0_BYTES_PER_BLOCK, 2);
+                if (!std::isfinite(h2f(h))) {
+                    cw.bad_scale = true;
+                    break;
+                }
+            }
+        }
+        void *raw = nullptr;
+        WL_CUDA(cudaMalloc(&cw.dptr, std::max<size_t>(cw.bytes, 16)));
+        if (used_bytes) {
+            WL_CUDA(cudaMalloc(&raw, used_bytes));
+            WL_CUDA(cudaMemcpy(raw, w->data, used_bytes, cudaMemcpyHostToDevice));
+            int rc = q6 ? wl_dev_q6k_repack((const uint8_t *)raw, (uint32_t)in_dim,
+                                            (uint32_t)out_dim, (uint8_t *)cw.dptr, c.stream)
+                        : wl_dev_q8_0_repack((const uint8_t *)raw, (uint32_t)in_dim,
+                                             (uint32_t)out_dim, (uint8_t *)cw.dptr, c.stream);
+            cudaError_t e = cudaStreamSynchronize(c.stream);
+            cudaFree(raw);
+            if (rc) return rc;
+            if (e != cudaSuccess) return fail(WL_ERR_CUDA, "repack: %s", cudaGetErrorString(e));
+        }
+    } else {
+        return fail_type(w->ggml_type);
+    }
+    auto res = c.cache.emplace(key, cw);
+    *out = &res.first->second;
+    return WL_OK;
+}
+
+// Copy the library's device status word back with the results of a call;
+// report a device-side timeout as an error.
+int finish_call(Ctx &c) {
+    cudaError_t e = cudaStreamSynchronize(c.stream);
+    if (e != cudaSuccess) return fail(WL_ERR_CUDA, "kernel execution: %s", cudaGetErrorString(e));
+    if (*c.h_status) {
+        const uint32_t f = *c.h_status;
+        *c.h_status = 0;
+        cudaMemset(c.d_status, 0, 4);
+        return fail(WL_ERR_DEVICE_TIMEOUT, "a device-side wait timed out (flags 0x%x)", f);
+    }
+    return WL_OK;
+}
+
+int stage_status(Ctx &c) {
+    WL_CUDA(cudaMemcpyAsync(c.h_status, c.d_status, 4, cudaMemcpyDeviceToHost, c.stream));
+    return WL_OK;
+}
+
+int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input_len,
+                  float *output, size_t output_len, size_t m, int32_t *acc_out,
+                  float *act_scale_out, int8_t *act_q_out) {
+    uint32_t K = 0, N = 0;
+    float w_scale = 0.f;
+    int rc = validate_i2s(weight, input_len, output_len, m == 1, &K, &N, &w_scale);
+    if (rc) return rc;
+    if (m == 0 || N == 0) return WL_OK;
+    if ((!input || !output)) return fail(WL_ERR_INVALID_ARGUMENT, "input/output is NULL");
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    if ((rc = ensure_init(c))) return rc;
+    CachedWeight *cw = nullptr;
+    if ((rc = get_weight(c, weight, K, N, (size_t)K / 4 * N, &cw))) return rc;
+    const size_t xin = m * (size_t)K * 4, yout = m * (size_t)N * 4;
+    if ((rc = grow(c.x, xin)) || (rc = grow(c.y, yout)) || (rc = grow(c.q, m * (size_t)K)) ||
+        (rc = grow(c.scale, m * 4)) || (rc = grow(c.acc, m * (size_t)N * 4)))
+        return rc;
+    if ((rc = grow_pinned(c, xin + 2 * yout + m * (size_t)K + m * 4 + 64))) return rc;
+    uint8_t *pin = (uint8_t *)c.pinned;
+    memcpy(pin, input, xin);
+    WL_CUDA(cudaMemcpyAsync(c.x.p, pin, xin, cudaMemcpyHostToDevice, c.stream));
+    if ((rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m, (int8_t *)c.q.p,
+                              (float *)c.scale.p, c.stream, false)))
+        return rc;
+    for (size_t t = 0; t < m; ++t) {
+        wl_i2s_dev_weight dw = {(const uint8_t *)cw->dptr, w_scale, N,
+                                (float *)c.y.p + t * N, (int32_t *)c.acc.p + t * N};
+        if ((rc = launch_i2s(&dw, 1, K, (const int8_t *)c.q.p + t * K,
+                             (const float *)c.scale.p + t, c.stream, true)))
+            return rc;
+    }
+    uint8_t *py = pin + xin, *pacc = py + yout, *pq = pacc + yout, *ps = pq + m * (size_t)K;
+    WL_CUDA(cudaMemcpyAsync(py, c.y.p, yout, cudaMemcpyDeviceToHost, c.stream));
+    if (acc_out) WL_CUDA(cudaMemcpyAsync(pacc, c.acc.p, yout, cudaMemcpyDeviceToHost, c.stream));
+    if (act_q_out) WL_CUDA(cudaMemcpyAsync(pq, c.q.p, m * (size_t)K, cudaMemcpyDeviceToHost, c.stream));
+    if (act_scale_out) WL_CUDA(cudaMemcpyAsync(ps, c.scale.p, m * 4, cudaMemcpyDeviceToHost, c.stream));
+    if ((rc = stage_status(c))) return rc;
+    if ((rc = finish_call(c))) return rc;
+    memcpy(output, py, yout);
+    if (acc_out) memcpy(acc_out, pacc, yout);
+    if (act_q_out) memcpy(act_q_out, pq, m * (size_t)K);
+    if (act_scale_out) memcpy(act_scale_out, ps, m * 4);
+    return WL_OK;
+}
+
+// lm_head.rs:35-85 validation for the Q6_K / Q8_0 arms.
+int validate_lm_head(const float *hidden, size_t hidden_len, const wl_tensor_view *t,
+                     uint32_t n_embd, uint32_t vocab, uint64_t *row_bytes) {
+    if (!t) return fail(WL_ERR_INVALID_ARGUMENT, "token_embd is NULL");
+    const uint32_t ty = t->ggml_type;
+    if (ty != WL_GGML_F16 && ty != WL_GGML_Q4_0 && ty != WL_GGML_Q4_K && ty != WL_GGML_Q6_K &&
+        ty != WL_GGML_Q8_0)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "compute_logits: token_embd is raw type %u, expected F16, Q4_0, Q4_K, Q6_K, "
+                    "or Q8_0",
+                    ty);
+    if (t->n_dims != 2 || !t->shape || t->shape[0] != n_embd || t->shape[1] != vocab)
+        return fail(WL_ERR_GGUF_PARSE, "compute_logits: token_embd shape != [%u, %u]", n_embd,
+                    vocab);
+    if (hidden_len != n_embd)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "compute_logits: final_hidden.len()=%zu != embedding_length=%u", hidden_len,
+                    n_embd);
+    if (ty != WL_GGML_Q6_K && ty != WL_GGML_Q8_0)
+        return fail(WL_ERR_NOT_IMPLEMENTED,
+                    "compute_logits: raw type %u rows are not on the B200 path", ty);
+    int rc = row_bytes_for(ty, n_embd, row_bytes);
+    if (rc) return rc;
+    if (t->data_len != *row_bytes * vocab)
+        return fail(WL_ERR_GGUF_PARSE, "compute_logits: token_embd.data.len()=%zu != expected %llu",
+                    t->data_len, (unsigned long long)(*row_bytes * vocab));
+    if (!t->data && t->data_len) return fail(WL_ERR_INVALID_ARGUMENT, "token_embd data is NULL");
+    if (!hidden && hidden_len) return fail(WL_ERR_INVALID_ARGUMENT, "final_hidden is NULL");
+    return WL_OK;
+}
+
+// Shared by compute_logits / lm_head_greedy / the quantized linear arms.
+int rows_host_call(const wl_tensor_view *t, uint32_t n_embd, uint32_t vocab, uint64_t row_bytes,
+                   const float *hidden, size_t batch, float *logits, uint32_t *ids) {
+    if (batch == 0 || vocab == 0) return WL_OK;
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    int rc = ensure_init(c);
+    if (rc) return rc;
+    CachedWeight *cw = nullptr;
+    if ((rc = get_weight(c, t, n_embd, vocab, (size_t)(row_bytes * vocab), &cw))) return rc;
+    if (cw->bad_scale) return fail(WL_ERR_GGUF_PARSE, "Q8_0 block has a non-finite scale");
+    const size_t xin = batch * (size_t)n_embd * 4, lout = batch * (size_t)vocab * 4;
+    if ((rc = grow(c.x, xin)) || (rc = grow(c.y, lout)) || (rc = grow(c.ids, batch * 4)) ||
+        (rc = grow(c.scratch, wl_q6k_scratch_bytes((uint32_t)batch))))
+        return rc;
+    if ((rc = grow_pinned(c, xin + lout + batch * 4 + 64))) return rc;
+    uint8_t *pin = (uint8_t *)c.pinned;
+    memcpy(pin, hidden, xin);
+    WL_CUDA(cudaMemcpyAsync(c.x.p, pin, xin, cudaMemcpyHostToDevice, c.stream));
+    float *dlog = logits ? (float *)c.y.p : nullptr;
+    if (t->ggml_type == WL_GGML_Q6_K) {
+        rc = launch_q6k((const uint8_t *)cw->dptr, n_embd, vocab, (const float *)c.x.p,
+                        (uint32_t)batch, dlog, ids ? (uint32_t *)c.ids.p : nullptr, c.scratch.p,
+                        c.stream, false);
+        if (rc) return rc;
+    } else {
+        for (size_t b = 0; b < batch; ++b) {
+            rc = launch_q8((const uint8_t *)cw->dptr, n_embd, vocab,
+                           (const float *)c.x.p + b * n_embd, (float *)c.y.p + b * vocab,
+                           c.stream, false);
+            if (rc) return rc;
+            if (ids) {
+                auto *slot = (unsigned long long *)c.scratch.p;
+                WL_CUDA(launch(argmax_kernel, dim3(std::min<uint32_t>(vocab / ARGMAX_THREADS + 1, 148)),
+                               dim3(ARGMAX_THREADS), 0, c.stream, true,
+                               (const float *)c.y.p + b * vocab, vocab, slot,
+                               (uint32_t *)(slot + 1), (uint32_t *)c.ids.p + b));
+            }
+        }
+        dlog = logits ? (float *)c.y.p : nullptr;
+    }
+    uint8_t *pl = pin + xin, *pid = pl + lout;
+    if (dlog) WL_CUDA(cudaMemcpyAsync(pl, dlog, lout, cudaMemcpyDeviceToHost, c.stream));
+    if (ids) WL_CUDA(cudaMemcpyAsync(pid, c.ids.p, batch * 4, cudaMemcpyDeviceToHost, c.stream));
+    if ((rc = stage_status(c))) return rc;
+    if ((rc = finish_call(c))) return rc;
+    if (logits) memcpy(logits, pl, lout);
+    if (ids) memcpy(ids, pid, batch * 4);
+    return WL_OK;
+}
+
+}  // namespace
+
+// ===================================================================== C ABI
+extern "C" {
+
+const char *wl_version(void) { return "willamette_b200 0.1.0 (sm_100a)"; }
+
+const char *wl_last_error(void) { return g_last_error.c_str(); }
+
+uint32_t wl_last_error_tensor_type(void) { return g_last_type; }
+
+int wl_init(int device) {
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    if (c.inited && c.device != device)
+        return fail(WL_ERR_INVALID_ARGUMENT, "already initialised on device %d", c.device);
+    return init_locked(c, device);
+}
+
+int wl_release_weights(void) {
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    for (auto &kv : c.cache) cudaFree(kv.second.dptr);
+    c.cache.clear();
+    return WL_OK;
+}
+
+int wl_device_status(uint32_t *flags) {
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    int rc = ensure_init(c);
+    if (rc) return rc;
+    uint32_t f = 0;
+    WL_CUDA(cudaMemcpy(&f, c.d_status, 4, cudaMemcpyDeviceToHost));
+    WL_CUDA(cudaMemset(c.d_status, 0, 4));
+    if (flags) *flags = f;
+    return WL_OK;
+}
+
+int wl_bitlinear_i2s_matvec_f32(const wl_tensor_view *weight, const float *input,
+                                size_t input_len, float *output, size_t output_len) {
+    return i2s_host_call(weight, input, input_len, output, output_len, 1, nullptr, nullptr,
+                         nullptr);
+}
+
+int wl_bitlinear_i2s_matvec_f32_dbg(const wl_tensor_view *weight, const float *input,
+                                    size_t input_len, float *output, size_t output_len,
+                                    int32_t *acc_out, float *act_scale_out, int8_t *act_q_out) {
+    return i2s_host_call(weight, input, input_len, output, output_len, 1, acc_out, act_scale_out,
+                         act_q_out);
+}
+
+int wl_bitlinear_i2s_gemm_f32(const wl_tensor_view *weight, const float *input, size_t m,
+                              float *output, int32_t *acc_out) {
+    return i2s_host_call(weight, input, 0, output, 0, m, acc_out, nullptr, nullptr);
+}
+
+int wl_linear_matvec_f32(const wl_tensor_view *weight, const float *input, size_t input_len,
+                         float *output, size_t output_len) {
+    if (!weight) return fail(WL_ERR_INVALID_ARGUMENT, "weight is NULL");
+    const uint32_t ty = weight->ggml_type;
+    if (ty == WL_GGML_I2_S)
+        return wl_bitlinear_i2s_matvec_f32(weight, input, input_len, output, output_len);
+    if (ty == WL_GGML_F16 || ty == WL_GGML_Q4_0 || ty == WL_GGML_Q4_K)
+        return fail(WL_ERR_NOT_IMPLEMENTED, "linear_matvec_f32: raw type %u is not on the B200 path",
+                    ty);
+    if (ty != WL_GGML_Q6_K && ty != WL_GGML_Q8_0) return fail_type(ty);
+    // quantized_matvec_f32 / q8_0_matvec_f32 validation (linear.rs:59-114, :171-213).
+    const char *nm = ty == WL_GGML_Q6_K ? "Q6_K" : "Q8_0";
+    if (weight->n_dims != 2 || !weight->shape)
+        return fail(WL_ERR_GGUF_PARSE, "%s linear \"%s\": expected 2 dimensions", nm,
+                    tname(weight));
+    const uint64_t K = weight->shape[0], N = weight->shape[1];
+    if (input_len != K || output_len != N)
+        return fail(WL_ERR_GGUF_PARSE, "%s linear \"%s\": input/output lengths %zu/%zu != %llu/%llu",
+                    nm, tname(weight), input_len, output_len, (unsigned long long)K,
+                    (unsigned long long)N);
+    uint64_t row_bytes = 0;
+    if (K != 0) {
+        int rc = row_bytes_for(ty, K, &row_bytes);
+        if (rc) return rc;
+    }
+    if (weight->data_len != row_bytes * N)
+        return fail(WL_ERR_GGUF_PARSE, "%s linear \"%s\": data length %zu != expected %llu", nm,
+                    tname(weight), weight->data_len, (unsigned long long)(row_bytes * N));
+    if (N == 0) return WL_OK;
+    if (K == 0) {
+        for (uint64_t i = 0; i < N; ++i) output[i] = 0.0f;
+        return WL_OK;
+    }
+    if (K > 0xFFFFFFFFull || N > 0xFFFFFFFFull)
+        return fail(WL_ERR_INVALID_ARGUMENT, "tensor too large");
+    return rows_host_call(weight, (uint32_t)K, (uint32_t)N, row_bytes, input, 1, output, nullptr);
+}
+
+int wl_compute_logits(const float *final_hidden, size_t hidden_len,
+                      const wl_tensor_view *token_embd, uint32_t embedding_length,
+                      uint32_t vocab_size, float *logits, size_t logits_len) {
+    uint64_t row_bytes = 0;
+    int rc = validate_lm_head(final_hidden, hidden_len, token_embd, embedding_length, vocab_size,
+                              &row_bytes);
+    if (rc) return rc;
+    if (logits_len != vocab_size)
+        return fail(WL_ERR_INVALID_ARGUMENT, "logits_len %zu != vocab_size %u", logits_len,
+                    vocab_size);
+    if (embedding_length == 0) {
+        for (uint32_t v = 0; v < vocab_size; ++v) logits[v] = 0.0f;
+        return WL_OK;
+    }
+    return rows_host_call(token_embd, embedding_length, vocab_size, row_bytes, final_hidden, 1,
+                          logits, nullptr);
+}
+
+int wl_argmax(const float *logits, size_t len, int64_t *out_id) {
+    if (!out_id) return fail(WL_ERR_INVALID_ARGUMENT, "out_id is NULL");
+    if (len == 0) {
+        *out_id = -1;
+        return WL_OK;
+    }
+    if (!logits) return fail(WL_ERR_INVALID_ARGUMENT, "logits is NULL");
+    if (len > 0xFFFFFFFEull) return fail(WL_ERR_INVALID_ARGUMENT, "logits too long");
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    int rc = ensure_init(c);
+    if (rc) return rc;
+    if ((rc = grow(c.x, len * 4)) || (rc = grow(c.ids, 16)) ||
+        (rc = grow(c.scratch, wl_q6k_scratch_bytes(1))) || (rc = grow_pinned(c, len * 4 + 64)))
+        return rc;
+    memcpy(c.pinned, logits, len * 4);
+    WL_CUDA(cudaMemcpyAsync(c.x.p, c.pinned, len * 4, cudaMemcpyHostToDevice, c.stream));
+    auto *slot = (unsigned long long *)c.scratch.p;
+    const uint32_t n = (uint32_t)len;
+    const uint32_t grid = std::min<uint32_t>((n + ARGMAX_THREADS - 1) / ARGMAX_THREADS,
+                                             (uint32_t)c.sm_count * 2u);
+    WL_CUDA(launch(argmax_kernel, dim3(grid), dim3(ARGMAX_THREADS), 0, c.stream, false,
+                   (const float *)c.x.p, n, slot, (uint32_t *)(slot + 1), (uint32_t *)c.ids.p));
+    uint32_t *pid = (uint32_t *)((uint8_t *)c.pinned + len * 4);
+    WL_CUDA(cudaMemcpyAsync(pid, c.ids.p, 4, cudaMemcpyDeviceToHost, c.stream));
+    if ((rc = stage_status(c))) return rc;
+    if ((rc = finish_call(c))) return rc;
+    *out_id = (int64_t)*pid;
+    return WL_OK;
+}
+
+int wl_lm_head_greedy(const float *hidden, size_t batch, const wl_tensor_view *token_embd,
+                      uint32_t embedding_length, uint32_t vocab_size, uint32_t *token_ids,
+                      float *logits) {
+    uint64_t row_bytes = 0;
+    int rc = validate_lm_head(hidden, embedding_length, token_embd, embedding_length, vocab_size,
+                              &row_bytes);
+    if (rc) return rc;
+    if (!token_ids && batch) return fail(WL_ERR_INVALID_ARGUMENT, "token_ids is NULL");
+    if (vocab_size == 0) return fail(WL_ERR_INVALID_ARGUMENT, "vocab_size is 0 (argmax of nothing)");
+    if (batch > 65535) return fail(WL_ERR_INVALID_ARGUMENT, "batch %zu > 65535", batch);
+    if (embedding_length == 0) {
+        for (size_t b = 0; b < batch; ++b) token_ids[b] = 0;
+        if (logits)
+            for (size_t i = 0; i < batch * (size_t)vocab_size; ++i) logits[i] = 0.0f;
+        return WL_OK;
+    }
+    return rows_host_call(token_embd, embedding_length, vocab_size, row_bytes, hidden, batch,
+                          logits, token_ids);
+}
+
+int wl_dev_quantize_absmax_i8(const float *x, uint32_t n, uint32_t m, int8_t *q, float *act_scale,
+                              void *stream) {
+    if (n % 4 != 0) return fail(WL_ERR_INVALID_ARGUMENT, "n must be a multiple of 4");
+    if (!aligned16(x) || !aligned16(q)) return fail(WL_ERR_INVALID_ARGUMENT, "x/q not 16-byte aligned");
+    if (!status_ptr()) return WL_ERR_NO_DEVICE;
+    return launch_quantize(x, n, m, q, act_scale, (cudaStream_t)stream, true);
+}
+
+int wl_dev_i2s_matvec(const wl_i2s_dev_weight *weights, uint32_t n_weights, uint32_t in_dim,
+                      const int8_t *q, const float *act_scale, void *stream) {
+    if (!weights || n_weights == 0 || n_weights > WL_I2S_MAX_FUSED)
+        return fail(WL_ERR_INVALID_ARGUMENT, "n_weights must be 1..%d", WL_I2S_MAX_FUSED);
+    if (in_dim == 0 || in_dim % 128 || in_dim > WL_I2S_MAX_IN_DIM)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128 <= %u", in_dim,
+                    WL_I2S_MAX_IN_DIM);
+    if (!aligned16(q)) return fail(WL_ERR_INVALID_ARGUMENT, "q not 16-byte aligned");
+    uint64_t rows = 0;
+    for (uint32_t j = 0; j < n_weights; ++j) {
+        if (!aligned16(weights[j].packed))
+            return fail(WL_ERR_INVALID_ARGUMENT, "weight %u not 16-byte aligned", j);
+        rows += weights[j].out_dim;
+    }
+    if (rows > 0x7FFFFFFFull) return fail(WL_ERR_INVALID_ARGUMENT, "too many rows");
+    return launch_i2s(weights, n_weights, in_dim, q, act_scale, (cudaStream_t)stream, true);
+}
+
+int wl_dev_i2s_matvec_f32(const uint8_t *packed, float w_scale, uint32_t in_dim,
+                          uint32_t out_dim, const float *x, float *y, int8_t *q_scratch,
+                          float *scale_scratch, void *stream) {
+    if (in_dim == 0 || in_dim % 128 || in_dim > WL_I2S_MAX_IN_DIM)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128 <= %u", in_dim,
+                    WL_I2S_MAX_IN_DIM);
+    if (!std::isfinite(w_scale))
+        return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale (%g)", w_scale);
+    int rc = wl_dev_quantize_absmax_i8(x, in_dim, 1, q_scratch, scale_scratch, stream);
+    if (rc) return rc;
+    wl_i2s_dev_weight w = {packed, w_scale, out_dim, y, nullptr};
+    return wl_dev_i2s_matvec(&w, 1, in_dim, q_scratch, scale_scratch, stream);
+}
+
+size_t wl_q6k_packed_bytes(uint32_t n_embd, uint32_t vocab) {
+    return (size_t)q6k_row_stride(n_embd / 256u) * vocab;
+}
+
+int wl_dev_q6k_repack(const uint8_t *raw, uint32_t n_embd, uint32_t vocab, uint8_t *packed,
+                      void *stream) {
+    if (n_embd == 0 || n_embd % 256) return fail(WL_ERR_GGUF_PARSE, "Q6_K row length %u", n_embd);
+    const size_t total = (size_t)vocab * (n_embd / 256u);
+    if (total == 0) return WL_OK;
+    const uint32_t grid = (uint32_t)std::min<size_t>((total + 255) / 256, 4096);
+    q6k_repack_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(raw, n_embd / 256u, vocab, packed);
+    WL_CUDA(cudaGetLastError());
+    return WL_OK;
+}
+
+size_t wl_q6k_scratch_bytes(uint32_t batch) { return (size_t)batch * 8u + 16u; }
+
+int wl_dev_q6k_lm_head(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, const float *hidden,
+                       uint32_t batch, float *logits, uint32_t *ids, void *scratch,
+                       void *stream) {
+    if (n_embd == 0 || n_embd % 256) return fail(WL_ERR_GGUF_PARSE, "Q6_K row length %u", n_embd);
+    if (!aligned16(packed) || !scratch || ((uintptr_t)scratch & 7u))
+        return fail(WL_ERR_INVALID_ARGUMENT, "packed must be 16-byte and scratch 8-byte aligned");
+    return launch_q6k(packed, n_embd, vocab, hidden, batch, logits, ids, scratch,
+                      (cudaStream_t)stream, true);
+}
+
+size_t wl_q8_0_packed_bytes(uint32_t in_dim, uint32_t out_dim) {
+    return (size_t)q8_row_stride(in_dim) * out_dim;
+}
+
+int wl_dev_q8_0_repack(const uint8_t *raw, uint32_t in_dim, uint32_t out_dim, uint8_t *packed,
+                       void *stream) {
+    if (in_dim == 0 || in_dim % 32) return fail(WL_ERR_GGUF_PARSE, "Q8_0 row length %u", in_dim);
+    const size_t total = (size_t)out_dim * (in_dim / 32u);
+    if (total == 0) return WL_OK;
+    const uint32_t grid = (uint32_t)std::min<size_t>((total + 255) / 256, 4096);
+    q8_0_repack_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(raw, in_dim, out_dim, packed);
+    WL_CUDA(cudaGetLastError());
+    return WL_OK;
+}
+
+int wl_dev_q8_0_matvec(const uint8_t *packed, uint32_t in_dim, uint32_t out_dim, const float *x,
+                       float *y, void *stream) {
+    if (in_dim == 0 || in_dim % 32) return fail(WL_ERR_GGUF_PARSE, "Q8_0 row length %u", in_dim);
+    if (!aligned16(packed)) return fail(WL_ERR_INVALID_ARGUMENT, "packed not 16-byte aligned");
+    if (!status_ptr()) return WL_ERR_NO_DEVICE;
+    return launch_q8(packed, in_dim, out_dim, x, y, (cudaStream_t)stream, true);
+}
+
+}  // extern "C"
