@@ -183,8 +183,9 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
 
         for (uint32_t c = group; c < nchunks; c += 2) {
             const uint32_t st = c % nst;
-            if (!mbar_wait(&full_bar[st], (c / nst) & 1u)) {
-                atomicOr(&s_timeout, 1u);
+            // Warp-uniform decision, so a timeout never splits a warp.
+            if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[st], (c / nst) & 1u))) {
+                if (lane == 0) atomicOr(&s_timeout, 1u);
                 break;
             }
             const uint32_t row = r0 + c * Q6K_ROWS_PER_CHUNK + row_local;

@@ -124,7 +124,8 @@ int init_locked(Ctx &c, int device) {
     c.sm_count = prop.multiProcessorCount;
     WL_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
     WL_CUDA(cudaMalloc(&c.d_status, 64));
-    WL_CUDA(cudaMemset(c.d_status, 0, 64));
+    WL_CUDA(cudaMemsetAsync(c.d_status, 0, 64, c.stream));
+    WL_CUDA(cudaStreamSynchronize(c.stream));
     WL_CUDA(cudaMallocHost(&c.h_status, 64));
     int rc = configure_kernels();
     if (rc) return rc;
@@ -147,7 +148,9 @@ int grow(DevBuf &b, size_t bytes) {
     b.cap = 0;
     size_t cap = bytes < 4096 ? 4096 : bytes;
     WL_CUDA(cudaMalloc(&b.p, cap));
-    WL_CUDA(cudaMemset(b.p, 0, cap));
+    // Zero on the library stream so the kernels that follow on it see zeros
+    // (scratch words such as the argmax slots must start at zero).
+    WL_CUDA(cudaMemsetAsync(b.p, 0, cap, ctx().stream));
     b.cap = cap;
     return WL_OK;
 }
@@ -440,7 +443,12 @@ int get_weight(Ctx &c, const wl_tensor_view *w, uint64_t in_dim, uint64_t out_di
     if (w->ggml_type == WL_GGML_I2_S) {
         cw.bytes = used_bytes;
         WL_CUDA(cudaMalloc(&cw.dptr, std::max<size_t>(cw.bytes, 16)));
-        if (cw.bytes) WL_CUDA(cudaMemcpy(cw.dptr, w->data, cw.bytes, cudaMemcpyHostToDevice));
+        // Upload on the library stream: the kernels run on that non-blocking
+        // stream, which does not order with the legacy default stream.
+        if (cw.bytes)
+            WL_CUDA(cudaMemcpyAsync(cw.dptr, w->data, cw.bytes, cudaMemcpyHostToDevice,
+                                    c.stream));
+        WL_CUDA(cudaStreamSynchronize(c.stream));
     } else if (w->ggml_type == WL_GGML_Q6_K || w->ggml_type == WL_GGML_Q8_0) {
         const bool q6 = w->ggml_type == WL_GGML_Q6_K;
         cw.bytes = q6 ? wl_q6k_packed_bytes((uint32_t)in_dim, (uint32_t)out_dim)
@@ -460,7 +468,7 @@ int get_weight(Ctx &c, const wl_tensor_view *w, uint64_t in_dim, uint64_t out_di
         WL_CUDA(cudaMalloc(&cw.dptr, std::max<size_t>(cw.bytes, 16)));
         if (used_bytes) {
             WL_CUDA(cudaMalloc(&raw, used_bytes));
-            WL_CUDA(cudaMemcpy(raw, w->data, used_bytes, cudaMemcpyHostToDevice));
+            WL_CUDA(cudaMemcpyAsync(raw, w->data, used_bytes, cudaMemcpyHostToDevice, c.stream));
             int rc = q6 ? wl_dev_q6k_repack((const uint8_t *)raw, (uint32_t)in_dim,
                                             (uint32_t)out_dim, (uint8_t *)cw.dptr, c.stream)
                         : wl_dev_q8_0_repack((const uint8_t *)raw, (uint32_t)in_dim,
@@ -486,7 +494,8 @@ int finish_call(Ctx &c) {
     if (*c.h_status) {
         const uint32_t f = *c.h_status;
         *c.h_status = 0;
-        cudaMemset(c.d_status, 0, 4);
+        cudaMemsetAsync(c.d_status, 0, 4, c.stream);
+        cudaStreamSynchronize(c.stream);
         return fail(WL_ERR_DEVICE_TIMEOUT, "a device-side wait timed out (flags 0x%x)", f);
     }
     return WL_OK;
@@ -658,8 +667,11 @@ int wl_device_status(uint32_t *flags) {
     int rc = ensure_init(c);
     if (rc) return rc;
     uint32_t f = 0;
+    // Kernels of every stream (library and caller streams) must have finished.
+    WL_CUDA(cudaDeviceSynchronize());
     WL_CUDA(cudaMemcpy(&f, c.d_status, 4, cudaMemcpyDeviceToHost));
     WL_CUDA(cudaMemset(c.d_status, 0, 4));
+    WL_CUDA(cudaDeviceSynchronize());
     if (flags) *flags = f;
     return WL_OK;
 }
