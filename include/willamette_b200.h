@@ -180,6 +180,23 @@ int wl_dev_i2s_matvec_f32(const uint8_t *packed, float w_scale, uint32_t in_dim,
                           uint32_t out_dim, const float *x, float *y, int8_t *q_scratch,
                           float *scale_scratch, void *stream);
 
+/* Same result as wl_dev_i2s_matvec_f32, but the library allocates nothing
+ * and the caller passes no scratch: the int8 activations and their scale live
+ * in a static device array of the library (about 16 KB per GPU, held by every
+ * GPU that loads the library until the process exits).  For callers that
+ * cannot call cudaMalloc -- a serving engine that has already reserved the
+ * device memory for its own pools, or a latency-critical decode loop where
+ * cudaMalloc/cudaFree would synchronise the device.  No counterpart in the
+ * reference (its CPU path needs no device memory).
+ * - in_dim must be <= WL_NOALLOC_MAX_IN_DIM (else WL_ERR_INVALID_ARGUMENT).
+ * - The first call on each device resolves the array's address and sets
+ *   kernel attributes; make that first call before any stream capture.
+ * - All calls share the one array: calls that overlap on the GPU (other
+ *   streams, other host threads) race and must be serialised by the caller. */
+#define WL_NOALLOC_MAX_IN_DIM 16384u
+int wl_dev_i2s_matvec_f32_noalloc(const uint8_t *packed, float w_scale, uint32_t in_dim,
+                                  uint32_t out_dim, const float *x, float *y, void *stream);
+
 /* Q6_K lm-head.  The raw GGUF rows (vocab x n_embd/256 x 210 bytes) are
  * repacked once into the device layout (wl_q6k_packed_bytes bytes). */
 size_t wl_q6k_packed_bytes(uint32_t n_embd, uint32_t vocab);

@@ -75,6 +75,7 @@ PROTOTYPES = {
     "wl_dev_quantize_absmax_i8": ([_vp, _u32, _u32, _vp, _vp, _vp], _i),
     "wl_dev_i2s_matvec": ([C.POINTER(WlI2sDevWeight), _u32, _u32, _vp, _vp, _vp], _i),
     "wl_dev_i2s_matvec_f32": ([_vp, C.c_float, _u32, _u32, _vp, _vp, _vp, _vp, _vp], _i),
+    "wl_dev_i2s_matvec_f32_noalloc": ([_vp, C.c_float, _u32, _u32, _vp, _vp, _vp], _i),
     "wl_q6k_packed_bytes": ([_u32, _u32], _sz),
     "wl_dev_q6k_repack": ([_vp, _u32, _u32, _vp, _vp], _i),
     "wl_q6k_scratch_bytes": ([_u32], _sz),

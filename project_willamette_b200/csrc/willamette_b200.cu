@@ -239,8 +239,20 @@ int launch_quantize(const float *x, uint32_t n, uint32_t m, int8_t *q, float *sc
     return WL_OK;
 }
 
+int launch_i2s_with_status(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K,
+                           const int8_t *q, const float *act_scale, cudaStream_t s, bool pdl,
+                           uint32_t *status);
+
 int launch_i2s(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K, const int8_t *q,
                const float *act_scale, cudaStream_t s, bool pdl) {
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    return launch_i2s_with_status(w, nw, K, q, act_scale, s, pdl, status);
+}
+
+int launch_i2s_with_status(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K,
+                           const int8_t *q, const float *act_scale, cudaStream_t s, bool pdl,
+                           uint32_t *status) {
     I2sMatvecParams p = {};
     uint32_t rows = 0;
     for (uint32_t j = 0; j < nw; ++j) {
@@ -258,8 +270,7 @@ int launch_i2s(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K, const int8_t
     p.total_rows = rows;
     p.q = q;
     p.act_scale = act_scale;
-    p.status = status_ptr();
-    if (!p.status) return WL_ERR_NO_DEVICE;
+    p.status = status;
     int lpr = 32;
     I2sKernel k = pick_i2s_kernel(K, &lpr);
     const uint32_t rpi = (uint32_t)I2S_WARPS * (32u / (uint32_t)lpr);
@@ -636,6 +647,49 @@ int rows_host_call(const wl_tensor_view *t, uint32_t n_embd, uint32_t vocab, uin
 
 }  // namespace
 
+// ------------------------------------------------------- no-allocation variant
+// Scratch of wl_dev_i2s_matvec_f32_noalloc, in static device memory instead of
+// caller- or library-allocated buffers: [0, 4) activation scale (f32),
+// [4, 8) device status word, [256, 256 + WL_NOALLOC_MAX_IN_DIM) the int8
+// activations.  Every GPU that loads this library holds these bytes until the
+// process exits.  In host code the name is only a host-side stand-in; the
+// device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[256 + WL_NOALLOC_MAX_IN_DIM];
+
+namespace {
+
+struct NoAllocDevice {
+    bool ready = false;
+    uint8_t *scratch = nullptr;  // device address of g_noalloc_scratch
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[64];
+
+// Once per device, with that device current: resolve the array's device
+// address and raise the kernels' shared-memory limit.  Allocates nothing.
+int noalloc_setup(uint8_t **scratch) {
+    int dev = 0;
+    WL_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(WL_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    NoAllocDevice &d = g_noalloc_dev[dev];
+    if (!d.ready) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(WL_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) on device %d: %s",
+                        dev, cudaGetErrorString(e));
+        int rc = configure_kernels();
+        if (rc) return rc;
+        d.scratch = static_cast<uint8_t *>(p);
+        d.ready = true;
+    }
+    *scratch = d.scratch;
+    return WL_OK;
+}
+
+}  // namespace
+
 // ===================================================================== C ABI
 extern "C" {
 
@@ -889,6 +943,34 @@ int wl_dev_q8_0_matvec(const uint8_t *packed, uint32_t in_dim, uint32_t out_dim,
     if (!aligned16(packed)) return fail(WL_ERR_INVALID_ARGUMENT, "packed not 16-byte aligned");
     if (!status_ptr()) return WL_ERR_NO_DEVICE;
     return launch_q8(packed, in_dim, out_dim, x, y, (cudaStream_t)stream, true);
+}
+
+int wl_dev_i2s_matvec_f32_noalloc(const uint8_t *packed, float w_scale, uint32_t in_dim,
+                                  uint32_t out_dim, const float *x, float *y, void *stream) {
+    if (in_dim == 0 || in_dim % 128)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128", in_dim);
+    if (in_dim > WL_NOALLOC_MAX_IN_DIM)
+        return fail(WL_ERR_INVALID_ARGUMENT,
+                    "wl_dev_i2s_matvec_f32_noalloc: in_dim %u exceeds the static scratch "
+                    "(WL_NOALLOC_MAX_IN_DIM = %u); use wl_dev_i2s_matvec_f32 with caller "
+                    "buffers",
+                    in_dim, WL_NOALLOC_MAX_IN_DIM);
+    if (!std::isfinite(w_scale))
+        return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale (%g)", w_scale);
+    if (!x || !y || !packed) return fail(WL_ERR_INVALID_ARGUMENT, "NULL pointer");
+    if (!aligned16(x) || !aligned16(packed))
+        return fail(WL_ERR_INVALID_ARGUMENT, "x / packed not 16-byte aligned");
+    if (out_dim == 0) return WL_OK;
+    uint8_t *scratch = nullptr;
+    int rc = noalloc_setup(&scratch);
+    if (rc) return rc;
+    float *act_scale = reinterpret_cast<float *>(scratch);
+    uint32_t *status = reinterpret_cast<uint32_t *>(scratch + 4);
+    int8_t *q = reinterpret_cast<int8_t *>(scratch + 256);
+    cudaStream_t s = (cudaStream_t)stream;
+    if ((rc = launch_quantize(x, in_dim, 1, q, act_scale, s, true))) return rc;
+    wl_i2s_dev_weight w = {packed, w_scale, out_dim, y, nullptr};
+    return launch_i2s_with_status(&w, 1, in_dim, q, act_scale, s, true, status);
 }
 
 }  // extern "C"
