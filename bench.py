@@ -11,8 +11,14 @@ is 4x the 126 MB L2, so no L2 flush is needed between steps.  The metric is
 BASELINE's "I2_S matvec HBM GB/s": algorithmic bytes (packed weights + scale +
 f32 activations in + f32 outputs) per second.
 
-`value` times the device-resident sweep (one CUDA graph per step, kernels
-chained with programmatic dependent launch), CUDA events, max over ranks.
+`value` is the sustained streaming rate (SURVEY's "sustains" reading: back to
+back over distinct weight buffers larger than L2): the 210 matvecs, each with
+its own input, as one persistent launch per step (wl_dev_i2s_stream_run:
+quantise all inputs, then stream every weight once), CUDA events on the
+launching stream, max over ranks.  `decode_chain` times the same 210 matvecs in
+decode order as 120 dependent launches (QKV and gate/up fused; every kernel
+waits for the previous one, quantises its input in-kernel, and prefetches its
+weights before that wait) -- the latency-bound batch-1 decode figure.
 `e2e` runs the same 210 matvecs through the drop-in host-buffer C ABI
 (wl_bitlinear_i2s_matvec_f32, one call per BitLinear as the reference's
 linear_matvec_f32 is called), host->device copy of each input and
@@ -168,86 +174,106 @@ def run_gpu(args) -> None:
     if rc:
         raise RuntimeError(L.wl_last_error().decode())
 
+    def ck(rc):
+        if rc:
+            raise RuntimeError(L.wl_last_error().decode())
+
     rng = np.random.default_rng(SEED + rank)
     layers = make_i2s_weights(torch, dev, rng)
     stream = torch.cuda.Stream(device=dev)
+    found = torch.zeros(1, dtype=torch.int32, device=dev)
 
-    # per-launch device buffers (tiny); outputs distinct per weight
-    plan = []
-    for groups in layers:
-        for in_dim, ws, x in groups:
-            q = torch.empty(in_dim, dtype=torch.int8, device=dev)
-            sc = torch.empty(4, dtype=torch.float32, device=dev)
+    # Per launch group: a fused-input weight array (decode-order chain) and the
+    # same weights as stream ops (persistent streaming launch).
+    groups, sops, outs = [], [], []
+    for lgroups in layers:
+        for in_dim, ws, x in lgroups:
             arr = (_abi.WlI2sDevWeight * len(ws))()
-            ys = []
             for i, (packed, s, n) in enumerate(ws):
+                ck(L.wl_dev_i2s_scan_code3(packed.data_ptr(), packed.numel(), found.data_ptr(),
+                                           stream.cuda_stream))
+                torch.cuda.synchronize()
                 y = torch.empty(n, dtype=torch.float32, device=dev)
-                ys.append(y)
+                outs.append(y)
                 arr[i].packed, arr[i].w_scale, arr[i].out_dim = packed.data_ptr(), s, n
                 arr[i].y, arr[i].acc = y.data_ptr(), None
-            plan.append((in_dim, x, q, sc, arr, len(ws), ys))
+                arr[i].flags = 0 if int(found.item()) else _abi.WL_I2S_NO_CODE3
+                op = _abi.WlI2sStreamOp()
+                op.packed, op.w_scale, op.in_dim, op.out_dim = packed.data_ptr(), s, in_dim, n
+                op.x, op.y, op.acc, op.flags = x.data_ptr(), y.data_ptr(), None, 0
+                sops.append(op)
+            groups.append((in_dim, x, arr, len(ws)))
+    ops_arr = (_abi.WlI2sStreamOp * len(sops))(*sops)
+    plan = C.c_void_p()
+    ck(L.wl_i2s_stream_plan_create(ops_arr, len(sops), C.byref(plan)))
 
-    def step(h: int) -> int:
-        n = 0
-        for in_dim, x, q, sc, arr, nw, _ in plan:
-            rc = L.wl_dev_quantize_absmax_i8(x.data_ptr(), in_dim, 1, q.data_ptr(),
-                                             sc.data_ptr(), h)
-            rc |= L.wl_dev_i2s_matvec(arr, nw, in_dim, q.data_ptr(), sc.data_ptr(), h)
-            if rc:
-                raise RuntimeError(L.wl_last_error().decode())
-            n += 2
-        return n
+    def stream_step(h: int) -> int:
+        ck(L.wl_dev_i2s_stream_run(plan, h))
+        return 2
 
-    launches_per_step = 0
-    with torch.cuda.stream(stream):
-        launches_per_step = step(stream.cuda_stream)  # eager warm-up / first-use paths
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step(torch.cuda.current_stream().cuda_stream)
-        for _ in range(max(args.warmup, 3)):
-            graph.replay()
-        torch.cuda.synchronize()
+    def chain_step(h: int) -> int:
+        for in_dim, x, arr, nw in groups:
+            ck(L.wl_dev_i2s_matvec_fused_f32(arr, nw, in_dim, x.data_ptr(), h))
+        return len(groups)
 
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as clk:
-            e0.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            e1.record(stream)
+    def capture(fn):
+        with torch.cuda.stream(stream):
+            n = fn(stream.cuda_stream)  # eager run: first-use paths
             torch.cuda.synchronize()
-        ms_total = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms_total = float(t.item())
-        torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                fn(torch.cuda.current_stream().cuda_stream)
+        return g, n
 
-        # Isolated per-launch durations of the matvec kernel (no PDL overlap):
-        # events around each launch of one eager step.
-        iso = []
-        for in_dim, x, q, sc, arr, nw, ys in plan:
-            L.wl_dev_quantize_absmax_i8(x.data_ptr(), in_dim, 1, q.data_ptr(), sc.data_ptr(),
-                                        stream.cuda_stream)
+    def timed(g, steps, clocks=None):
+        with torch.cuda.stream(stream):
+            for _ in range(max(args.warmup, 3)):
+                g.replay()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ctx = clocks if clocks is not None else _Null()
+            with ctx:
+                e0.record(stream)
+                for _ in range(steps):
+                    g.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    g_stream, launches_per_step = capture(stream_step)
+    g_chain, chain_launches = capture(chain_step)
+    clk = ClockSampler(local)
+    ms_total = timed(g_stream, args.steps, clk)
+    chain_steps = max(1, args.steps // 4)
+    ms_chain = timed(g_chain, chain_steps)
+
+    # Isolated per-launch duration of the per-op kernel (events around each
+    # launch of one eager decode-order step; no overlap between launches).
+    iso = []
+    with torch.cuda.stream(stream):
+        for in_dim, x, arr, nw in groups:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            L.wl_dev_i2s_matvec(arr, nw, in_dim, q.data_ptr(), sc.data_ptr(), stream.cuda_stream)
+            ck(L.wl_dev_i2s_matvec_fused_f32(arr, nw, in_dim, x.data_ptr(), stream.cuda_stream))
             b.record(stream)
-            iso.append((a, b, sum(algorithmic_bytes(in_dim, ws_n) for ws_n in
-                                  [arr[i].out_dim for i in range(nw)])))
+            iso.append((a, b, sum(algorithmic_bytes(in_dim, arr[i].out_dim) for i in range(nw))))
         torch.cuda.synchronize()
-        iso_ms = sum(a.elapsed_time(b) for a, b, _ in iso)
-        iso_bytes = sum(nb for _, _, nb in iso)
+    iso_ms = sum(a.elapsed_time(b) for a, b, _ in iso)
+    iso_bytes = sum(nb for _, _, nb in iso)
 
     bytes_step = sweep_bytes()
     ms_step = ms_total / args.steps
     value = world * bytes_step / (ms_step * 1e-3) / 1e9
-    matvec_launches = LAYERS * len(GROUPS)
-    avg_launch_s = ms_step * 1e-3 / matvec_launches
-    achieved = (bytes_step / matvec_launches) / avg_launch_s / 1e9
+    achieved = bytes_step / (ms_step * 1e-3) / 1e9  # one stream launch per step
+    ms_chain_step = ms_chain / chain_steps
     pk = peaks()
 
     # ---- lm-head (Q6_K 128256 x 2560, batch 1) timed separately
@@ -274,15 +300,18 @@ def run_gpu(args) -> None:
             "config": {"workload": WORKLOAD, "layers": LAYERS, "d_model": D_MODEL, "d_ff": D_FF,
                        "kv_dim": D_KV, "matvecs_per_step": LAYERS * 7,
                        "bytes_per_step": bytes_step, "batch": 1,
+                       "mode": "sustained: 210 independent matvecs, one persistent launch",
                        "l2": "inputs larger than L2 (521 MB of distinct weights per step)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                         "traffic": TRAFFIC_PER_STEP_BYTES / matvec_launches
-                         if TRAFFIC_PER_STEP_BYTES else None,
-                         "peak_source": pk["source"],
-                         "kernel": "i2s_matvec_kernel",
-                         "isolated_launch_gbs": round(iso_bytes / (iso_ms * 1e-3) / 1e9, 2)},
+                         "traffic": TRAFFIC_PER_STEP_BYTES,
+                         "peak_source": pk["source"], "kernel": "i2s_stream_kernel"},
+            "decode_chain": {
+                "gbs": round(world * bytes_step / (ms_chain_step * 1e-3) / 1e9, 2),
+                "ms_per_step": round(ms_chain_step, 5), "launches_per_step": chain_launches,
+                "note": "decode order: 120 dependent fused quantise+matvec kernels (PDL)",
+                "isolated_launch_gbs": round(iso_bytes / (iso_ms * 1e-3) / 1e9, 2)},
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT,
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "api": "wl_bitlinear_i2s_matvec_f32 (host buffers, one call per BitLinear)"},
@@ -293,10 +322,19 @@ def run_gpu(args) -> None:
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    del graph
+    del g_stream, g_chain
+    L.wl_i2s_stream_plan_destroy(plan)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
 
 
 # Measured DRAM traffic of the sweep per step (ncu, see profiles/); None until

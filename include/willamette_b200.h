@@ -164,15 +164,45 @@ int wl_dev_quantize_absmax_i8(const float *x, uint32_t n, uint32_t m, int8_t *q,
  * input (e.g. Q/K/V or gate/up), one launch: y_i[out_dim_i] =
  * (w_scale_i * act_scale[0]) * acc.  acc_i may be NULL. */
 #define WL_I2S_MAX_FUSED 4
+#define WL_I2S_NO_CODE3 1u /* flags: the weight holds no 0b11 code (wl_dev_i2s_scan_code3) */
 typedef struct wl_i2s_dev_weight {
     const uint8_t *packed; /* out_dim x in_dim/4 bytes, device */
     float w_scale;
     uint32_t out_dim;
     float *y;              /* device, out_dim f32 */
     int32_t *acc;          /* device, out_dim i32, or NULL */
+    uint32_t flags;        /* 0, or WL_I2S_NO_CODE3 (skips the per-row code-3 check) */
 } wl_i2s_dev_weight;
 int wl_dev_i2s_matvec(const wl_i2s_dev_weight *weights, uint32_t n_weights, uint32_t in_dim,
                       const int8_t *q, const float *act_scale, void *stream);
+
+/* As wl_dev_i2s_matvec, but from the f32 input: every CTA quantises x itself
+ * (bitlinear_sse2.rs:285-304, same IEEE steps), so one kernel per BitLinear
+ * (or per fused Q/K/V or gate/up group).  in_dim <= 8192. */
+int wl_dev_i2s_matvec_fused_f32(const wl_i2s_dev_weight *weights, uint32_t n_weights,
+                                uint32_t in_dim, const float *x, void *stream);
+
+/* *found (device u32) = 1 if the packed tensor contains a 0b11 code, else 0. */
+int wl_dev_i2s_scan_code3(const uint8_t *packed, size_t bytes, uint32_t *found, void *stream);
+
+/* Many independent BitLinear matvecs in one persistent launch (sustained HBM
+ * streaming).  Ops sharing an input pointer share one quantisation.  The plan
+ * holds the device-side descriptors and scratch; runs are asynchronous.
+ * in_dim <= 7168 per op. */
+typedef struct wl_i2s_stream_op {
+    const uint8_t *packed; /* device */
+    float w_scale;
+    uint32_t in_dim, out_dim;
+    const float *x;        /* device f32 input */
+    float *y;              /* device f32 output */
+    int32_t *acc;          /* device, or NULL */
+    uint32_t flags;        /* WL_I2S_NO_CODE3 or 0 */
+} wl_i2s_stream_op;
+typedef struct wl_i2s_stream_plan wl_i2s_stream_plan;
+int wl_i2s_stream_plan_create(const wl_i2s_stream_op *ops, uint32_t n_ops,
+                              wl_i2s_stream_plan **plan);
+int wl_dev_i2s_stream_run(wl_i2s_stream_plan *plan, void *stream);
+int wl_i2s_stream_plan_destroy(wl_i2s_stream_plan *plan);
 
 /* Quantise x then matvec (the two kernels chained with programmatic
  * dependent launch).  q_scratch: in_dim int8, scale_scratch: 1 f32. */

@@ -47,6 +47,23 @@ class WlI2sDevWeight(C.Structure):
         ("out_dim", C.c_uint32),
         ("y", C.c_void_p),
         ("acc", C.c_void_p),
+        ("flags", C.c_uint32),
+    ]
+
+
+WL_I2S_NO_CODE3 = 1
+
+
+class WlI2sStreamOp(C.Structure):
+    _fields_ = [
+        ("packed", C.c_void_p),
+        ("w_scale", C.c_float),
+        ("in_dim", C.c_uint32),
+        ("out_dim", C.c_uint32),
+        ("x", C.c_void_p),
+        ("y", C.c_void_p),
+        ("acc", C.c_void_p),
+        ("flags", C.c_uint32),
     ]
 
 
@@ -75,6 +92,11 @@ PROTOTYPES = {
     "wl_dev_quantize_absmax_i8": ([_vp, _u32, _u32, _vp, _vp, _vp], _i),
     "wl_dev_i2s_matvec": ([C.POINTER(WlI2sDevWeight), _u32, _u32, _vp, _vp, _vp], _i),
     "wl_dev_i2s_matvec_f32": ([_vp, C.c_float, _u32, _u32, _vp, _vp, _vp, _vp, _vp], _i),
+    "wl_dev_i2s_matvec_fused_f32": ([C.POINTER(WlI2sDevWeight), _u32, _u32, _vp, _vp], _i),
+    "wl_dev_i2s_scan_code3": ([_vp, _sz, _vp, _vp], _i),
+    "wl_i2s_stream_plan_create": ([C.POINTER(WlI2sStreamOp), _u32, C.POINTER(_vp)], _i),
+    "wl_dev_i2s_stream_run": ([_vp, _vp], _i),
+    "wl_i2s_stream_plan_destroy": ([_vp], _i),
     "wl_dev_i2s_matvec_f32_noalloc": ([_vp, C.c_float, _u32, _u32, _vp, _vp, _vp], _i),
     "wl_q6k_packed_bytes": ([_u32, _u32], _sz),
     "wl_dev_q6k_repack": ([_vp, _u32, _u32, _vp, _vp], _i),

@@ -35,7 +35,8 @@ namespace wl {
 constexpr int I2S_THREADS = 256;
 constexpr int I2S_WARPS = I2S_THREADS / 32;
 constexpr int I2S_MAX_STAGES = 8;
-constexpr uint32_t I2S_STAGE_BUDGET = 96u * 1024u;  // bytes of weight stages per CTA
+constexpr uint32_t I2S_STAGE_BUDGET = 64u * 1024u;  // weight stages per CTA (2 CTAs/SM)
+constexpr uint32_t I2S_FUSE_Q_MAX_K = 8192;         // x (f32) + q (int8) staged in smem
 constexpr int QUANT_THREADS = 512;
 
 struct I2sJob {
@@ -55,8 +56,11 @@ struct I2sMatvecParams {
     uint32_t rows_per_cta;
     uint32_t nstages;
     uint32_t use_pdl;
-    const int8_t *q;        // quantised activations, K bytes, 16-byte aligned
-    const float *act_scale; // 1 f32
+    const int8_t *q;        // quantised activations, K bytes, 16-byte aligned (!FUSE_Q)
+    const float *act_scale; // 1 f32 (!FUSE_Q)
+    const float *x;         // f32 input, K floats, 16-byte aligned (FUSE_Q)
+    int8_t *q_out;          // FUSE_Q: optional copy of the quantised input (CTA 0)
+    float *scale_out;       // FUSE_Q: optional activation scale (CTA 0)
     uint32_t *status;
 };
 
@@ -115,7 +119,128 @@ __global__ void __launch_bounds__(QUANT_THREADS)
 }
 
 // ---------------------------------------------------------------------------
-// Kernel 2 helpers.
+// Row-dot building blocks shared by the per-op and the streaming kernels.
+
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Four accumulators, one per code position in a byte.  Masking without
+// shifting leaves the codes of bits 7:6 / 5:4 / 3:2 / 1:0 scaled by 64 / 16 /
+// 4 / 1, so a6 = 64*sum(c*a) etc.; every term is an exact multiple, so the
+// arithmetic right shifts in i2s_acc_total are exact.  |a6| <= 192*127*K/4
+// stays below 2^31 for K <= 65536.
+struct I2sAcc {
+    int32_t a6, a4, a2, a0;
+};
+
+template <bool C3>
+__device__ __forceinline__ void i2s_word(uint32_t w, uint32_t x0, uint32_t x1, uint32_t x2,
+                                         uint32_t x3, I2sAcc &acc, uint32_t &c3) {
+    acc.a6 = dp4a_us(w & 0xC0C0C0C0u, x0, acc.a6);
+    acc.a4 = dp4a_us(w & 0x30303030u, x1, acc.a4);
+    acc.a2 = dp4a_us(w & 0x0C0C0C0Cu, x2, acc.a2);
+    acc.a0 = dp4a_us(w & 0x03030303u, x3, acc.a0);
+    if constexpr (C3) c3 |= w & (w >> 1);
+}
+
+// One 16-byte weight slot (64 codes) against its four activation vectors.
+template <bool C3>
+__device__ __forceinline__ void i2s_slot(const uint4 &wv, const uint4 (&a)[4], I2sAcc &acc,
+                                         uint32_t &c3) {
+    i2s_word<C3>(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, acc, c3);
+    i2s_word<C3>(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, acc, c3);
+    i2s_word<C3>(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, acc, c3);
+    i2s_word<C3>(wv.w, a[0].w, a[1].w, a[2].w, a[3].w, acc, c3);
+}
+
+__device__ __forceinline__ int32_t i2s_acc_total(const I2sAcc &acc) {
+    return (acc.a6 >> 6) + (acc.a4 >> 4) + (acc.a2 >> 2) + acc.a0;
+}
+
+// Sum of the activations at code-3 positions of one word (rare path; the
+// reference quantiser never emits code 3, but the reference maps it to 0).
+__device__ __forceinline__ int32_t i2s_word_c3(uint32_t w, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, int32_t acc) {
+    const uint32_t m = w & (w >> 1) & 0x55555555u;
+    acc = __dp4a((int)((m >> 6) & 0x01010101u), (int)a0, acc);
+    acc = __dp4a((int)((m >> 4) & 0x01010101u), (int)a1, acc);
+    acc = __dp4a((int)((m >> 2) & 0x01010101u), (int)a2, acc);
+    acc = __dp4a((int)(m & 0x01010101u), (int)a3, acc);
+    return acc;
+}
+
+__device__ __forceinline__ int32_t sum_bytes(uint4 v) {
+    int32_t s = __dp4a((int)v.x, 0x01010101, 0);
+    s = __dp4a((int)v.y, 0x01010101, s);
+    s = __dp4a((int)v.z, 0x01010101, s);
+    return __dp4a((int)v.w, 0x01010101, s);
+}
+
+// The four 16-byte activation vectors that line up with weight slot pp.
+__device__ __forceinline__ void i2s_load_act(const int8_t *q, uint32_t pp, uint4 (&a)[4]) {
+    const int8_t *base = q + (pp >> 1) * 128u + (pp & 1u) * 16u;
+#pragma unroll
+    for (int o = 0; o < 4; ++o) a[o] = *reinterpret_cast<const uint4 *>(base + 32 * o);
+}
+
+// Correction for code-3 codes of one row (slots pp = s, s+stride, ... < P).
+__device__ __forceinline__ int32_t i2s_row_c3(const uint8_t *rp, const int8_t *q, uint32_t s,
+                                              uint32_t stride, uint32_t P) {
+    int32_t corr = 0;
+    for (uint32_t pp = s; pp < P; pp += stride) {
+        const uint4 wv = *reinterpret_cast<const uint4 *>(rp + 16 * pp);
+        uint4 a[4];
+        i2s_load_act(q, pp, a);
+        corr = i2s_word_c3(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, corr);
+        corr = i2s_word_c3(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, corr);
+        corr = i2s_word_c3(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, corr);
+        corr = i2s_word_c3(wv.w, a[0].w, a[1].w, a[2].w, a[3].w, corr);
+    }
+    return corr;
+}
+
+// Absmax quantisation of x[0..K) by the whole CTA into shared memory (same
+// IEEE steps as quantize_absmax_kernel).  Returns the activation scale.
+__device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint32_t K, float *xs,
+                                              int8_t *qs, float *red) {
+    const uint32_t tid = threadIdx.x, nthr = blockDim.x;
+    float m = 0.0f;
+    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(x + i);
+        *reinterpret_cast<float4 *>(xs + i) = v;
+        m = fmaxf(fmaxf(fmaxf(m, fabsf(v.x)), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    float max_abs = red[0];
+    for (uint32_t w = 1; w < nthr / 32; ++w) max_abs = fmaxf(max_abs, red[w]);
+    const float inv = max_abs == 0.0f ? 0.0f : __fdiv_rn(127.0f, max_abs);
+    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(xs + i);
+        const float e[4] = {v.x, v.y, v.z, v.w};
+        uint32_t packed = 0;
+        if (max_abs != 0.0f) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float r = roundf(__fmul_rn(e[k], inv));
+                const int qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+                packed |= (uint32_t)(qi & 0xFF) << (8 * k);
+            }
+        }
+        *reinterpret_cast<uint32_t *>(qs + i) = packed;
+    }
+    __syncthreads();
+    return max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 2: per-op matvec (one BitLinear, or several sharing one input).
 
 // Issue chunk `c` of this CTA's row range [r0, r1) into `stage`.  A chunk
 // may span two fused weights; each contiguous segment is one bulk copy.
@@ -139,52 +264,27 @@ __device__ __forceinline__ void i2s_issue_chunk(const I2sMatvecParams &p, uint32
     }
 }
 
-// One 32-bit weight word (16 codes) against the four activation words it
-// lines up with.  Accumulates sum(c*a) and ORs the code-3 detector.
-__device__ __forceinline__ int32_t i2s_word(uint32_t w, uint32_t a0, uint32_t a1, uint32_t a2,
-                                            uint32_t a3, int32_t acc, uint32_t &c3) {
-    acc = __dp4a((int)((w >> 6) & 0x03030303u), (int)a0, acc);
-    acc = __dp4a((int)((w >> 4) & 0x03030303u), (int)a1, acc);
-    acc = __dp4a((int)((w >> 2) & 0x03030303u), (int)a2, acc);
-    acc = __dp4a((int)(w & 0x03030303u), (int)a3, acc);
-    c3 |= w & (w >> 1);
-    return acc;
-}
-
-// Sum over the code-3 positions of one word (rare path; the reference
-// quantiser never emits code 3, but the reference maps it to 0).
-__device__ __forceinline__ int32_t i2s_word_c3(uint32_t w, uint32_t a0, uint32_t a1, uint32_t a2,
-                                               uint32_t a3, int32_t acc) {
-    const uint32_t m = w & (w >> 1) & 0x55555555u;
-    acc = __dp4a((int)((m >> 6) & 0x01010101u), (int)a0, acc);
-    acc = __dp4a((int)((m >> 4) & 0x01010101u), (int)a1, acc);
-    acc = __dp4a((int)((m >> 2) & 0x01010101u), (int)a2, acc);
-    acc = __dp4a((int)(m & 0x01010101u), (int)a3, acc);
-    return acc;
-}
-
-__device__ __forceinline__ int32_t sum_bytes(uint4 v) {
-    int32_t s = __dp4a((int)v.x, 0x01010101, 0);
-    s = __dp4a((int)v.y, 0x01010101, s);
-    s = __dp4a((int)v.z, 0x01010101, s);
-    return __dp4a((int)v.w, 0x01010101, s);
-}
-
-// Kernel 2.  LPR lanes cooperate on one row (RPW = 32/LPR rows per warp),
-// lane s of a row owns the 16-byte weight slots p = s + LPR*i.  NP > 0: the
-// NP slots' activations (4 x 16 bytes each) live in registers for the whole
-// kernel; NP == 0: activations are re-read from L1 per row (very large K).
-template <int LPR, int NP>
-__global__ void __launch_bounds__(I2S_THREADS, 1)
+// LPR lanes cooperate on one row (RPW = 32/LPR rows per warp); lane s owns
+// the 16-byte weight slots pp = s + LPR*i.  NP > 0: those slots' activations
+// (4 x 16 bytes each) live in registers for the whole kernel; NP == 0: they
+// are re-read from L1 per row (very large K).  FUSE_Q: the CTA quantises the
+// f32 input itself (no separate kernel, one dependency hop less).  C3: the
+// weights may contain code 0b11 (checked per row; the fast path otherwise).
+// At most 128 registers per thread, so the next op's CTA fits on the same SM
+// and its weight prefetch overlaps this op (programmatic dependent launch).
+template <int LPR, int NP, bool FUSE_Q, bool C3>
+__global__ void __launch_bounds__(I2S_THREADS, 2)
     i2s_matvec_kernel(const __grid_constant__ I2sMatvecParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[I2S_MAX_STAGES];
+    __shared__ float red[I2S_WARPS];
     constexpr int RPW = 32 / LPR;
     constexpr uint32_t RPI = I2S_WARPS * RPW;
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t row_bytes = p.K >> 2;
-    const uint32_t P = p.K >> 6;
+    const uint32_t K = p.K;
+    const uint32_t row_bytes = K >> 2;
+    const uint32_t P = K >> 6;
     const uint32_t stage_bytes = RPI * row_bytes;
     const uint32_t r0 = blockIdx.x * p.rows_per_cta;
     const uint32_t r1 = min(r0 + p.rows_per_cta, p.total_rows);
@@ -206,35 +306,49 @@ __global__ void __launch_bounds__(I2S_THREADS, 1)
     }
     __syncthreads();
     pdl_launch_dependents();
-    pdl_wait();  // the quantised activations come from the previous kernel
+    pdl_wait();  // the input comes from the previous kernel
+
+    float act_scale;
+    const int8_t *q;
+    if constexpr (FUSE_Q) {
+        float *xs = reinterpret_cast<float *>(smem + nst * stage_bytes);
+        int8_t *qs = reinterpret_cast<int8_t *>(xs + K);
+        act_scale = cta_quantize(p.x, K, xs, qs, red);
+        if (blockIdx.x == 0) {
+            if (p.q_out)
+                for (uint32_t i = tid * 16; i < K; i += I2S_THREADS * 16)
+                    *reinterpret_cast<uint4 *>(p.q_out + i) = *reinterpret_cast<const uint4 *>(qs + i);
+            if (p.scale_out && tid == 0) *p.scale_out = act_scale;
+        }
+        q = qs;
+    } else {
+        act_scale = *p.act_scale;
+        q = p.q;
+    }
 
     const uint32_t s = lane % LPR;
     const uint32_t sub = lane / LPR;
-    const float act_scale = *p.act_scale;
-
     uint4 act[NP > 0 ? NP : 1][4];
     int32_t asum = 0;
     if constexpr (NP > 0) {
 #pragma unroll
         for (int i = 0; i < NP; ++i) {
             const uint32_t pp = s + LPR * i;
+            if (pp < P) {
+                i2s_load_act(q, pp, act[i]);
 #pragma unroll
-            for (int o = 0; o < 4; ++o) {
-                if (pp < P) {
-                    act[i][o] = __ldg(reinterpret_cast<const uint4 *>(
-                        p.q + (pp >> 1) * 128 + (pp & 1) * 16 + 32 * o));
-                    asum += sum_bytes(act[i][o]);
-                } else {
-                    act[i][o] = make_uint4(0, 0, 0, 0);
-                }
+                for (int o = 0; o < 4; ++o) asum += sum_bytes(act[i][o]);
+            } else {
+#pragma unroll
+                for (int o = 0; o < 4; ++o) act[i][o] = make_uint4(0, 0, 0, 0);
             }
         }
     } else {
         for (uint32_t pp = s; pp < P; pp += LPR) {
+            uint4 a[4];
+            i2s_load_act(q, pp, a);
 #pragma unroll
-            for (int o = 0; o < 4; ++o)
-                asum += sum_bytes(__ldg(reinterpret_cast<const uint4 *>(
-                    p.q + (pp >> 1) * 128 + (pp & 1) * 16 + 32 * o)));
+            for (int o = 0; o < 4; ++o) asum += sum_bytes(a[o]);
         }
     }
 
@@ -252,67 +366,41 @@ __global__ void __launch_bounds__(I2S_THREADS, 1)
         const uint32_t row_local = warp * RPW + sub;
         const uint32_t row = r0 + c * RPI + row_local;
         const uint8_t *rp = smem + st * stage_bytes + row_local * row_bytes;
-        int32_t dot = -asum;
+        I2sAcc acc = {0, 0, 0, 0};
         uint32_t c3 = 0;
         if (row < r1) {
             if constexpr (NP > 0) {
 #pragma unroll
                 for (int i = 0; i < NP; ++i) {
                     const uint32_t pp = s + LPR * i;
-                    if (pp < P) {
-                        const uint4 wv = *reinterpret_cast<const uint4 *>(rp + 16 * pp);
-                        dot = i2s_word(wv.x, act[i][0].x, act[i][1].x, act[i][2].x, act[i][3].x,
-                                       dot, c3);
-                        dot = i2s_word(wv.y, act[i][0].y, act[i][1].y, act[i][2].y, act[i][3].y,
-                                       dot, c3);
-                        dot = i2s_word(wv.z, act[i][0].z, act[i][1].z, act[i][2].z, act[i][3].z,
-                                       dot, c3);
-                        dot = i2s_word(wv.w, act[i][0].w, act[i][1].w, act[i][2].w, act[i][3].w,
-                                       dot, c3);
-                    }
+                    if (pp < P)
+                        i2s_slot<C3>(*reinterpret_cast<const uint4 *>(rp + 16 * pp), act[i], acc,
+                                     c3);
                 }
             } else {
                 for (uint32_t pp = s; pp < P; pp += LPR) {
-                    const uint4 wv = *reinterpret_cast<const uint4 *>(rp + 16 * pp);
                     uint4 a[4];
-#pragma unroll
-                    for (int o = 0; o < 4; ++o)
-                        a[o] = __ldg(reinterpret_cast<const uint4 *>(
-                            p.q + (pp >> 1) * 128 + (pp & 1) * 16 + 32 * o));
-                    dot = i2s_word(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, dot, c3);
-                    dot = i2s_word(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, dot, c3);
-                    dot = i2s_word(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, dot, c3);
-                    dot = i2s_word(wv.w, a[0].w, a[1].w, a[2].w, a[3].w, dot, c3);
+                    i2s_load_act(q, pp, a);
+                    i2s_slot<C3>(*reinterpret_cast<const uint4 *>(rp + 16 * pp), a, acc, c3);
                 }
             }
         }
+        int32_t dot = i2s_acc_total(acc) - asum;
 #pragma unroll
         for (int off = LPR / 2; off > 0; off >>= 1) {
             dot += __shfl_xor_sync(0xffffffffu, dot, off);
-            c3 |= __shfl_xor_sync(0xffffffffu, c3, off);
+            if constexpr (C3) c3 |= __shfl_xor_sync(0xffffffffu, c3, off);
         }
-        if ((c3 & 0x55555555u) != 0u) {  // uniform across the LPR lanes of this row
-            int32_t corr = 0;
-            if (row < r1) {
-                for (uint32_t pp = s; pp < P; pp += LPR) {
-                    const uint4 wv = *reinterpret_cast<const uint4 *>(rp + 16 * pp);
-                    uint4 a[4];
+        if constexpr (C3) {
+            if ((c3 & 0x55555555u) != 0u) {  // uniform across the LPR lanes of this row
+                int32_t corr = row < r1 ? i2s_row_c3(rp, q, s, LPR, P) : 0;
+                // Only the lanes of rows that took this branch participate.
+                const uint32_t grp = __match_any_sync(__activemask(), row_local);
 #pragma unroll
-                    for (int o = 0; o < 4; ++o)
-                        a[o] = __ldg(reinterpret_cast<const uint4 *>(
-                            p.q + (pp >> 1) * 128 + (pp & 1) * 16 + 32 * o));
-                    corr = i2s_word_c3(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, corr);
-                    corr = i2s_word_c3(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, corr);
-                    corr = i2s_word_c3(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, corr);
-                    corr = i2s_word_c3(wv.w, a[0].w, a[1].w, a[2].w, a[3].w, corr);
-                }
+                for (int off = LPR / 2; off > 0; off >>= 1)
+                    corr += __shfl_xor_sync(grp, corr, off);
+                dot -= 2 * corr;
             }
-            // Only the lanes of rows that took this branch participate.
-            const uint32_t grp = __match_any_sync(__activemask(), row_local);
-#pragma unroll
-            for (int off = LPR / 2; off > 0; off >>= 1)
-                corr += __shfl_xor_sync(grp, corr, off);
-            dot -= 2 * corr;
         }
         if (s == 0 && row < r1) {
             int j = 0;
@@ -329,6 +417,19 @@ __global__ void __launch_bounds__(I2S_THREADS, 1)
             i2s_issue_chunk(p, c + nst, r0, r1, RPI, row_bytes, smem + st * stage_bytes,
                             &full_bar[st], policy);
     }
+}
+
+// One-time scan: does a packed I2_S tensor contain code 0b11 anywhere?
+__global__ void i2s_scan_code3_kernel(const uint4 *__restrict__ w, size_t n16,
+                                      uint32_t *__restrict__ found) {
+    uint32_t any = 0;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const uint4 v = w[i];
+        any |= (v.x & (v.x >> 1)) | (v.y & (v.y >> 1)) | (v.z & (v.z >> 1)) | (v.w & (v.w >> 1));
+    }
+    if (__any_sync(0xffffffffu, (any & 0x55555555u) != 0u) && (threadIdx.x & 31) == 0)
+        atomicOr(found, 1u);
 }
 
 }  // namespace wl

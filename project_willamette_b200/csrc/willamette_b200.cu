@@ -19,6 +19,7 @@
 #include "../../include/willamette_b200.h"
 #include "argmax.cuh"
 #include "i2s_matvec.cuh"
+#include "i2s_stream.cuh"
 #include "q6k_lmhead.cuh"
 #include "q8_0.cuh"
 
@@ -64,6 +65,7 @@ struct CachedWeight {
     void *dptr = nullptr;
     size_t bytes = 0;
     bool bad_scale = false;  // Q8_0: some block scale is not finite
+    bool has_code3 = true;   // I2_S: some 2-bit code is 0b11 (scanned on upload)
 };
 
 using CacheKey = std::tuple<const void *, size_t, uint32_t, uint64_t, uint64_t>;
@@ -89,20 +91,35 @@ Ctx &ctx() {
 
 constexpr int WL_MAX_DYN_SMEM = 227 * 1024 - 1024;
 
+using I2sKernel = void (*)(I2sMatvecParams);
+using I2sStreamKernel = void (*)(I2sStreamParams);
+
+// Every I2_S per-op kernel variant, indexed [shape][fuse_q][c3]:
+// shape 0 = 8 lanes/row x 5 slots (in_dim <= 2560), 1 = 32 x 4 (<= 8192),
+// 2 = 32 lanes, activations re-read from L1 (larger; never fused).
+const I2sKernel kI2s[3][2][2] = {
+    {{i2s_matvec_kernel<8, 5, false, false>, i2s_matvec_kernel<8, 5, false, true>},
+     {i2s_matvec_kernel<8, 5, true, false>, i2s_matvec_kernel<8, 5, true, true>}},
+    {{i2s_matvec_kernel<32, 4, false, false>, i2s_matvec_kernel<32, 4, false, true>},
+     {i2s_matvec_kernel<32, 4, true, false>, i2s_matvec_kernel<32, 4, true, true>}},
+    {{i2s_matvec_kernel<32, 0, false, false>, i2s_matvec_kernel<32, 0, false, true>},
+     {i2s_matvec_kernel<32, 0, false, false>, i2s_matvec_kernel<32, 0, false, true>}},
+};
+const I2sStreamKernel kStream[2] = {i2s_stream_kernel<false>, i2s_stream_kernel<true>};
+
 // Raise the dynamic shared-memory limit of every kernel once, at init, so
 // launches never call cudaFuncSetAttribute (they can be captured in graphs).
 int configure_kernels() {
-    const void *kernels[] = {
-        (const void *)i2s_matvec_kernel<8, 1>,  (const void *)i2s_matvec_kernel<8, 2>,
-        (const void *)i2s_matvec_kernel<8, 3>,  (const void *)i2s_matvec_kernel<8, 4>,
-        (const void *)i2s_matvec_kernel<8, 5>,  (const void *)i2s_matvec_kernel<32, 0>,
-        (const void *)i2s_matvec_kernel<32, 2>, (const void *)i2s_matvec_kernel<32, 3>,
-        (const void *)i2s_matvec_kernel<32, 4>, (const void *)i2s_matvec_kernel<32, 5>,
-        (const void *)i2s_matvec_kernel<32, 6>, (const void *)i2s_matvec_kernel<32, 7>,
-        (const void *)i2s_matvec_kernel<32, 8>, (const void *)q6k_lmhead_kernel<1>,
-        (const void *)q6k_lmhead_kernel<4>,     (const void *)q8_0_matvec_kernel,
-    };
-    for (const void *k : kernels)
+    for (auto &a : kI2s)
+        for (auto &b : a)
+            for (I2sKernel k : b)
+                WL_CUDA(cudaFuncSetAttribute((const void *)k,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             WL_MAX_DYN_SMEM / 2));
+    const void *others[] = {(const void *)kStream[0], (const void *)kStream[1],
+                            (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<4>,
+                            (const void *)q8_0_matvec_kernel};
+    for (const void *k : others)
         WL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      WL_MAX_DYN_SMEM));
     return WL_OK;
@@ -204,31 +221,14 @@ uint32_t *status_ptr() {
     return c.d_status;
 }
 
-using I2sKernel = void (*)(I2sMatvecParams);
-
-I2sKernel pick_i2s_kernel(uint32_t K, int *lpr) {
+int i2s_shape_index(uint32_t K, int *lpr) {
     const uint32_t P = K / 64u;
     if (P <= 40) {
         *lpr = 8;
-        switch ((P + 7) / 8) {
-        case 1: return i2s_matvec_kernel<8, 1>;
-        case 2: return i2s_matvec_kernel<8, 2>;
-        case 3: return i2s_matvec_kernel<8, 3>;
-        case 4: return i2s_matvec_kernel<8, 4>;
-        default: return i2s_matvec_kernel<8, 5>;
-        }
+        return 0;
     }
     *lpr = 32;
-    switch ((P + 31) / 32) {
-    case 2: return i2s_matvec_kernel<32, 2>;
-    case 3: return i2s_matvec_kernel<32, 3>;
-    case 4: return i2s_matvec_kernel<32, 4>;
-    case 5: return i2s_matvec_kernel<32, 5>;
-    case 6: return i2s_matvec_kernel<32, 6>;
-    case 7: return i2s_matvec_kernel<32, 7>;
-    case 8: return i2s_matvec_kernel<32, 8>;
-    default: return i2s_matvec_kernel<32, 0>;
-    }
+    return P <= 128 ? 1 : 2;
 }
 
 int launch_quantize(const float *x, uint32_t n, uint32_t m, int8_t *q, float *scale,
@@ -239,40 +239,55 @@ int launch_quantize(const float *x, uint32_t n, uint32_t m, int8_t *q, float *sc
     return WL_OK;
 }
 
-int launch_i2s_with_status(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K,
-                           const int8_t *q, const float *act_scale, cudaStream_t s, bool pdl,
-                           uint32_t *status);
+// One launch of the per-op I2_S kernel over up to four weights that share an
+// input: either pre-quantised (q, act_scale) or f32 (x, quantised in-kernel,
+// optional copies of q / scale to q_out / scale_out).
+struct I2sLaunch {
+    const wl_i2s_dev_weight *w = nullptr;
+    uint32_t nw = 0, K = 0;
+    const int8_t *q = nullptr;
+    const float *act_scale = nullptr;
+    const float *x = nullptr;
+    int8_t *q_out = nullptr;
+    float *scale_out = nullptr;
+};
 
-int launch_i2s(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K, const int8_t *q,
-               const float *act_scale, cudaStream_t s, bool pdl) {
-    uint32_t *status = status_ptr();
-    if (!status) return WL_ERR_NO_DEVICE;
-    return launch_i2s_with_status(w, nw, K, q, act_scale, s, pdl, status);
+bool weights_may_have_code3(const wl_i2s_dev_weight *w, uint32_t nw) {
+    for (uint32_t j = 0; j < nw; ++j)
+        if (!(w[j].flags & WL_I2S_NO_CODE3)) return true;
+    return false;
 }
 
-int launch_i2s_with_status(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K,
-                           const int8_t *q, const float *act_scale, cudaStream_t s, bool pdl,
-                           uint32_t *status) {
+int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_t *status) {
     I2sMatvecParams p = {};
     uint32_t rows = 0;
-    for (uint32_t j = 0; j < nw; ++j) {
-        p.jobs[j].w = w[j].packed;
-        p.jobs[j].w_scale = w[j].w_scale;
-        p.jobs[j].out_dim = w[j].out_dim;
+    for (uint32_t j = 0; j < L.nw; ++j) {
+        p.jobs[j].w = L.w[j].packed;
+        p.jobs[j].w_scale = L.w[j].w_scale;
+        p.jobs[j].out_dim = L.w[j].out_dim;
         p.jobs[j].row_begin = rows;
-        p.jobs[j].y = w[j].y;
-        p.jobs[j].acc = w[j].acc;
-        rows += w[j].out_dim;
+        p.jobs[j].y = L.w[j].y;
+        p.jobs[j].acc = L.w[j].acc;
+        rows += L.w[j].out_dim;
     }
     if (rows == 0) return WL_OK;
-    p.njobs = (int)nw;
+    const uint32_t K = L.K;
+    p.njobs = (int)L.nw;
     p.K = K;
     p.total_rows = rows;
-    p.q = q;
-    p.act_scale = act_scale;
+    p.q = L.q;
+    p.act_scale = L.act_scale;
+    p.x = L.x;
+    p.q_out = L.q_out;
+    p.scale_out = L.scale_out;
     p.status = status;
+    const bool fuse = L.x != nullptr;
     int lpr = 32;
-    I2sKernel k = pick_i2s_kernel(K, &lpr);
+    const int shape = i2s_shape_index(K, &lpr);
+    if (fuse && (shape == 2 || K > I2S_FUSE_Q_MAX_K))
+        return fail(WL_ERR_INVALID_ARGUMENT, "fused quantisation needs in_dim <= %u",
+                    I2S_FUSE_Q_MAX_K);
+    I2sKernel k = kI2s[shape][fuse ? 1 : 0][weights_may_have_code3(L.w, L.nw) ? 1 : 0];
     const uint32_t rpi = (uint32_t)I2S_WARPS * (32u / (uint32_t)lpr);
     const uint32_t G = std::min<uint32_t>((uint32_t)sm_count_for_launch(), rows);
     p.rows_per_cta = (rows + G - 1) / G;
@@ -282,12 +297,18 @@ int launch_i2s_with_status(const wl_i2s_dev_weight *w, uint32_t nw, uint32_t K,
     nst = std::min<uint32_t>(nst, (uint32_t)I2S_MAX_STAGES);
     nst = std::min<uint32_t>(nst, nchunks);
     p.nstages = nst;
-    const size_t smem = (size_t)nst * stage_bytes;
-    if (smem > (size_t)WL_MAX_DYN_SMEM)
+    const size_t smem = (size_t)nst * stage_bytes + (fuse ? (size_t)K * 5u : 0u);
+    if (smem > (size_t)WL_MAX_DYN_SMEM / 2)
         return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for one shared-memory stage", K);
     const uint32_t grid = (rows + p.rows_per_cta - 1) / p.rows_per_cta;
     WL_CUDA(launch(k, dim3(grid), dim3(I2S_THREADS), smem, s, pdl, p));
     return WL_OK;
+}
+
+int launch_i2s(const I2sLaunch &L, cudaStream_t s, bool pdl) {
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    return launch_i2s_with_status(L, s, pdl, status);
 }
 
 int q6k_launch_cfg(uint32_t n_embd, int bg, uint32_t *nst, size_t *smem) {
@@ -459,7 +480,21 @@ int get_weight(Ctx &c, const wl_tensor_view *w, uint64_t in_dim, uint64_t out_di
         if (cw.bytes)
             WL_CUDA(cudaMemcpyAsync(cw.dptr, w->data, cw.bytes, cudaMemcpyHostToDevice,
                                     c.stream));
+        // One-time scan for code 0b11, so calls on code-3-free weights (all
+        // weights the reference's quantiser writes) take the fast path.
+        uint32_t *found = c.d_status + 8;
+        WL_CUDA(cudaMemsetAsync(found, 0, 4, c.stream));
+        if (cw.bytes >= 16) {
+            const size_t n16 = cw.bytes / 16;
+            const uint32_t grid = (uint32_t)std::min<size_t>((n16 + 255) / 256, 2048);
+            i2s_scan_code3_kernel<<<grid, 256, 0, c.stream>>>((const uint4 *)cw.dptr, n16, found);
+            WL_CUDA(cudaGetLastError());
+        }
+        uint32_t h_found = 0;
+        WL_CUDA(cudaMemcpyAsync(c.h_status + 8, found, 4, cudaMemcpyDeviceToHost, c.stream));
         WL_CUDA(cudaStreamSynchronize(c.stream));
+        h_found = c.h_status[8];
+        cw.has_code3 = h_found != 0;
     } else if (w->ggml_type == WL_GGML_Q6_K || w->ggml_type == WL_GGML_Q8_0) {
         const bool q6 = w->ggml_type == WL_GGML_Q6_K;
         cw.bytes = q6 ? wl_q6k_packed_bytes((uint32_t)in_dim, (uint32_t)out_dim)
@@ -539,15 +574,27 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
     uint8_t *pin = (uint8_t *)c.pinned;
     memcpy(pin, input, xin);
     WL_CUDA(cudaMemcpyAsync(c.x.p, pin, xin, cudaMemcpyHostToDevice, c.stream));
-    if ((rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m, (int8_t *)c.q.p,
-                              (float *)c.scale.p, c.stream, false)))
+    const bool fuse = K <= I2S_FUSE_Q_MAX_K;
+    if (!fuse && (rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m, (int8_t *)c.q.p,
+                                       (float *)c.scale.p, c.stream, false)))
         return rc;
     for (size_t t = 0; t < m; ++t) {
-        wl_i2s_dev_weight dw = {(const uint8_t *)cw->dptr, w_scale, N,
-                                (float *)c.y.p + t * N, (int32_t *)c.acc.p + t * N};
-        if ((rc = launch_i2s(&dw, 1, K, (const int8_t *)c.q.p + t * K,
-                             (const float *)c.scale.p + t, c.stream, true)))
-            return rc;
+        wl_i2s_dev_weight dw = {(const uint8_t *)cw->dptr, w_scale, N, (float *)c.y.p + t * N,
+                                (int32_t *)c.acc.p + t * N,
+                                cw->has_code3 ? 0u : WL_I2S_NO_CODE3};
+        I2sLaunch L;
+        L.w = &dw;
+        L.nw = 1;
+        L.K = K;
+        if (fuse) {
+            L.x = (const float *)c.x.p + t * K;
+            L.q_out = (int8_t *)c.q.p + t * K;
+            L.scale_out = (float *)c.scale.p + t;
+        } else {
+            L.q = (const int8_t *)c.q.p + t * K;
+            L.act_scale = (const float *)c.scale.p + t;
+        }
+        if ((rc = launch_i2s(L, c.stream, t > 0 || !fuse))) return rc;
     }
     uint8_t *py = pin + xin, *pacc = py + yout, *pq = pacc + yout, *ps = pq + m * (size_t)K;
     WL_CUDA(cudaMemcpyAsync(py, c.y.p, yout, cudaMemcpyDeviceToHost, c.stream));
@@ -685,6 +732,143 @@ int noalloc_setup(uint8_t **scratch) {
         d.ready = true;
     }
     *scratch = d.scratch;
+    return WL_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- stream plans
+struct wl_i2s_stream_plan {
+    int device = 0;
+    uint32_t n_ops = 0, n_quant = 0, grid = 0;
+    bool c3 = true;
+    void *d_block = nullptr;  // ops | cta_rows | quant jobs | scales | q buffers
+    I2sStreamOp *d_ops = nullptr;
+    uint32_t *d_cta_rows = nullptr;
+    QuantJob *d_qjobs = nullptr;
+    uint32_t *status = nullptr;
+};
+
+namespace {
+
+size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream_plan *plan) {
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    int rc = ensure_init(c);
+    if (rc) return rc;
+    // distinct inputs -> one quantisation each
+    std::map<const float *, uint32_t> xid;
+    std::vector<uint32_t> qK;
+    uint64_t total_rows = 0, total_bytes = 0;
+    for (uint32_t j = 0; j < n_ops; ++j) {
+        const wl_i2s_stream_op &o = ops[j];
+        if (o.in_dim == 0 || o.in_dim % 128 || o.in_dim > STREAM_MAX_K)
+            return fail(WL_ERR_GGUF_PARSE, "op %u: in_dim %u is not a positive multiple of 128 <= %u",
+                        j, o.in_dim, STREAM_MAX_K);
+        if (!o.packed || !aligned16(o.packed) || !o.x || !aligned16(o.x) || (!o.y && o.out_dim))
+            return fail(WL_ERR_INVALID_ARGUMENT, "op %u: NULL or misaligned pointer", j);
+        if (!std::isfinite(o.w_scale))
+            return fail(WL_ERR_GGUF_PARSE, "op %u: i2s_scale: non-finite scale", j);
+        auto it = xid.find(o.x);
+        if (it == xid.end()) {
+            xid.emplace(o.x, (uint32_t)qK.size());
+            qK.push_back(o.in_dim);
+        } else if (qK[it->second] != o.in_dim) {
+            return fail(WL_ERR_INVALID_ARGUMENT, "op %u: input shared with a different in_dim", j);
+        }
+        total_rows += o.out_dim;
+        total_bytes += (uint64_t)o.out_dim * (o.in_dim / 4);
+    }
+    if (total_rows > 0x7FFFFFFFull) return fail(WL_ERR_INVALID_ARGUMENT, "too many rows");
+    const uint32_t G = (uint32_t)std::max(1, c.sm_count);
+    const uint32_t nq = (uint32_t)qK.size();
+    size_t off_ops = 0, off_rows = align16(off_ops + sizeof(I2sStreamOp) * n_ops);
+    size_t off_q = align16(off_rows + sizeof(uint32_t) * (G + 1));
+    size_t off_sc = align16(off_q + sizeof(QuantJob) * nq);
+    size_t off_buf = align16(off_sc + sizeof(float) * nq);
+    size_t bytes = off_buf;
+    std::vector<size_t> qoff(nq);
+    for (uint32_t i = 0; i < nq; ++i) {
+        qoff[i] = bytes;
+        bytes = align16(bytes + qK[i]);
+    }
+    WL_CUDA(cudaMalloc(&plan->d_block, bytes));
+    uint8_t *base = (uint8_t *)plan->d_block;
+    std::vector<uint8_t> host(bytes, 0);
+    // ops
+    std::vector<I2sStreamOp> hops(n_ops);
+    uint32_t row = 0;
+    bool any_c3 = false;
+    uint32_t *found = c.d_status + 8;
+    for (uint32_t j = 0; j < n_ops; ++j) {
+        const wl_i2s_stream_op &o = ops[j];
+        const uint32_t qi = xid[o.x];
+        hops[j].w = o.packed;
+        hops[j].q = (const int8_t *)(base + qoff[qi]);
+        hops[j].act_scale = (const float *)(base + off_sc) + qi;
+        hops[j].y = o.y;
+        hops[j].acc = o.acc;
+        hops[j].w_scale = o.w_scale;
+        hops[j].K = o.in_dim;
+        hops[j].N = o.out_dim;
+        hops[j].row_begin = row;
+        row += o.out_dim;
+        if (!(o.flags & WL_I2S_NO_CODE3) && !any_c3 && o.out_dim) {
+            const size_t n16 = (size_t)o.out_dim * (o.in_dim / 4) / 16;
+            WL_CUDA(cudaMemsetAsync(found, 0, 4, c.stream));
+            const uint32_t grid = (uint32_t)std::min<size_t>((n16 + 255) / 256, 2048);
+            i2s_scan_code3_kernel<<<grid, 256, 0, c.stream>>>((const uint4 *)o.packed, n16, found);
+            WL_CUDA(cudaGetLastError());
+            WL_CUDA(cudaMemcpyAsync(c.h_status + 8, found, 4, cudaMemcpyDeviceToHost, c.stream));
+            WL_CUDA(cudaStreamSynchronize(c.stream));
+            any_c3 = c.h_status[8] != 0;
+        }
+    }
+    memcpy(host.data() + off_ops, hops.data(), sizeof(I2sStreamOp) * n_ops);
+    // byte-balanced row boundaries per CTA
+    std::vector<uint32_t> rows(G + 1, 0);
+    {
+        uint32_t j = 0;
+        uint64_t cum = 0;  // bytes before op j
+        for (uint32_t b = 1; b < G; ++b) {
+            const uint64_t target = total_bytes * b / G;
+            while (j < n_ops && cum + (uint64_t)ops[j].out_dim * (ops[j].in_dim / 4) <= target) {
+                cum += (uint64_t)ops[j].out_dim * (ops[j].in_dim / 4);
+                ++j;
+            }
+            if (j >= n_ops) {
+                rows[b] = (uint32_t)total_rows;
+                continue;
+            }
+            const uint64_t rb = ops[j].in_dim / 4;
+            const uint64_t r = (target - cum + rb - 1) / rb;
+            rows[b] = std::max<uint32_t>(rows[b - 1], hops[j].row_begin + (uint32_t)r);
+        }
+        rows[G] = (uint32_t)total_rows;
+    }
+    memcpy(host.data() + off_rows, rows.data(), sizeof(uint32_t) * (G + 1));
+    std::vector<QuantJob> qj(nq);
+    for (auto &kv : xid) {
+        const uint32_t i = kv.second;
+        qj[i].x = kv.first;
+        qj[i].q = (int8_t *)(base + qoff[i]);
+        qj[i].scale = (float *)(base + off_sc) + i;
+        qj[i].n = qK[i];
+    }
+    memcpy(host.data() + off_q, qj.data(), sizeof(QuantJob) * nq);
+    WL_CUDA(cudaMemcpyAsync(base, host.data(), bytes, cudaMemcpyHostToDevice, c.stream));
+    WL_CUDA(cudaStreamSynchronize(c.stream));
+    plan->device = c.device;
+    plan->n_ops = n_ops;
+    plan->n_quant = nq;
+    plan->grid = G;
+    plan->c3 = any_c3;
+    plan->d_ops = (I2sStreamOp *)(base + off_ops);
+    plan->d_cta_rows = (uint32_t *)(base + off_rows);
+    plan->d_qjobs = (QuantJob *)(base + off_q);
+    plan->status = c.d_status;
     return WL_OK;
 }
 
@@ -878,7 +1062,49 @@ int wl_dev_i2s_matvec(const wl_i2s_dev_weight *weights, uint32_t n_weights, uint
         rows += weights[j].out_dim;
     }
     if (rows > 0x7FFFFFFFull) return fail(WL_ERR_INVALID_ARGUMENT, "too many rows");
-    return launch_i2s(weights, n_weights, in_dim, q, act_scale, (cudaStream_t)stream, true);
+    I2sLaunch L;
+    L.w = weights;
+    L.nw = n_weights;
+    L.K = in_dim;
+    L.q = q;
+    L.act_scale = act_scale;
+    return launch_i2s(L, (cudaStream_t)stream, true);
+}
+
+int wl_dev_i2s_matvec_fused_f32(const wl_i2s_dev_weight *weights, uint32_t n_weights,
+                                uint32_t in_dim, const float *x, void *stream) {
+    if (!weights || n_weights == 0 || n_weights > WL_I2S_MAX_FUSED)
+        return fail(WL_ERR_INVALID_ARGUMENT, "n_weights must be 1..%d", WL_I2S_MAX_FUSED);
+    if (in_dim == 0 || in_dim % 128 || in_dim > I2S_FUSE_Q_MAX_K)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128 <= %u", in_dim,
+                    I2S_FUSE_Q_MAX_K);
+    if (!aligned16(x)) return fail(WL_ERR_INVALID_ARGUMENT, "x not 16-byte aligned");
+    for (uint32_t j = 0; j < n_weights; ++j) {
+        if (!aligned16(weights[j].packed))
+            return fail(WL_ERR_INVALID_ARGUMENT, "weight %u not 16-byte aligned", j);
+        if (!std::isfinite(weights[j].w_scale))
+            return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale for weight %u", j);
+    }
+    I2sLaunch L;
+    L.w = weights;
+    L.nw = n_weights;
+    L.K = in_dim;
+    L.x = x;
+    return launch_i2s(L, (cudaStream_t)stream, true);
+}
+
+int wl_dev_i2s_scan_code3(const uint8_t *packed, size_t bytes, uint32_t *found, void *stream) {
+    if (!aligned16(packed) || bytes % 16)
+        return fail(WL_ERR_INVALID_ARGUMENT, "packed must be 16-byte aligned, bytes a multiple of 16");
+    if (!status_ptr()) return WL_ERR_NO_DEVICE;
+    cudaStream_t s = (cudaStream_t)stream;
+    WL_CUDA(cudaMemsetAsync(found, 0, 4, s));
+    if (bytes == 0) return WL_OK;
+    const size_t n16 = bytes / 16;
+    const uint32_t grid = (uint32_t)std::min<size_t>((n16 + 255) / 256, 2048);
+    i2s_scan_code3_kernel<<<grid, 256, 0, s>>>((const uint4 *)packed, n16, found);
+    WL_CUDA(cudaGetLastError());
+    return WL_OK;
 }
 
 int wl_dev_i2s_matvec_f32(const uint8_t *packed, float w_scale, uint32_t in_dim,
@@ -889,9 +1115,23 @@ int wl_dev_i2s_matvec_f32(const uint8_t *packed, float w_scale, uint32_t in_dim,
                     WL_I2S_MAX_IN_DIM);
     if (!std::isfinite(w_scale))
         return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale (%g)", w_scale);
+    wl_i2s_dev_weight w = {packed, w_scale, out_dim, y, nullptr, 0};
+    if (in_dim <= I2S_FUSE_Q_MAX_K) {
+        if (!aligned16(x)) return fail(WL_ERR_INVALID_ARGUMENT, "x not 16-byte aligned");
+        if (!aligned16(packed)) return fail(WL_ERR_INVALID_ARGUMENT, "packed not 16-byte aligned");
+        if (q_scratch && !aligned16(q_scratch))
+            return fail(WL_ERR_INVALID_ARGUMENT, "q_scratch not 16-byte aligned");
+        I2sLaunch L;
+        L.w = &w;
+        L.nw = 1;
+        L.K = in_dim;
+        L.x = x;
+        L.q_out = q_scratch;
+        L.scale_out = scale_scratch;
+        return launch_i2s(L, (cudaStream_t)stream, true);
+    }
     int rc = wl_dev_quantize_absmax_i8(x, in_dim, 1, q_scratch, scale_scratch, stream);
     if (rc) return rc;
-    wl_i2s_dev_weight w = {packed, w_scale, out_dim, y, nullptr};
     return wl_dev_i2s_matvec(&w, 1, in_dim, q_scratch, scale_scratch, stream);
 }
 
@@ -969,8 +1209,52 @@ int wl_dev_i2s_matvec_f32_noalloc(const uint8_t *packed, float w_scale, uint32_t
     int8_t *q = reinterpret_cast<int8_t *>(scratch + 256);
     cudaStream_t s = (cudaStream_t)stream;
     if ((rc = launch_quantize(x, in_dim, 1, q, act_scale, s, true))) return rc;
-    wl_i2s_dev_weight w = {packed, w_scale, out_dim, y, nullptr};
-    return launch_i2s_with_status(&w, 1, in_dim, q, act_scale, s, true, status);
+    wl_i2s_dev_weight w = {packed, w_scale, out_dim, y, nullptr, 0};
+    I2sLaunch L;
+    L.w = &w;
+    L.nw = 1;
+    L.K = in_dim;
+    L.q = q;
+    L.act_scale = act_scale;
+    return launch_i2s_with_status(L, s, true, status);
+}
+
+int wl_i2s_stream_plan_create(const wl_i2s_stream_op *ops, uint32_t n_ops,
+                              wl_i2s_stream_plan **plan) {
+    if (!plan || (!ops && n_ops)) return fail(WL_ERR_INVALID_ARGUMENT, "NULL argument");
+    *plan = nullptr;
+    if (n_ops == 0) return fail(WL_ERR_INVALID_ARGUMENT, "a stream plan needs at least one op");
+    auto *p = new wl_i2s_stream_plan();
+    int rc = build_stream_plan(ops, n_ops, p);
+    if (rc) {
+        if (p->d_block) cudaFree(p->d_block);
+        delete p;
+        return rc;
+    }
+    *plan = p;
+    return WL_OK;
+}
+
+int wl_dev_i2s_stream_run(wl_i2s_stream_plan *plan, void *stream) {
+    if (!plan) return fail(WL_ERR_INVALID_ARGUMENT, "plan is NULL");
+    cudaStream_t s = (cudaStream_t)stream;
+    WL_CUDA(launch(quantize_jobs_kernel, dim3(plan->n_quant), dim3(QUANT_THREADS), 0, s, true,
+                   (const QuantJob *)plan->d_qjobs));
+    I2sStreamParams p;
+    p.ops = plan->d_ops;
+    p.n_ops = plan->n_ops;
+    p.cta_rows = plan->d_cta_rows;
+    p.status = plan->status;
+    WL_CUDA(launch(kStream[plan->c3 ? 1 : 0], dim3(plan->grid), dim3(STREAM_THREADS),
+                   (size_t)STREAM_STAGES * STREAM_STAGE_BYTES, s, true, p));
+    return WL_OK;
+}
+
+int wl_i2s_stream_plan_destroy(wl_i2s_stream_plan *plan) {
+    if (!plan) return WL_OK;
+    if (plan->d_block) cudaFree(plan->d_block);
+    delete plan;
+    return WL_OK;
 }
 
 }  // extern "C"

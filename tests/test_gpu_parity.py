@@ -169,6 +169,85 @@ def test_i2s_dev_fused_weights_match_separate():
         assert_bitexact(yd.cpu().numpy(), ry, "fused")
 
 
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda")
+
+
+def test_i2s_fused_input_and_code3_scan():
+    """wl_dev_i2s_matvec_fused_f32 (in-kernel quantisation) over Q/K/V- and
+    gate/up-shaped groups, with and without the no-code-3 fast path."""
+    import torch
+    L = wl.lib()
+    rng = np.random.default_rng(12)
+    stream = torch.cuda.current_stream().cuda_stream
+    found = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for K, shapes, c3 in [(2560, [2560, 640, 640], 0.0), (2560, [6912, 6912], 0.001),
+                          (6912, [2560], 0.0), (128, [3, 5], 0.05), (8192, [33], 0.0)]:
+        x = synth.activations(rng, K)
+        ws = [(synth.i2s_packed(rng, K, n, c3), synth.i2s_scale(rng), n) for n in shapes]
+        arr = (wl._abi.WlI2sDevWeight * len(ws))()
+        keep = []
+        for i, (p, s, n) in enumerate(ws):
+            pd = _dev(torch, p)
+            assert L.wl_dev_i2s_scan_code3(pd.data_ptr(), pd.numel(), found.data_ptr(), stream) == 0
+            torch.cuda.synchronize()
+            has3 = bool(((p & (p >> 1)) & 0x55).any())
+            assert int(found.item()) == int(has3)
+            yd = torch.empty(n, dtype=torch.float32, device="cuda")
+            ad = torch.empty(n, dtype=torch.int32, device="cuda")
+            keep += [pd, yd, ad]
+            arr[i].packed, arr[i].w_scale, arr[i].out_dim = pd.data_ptr(), s, n
+            arr[i].y, arr[i].acc = yd.data_ptr(), ad.data_ptr()
+            arr[i].flags = 0 if has3 else wl._abi.WL_I2S_NO_CODE3
+        xd = _dev(torch, x)
+        assert L.wl_dev_i2s_matvec_fused_f32(arr, len(ws), K, xd.data_ptr(), stream) == 0
+        torch.cuda.synchronize()
+        for i, (p, s, n) in enumerate(ws):
+            ry, racc, _, _ = oracle.i2s_matvec_sse2_i8(p, s, K, n, x)
+            yd, ad = keep[3 * i + 1], keep[3 * i + 2]
+            assert np.array_equal(ad.cpu().numpy(), racc), (K, n)
+            assert_bitexact(yd.cpu().numpy(), ry, f"fused {K}x{n}")
+
+
+@pytest.mark.parametrize("with_code3", [False, True])
+def test_i2s_stream_plan_bit_exact(with_code3):
+    """Many independent matvecs (mixed in_dim, shared and distinct inputs,
+    tiny and large ops) in one persistent launch, run twice."""
+    import ctypes
+    import torch
+    L = wl.lib()
+    rng = np.random.default_rng(99 + with_code3)
+    specs = [(2560, 2560, 0), (2560, 640, 0), (2560, 640, 0), (6912, 2560, 1), (128, 1, 2),
+             (2560, 6912, 3), (2560, 6912, 3), (384, 37, 4), (6912, 100, 5), (7168, 300, 6)]
+    xs = {}
+    ops, keep, ref = [], [], []
+    for K, N, xi in specs:
+        if xi not in xs:
+            xs[xi] = synth.activations(rng, K)
+        p = synth.i2s_packed(rng, K, N, 0.002 if (with_code3 and N == 37) else 0.0)
+        s = synth.i2s_scale(rng)
+        pd, xd = _dev(torch, p), _dev(torch, xs[xi])
+        yd = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+        ad = torch.empty(N, dtype=torch.int32, device="cuda")
+        keep += [pd, xd, yd, ad]
+        op = wl._abi.WlI2sStreamOp()
+        op.packed, op.w_scale, op.in_dim, op.out_dim = pd.data_ptr(), s, K, N
+        op.x, op.y, op.acc, op.flags = xd.data_ptr(), yd.data_ptr(), ad.data_ptr(), 0
+        ops.append(op)
+        ref.append((yd, ad) + oracle.i2s_matvec_sse2_i8(p, s, K, N, xs[xi])[:2])
+    arr = (wl._abi.WlI2sStreamOp * len(ops))(*ops)
+    plan = ctypes.c_void_p()
+    assert L.wl_i2s_stream_plan_create(arr, len(ops), ctypes.byref(plan)) == 0, L.wl_last_error()
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        assert L.wl_dev_i2s_stream_run(plan, stream) == 0
+        torch.cuda.synchronize()
+        for yd, ad, ry, racc in ref:
+            assert np.array_equal(ad.cpu().numpy(), racc)
+            assert_bitexact(yd.cpu().numpy(), ry, "stream")
+    assert L.wl_i2s_stream_plan_destroy(plan) == 0
+
+
 def test_i2s_properties_full_size():
     """Size-independent properties at the BitNet-2B shapes: y(-x) = -y(x)
     (round-half-away-from-zero is odd), y(2^k x) = 2^k y(x) exactly."""
