@@ -188,7 +188,7 @@ int wl_dev_i2s_scan_code3(const uint8_t *packed, size_t bytes, uint32_t *found, 
 /* Many independent BitLinear matvecs in one persistent launch (sustained HBM
  * streaming).  Ops sharing an input pointer share one quantisation.  The plan
  * holds the device-side descriptors and scratch; runs are asynchronous.
- * in_dim <= 7168 per op. */
+ * 512 <= in_dim <= 65536 per op. */
 typedef struct wl_i2s_stream_op {
     const uint8_t *packed; /* device */
     float w_scale;

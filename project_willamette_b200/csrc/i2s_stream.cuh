@@ -1,14 +1,23 @@
 // i2s_stream.cuh -- many independent I2_S matvecs in one persistent launch.
 //
 // Same arithmetic as i2s_matvec_kernel (bitlinear_sse2.rs:313-342 semantics,
-// bit-exact), organised for sustained HBM streaming: the rows of all ops
-// are concatenated into one row space, each of the (one per SM) CTAs owns a
-// contiguous, byte-balanced range of it, a producer warp streams that range
-// through a 6-stage shared-memory ring with 1-D bulk copies, and eight
-// consumer warps compute rows as stages land.  A CTA's range touches only a
-// few ops, so activation reloads (op switches) are rare.  Inputs are
-// quantised beforehand by quantize_jobs_kernel (one CTA per distinct input).
+// bit-exact), organised for sustained HBM streaming:
+//  * every op's weight is cut into 32-row blocks; the blocks of all ops form
+//    one list, and each CTA (one per SM) owns a contiguous, byte-balanced
+//    range of it;
+//  * each of the 16 warps of a CTA takes every 16th block of that range and
+//    streams it as 32-row x 128-byte boxes with 2-D TMA tensor copies
+//    (cp.async.bulk.tensor, 128-byte swizzle) through its own 3-stage
+//    shared-memory ring -- lane l owns row l of the box, so there are no
+//    cross-lane reductions, and the swizzle makes the 32 lanes' 16-byte reads
+//    (one per row) hit distinct banks;
+//  * activations (quantised beforehand by quantize_jobs_kernel, one CTA per
+//    distinct input) are read with warp-uniform loads that L1 broadcasts.
+// Rows past an op's end and bytes past a row's end arrive as zeros (TMA
+// out-of-bounds fill) and are skipped.
 #pragma once
+
+#include <cuda.h>
 
 #include <cstdint>
 
@@ -17,29 +26,31 @@
 
 namespace wl {
 
-constexpr int STREAM_CONSUMER_WARPS = 8;
-constexpr int STREAM_THREADS = (STREAM_CONSUMER_WARPS + 1) * 32;
-constexpr int STREAM_LPR = 16;  // lanes per row
-constexpr int STREAM_NP = 7;    // 16-byte weight slots per lane -> K <= 7168
-constexpr uint32_t STREAM_MAX_K = STREAM_LPR * STREAM_NP * 64;
-constexpr int STREAM_STAGES = 6;
-constexpr uint32_t STREAM_STAGE_BYTES = 32u * 1024u;
-constexpr uint32_t STREAM_ROWS_PER_PASS = STREAM_CONSUMER_WARPS * (32 / STREAM_LPR);
+constexpr int STREAM_WARPS = 16;
+constexpr int STREAM_THREADS = STREAM_WARPS * 32;
+constexpr int STREAM_WSTAGES = 3;            // TMA boxes in flight per warp
+constexpr uint32_t STREAM_BOX_ROWS = 32;
+constexpr uint32_t STREAM_BOX_BYTES = 128;   // 8 weight slots of 16 bytes
+constexpr uint32_t STREAM_BOX = STREAM_BOX_ROWS * STREAM_BOX_BYTES;
+constexpr uint32_t STREAM_MIN_K = 512;   // a row spans at least one 128-byte box
+constexpr uint32_t STREAM_MAX_K = 65536;
+constexpr size_t STREAM_SMEM = (size_t)STREAM_WARPS * STREAM_WSTAGES * STREAM_BOX + 1024;
 
 struct I2sStreamOp {
-    const uint8_t *w;         // N x K/4 packed bytes, 16-byte aligned
     const int8_t *q;          // quantised input, K bytes
     const float *act_scale;   // its scale
     float *y;
     int32_t *acc;             // may be null
     float w_scale;
-    uint32_t K, N, row_begin;
+    uint32_t K, N;
+    uint32_t block_begin;     // first 32-row block of this op in the block list
 };
 
 struct I2sStreamParams {
     const I2sStreamOp *ops;
+    const CUtensorMap *maps;  // one per op, 64-byte aligned, in global memory
     uint32_t n_ops;
-    const uint32_t *cta_rows;  // gridDim.x + 1 row boundaries
+    const uint32_t *cta_blocks;  // gridDim.x + 1 block boundaries
     uint32_t *status;
 };
 
@@ -87,158 +98,156 @@ __global__ void __launch_bounds__(QUANT_THREADS)
     if (threadIdx.x == 0) *j.scale = max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
 }
 
-__host__ __device__ constexpr uint32_t stream_chunk_rows(uint32_t K) {
-    return (STREAM_STAGE_BYTES / (STREAM_ROWS_PER_PASS * (K >> 2)) > 0
-                ? STREAM_STAGE_BYTES / (STREAM_ROWS_PER_PASS * (K >> 2))
-                : 1u) *
-           STREAM_ROWS_PER_PASS;
+// 2-D TMA tile load: box at (x bytes, y rows) of `map` into shared memory.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint32_t x,
+                                            uint32_t y, uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
 }
 
-// Deterministic chunk walk over [r, r1): producer and consumers step through
-// the same sequence.  A chunk never crosses an op boundary.
-struct ChunkWalk {
-    uint32_t j, r, n;
+// A warp's walk over (block, slice) boxes: blocks bi = first, first+16, ...
+// below `end`; slices 0 .. ceil(K/512)-1 of each block.
+struct BoxWalk {
+    uint32_t bi, end, j, si, S;
+
+    __device__ __forceinline__ bool valid() const { return bi < end; }
+
+    __device__ __forceinline__ void seek_op(const I2sStreamOp *ops, uint32_t n_ops) {
+        while (j + 1 < n_ops && bi >= ops[j + 1].block_begin) ++j;
+        S = (ops[j].K + 511u) / 512u;
+    }
+
+    __device__ __forceinline__ void next(const I2sStreamOp *ops, uint32_t n_ops) {
+        if (++si < S) return;
+        si = 0;
+        bi += STREAM_WARPS;
+        if (bi < end) seek_op(ops, n_ops);
+    }
 };
-
-__device__ __forceinline__ bool chunk_next(const I2sStreamOp *__restrict__ ops, uint32_t n_ops,
-                                           uint32_t r1, ChunkWalk &w) {
-    w.r += w.n;
-    if (w.r >= r1) return false;
-    while (w.j < n_ops && w.r >= ops[w.j].row_begin + ops[w.j].N) ++w.j;
-    if (w.j >= n_ops) return false;
-    const I2sStreamOp &op = ops[w.j];
-    w.n = min(min(stream_chunk_rows(op.K), op.row_begin + op.N - w.r), r1 - w.r);
-    return true;
-}
 
 template <bool C3>
 __global__ void __launch_bounds__(STREAM_THREADS, 1)
     i2s_stream_kernel(const __grid_constant__ I2sStreamParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full_bar[STREAM_STAGES];
-    __shared__ __align__(8) uint64_t empty_bar[STREAM_STAGES];
-    __shared__ uint32_t s_timeout;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[STREAM_WARPS * STREAM_WSTAGES];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~(uintptr_t)1023);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t *ring = smem + (size_t)warp * STREAM_WSTAGES * STREAM_BOX;
+    uint64_t *bar = bars + warp * STREAM_WSTAGES;
+    const uint32_t b0 = p.cta_blocks[blockIdx.x], b1 = p.cta_blocks[blockIdx.x + 1];
 
-    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t r0 = p.cta_rows[blockIdx.x], r1 = p.cta_rows[blockIdx.x + 1];
-    // first op of the range
-    uint32_t j0 = 0;
-    {
+    // first op of this warp's first block
+    BoxWalk walk = {b0 + warp, b1, 0, 0, 1};
+    if (walk.valid()) {
         uint32_t lo = 0, hi = p.n_ops;
         while (lo + 1 < hi) {
             const uint32_t mid = (lo + hi) / 2;
-            if (p.ops[mid].row_begin <= r0) lo = mid; else hi = mid;
+            if (p.ops[mid].block_begin <= walk.bi) lo = mid; else hi = mid;
         }
-        j0 = lo;
+        walk.j = lo;
+        walk.seek_op(p.ops, p.n_ops);
     }
-    if (tid == 0) {
-        for (int s = 0; s < STREAM_STAGES; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], STREAM_CONSUMER_WARPS);
-        }
+    BoxWalk ahead = walk;  // the issue cursor runs STREAM_WSTAGES boxes ahead
+    const uint64_t policy = l2_policy_evict_first();
+    if (lane == 0) {
+        for (int s = 0; s < STREAM_WSTAGES; ++s) mbar_init(&bar[s], 1);
         fence_mbar_init();
-        s_timeout = 0;
     }
-    __syncthreads();
+    __syncwarp();
+    uint32_t issued = 0;
+    auto issue = [&](uint32_t stage) {
+        const I2sStreamOp &op = p.ops[ahead.j];
+        mbar_arrive_expect_tx(&bar[stage], STREAM_BOX);
+        tma_load_2d(ring + stage * STREAM_BOX, p.maps + ahead.j, ahead.si * STREAM_BOX_BYTES,
+                    (ahead.bi - op.block_begin) * STREAM_BOX_ROWS, &bar[stage], policy);
+        ahead.next(p.ops, p.n_ops);
+        ++issued;
+    };
+    if (lane == 0)
+        for (int s = 0; s < STREAM_WSTAGES && ahead.valid(); ++s) issue(s);
+    __syncwarp();
     pdl_launch_dependents();
+    pdl_wait();  // quantised inputs come from the previous kernel
 
-    if (warp == STREAM_CONSUMER_WARPS) {
-        if (lane == 0) {  // producer: weights do not depend on the previous kernel
-            const uint64_t policy = l2_policy_evict_first();
-            ChunkWalk w = {j0, r0, 0};
-            for (uint32_t k = 0; chunk_next(p.ops, p.n_ops, r1, w); ++k) {
-                const uint32_t st = k % STREAM_STAGES;
-                if (k >= STREAM_STAGES &&
-                    !mbar_wait(&empty_bar[st], ((k / STREAM_STAGES) - 1u) & 1u)) {
-                    atomicOr(&s_timeout, 1u);
-                    break;
-                }
-                const I2sStreamOp &op = p.ops[w.j];
-                const uint32_t rb = op.K >> 2;
-                mbar_arrive_expect_tx(&full_bar[st], w.n * rb);
-                bulk_g2s_evict_first(smem + st * STREAM_STAGE_BYTES,
-                                     op.w + (size_t)(w.r - op.row_begin) * rb, w.n * rb,
-                                     &full_bar[st], policy);
+    uint32_t cur = 0xFFFFFFFFu, P = 0;
+    int32_t asum = 0;
+    float combined = 0.0f;
+    I2sAcc acc = {0, 0, 0, 0};
+    int32_t corr = 0;
+    bool timeout = false;
+    for (uint32_t k = 0; walk.valid(); ++k) {
+        const uint32_t st = k % STREAM_WSTAGES;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[st], (k / STREAM_WSTAGES) & 1u))) {
+            timeout = true;
+            // Give the boxes still in flight a bounded chance to land before
+            // this warp's shared memory is released.
+            if (lane == 0)
+                for (uint32_t kk = k + 1; kk < issued; ++kk)
+                    (void)mbar_wait(&bar[kk % STREAM_WSTAGES], (kk / STREAM_WSTAGES) & 1u);
+            break;
+        }
+        const I2sStreamOp &op = p.ops[walk.j];
+        if (walk.j != cur) {  // op switch: sum of this op's activations
+            cur = walk.j;
+            P = op.K >> 6;
+            int32_t s = 0;
+            for (uint32_t i = lane * 16; i < op.K; i += 32 * 16)
+                s += sum_bytes(__ldg(reinterpret_cast<const uint4 *>(op.q + i)));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            asum = s;
+            combined = __fmul_rn(op.w_scale, __ldg(op.act_scale));
+        }
+        const uint8_t *line = ring + st * STREAM_BOX + lane * STREAM_BOX_BYTES;
+        uint32_t c3 = 0;
+#pragma unroll
+        for (uint32_t s = 0; s < 8; ++s) {
+            const uint32_t pp = walk.si * 8 + s;
+            if (pp < P) {
+                const uint4 wv =
+                    *reinterpret_cast<const uint4 *>(line + ((s ^ (lane & 7u)) << 4));
+                const int8_t *qa = op.q + (pp >> 1) * 128u + (pp & 1u) * 16u;
+                uint4 a[4];
+#pragma unroll
+                for (int o = 0; o < 4; ++o) a[o] = __ldg(reinterpret_cast<const uint4 *>(qa + 32 * o));
+                i2s_slot<C3>(wv, a, acc, c3);
             }
         }
-    } else {
-        pdl_wait();  // quantised inputs come from the previous kernel
-        const uint32_t s = lane % STREAM_LPR, sub = lane / STREAM_LPR;
-        uint4 act[STREAM_NP][4];
-        int32_t asum = 0;
-        float combined = 0.0f;
-        uint32_t cur = 0xFFFFFFFFu, P = 0;
-        ChunkWalk w = {j0, r0, 0};
-        for (uint32_t k = 0; chunk_next(p.ops, p.n_ops, r1, w); ++k) {
-            const uint32_t st = k % STREAM_STAGES;
-            if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[st], (k / STREAM_STAGES) & 1u))) {
-                if (lane == 0) atomicOr(&s_timeout, 1u);
-                break;
-            }
-            const I2sStreamOp &op = p.ops[w.j];
-            if (w.j != cur) {  // op switch: reload this lane's activations
-                cur = w.j;
-                P = op.K >> 6;
-                asum = 0;
-#pragma unroll
-                for (int i = 0; i < STREAM_NP; ++i) {
-                    const uint32_t pp = s + STREAM_LPR * i;
-                    if (pp < P) {
-                        i2s_load_act(op.q, pp, act[i]);
-#pragma unroll
-                        for (int o = 0; o < 4; ++o) asum += sum_bytes(act[i][o]);
-                    } else {
-#pragma unroll
-                        for (int o = 0; o < 4; ++o) act[i][o] = make_uint4(0, 0, 0, 0);
-                    }
-                }
-                combined = __fmul_rn(op.w_scale, *op.act_scale);
-            }
-            const uint32_t rb = op.K >> 2;
-            const uint8_t *stage = smem + st * STREAM_STAGE_BYTES;
-            for (uint32_t base = 0; base < w.n; base += STREAM_ROWS_PER_PASS) {
-                const uint32_t row_local = base + warp * (32 / STREAM_LPR) + sub;
-                const bool valid = row_local < w.n;
-                const uint8_t *rp = stage + row_local * rb;
-                I2sAcc acc = {0, 0, 0, 0};
-                uint32_t c3 = 0;
-                if (valid) {
-#pragma unroll
-                    for (int i = 0; i < STREAM_NP; ++i) {
-                        const uint32_t pp = s + STREAM_LPR * i;
-                        if (pp < P)
-                            i2s_slot<C3>(*reinterpret_cast<const uint4 *>(rp + 16 * pp), act[i],
-                                         acc, c3);
-                    }
-                }
-                int32_t dot = i2s_acc_total(acc) - asum;
-#pragma unroll
-                for (int off = STREAM_LPR / 2; off > 0; off >>= 1) {
-                    dot += __shfl_xor_sync(0xffffffffu, dot, off);
-                    if constexpr (C3) c3 |= __shfl_xor_sync(0xffffffffu, c3, off);
-                }
-                if constexpr (C3) {
-                    if ((c3 & 0x55555555u) != 0u) {
-                        int32_t corr = valid ? i2s_row_c3(rp, op.q, s, STREAM_LPR, P) : 0;
-                        const uint32_t grp = __match_any_sync(__activemask(), row_local);
-#pragma unroll
-                        for (int off = STREAM_LPR / 2; off > 0; off >>= 1)
-                            corr += __shfl_xor_sync(grp, corr, off);
-                        dot -= 2 * corr;
-                    }
-                }
-                if (s == 0 && valid) {
-                    const uint32_t local = w.r + row_local - op.row_begin;
-                    op.y[local] = __fmul_rn(combined, __int2float_rn(dot));
-                    if (op.acc) op.acc[local] = dot;
+        if constexpr (C3) {
+            if ((c3 & 0x55555555u) != 0u) {  // this lane's row has code 0b11 in this box
+                for (uint32_t s = 0; s < 8; ++s) {
+                    const uint32_t pp = walk.si * 8 + s;
+                    if (pp >= P) break;
+                    const uint4 wv =
+                        *reinterpret_cast<const uint4 *>(line + ((s ^ (lane & 7u)) << 4));
+                    uint4 a[4];
+                    i2s_load_act(op.q, pp, a);
+                    corr = i2s_word_c3(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, corr);
+                    corr = i2s_word_c3(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, corr);
+                    corr = i2s_word_c3(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, corr);
+                    corr = i2s_word_c3(wv.w, a[0].w, a[1].w, a[2].w, a[3].w, corr);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty_bar[st]);
         }
+        __syncwarp();  // every lane is done with this stage
+        if (lane == 0 && ahead.valid()) issue(st);
+        if (walk.si + 1 == walk.S) {  // last box of the block: finish the row
+            const uint32_t row = (walk.bi - op.block_begin) * STREAM_BOX_ROWS + lane;
+            if (row < op.N) {
+                const int32_t dot = i2s_acc_total(acc) - asum - 2 * corr;
+                op.y[row] = __fmul_rn(combined, __int2float_rn(dot));
+                if (op.acc) op.acc[row] = dot;
+            }
+            acc = {0, 0, 0, 0};
+            corr = 0;
+        }
+        walk.next(p.ops, p.n_ops);
     }
-    __syncthreads();
-    if (tid == 0 && s_timeout) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
+    if (timeout && lane == 0) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
 }
 
 }  // namespace wl

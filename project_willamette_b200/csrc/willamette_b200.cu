@@ -742,31 +742,66 @@ struct wl_i2s_stream_plan {
     int device = 0;
     uint32_t n_ops = 0, n_quant = 0, grid = 0;
     bool c3 = true;
-    void *d_block = nullptr;  // ops | cta_rows | quant jobs | scales | q buffers
+    void *d_block = nullptr;  // maps | ops | cta_blocks | quant jobs | scales | q buffers
+    CUtensorMap *d_maps = nullptr;
     I2sStreamOp *d_ops = nullptr;
-    uint32_t *d_cta_rows = nullptr;
+    uint32_t *d_cta_blocks = nullptr;
     QuantJob *d_qjobs = nullptr;
     uint32_t *status = nullptr;
 };
 
 namespace {
 
-size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_tiled(EncodeTiledFn *fn) {
+    static EncodeTiledFn cached = nullptr;
+    if (!cached) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f)
+            return fail(WL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+        cached = (EncodeTiledFn)f;
+    }
+    *fn = cached;
+    return WL_OK;
+}
+
+// Tensor map of one packed I2_S weight: 2-D (row bytes, rows), 32-row x
+// 128-byte boxes, 128-byte swizzle, zero fill out of bounds.
+int encode_i2s_map(const uint8_t *packed, uint32_t K, uint32_t N, CUtensorMap *map) {
+    EncodeTiledFn enc;
+    int rc = get_encode_tiled(&enc);
+    if (rc) return rc;
+    const cuuint64_t dims[2] = {K / 4u, N};
+    const cuuint64_t strides[1] = {K / 4u};
+    const cuuint32_t box[2] = {STREAM_BOX_BYTES, STREAM_BOX_ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)packed, dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(WL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return WL_OK;
+}
 
 int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream_plan *plan) {
-    Ctx &c = ctx();
-    std::lock_guard<std::mutex> g(c.mu);
-    int rc = ensure_init(c);
-    if (rc) return rc;
     // distinct inputs -> one quantisation each
     std::map<const float *, uint32_t> xid;
     std::vector<uint32_t> qK;
-    uint64_t total_rows = 0, total_bytes = 0;
+    std::vector<uint32_t> block_begin(n_ops);
+    uint64_t total_blocks = 0;
     for (uint32_t j = 0; j < n_ops; ++j) {
         const wl_i2s_stream_op &o = ops[j];
-        if (o.in_dim == 0 || o.in_dim % 128 || o.in_dim > STREAM_MAX_K)
-            return fail(WL_ERR_GGUF_PARSE, "op %u: in_dim %u is not a positive multiple of 128 <= %u",
-                        j, o.in_dim, STREAM_MAX_K);
+        if (o.in_dim < STREAM_MIN_K || o.in_dim % 128 || o.in_dim > STREAM_MAX_K)
+            return fail(WL_ERR_INVALID_ARGUMENT,
+                        "op %u: in_dim %u must be a multiple of 128 in [%u, %u] for a stream plan",
+                        j, o.in_dim, STREAM_MIN_K, STREAM_MAX_K);
         if (!o.packed || !aligned16(o.packed) || !o.x || !aligned16(o.x) || (!o.y && o.out_dim))
             return fail(WL_ERR_INVALID_ARGUMENT, "op %u: NULL or misaligned pointer", j);
         if (!std::isfinite(o.w_scale))
@@ -778,34 +813,36 @@ int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream
         } else if (qK[it->second] != o.in_dim) {
             return fail(WL_ERR_INVALID_ARGUMENT, "op %u: input shared with a different in_dim", j);
         }
-        total_rows += o.out_dim;
-        total_bytes += (uint64_t)o.out_dim * (o.in_dim / 4);
+        block_begin[j] = (uint32_t)total_blocks;
+        total_blocks += (o.out_dim + STREAM_BOX_ROWS - 1) / STREAM_BOX_ROWS;
     }
-    if (total_rows > 0x7FFFFFFFull) return fail(WL_ERR_INVALID_ARGUMENT, "too many rows");
+    if (total_blocks > 0x7FFFFFFFull) return fail(WL_ERR_INVALID_ARGUMENT, "too many rows");
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    int rc = ensure_init(c);
+    if (rc) return rc;
     const uint32_t G = (uint32_t)std::max(1, c.sm_count);
     const uint32_t nq = (uint32_t)qK.size();
-    size_t off_ops = 0, off_rows = align16(off_ops + sizeof(I2sStreamOp) * n_ops);
-    size_t off_q = align16(off_rows + sizeof(uint32_t) * (G + 1));
-    size_t off_sc = align16(off_q + sizeof(QuantJob) * nq);
-    size_t off_buf = align16(off_sc + sizeof(float) * nq);
-    size_t bytes = off_buf;
+    const size_t off_maps = 0;
+    const size_t off_ops = align_up(off_maps + sizeof(CUtensorMap) * n_ops, 64);
+    const size_t off_cta = align_up(off_ops + sizeof(I2sStreamOp) * n_ops, 16);
+    const size_t off_q = align_up(off_cta + sizeof(uint32_t) * (G + 1), 16);
+    const size_t off_sc = align_up(off_q + sizeof(QuantJob) * nq, 16);
+    size_t bytes = align_up(off_sc + sizeof(float) * nq, 16);
     std::vector<size_t> qoff(nq);
     for (uint32_t i = 0; i < nq; ++i) {
         qoff[i] = bytes;
-        bytes = align16(bytes + qK[i]);
+        bytes = align_up(bytes + qK[i], 16);
     }
     WL_CUDA(cudaMalloc(&plan->d_block, bytes));
     uint8_t *base = (uint8_t *)plan->d_block;
     std::vector<uint8_t> host(bytes, 0);
-    // ops
     std::vector<I2sStreamOp> hops(n_ops);
-    uint32_t row = 0;
     bool any_c3 = false;
     uint32_t *found = c.d_status + 8;
     for (uint32_t j = 0; j < n_ops; ++j) {
         const wl_i2s_stream_op &o = ops[j];
         const uint32_t qi = xid[o.x];
-        hops[j].w = o.packed;
         hops[j].q = (const int8_t *)(base + qoff[qi]);
         hops[j].act_scale = (const float *)(base + off_sc) + qi;
         hops[j].y = o.y;
@@ -813,8 +850,12 @@ int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream
         hops[j].w_scale = o.w_scale;
         hops[j].K = o.in_dim;
         hops[j].N = o.out_dim;
-        hops[j].row_begin = row;
-        row += o.out_dim;
+        hops[j].block_begin = block_begin[j];
+        if (o.out_dim) {
+            CUtensorMap m;
+            if ((rc = encode_i2s_map(o.packed, o.in_dim, o.out_dim, &m))) return rc;
+            memcpy(host.data() + off_maps + sizeof(CUtensorMap) * j, &m, sizeof m);
+        }
         if (!(o.flags & WL_I2S_NO_CODE3) && !any_c3 && o.out_dim) {
             const size_t n16 = (size_t)o.out_dim * (o.in_dim / 4) / 16;
             WL_CUDA(cudaMemsetAsync(found, 0, 4, c.stream));
@@ -827,28 +868,24 @@ int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream
         }
     }
     memcpy(host.data() + off_ops, hops.data(), sizeof(I2sStreamOp) * n_ops);
-    // byte-balanced row boundaries per CTA
-    std::vector<uint32_t> rows(G + 1, 0);
+    // byte-balanced block boundaries per CTA
+    std::vector<uint32_t> cb(G + 1, 0);
     {
-        uint32_t j = 0;
-        uint64_t cum = 0;  // bytes before op j
-        for (uint32_t b = 1; b < G; ++b) {
-            const uint64_t target = total_bytes * b / G;
-            while (j < n_ops && cum + (uint64_t)ops[j].out_dim * (ops[j].in_dim / 4) <= target) {
-                cum += (uint64_t)ops[j].out_dim * (ops[j].in_dim / 4);
-                ++j;
-            }
-            if (j >= n_ops) {
-                rows[b] = (uint32_t)total_rows;
-                continue;
-            }
-            const uint64_t rb = ops[j].in_dim / 4;
-            const uint64_t r = (target - cum + rb - 1) / rb;
-            rows[b] = std::max<uint32_t>(rows[b - 1], hops[j].row_begin + (uint32_t)r);
+        uint64_t total_bytes = 0;
+        for (uint32_t j = 0; j < n_ops; ++j)
+            total_bytes += (uint64_t)(ops[j].out_dim + STREAM_BOX_ROWS - 1) / STREAM_BOX_ROWS *
+                           STREAM_BOX_ROWS * (ops[j].in_dim / 4);
+        uint32_t j = 0, b = 1;
+        uint64_t cum = 0;
+        for (uint32_t blk = 0; blk < (uint32_t)total_blocks && b < G; ++blk) {
+            while (j + 1 < n_ops && blk >= block_begin[j + 1]) ++j;
+            cum += (uint64_t)STREAM_BOX_ROWS * (ops[j].in_dim / 4);
+            while (b < G && cum >= total_bytes * b / G) cb[b++] = blk + 1;
         }
-        rows[G] = (uint32_t)total_rows;
+        for (; b < G; ++b) cb[b] = (uint32_t)total_blocks;
+        cb[G] = (uint32_t)total_blocks;
     }
-    memcpy(host.data() + off_rows, rows.data(), sizeof(uint32_t) * (G + 1));
+    memcpy(host.data() + off_cta, cb.data(), sizeof(uint32_t) * (G + 1));
     std::vector<QuantJob> qj(nq);
     for (auto &kv : xid) {
         const uint32_t i = kv.second;
@@ -865,8 +902,9 @@ int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream
     plan->n_quant = nq;
     plan->grid = G;
     plan->c3 = any_c3;
+    plan->d_maps = (CUtensorMap *)(base + off_maps);
     plan->d_ops = (I2sStreamOp *)(base + off_ops);
-    plan->d_cta_rows = (uint32_t *)(base + off_rows);
+    plan->d_cta_blocks = (uint32_t *)(base + off_cta);
     plan->d_qjobs = (QuantJob *)(base + off_q);
     plan->status = c.d_status;
     return WL_OK;
@@ -1242,11 +1280,12 @@ int wl_dev_i2s_stream_run(wl_i2s_stream_plan *plan, void *stream) {
                    (const QuantJob *)plan->d_qjobs));
     I2sStreamParams p;
     p.ops = plan->d_ops;
+    p.maps = plan->d_maps;
     p.n_ops = plan->n_ops;
-    p.cta_rows = plan->d_cta_rows;
+    p.cta_blocks = plan->d_cta_blocks;
     p.status = plan->status;
     WL_CUDA(launch(kStream[plan->c3 ? 1 : 0], dim3(plan->grid), dim3(STREAM_THREADS),
-                   (size_t)STREAM_STAGES * STREAM_STAGE_BYTES, s, true, p));
+                   STREAM_SMEM, s, true, p));
     return WL_OK;
 }
 

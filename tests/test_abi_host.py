@@ -143,3 +143,25 @@ def test_header_documents_reference_for_each_hot_entry_point():
     for ref in ("bitlinear.rs:67", "bitlinear_sse2.rs:313", "linear.rs:11", "lm_head.rs:29",
                 "lm_head.rs:161", "q6_k_sse2.rs:46", "q8_0_simd.rs:72"):
         assert ref in src, ref
+
+
+def test_stream_plan_validation_before_any_device_work():
+    """A stream plan rejects shapes it cannot stream before touching a device."""
+    import ctypes
+    from project_willamette_b200._abi import WlI2sStreamOp
+    L = lib()
+    buf = (ctypes.c_uint8 * 4096 * 4)()
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    op = WlI2sStreamOp()
+    op.packed, op.w_scale, op.in_dim, op.out_dim = base, 0.05, 384, 4
+    op.x, op.y, op.acc, op.flags = base, base, None, 0
+    plan = ctypes.c_void_p()
+    assert L.wl_i2s_stream_plan_create(ctypes.byref(op), 1, ctypes.byref(plan)) == WLStatus.INVALID_ARGUMENT
+    assert b"in_dim 384" in L.wl_last_error()
+    op.in_dim = 512
+    op.packed = base + 4  # misaligned
+    assert L.wl_i2s_stream_plan_create(ctypes.byref(op), 1, ctypes.byref(plan)) == WLStatus.INVALID_ARGUMENT
+    op.packed = base
+    op.w_scale = float("nan")
+    assert L.wl_i2s_stream_plan_create(ctypes.byref(op), 1, ctypes.byref(plan)) == WLStatus.GGUF_PARSE
+    assert not plan.value

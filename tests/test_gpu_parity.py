@@ -217,14 +217,17 @@ def test_i2s_stream_plan_bit_exact(with_code3):
     import torch
     L = wl.lib()
     rng = np.random.default_rng(99 + with_code3)
-    specs = [(2560, 2560, 0), (2560, 640, 0), (2560, 640, 0), (6912, 2560, 1), (128, 1, 2),
-             (2560, 6912, 3), (2560, 6912, 3), (384, 37, 4), (6912, 100, 5), (7168, 300, 6)]
+    specs = [(2560, 2560, 0), (2560, 640, 0), (2560, 640, 0), (6912, 2560, 1), (512, 1, 2),
+             (2560, 6912, 3), (2560, 6912, 3), (640, 37, 4), (6912, 100, 5), (7168, 300, 6),
+             (12288, 45, 7), (2560, 0, 0), (1024, 64, 8)]
     xs = {}
     ops, keep, ref = [], [], []
     for K, N, xi in specs:
         if xi not in xs:
             xs[xi] = synth.activations(rng, K)
         p = synth.i2s_packed(rng, K, N, 0.002 if (with_code3 and N == 37) else 0.0)
+        if N == 0:
+            p = np.zeros(16, np.uint8)
         s = synth.i2s_scale(rng)
         pd, xd = _dev(torch, p), _dev(torch, xs[xi])
         yd = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
