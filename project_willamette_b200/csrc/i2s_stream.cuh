@@ -5,14 +5,16 @@
 //  * every op's weight is cut into 32-row blocks; the blocks of all ops form
 //    one list, and each CTA (one per SM) owns a contiguous, byte-balanced
 //    range of it;
-//  * each of the 16 warps of a CTA takes every 16th block of that range and
-//    streams it as 32-row x 128-byte boxes with 2-D TMA tensor copies
+//  * each of the 8 warps of a CTA takes every 8th block of that range and
+//    streams it as 64-row x 128-byte boxes with 2-D TMA tensor copies
 //    (cp.async.bulk.tensor, 128-byte swizzle) through its own 3-stage
-//    shared-memory ring -- lane l owns row l of the box, so there are no
-//    cross-lane reductions, and the swizzle makes the 32 lanes' 16-byte reads
-//    (one per row) hit distinct banks;
+//    shared-memory ring -- lane l owns rows l and l+32 of the box, so there
+//    are no cross-lane reductions, and the swizzle makes the 32 lanes' 16-byte
+//    reads (one per row) hit distinct banks;
 //  * activations (quantised beforehand by quantize_jobs_kernel, one CTA per
-//    distinct input) are read with warp-uniform loads that L1 broadcasts.
+//    distinct input) are read with warp-uniform loads that L1 broadcasts, and
+//    each load serves two rows: register write-back of the broadcast
+//    activations, not DRAM, limited the one-row-per-lane form.
 // Rows past an op's end and bytes past a row's end arrive as zeros (TMA
 // out-of-bounds fill) and are skipped.
 #pragma once
@@ -26,10 +28,11 @@
 
 namespace wl {
 
-constexpr int STREAM_WARPS = 16;
+constexpr int STREAM_WARPS = 8;
 constexpr int STREAM_THREADS = STREAM_WARPS * 32;
 constexpr int STREAM_WSTAGES = 3;            // TMA boxes in flight per warp
-constexpr uint32_t STREAM_BOX_ROWS = 32;
+constexpr int STREAM_RPL = 2;                // rows per lane: activations loaded once per 2 rows
+constexpr uint32_t STREAM_BOX_ROWS = 32 * STREAM_RPL;
 constexpr uint32_t STREAM_BOX_BYTES = 128;   // 8 weight slots of 16 bytes
 constexpr uint32_t STREAM_BOX = STREAM_BOX_ROWS * STREAM_BOX_BYTES;
 constexpr uint32_t STREAM_MIN_K = 512;   // a row spans at least one 128-byte box
@@ -108,7 +111,7 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
-// A warp's walk over (block, slice) boxes: blocks bi = first, first+16, ...
+// A warp's walk over (block, slice) boxes: blocks bi = first, first+8, ...
 // below `end`; slices 0 .. ceil(K/512)-1 of each block.
 struct BoxWalk {
     uint32_t bi, end, j, si, S;
@@ -176,8 +179,13 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     uint32_t cur = 0xFFFFFFFFu, P = 0;
     int32_t asum = 0;
     float combined = 0.0f;
-    I2sAcc acc = {0, 0, 0, 0};
-    int32_t corr = 0;
+    I2sAcc acc[STREAM_RPL];
+    int32_t corr[STREAM_RPL];
+#pragma unroll
+    for (int r = 0; r < STREAM_RPL; ++r) {
+        acc[r] = {0, 0, 0, 0};
+        corr[r] = 0;
+    }
     bool timeout = false;
     for (uint32_t k = 0; walk.valid(); ++k) {
         const uint32_t st = k % STREAM_WSTAGES;
@@ -202,48 +210,64 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
             asum = s;
             combined = __fmul_rn(op.w_scale, __ldg(op.act_scale));
         }
-        const uint8_t *line = ring + st * STREAM_BOX + lane * STREAM_BOX_BYTES;
-        uint32_t c3 = 0;
+        const uint8_t *box = ring + st * STREAM_BOX;
+        uint32_t c3[STREAM_RPL];
+#pragma unroll
+        for (int r = 0; r < STREAM_RPL; ++r) c3[r] = 0;
 #pragma unroll
         for (uint32_t s = 0; s < 8; ++s) {
             const uint32_t pp = walk.si * 8 + s;
             if (pp < P) {
-                const uint4 wv =
-                    *reinterpret_cast<const uint4 *>(line + ((s ^ (lane & 7u)) << 4));
                 const int8_t *qa = op.q + (pp >> 1) * 128u + (pp & 1u) * 16u;
                 uint4 a[4];
 #pragma unroll
                 for (int o = 0; o < 4; ++o) a[o] = __ldg(reinterpret_cast<const uint4 *>(qa + 32 * o));
-                i2s_slot<C3>(wv, a, acc, c3);
+#pragma unroll
+                for (int r = 0; r < STREAM_RPL; ++r) {
+                    // row lane + 32r sits in 128-byte line lane + 32r; its swizzle
+                    // phase is (lane + 32r) & 7 = lane & 7
+                    const uint4 wv = *reinterpret_cast<const uint4 *>(
+                        box + (lane + 32u * r) * STREAM_BOX_BYTES + ((s ^ (lane & 7u)) << 4));
+                    i2s_slot<C3>(wv, a, acc[r], c3[r]);
+                }
             }
         }
         if constexpr (C3) {
-            if ((c3 & 0x55555555u) != 0u) {  // this lane's row has code 0b11 in this box
-                for (uint32_t s = 0; s < 8; ++s) {
-                    const uint32_t pp = walk.si * 8 + s;
-                    if (pp >= P) break;
-                    const uint4 wv =
-                        *reinterpret_cast<const uint4 *>(line + ((s ^ (lane & 7u)) << 4));
-                    uint4 a[4];
-                    i2s_load_act(op.q, pp, a);
-                    corr = i2s_word_c3(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, corr);
-                    corr = i2s_word_c3(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, corr);
-                    corr = i2s_word_c3(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, corr);
-                    corr = i2s_word_c3(wv.w, a[0].w, a[1].w, a[2].w, a[3].w, corr);
+#pragma unroll
+            for (int r = 0; r < STREAM_RPL; ++r) {
+                if ((c3[r] & 0x55555555u) != 0u) {  // this row has code 0b11 in this box
+                    const uint8_t *line = box + (lane + 32u * r) * STREAM_BOX_BYTES;
+                    for (uint32_t s = 0; s < 8; ++s) {
+                        const uint32_t pp = walk.si * 8 + s;
+                        if (pp >= P) break;
+                        const uint4 wv =
+                            *reinterpret_cast<const uint4 *>(line + ((s ^ (lane & 7u)) << 4));
+                        uint4 a[4];
+                        i2s_load_act(op.q, pp, a);
+                        int32_t c = corr[r];
+                        c = i2s_word_c3(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, c);
+                        c = i2s_word_c3(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, c);
+                        c = i2s_word_c3(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, c);
+                        c = i2s_word_c3(wv.w, a[0].w, a[1].w, a[2].w, a[3].w, c);
+                        corr[r] = c;
+                    }
                 }
             }
         }
         __syncwarp();  // every lane is done with this stage
         if (lane == 0 && ahead.valid()) issue(st);
-        if (walk.si + 1 == walk.S) {  // last box of the block: finish the row
-            const uint32_t row = (walk.bi - op.block_begin) * STREAM_BOX_ROWS + lane;
-            if (row < op.N) {
-                const int32_t dot = i2s_acc_total(acc) - asum - 2 * corr;
-                op.y[row] = __fmul_rn(combined, __int2float_rn(dot));
-                if (op.acc) op.acc[row] = dot;
+        if (walk.si + 1 == walk.S) {  // last box of the block: finish the rows
+#pragma unroll
+            for (int r = 0; r < STREAM_RPL; ++r) {
+                const uint32_t row = (walk.bi - op.block_begin) * STREAM_BOX_ROWS + lane + 32u * r;
+                if (row < op.N) {
+                    const int32_t dot = i2s_acc_total(acc[r]) - asum - 2 * corr[r];
+                    op.y[row] = __fmul_rn(combined, __int2float_rn(dot));
+                    if (op.acc) op.acc[row] = dot;
+                }
+                acc[r] = {0, 0, 0, 0};
+                corr[r] = 0;
             }
-            acc = {0, 0, 0, 0};
-            corr = 0;
         }
         walk.next(p.ops, p.n_ops);
     }
