@@ -182,6 +182,16 @@ int wl_dev_i2s_matvec(const wl_i2s_dev_weight *weights, uint32_t n_weights, uint
 int wl_dev_i2s_matvec_fused_f32(const wl_i2s_dev_weight *weights, uint32_t n_weights,
                                 uint32_t in_dim, const float *x, void *stream);
 
+/* Prefill GEMM from f32 activations: x is m x in_dim, y m x out_dim (acc
+ * optional), row-major, device.  With WL_I2S_NO_CODE3 in flags it is one
+ * tcgen05 int8 tensor-core GEMM (kind::i8, accumulators in tensor memory);
+ * otherwise one exact matvec per token.  workspace: wl_i2s_gemm_workspace_bytes
+ * bytes, 16-byte aligned (quantised activations, scales, row sums). */
+size_t wl_i2s_gemm_workspace_bytes(uint32_t m, uint32_t in_dim);
+int wl_dev_i2s_gemm_f32(const uint8_t *packed, float w_scale, uint32_t in_dim, uint32_t out_dim,
+                        uint32_t m, const float *x, float *y, int32_t *acc, void *workspace,
+                        uint32_t flags, void *stream);
+
 /* *found (device u32) = 1 if the packed tensor contains a 0b11 code, else 0. */
 int wl_dev_i2s_scan_code3(const uint8_t *packed, size_t bytes, uint32_t *found, void *stream);
 

@@ -72,7 +72,7 @@ struct I2sMatvecParams {
 // scale = max/127, or 1.0 and all-zero q for an all-zero row.
 __global__ void __launch_bounds__(QUANT_THREADS)
     quantize_absmax_kernel(const float *__restrict__ x, uint32_t n, int8_t *__restrict__ q,
-                           float *__restrict__ act_scale) {
+                           float *__restrict__ act_scale, int32_t *__restrict__ rowsum) {
     pdl_launch_dependents();
     pdl_wait();
     const float *xr = x + (size_t)blockIdx.x * n;
@@ -98,10 +98,14 @@ __global__ void __launch_bounds__(QUANT_THREADS)
     if (max_abs == 0.0f) {
         for (uint32_t i = threadIdx.x * 4; i < n; i += QUANT_THREADS * 4)
             *reinterpret_cast<uint32_t *>(qr + i) = 0u;
-        if (threadIdx.x == 0) act_scale[blockIdx.x] = 1.0f;
+        if (threadIdx.x == 0) {
+            act_scale[blockIdx.x] = 1.0f;
+            if (rowsum) rowsum[blockIdx.x] = 0;
+        }
         return;
     }
     const float inv = __fdiv_rn(127.0f, max_abs);
+    int32_t rsum = 0;
     for (uint32_t i = threadIdx.x * 4; i < n; i += QUANT_THREADS * 4) {
         const float4 v = *reinterpret_cast<const float4 *>(xr + i);
         const float e[4] = {v.x, v.y, v.z, v.w};
@@ -114,8 +118,21 @@ __global__ void __launch_bounds__(QUANT_THREADS)
             packed |= (uint32_t)(qi & 0xFF) << (8 * k);
         }
         *reinterpret_cast<uint32_t *>(qr + i) = packed;
+        rsum = __dp4a((int)packed, 0x01010101, rsum);
     }
     if (threadIdx.x == 0) act_scale[blockIdx.x] = __fdiv_rn(max_abs, 127.0f);
+    if (rowsum) {  // sum of the quantised row (the GEMM's code-offset term)
+        __shared__ int32_t ired[QUANT_THREADS / 32];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, off);
+        if ((threadIdx.x & 31) == 0) ired[threadIdx.x >> 5] = rsum;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int32_t t = 0;
+            for (int w = 0; w < QUANT_THREADS / 32; ++w) t += ired[w];
+            rowsum[blockIdx.x] = t;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------

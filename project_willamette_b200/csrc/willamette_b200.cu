@@ -20,6 +20,7 @@
 #include "argmax.cuh"
 #include "i2s_matvec.cuh"
 #include "i2s_stream.cuh"
+#include "i2s_gemm.cuh"
 #include "q6k_lmhead.cuh"
 #include "q8_0.cuh"
 
@@ -80,7 +81,7 @@ struct Ctx {
     uint32_t *h_status = nullptr;  // pinned
     void *pinned = nullptr;
     size_t pinned_cap = 0;
-    DevBuf x, y, q, scale, acc, ids, scratch;
+    DevBuf x, y, q, scale, acc, ids, scratch, rowsum;
     std::map<CacheKey, CachedWeight> cache;
 };
 
@@ -90,6 +91,12 @@ Ctx &ctx() {
 }
 
 constexpr int WL_MAX_DYN_SMEM = 227 * 1024 - 1024;
+// From this many tokens on, prefill runs as one tensor-core GEMM.
+constexpr size_t I2S_GEMM_MIN_TOKENS = 16;
+
+int launch_i2s_gemm(const uint8_t *packed, float w_scale, uint32_t K, uint32_t N, uint32_t M,
+                    const int8_t *q, const float *act_scale, const int32_t *rowsum, float *y,
+                    int32_t *acc, cudaStream_t s, bool pdl, uint32_t *status);
 
 using I2sKernel = void (*)(I2sMatvecParams);
 using I2sStreamKernel = void (*)(I2sStreamParams);
@@ -116,7 +123,9 @@ int configure_kernels() {
                 WL_CUDA(cudaFuncSetAttribute((const void *)k,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              WL_MAX_DYN_SMEM / 2));
-    const void *others[] = {(const void *)kStream[0], (const void *)kStream[1],
+    const void *others[] = {(const void *)i2s_gemm_kernel<64>, (const void *)i2s_gemm_kernel<128>,
+                            (const void *)i2s_gemm_kernel<256>,
+                            (const void *)kStream[0], (const void *)kStream[1],
                             (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<4>,
                             (const void *)q8_0_matvec_kernel};
     for (const void *k : others)
@@ -232,10 +241,10 @@ int i2s_shape_index(uint32_t K, int *lpr) {
 }
 
 int launch_quantize(const float *x, uint32_t n, uint32_t m, int8_t *q, float *scale,
-                    cudaStream_t s, bool pdl) {
+                    cudaStream_t s, bool pdl, int32_t *rowsum = nullptr) {
     if (m == 0 || n == 0) return WL_OK;
     WL_CUDA(launch(quantize_absmax_kernel, dim3(m), dim3(QUANT_THREADS), 0, s, pdl, x, n, q,
-                   scale));
+                   scale, rowsum));
     return WL_OK;
 }
 
@@ -574,10 +583,26 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
     uint8_t *pin = (uint8_t *)c.pinned;
     memcpy(pin, input, xin);
     WL_CUDA(cudaMemcpyAsync(c.x.p, pin, xin, cudaMemcpyHostToDevice, c.stream));
-    const bool fuse = K <= I2S_FUSE_Q_MAX_K;
-    if (!fuse && (rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m, (int8_t *)c.q.p,
-                                       (float *)c.scale.p, c.stream, false)))
+    // Prefill of many tokens on code-3-free weights: one tensor-core GEMM.
+    const bool gemm = m >= I2S_GEMM_MIN_TOKENS && !cw->has_code3 && m <= 0x7FFFFFFFu;
+    const bool fuse = !gemm && K <= I2S_FUSE_Q_MAX_K;
+    if (gemm) {
+        if ((rc = grow(c.rowsum, m * 4))) return rc;
+        if ((rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m, (int8_t *)c.q.p,
+                                  (float *)c.scale.p, c.stream, false, (int32_t *)c.rowsum.p)))
+            return rc;
+        if ((rc = launch_i2s_gemm((const uint8_t *)cw->dptr, w_scale, K, N, (uint32_t)m,
+                                  (const int8_t *)c.q.p, (const float *)c.scale.p,
+                                  (const int32_t *)c.rowsum.p, (float *)c.y.p,
+                                  acc_out ? (int32_t *)c.acc.p : nullptr, c.stream, true,
+                                  c.d_status)))
+            return rc;
+        m = 0;  // no per-token launches below
+    } else if (!fuse && (rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m,
+                                              (int8_t *)c.q.p, (float *)c.scale.p, c.stream,
+                                              false)))
         return rc;
+    const size_t m_rows = gemm ? (yout / 4 / N) : m;
     for (size_t t = 0; t < m; ++t) {
         wl_i2s_dev_weight dw = {(const uint8_t *)cw->dptr, w_scale, N, (float *)c.y.p + t * N,
                                 (int32_t *)c.acc.p + t * N,
@@ -596,6 +621,7 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
         }
         if ((rc = launch_i2s(L, c.stream, t > 0 || !fuse))) return rc;
     }
+    m = m_rows;
     uint8_t *py = pin + xin, *pacc = py + yout, *pq = pacc + yout, *ps = pq + m * (size_t)K;
     WL_CUDA(cudaMemcpyAsync(py, c.y.p, yout, cudaMemcpyDeviceToHost, c.stream));
     if (acc_out) WL_CUDA(cudaMemcpyAsync(pacc, c.acc.p, yout, cudaMemcpyDeviceToHost, c.stream));
@@ -787,6 +813,61 @@ int encode_i2s_map(const uint8_t *packed, uint32_t K, uint32_t N, CUtensorMap *m
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(WL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return WL_OK;
+}
+
+// ------------------------------------------------------------------ prefill GEMM
+int encode_2d(EncodeTiledFn enc, CUtensorMap *map, const void *base, uint64_t inner_bytes,
+              uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+    const cuuint64_t dims[2] = {inner_bytes, rows};
+    const cuuint64_t strides[1] = {inner_bytes};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(WL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return WL_OK;
+}
+
+// Y[m][n] for m tokens from pre-quantised activations q [m][K] (with their
+// scales and row sums) and code-3-free packed weights [N][K/4].
+int launch_i2s_gemm(const uint8_t *packed, float w_scale, uint32_t K, uint32_t N, uint32_t M,
+                    const int8_t *q, const float *act_scale, const int32_t *rowsum, float *y,
+                    int32_t *acc, cudaStream_t s, bool pdl, uint32_t *status) {
+    if (M == 0 || N == 0) return WL_OK;
+    EncodeTiledFn enc;
+    int rc = get_encode_tiled(&enc);
+    if (rc) return rc;
+    const uint32_t mt = (M + GEMM_BM - 1) / GEMM_BM;
+    const uint32_t sms = (uint32_t)sm_count_for_launch();
+    // widest tile that still gives every SM work
+    int bn = 256;
+    if ((uint64_t)mt * ((N + 255) / 256) < sms) bn = 128;
+    if (bn == 128 && (uint64_t)mt * ((N + 127) / 128) < sms) bn = 64;
+    I2sGemmParams p;
+    memset(&p, 0, sizeof p);
+    if ((rc = encode_2d(enc, &p.a_map, q, K, M, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    if ((rc = encode_2d(enc, &p.bp_map, packed, K / 4u, N, GEMM_BK / 4, (uint32_t)bn,
+                        CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return rc;
+    p.act_scale = act_scale;
+    p.rowsum = rowsum;
+    p.w_scale = w_scale;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.y = y;
+    p.acc = acc;
+    p.status = status;
+    const dim3 grid((N + bn - 1) / bn, mt);
+    if (bn == 256)
+        WL_CUDA(launch(i2s_gemm_kernel<256>, grid, dim3(GEMM_THREADS), GemmSmem<256>::DYN, s, pdl, p));
+    else if (bn == 128)
+        WL_CUDA(launch(i2s_gemm_kernel<128>, grid, dim3(GEMM_THREADS), GemmSmem<128>::DYN, s, pdl, p));
+    else
+        WL_CUDA(launch(i2s_gemm_kernel<64>, grid, dim3(GEMM_THREADS), GemmSmem<64>::DYN, s, pdl, p));
     return WL_OK;
 }
 
@@ -1293,6 +1374,49 @@ int wl_i2s_stream_plan_destroy(wl_i2s_stream_plan *plan) {
     if (!plan) return WL_OK;
     if (plan->d_block) cudaFree(plan->d_block);
     delete plan;
+    return WL_OK;
+}
+
+size_t wl_i2s_gemm_workspace_bytes(uint32_t m, uint32_t in_dim) {
+    return (size_t)m * in_dim + 2u * (((size_t)m * 4u + 15u) & ~(size_t)15u) + 16u;
+}
+
+int wl_dev_i2s_gemm_f32(const uint8_t *packed, float w_scale, uint32_t in_dim, uint32_t out_dim,
+                        uint32_t m, const float *x, float *y, int32_t *acc, void *workspace,
+                        uint32_t flags, void *stream) {
+    if (in_dim == 0 || in_dim % 128 || in_dim > WL_I2S_MAX_IN_DIM)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128 <= %u", in_dim,
+                    WL_I2S_MAX_IN_DIM);
+    if (!std::isfinite(w_scale)) return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale");
+    if (!packed || !x || !y || !workspace || !aligned16(packed) || !aligned16(x) ||
+        !aligned16(workspace))
+        return fail(WL_ERR_INVALID_ARGUMENT, "NULL or misaligned pointer");
+    if (m == 0 || out_dim == 0) return WL_OK;
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    cudaStream_t s = (cudaStream_t)stream;
+    int8_t *q = (int8_t *)workspace;
+    float *scale = (float *)((uint8_t *)workspace + (size_t)m * in_dim);
+    int32_t *rowsum = (int32_t *)((uint8_t *)scale + (((size_t)m * 4u + 15u) & ~(size_t)15u));
+    int rc;
+    if (flags & WL_I2S_NO_CODE3) {
+        if ((rc = launch_quantize(x, in_dim, m, q, scale, s, true, rowsum))) return rc;
+        return launch_i2s_gemm(packed, w_scale, in_dim, out_dim, m, q, scale, rowsum, y, acc, s,
+                               true, status);
+    }
+    // Weights that may hold code 0b11: one exact matvec per token.
+    if ((rc = launch_quantize(x, in_dim, m, q, scale, s, true))) return rc;
+    for (uint32_t t = 0; t < m; ++t) {
+        wl_i2s_dev_weight w = {packed, w_scale, out_dim, y + (size_t)t * out_dim,
+                               acc ? acc + (size_t)t * out_dim : nullptr, 0};
+        I2sLaunch L;
+        L.w = &w;
+        L.nw = 1;
+        L.K = in_dim;
+        L.q = q + (size_t)t * in_dim;
+        L.act_scale = scale + t;
+        if ((rc = launch_i2s(L, s, true))) return rc;
+    }
     return WL_OK;
 }
 

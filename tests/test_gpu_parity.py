@@ -139,6 +139,56 @@ def test_i2s_gemm_rows_match_per_token_matvec():
     assert_bitexact(Y, RY, "gemm")
 
 
+@pytest.mark.parametrize("in_dim,out_dim,m", [(2560, 2560, 16), (2560, 640, 33), (640, 1000, 128),
+                                              (512, 64, 200), (6912, 2560, 130),
+                                              (2560, 6912, 256), (128, 3, 40)])
+def test_i2s_gemm_tensor_core_bit_exact(in_dim, out_dim, m):
+    """Prefill (>= 16 tokens, code-3-free weights) runs as one tcgen05 GEMM;
+    every token must match the reference's per-token matvec bit for bit."""
+    rng = np.random.default_rng(in_dim + out_dim + m)
+    packed = synth.i2s_packed(rng, in_dim, out_dim)
+    scale = synth.i2s_scale(rng)
+    X = synth.activations(rng, m, in_dim)
+    X[1] = 0.0
+    X[m // 2, 7] = 1e5
+    t = TensorView.i2s("gemm", in_dim, out_dim, packed, scale)
+    Y, acc = wl.bitlinear_i2s_gemm_f32(t, X, with_acc=True)
+    RY, racc, _ = oracle.i2s_gemm_rows(packed, scale, in_dim, out_dim, X, n_threads=0)
+    assert np.array_equal(acc, racc)
+    assert_bitexact(Y, RY, "tcgen05 gemm")
+
+
+def test_i2s_gemm_with_code3_falls_back_exactly():
+    rng = np.random.default_rng(8)
+    in_dim, out_dim, m = 1024, 300, 48
+    packed = synth.i2s_packed(rng, in_dim, out_dim, code3_fraction=0.01)
+    scale = synth.i2s_scale(rng)
+    X = synth.activations(rng, m, in_dim)
+    Y, acc = wl.bitlinear_i2s_gemm_f32(TensorView.i2s("g3", in_dim, out_dim, packed, scale), X,
+                                       with_acc=True)
+    RY, racc, _ = oracle.i2s_gemm_rows(packed, scale, in_dim, out_dim, X, n_threads=0)
+    assert np.array_equal(acc, racc)
+    assert_bitexact(Y, RY, "gemm code-3 fallback")
+
+
+def test_i2s_gemm_config3_full_size_sampled():
+    """BASELINE config 3 at M = 2048 for the 6912 x 2560 weight: all rows
+    checked against the oracle on a sample of tokens, plus y(-X) = -y(X)."""
+    rng = np.random.default_rng(0x5EED + 3)
+    in_dim, out_dim, m = 2560, 6912, 2048
+    packed = synth.i2s_packed(rng, in_dim, out_dim)
+    scale = synth.i2s_scale(rng)
+    X = synth.activations(rng, m, in_dim)
+    t = TensorView.i2s("cfg3", in_dim, out_dim, packed, scale)
+    Y, acc = wl.bitlinear_i2s_gemm_f32(t, X, with_acc=True)
+    sample = np.array([0, 1, 127, 128, 1000, 2047])
+    RY, racc, _ = oracle.i2s_gemm_rows(packed, scale, in_dim, out_dim, X[sample], n_threads=0)
+    assert np.array_equal(acc[sample], racc)
+    assert_bitexact(Y[sample], RY, "config 3 sample")
+    Yn, accn = wl.bitlinear_i2s_gemm_f32(t, -X, with_acc=True)
+    assert np.array_equal(accn, -acc)
+
+
 def test_i2s_dev_fused_weights_match_separate():
     """One launch over Q/K/V-shaped weights sharing one quantised input."""
     import torch
