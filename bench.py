@@ -276,8 +276,9 @@ def run_gpu(args) -> None:
     ms_chain_step = ms_chain / chain_steps
     pk = peaks()
 
-    # ---- lm-head (Q6_K 128256 x 2560, batch 1) timed separately
+    # ---- lm-head (Q6_K 128256 x 2560, batch 1 and 64) and prefill GEMM (config 3)
     lm = lm_head_bench(torch, dev, L, stream, rng, reps=max(20, min(args.steps, 200)))
+    gemm = gemm_bench(torch, dev, L, stream, rng)
 
     # ---- e2e through the host-buffer C ABI
     e2e = e2e_bench(torch, layers, wl, rng, steps=max(1, min(args.steps, 20)))
@@ -317,6 +318,7 @@ def run_gpu(args) -> None:
                     "api": "wl_bitlinear_i2s_matvec_f32 (host buffers, one call per BitLinear)"},
             "gpu_launches": launches_per_step * args.steps,
             "lm_head": lm,
+            "prefill_gemm": gemm,
             "clocks": clk.summary(),
         }
         if cpu is not None:
@@ -373,8 +375,81 @@ def lm_head_bench(torch, dev, L, stream, rng, reps: int) -> dict:
         torch.cuda.synchronize()
     us = a.elapsed_time(b) * 1e3 / reps
     alg = 269337600 + 4 * D_MODEL + 4
+    # batch 64 (config 4), same exact arithmetic
+    H = torch.randn(64, D_MODEL, device=dev)
+    ids64 = torch.zeros(64, dtype=torch.int32, device=dev)
+    scratch64 = torch.zeros(L.wl_q6k_scratch_bytes(64), dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        def once64():
+            rc = L.wl_dev_q6k_lm_head(packed.data_ptr(), D_MODEL, VOCAB, H.data_ptr(), 64, None,
+                                      ids64.data_ptr(), scratch64.data_ptr(), s)
+            if rc:
+                raise RuntimeError(L.wl_last_error().decode())
+        once64()
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(5):
+            once64()
+        b.record(stream)
+        torch.cuda.synchronize()
+    us64 = a.elapsed_time(b) * 1e3 / 5
     return {"us_per_call": round(us, 2), "gbs": round(alg / (us * 1e-6) / 1e9, 1),
-            "algorithmic_bytes": alg, "vocab": VOCAB, "batch": 1, "exact_logits": True}
+            "algorithmic_bytes": alg, "vocab": VOCAB, "batch": 1, "exact_logits": True,
+            "batch64_us_per_call": round(us64, 1),
+            "batch64_gflops": round(2 * 64 * D_MODEL * VOCAB / (us64 * 1e-6) / 1e9, 1)}
+
+
+def int8_peak_tops() -> dict:
+    """Dense int8 tensor peak: MEASURED_PEAKS.json has the cuBLAS bf16 figure;
+    B200's dense int8 rate is twice its dense bf16 rate."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return {"tops": 2.0 * float(json.load(f)["bf16_tflops"]),
+                    "source": "2 x measured bf16 (burst)"}
+    except Exception:
+        return {"tops": 4500.0, "source": "nominal dense int8"}
+
+
+def gemm_bench(torch, dev, L, stream, rng) -> dict:
+    """prefill GEMM, M in {2048, 512, 128} x the three
+    BitNet-2B weight shapes, one tcgen05 GEMM per call (bit-exact path)."""
+    from project_willamette_b200 import _abi, synth
+    pk = int8_peak_tops()
+    shapes = [(2560, 6912), (2560, 2560), (6912, 2560)]  # (K, N)
+    rows = []
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for M in (2048, 512, 128):
+            for K, N in shapes:
+                packed = torch.from_numpy(synth.i2s_packed(rng, K, N)).to(dev)
+                x = torch.randn(M, K, device=dev)
+                y = torch.empty(M, N, device=dev)
+                ws = torch.empty(L.wl_i2s_gemm_workspace_bytes(M, K), dtype=torch.uint8, device=dev)
+                scale = float(np.float32(rng.uniform(0.01, 0.1)))
+
+                def once():
+                    rc = L.wl_dev_i2s_gemm_f32(packed.data_ptr(), scale, K, N, M, x.data_ptr(),
+                                               y.data_ptr(), None, ws.data_ptr(),
+                                               _abi.WL_I2S_NO_CODE3, s)
+                    if rc:
+                        raise RuntimeError(L.wl_last_error().decode())
+
+                for _ in range(3):
+                    once()
+                reps = 50
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(reps):
+                    once()
+                b.record(stream)
+                torch.cuda.synchronize()
+                us = a.elapsed_time(b) * 1e3 / reps
+                tops = 2.0 * M * N * K / (us * 1e-6) / 1e12
+                rows.append({"M": M, "N": N, "K": K, "us": round(us, 2), "tops": round(tops, 1),
+                             "frac": round(tops / pk["tops"], 4)})
+    return {"peak_tops": pk["tops"], "peak_source": pk["source"],
+            "note": "per call: quantise + tcgen05 GEMM (2 kernels); ops = 2*M*N*K",
+            "cases": rows}
 
 
 def e2e_bench(torch, layers, wl, rng, steps: int) -> dict:

@@ -207,6 +207,7 @@ typedef struct wl_i2s_stream_op {
     float *y;              /* device f32 output */
     int32_t *acc;          /* device, or NULL */
     uint32_t flags;        /* WL_I2S_NO_CODE3 or 0 */
+    uint32_t row_off;      /* tensor parallel: this slice's first row in y (else 0) */
 } wl_i2s_stream_op;
 typedef struct wl_i2s_stream_plan wl_i2s_stream_plan;
 int wl_i2s_stream_plan_create(const wl_i2s_stream_op *ops, uint32_t n_ops,
@@ -236,6 +237,46 @@ int wl_dev_i2s_matvec_f32(const uint8_t *packed, float w_scale, uint32_t in_dim,
 #define WL_NOALLOC_MAX_IN_DIM 16384u
 int wl_dev_i2s_matvec_f32_noalloc(const uint8_t *packed, float w_scale, uint32_t in_dim,
                                   uint32_t out_dim, const float *x, float *y, void *stream);
+
+/* ------------------------------------------------ tensor parallel (one GPU per process)
+ * North star: BitLinear output rows split across the GPUs of one box with an
+ * all-gather; the lm-head split by vocab rows with a (max, index) reduction.
+ * Here the kernels themselves store their outputs into every rank's
+ * symmetric block over NVLink (CUDA IPC) and signal arrival counters there
+ * (system-scope release/acquire); the consumer's kernel waits, bounded, on
+ * its own memory.  Every rank must issue the same sequence of wl_tp_* calls.
+ * Setup: wl_tp_create on every rank, exchange the WL_TP_HANDLE_BYTES handles
+ * (any host channel), wl_tp_connect with all world handles in rank order. */
+#define WL_TP_HANDLE_BYTES 64
+typedef struct wl_tp_group wl_tp_group;
+int wl_tp_create(int rank, int world, size_t sym_bytes, wl_tp_group **group,
+                 uint8_t *handle_out);
+int wl_tp_connect(wl_tp_group *group, const uint8_t *handles);
+/* Device pointer at `offset` in this rank's symmetric region (NULL past its end). */
+void *wl_tp_buffer(wl_tp_group *group, size_t offset);
+int wl_tp_destroy(wl_tp_group *group);
+/* Enqueue a wait until every rank's outputs so far are visible here. */
+int wl_tp_wait(wl_tp_group *group, void *stream);
+/* Row slice of up to WL_I2S_MAX_FUSED BitLinears sharing x: weights[j] holds
+ * rows [row_offsets[j], row_offsets[j] + out_dim) of the full weight and its
+ * y is the FULL output vector in the symmetric region; every rank ends up
+ * with the complete y.  wait_for_input: the kernel first waits until every
+ * rank has finished every earlier wl_tp_* op -- needed when x was gathered by
+ * one of them, or when y overwrites a vector a peer may still be reading. */
+int wl_tp_i2s_matvec_fused_f32(wl_tp_group *group, const wl_i2s_dev_weight *weights,
+                               const uint32_t *row_offsets, uint32_t n_weights, uint32_t in_dim,
+                               const float *x, int wait_for_input, void *stream);
+/* A stream plan whose ops are row slices (wl_i2s_stream_op.row_off) with y in
+ * the symmetric region; outputs are gathered on every rank.  It does not wait:
+ * precede it with wl_tp_wait when its inputs were gathered. */
+int wl_tp_i2s_stream_run(wl_tp_group *group, wl_i2s_stream_plan *plan, void *stream);
+/* Vocab-sharded greedy lm-head: this rank holds rows [row_offset, row_offset +
+ * vocab_shard) (repacked, wl_dev_q6k_repack); ids (batch <= 64) are the
+ * global argmax with the reference's tie / NaN rules, on every rank.
+ * scratch: wl_q6k_scratch_bytes(batch) bytes, zero before the first use. */
+int wl_tp_q6k_lm_head_greedy(wl_tp_group *group, const uint8_t *packed_shard, uint32_t n_embd,
+                             uint32_t vocab_shard, uint32_t row_offset, const float *hidden,
+                             uint32_t batch, uint32_t *ids, void *scratch, void *stream);
 
 /* Q6_K lm-head.  The raw GGUF rows (vocab x n_embd/256 x 210 bytes) are
  * repacked once into the device layout (wl_q6k_packed_bytes bytes). */

@@ -64,8 +64,11 @@ class WlI2sStreamOp(C.Structure):
         ("y", C.c_void_p),
         ("acc", C.c_void_p),
         ("flags", C.c_uint32),
+        ("row_off", C.c_uint32),
     ]
 
+
+WL_TP_HANDLE_BYTES = 64
 
 _vp = C.c_void_p
 _sz = C.c_size_t
@@ -107,6 +110,15 @@ PROTOTYPES = {
     "wl_q8_0_packed_bytes": ([_u32, _u32], _sz),
     "wl_dev_q8_0_repack": ([_vp, _u32, _u32, _vp, _vp], _i),
     "wl_dev_q8_0_matvec": ([_vp, _u32, _u32, _vp, _vp, _vp], _i),
+    "wl_tp_create": ([_i, _i, _sz, C.POINTER(_vp), C.POINTER(C.c_uint8)], _i),
+    "wl_tp_connect": ([_vp, C.POINTER(C.c_uint8)], _i),
+    "wl_tp_buffer": ([_vp, _sz], _vp),
+    "wl_tp_destroy": ([_vp], _i),
+    "wl_tp_wait": ([_vp, _vp], _i),
+    "wl_tp_i2s_matvec_fused_f32": ([_vp, C.POINTER(WlI2sDevWeight), C.POINTER(_u32), _u32, _u32,
+                                    _vp, _i, _vp], _i),
+    "wl_tp_i2s_stream_run": ([_vp, _vp, _vp], _i),
+    "wl_tp_q6k_lm_head_greedy": ([_vp, _vp, _u32, _u32, _u32, _vp, _u32, _vp, _vp, _vp], _i),
 }
 
 _lib = None

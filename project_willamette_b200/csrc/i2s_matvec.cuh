@@ -28,6 +28,7 @@
 
 #include <cstdint>
 
+#include "tp.cuh"
 #include "wl_ptx.cuh"
 
 namespace wl {
@@ -46,6 +47,7 @@ struct I2sJob {
     uint32_t row_begin;  // first row of this job in the concatenated row space
     float *y;
     int32_t *acc;        // may be null
+    uint32_t row_off;    // tensor parallel: first global row of this slice in y/acc
 };
 
 struct I2sMatvecParams {
@@ -62,6 +64,7 @@ struct I2sMatvecParams {
     int8_t *q_out;          // FUSE_Q: optional copy of the quantised input (CTA 0)
     float *scale_out;       // FUSE_Q: optional activation scale (CTA 0)
     uint32_t *status;
+    TpParams tp;            // world 0: single GPU
 };
 
 // ---------------------------------------------------------------------------
@@ -307,6 +310,12 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     const uint32_t r1 = min(r0 + p.rows_per_cta, p.total_rows);
     if (r0 >= r1) {
         pdl_launch_dependents();
+        if (p.tp.world) {
+            // the CTA-done counter is shared with the previous kernel, whose
+            // last CTA re-arms it: count only once that kernel has finished
+            pdl_wait();
+            if (tid == 0) tp_arrive(p.tp);
+        }
         return;
     }
     const uint32_t nchunks = (r1 - r0 + RPI - 1) / RPI;
@@ -324,6 +333,11 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();  // the input comes from the previous kernel
+    if (p.tp.world && p.tp.wait_target) {
+        // the input is a vector all ranks gathered into this rank's block
+        if (tid == 0 && !tp_wait(p.tp, p.tp.wait_target)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
+        __syncthreads();
+    }
 
     float act_scale;
     const int8_t *q;
@@ -378,6 +392,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             // before this CTA's shared memory is released.
             for (uint32_t k = c; k < min(nchunks, c + nst); ++k)
                 (void)mbar_wait(&full_bar[k % nst], (k / nst) & 1u);
+            if (p.tp.world && tid == 0) tp_arrive(p.tp);
             return;
         }
         const uint32_t row_local = warp * RPW + sub;
@@ -425,8 +440,13 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             const I2sJob &job = p.jobs[j];
             const uint32_t local = row - job.row_begin;
             const float combined = __fmul_rn(job.w_scale, act_scale);
-            job.y[local] = __fmul_rn(combined, __int2float_rn(dot));
-            if (job.acc) job.acc[local] = dot;
+            const float yv = __fmul_rn(combined, __int2float_rn(dot));
+            if (p.tp.world) {
+                tp_store_all(p.tp, job.y + job.row_off + local, yv);
+            } else {
+                job.y[job.row_off + local] = yv;
+            }
+            if (job.acc) job.acc[job.row_off + local] = dot;
         }
         // Every thread is done with stage st: refill it with chunk c + nst.
         __syncthreads();
@@ -434,6 +454,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             i2s_issue_chunk(p, c + nst, r0, r1, RPI, row_bytes, smem + st * stage_bytes,
                             &full_bar[st], policy);
     }
+    if (p.tp.world && tid == 0) tp_arrive(p.tp);  // after the loop's final barrier
 }
 
 // One-time scan: does a packed I2_S tensor contain code 0b11 anywhere?

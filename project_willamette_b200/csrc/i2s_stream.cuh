@@ -24,6 +24,7 @@
 #include <cstdint>
 
 #include "i2s_matvec.cuh"
+#include "tp.cuh"
 #include "wl_ptx.cuh"
 
 namespace wl {
@@ -47,6 +48,7 @@ struct I2sStreamOp {
     float w_scale;
     uint32_t K, N;
     uint32_t block_begin;     // first 32-row block of this op in the block list
+    uint32_t row_off;         // tensor parallel: first global row of this slice in y
 };
 
 struct I2sStreamParams {
@@ -55,6 +57,7 @@ struct I2sStreamParams {
     uint32_t n_ops;
     const uint32_t *cta_blocks;  // gridDim.x + 1 block boundaries
     uint32_t *status;
+    TpParams tp;                 // world 0: single GPU
 };
 
 struct QuantJob {
@@ -262,8 +265,10 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
                 const uint32_t row = (walk.bi - op.block_begin) * STREAM_BOX_ROWS + lane + 32u * r;
                 if (row < op.N) {
                     const int32_t dot = i2s_acc_total(acc[r]) - asum - 2 * corr[r];
-                    op.y[row] = __fmul_rn(combined, __int2float_rn(dot));
-                    if (op.acc) op.acc[row] = dot;
+                    const float yv = __fmul_rn(combined, __int2float_rn(dot));
+                    if (p.tp.world) tp_store_all(p.tp, op.y + op.row_off + row, yv);
+                    else op.y[op.row_off + row] = yv;
+                    if (op.acc) op.acc[op.row_off + row] = dot;
                 }
                 acc[r] = {0, 0, 0, 0};
                 corr[r] = 0;
@@ -272,6 +277,10 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         walk.next(p.ops, p.n_ops);
     }
     if (timeout && lane == 0) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
+    if (p.tp.world) {  // count this CTA in every rank once all its stores are out
+        __syncthreads();
+        if (threadIdx.x == 0) tp_arrive(p.tp);
+    }
 }
 
 }  // namespace wl

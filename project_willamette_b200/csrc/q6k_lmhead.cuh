@@ -36,6 +36,7 @@
 
 #include <cstdint>
 
+#include "tp.cuh"
 #include "wl_ptx.cuh"
 
 namespace wl {
@@ -65,7 +66,45 @@ struct Q6kParams {
     unsigned long long *slots;  // BG argmax slots (zero on entry)
     uint32_t *counter;          // CTA completion counter (zero on entry)
     uint32_t *status;
+    uint32_t row_offset;        // vocab shard: global id of local row 0
+    uint32_t batch_off;         // first batch row of this launch (key slots)
+    uint32_t key_set;           // which of the two key-slot sets this call uses
+    TpParams tp;                // world 0: single GPU (ids written here)
 };
+
+// Vocab-sharded argmax exchange: rank s writes its best key for batch row b
+// to keys[s][b] of every rank's symmetric block.
+constexpr uint32_t TP_KEYS_OFF = 1024;
+constexpr uint32_t TP_MAX_BATCH = 64;
+// Key slots: [set 0..1][source rank][batch row].  Successive lm-head calls
+// alternate sets, so a rank that runs ahead into the next call cannot
+// overwrite keys a slower rank has not reduced yet (it can only get one call
+// ahead: its next finalize waits for the slower rank's lm-head arrivals).
+static_assert(TP_KEYS_OFF + 2 * TP_MAX_WORLD * TP_MAX_BATCH * 8 <= TP_HEADER_BYTES, "key slots");
+__device__ __forceinline__ unsigned long long *tp_key_slot(uint8_t *base, uint32_t set, int src,
+                                                           uint32_t b) {
+    return reinterpret_cast<unsigned long long *>(base + TP_KEYS_OFF) +
+           (set * TP_MAX_WORLD + src) * TP_MAX_BATCH + b;
+}
+
+// After every rank's lm-head shard: wait for all keys, reduce, decode ids.
+__global__ void q6k_tp_finalize_kernel(const TpParams tp, uint32_t target, uint32_t key_set,
+                                       uint32_t batch, uint32_t *ids, uint32_t *status) {
+    __shared__ uint32_t ok;
+    if (threadIdx.x == 0) {
+        ok = tp_wait(tp, target) ? 1u : 0u;
+        if (!ok) atomicOr(status, WL_DEV_ERR_PEER_TIMEOUT);
+    }
+    __syncthreads();
+    for (uint32_t b = threadIdx.x; b < batch; b += blockDim.x) {
+        unsigned long long best = 0ull;
+        for (int s = 0; s < tp.world; ++s) {
+            const unsigned long long k = *(volatile unsigned long long *)tp_key_slot(tp.local_base, key_set, s, b);
+            best = best > k ? best : k;
+        }
+        ids[b] = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull);
+    }
+}
 
 __device__ __forceinline__ uint32_t f32_order_key(float v, uint32_t row) {
     if (isnan(v)) return row == 0 ? 0xFFFFFFFFu : 0u;
@@ -265,8 +304,8 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
                 if (a == 0 && row < r1) {
                     if (p.logits) p.logits[(size_t)g * p.vocab + row] = logit;
                     const unsigned long long key =
-                        ((unsigned long long)f32_order_key(logit, row) << 32) |
-                        (unsigned long long)(0xFFFFFFFFu - row);
+                        ((unsigned long long)f32_order_key(logit, row + p.row_offset) << 32) |
+                        (unsigned long long)(0xFFFFFFFFu - (row + p.row_offset));
                     best[g] = best[g] > key ? best[g] : key;
                 }
             }
@@ -299,8 +338,17 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
     if (s_last && tid < BG) {
         __threadfence();
         const unsigned long long k = atomicExch(&p.slots[tid], 0ull);
-        p.ids[tid] = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+        if (p.tp.world) {
+            for (int r = 0; r < p.tp.world; ++r)
+                *tp_key_slot(p.tp.peer_base[r], p.key_set, p.tp.rank, p.batch_off + tid) = k;
+        } else {
+            p.ids[tid] = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+        }
         if (tid == 0) *p.counter = 0u;
+    }
+    if (p.tp.world && s_last) {  // one arrival per rank per launch, after the key stores
+        __syncthreads();
+        if (tid == 0) tp_signal(p.tp);
     }
 }
 

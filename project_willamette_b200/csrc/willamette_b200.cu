@@ -259,6 +259,8 @@ struct I2sLaunch {
     const float *x = nullptr;
     int8_t *q_out = nullptr;
     float *scale_out = nullptr;
+    const TpParams *tp = nullptr;      // tensor-parallel exchange, or null
+    const uint32_t *row_offs = nullptr;  // per weight (tensor parallel)
 };
 
 bool weights_may_have_code3(const wl_i2s_dev_weight *w, uint32_t nw) {
@@ -277,9 +279,10 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
         p.jobs[j].row_begin = rows;
         p.jobs[j].y = L.w[j].y;
         p.jobs[j].acc = L.w[j].acc;
+        p.jobs[j].row_off = L.row_offs ? L.row_offs[j] : 0u;
         rows += L.w[j].out_dim;
     }
-    if (rows == 0) return WL_OK;
+    if (rows == 0 && !L.tp) return WL_OK;
     const uint32_t K = L.K;
     p.njobs = (int)L.nw;
     p.K = K;
@@ -290,6 +293,7 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     p.q_out = L.q_out;
     p.scale_out = L.scale_out;
     p.status = status;
+    if (L.tp) p.tp = *L.tp;
     const bool fuse = L.x != nullptr;
     int lpr = 32;
     const int shape = i2s_shape_index(K, &lpr);
@@ -298,8 +302,10 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
                     I2S_FUSE_Q_MAX_K);
     I2sKernel k = kI2s[shape][fuse ? 1 : 0][weights_may_have_code3(L.w, L.nw) ? 1 : 0];
     const uint32_t rpi = (uint32_t)I2S_WARPS * (32u / (uint32_t)lpr);
-    const uint32_t G = std::min<uint32_t>((uint32_t)sm_count_for_launch(), rows);
-    p.rows_per_cta = (rows + G - 1) / G;
+    // (a tensor-parallel rank with an empty slice still launches one CTA,
+    // which only signals its arrival)
+    const uint32_t G = std::max<uint32_t>(1u, std::min<uint32_t>((uint32_t)sm_count_for_launch(), rows));
+    p.rows_per_cta = std::max<uint32_t>(1u, (rows + G - 1) / G);
     const uint32_t stage_bytes = rpi * (K / 4u);
     const uint32_t nchunks = (p.rows_per_cta + rpi - 1) / rpi;
     uint32_t nst = std::max<uint32_t>(1u, I2S_STAGE_BUDGET / stage_bytes);
@@ -309,7 +315,7 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     const size_t smem = (size_t)nst * stage_bytes + (fuse ? (size_t)K * 5u : 0u);
     if (smem > (size_t)WL_MAX_DYN_SMEM / 2)
         return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for one shared-memory stage", K);
-    const uint32_t grid = (rows + p.rows_per_cta - 1) / p.rows_per_cta;
+    const uint32_t grid = std::max<uint32_t>(1u, (rows + p.rows_per_cta - 1) / p.rows_per_cta);
     WL_CUDA(launch(k, dim3(grid), dim3(I2S_THREADS), smem, s, pdl, p));
     return WL_OK;
 }
@@ -774,6 +780,7 @@ struct wl_i2s_stream_plan {
     uint32_t *d_cta_blocks = nullptr;
     QuantJob *d_qjobs = nullptr;
     uint32_t *status = nullptr;
+    uintptr_t y_lo = 0, y_hi = 0;  // extent of the ops' outputs (tensor-parallel checks)
 };
 
 namespace {
@@ -932,6 +939,13 @@ int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream
         hops[j].K = o.in_dim;
         hops[j].N = o.out_dim;
         hops[j].block_begin = block_begin[j];
+        hops[j].row_off = o.row_off;
+        if (o.out_dim) {
+            const uintptr_t lo = (uintptr_t)(o.y + o.row_off);
+            const uintptr_t hi = lo + (uintptr_t)o.out_dim * sizeof(float);
+            plan->y_lo = plan->y_lo ? std::min(plan->y_lo, lo) : lo;
+            plan->y_hi = std::max(plan->y_hi, hi);
+        }
         if (o.out_dim) {
             CUtensorMap m;
             if ((rc = encode_i2s_map(o.packed, o.in_dim, o.out_dim, &m))) return rc;
@@ -988,6 +1002,89 @@ int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream
     plan->d_cta_blocks = (uint32_t *)(base + off_cta);
     plan->d_qjobs = (QuantJob *)(base + off_q);
     plan->status = c.d_status;
+    return WL_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------- tensor-parallel group
+struct wl_tp_group {
+    int device = 0, rank = 0, world = 0;
+    uint8_t *local = nullptr;  // header + caller region, cudaMalloc'd (IPC-exportable)
+    size_t bytes = 0;
+    uint8_t *peers[TP_MAX_WORLD] = {};
+    bool connected = false;
+    uint32_t arrivals = 0;  // arrivals each rank has signalled so far (equal on all ranks)
+    uint32_t lm_calls = 0;  // lm-head calls so far (selects the key-slot set)
+};
+
+namespace {
+
+int tp_params(wl_tp_group *g, uint32_t wait_target, TpParams *tp) {
+    if (!g) return fail(WL_ERR_INVALID_ARGUMENT, "group is NULL");
+    if (!g->connected) return fail(WL_ERR_COMM, "group is not connected (wl_tp_connect)");
+    memset(tp, 0, sizeof *tp);
+    tp->world = g->world;
+    tp->rank = g->rank;
+    tp->local_base = g->local;
+    for (int r = 0; r < g->world; ++r) tp->peer_base[r] = g->peers[r];
+    tp->wait_target = wait_target;
+    return WL_OK;
+}
+
+// Outputs written to peers are addressed by their offset in this rank's
+// block, so they must lie inside the caller region of the block.
+int check_sym_range(wl_tp_group *g, const float *y, size_t n_floats) {
+    const uintptr_t lo = (uintptr_t)y, hi = lo + n_floats * sizeof(float);
+    if (!y || lo < (uintptr_t)(g->local + TP_HEADER_BYTES) || hi > (uintptr_t)(g->local + g->bytes) ||
+        (lo & 3u))
+        return fail(WL_ERR_INVALID_ARGUMENT,
+                    "a gathered output must lie in the group's block (wl_tp_buffer)");
+    return WL_OK;
+}
+
+int launch_q6k_tp(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, uint32_t row_offset,
+                  const float *hidden, uint32_t batch, uint32_t *ids, void *scratch,
+                  cudaStream_t s, const TpParams *tp, uint32_t key_set, uint32_t *launches) {
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    unsigned long long *slots = reinterpret_cast<unsigned long long *>(scratch);
+    uint32_t *counter = reinterpret_cast<uint32_t *>(slots + batch);
+    const uint32_t v = std::max(vocab, 1u);
+    const uint32_t G = std::min<uint32_t>((uint32_t)sm_count_for_launch(), v);
+    Q6kParams p = {};
+    p.packed = packed;
+    p.n_embd = n_embd;
+    p.vocab = vocab;
+    p.nb = n_embd / 256u;
+    p.row_stride = q6k_row_stride(p.nb);
+    p.rows_per_cta = (v + G - 1) / G;
+    p.counter = counter;
+    p.status = status;
+    p.row_offset = row_offset;
+    p.key_set = key_set;
+    p.tp = *tp;
+    const uint32_t grid = (v + p.rows_per_cta - 1) / p.rows_per_cta;
+    *launches = 0;
+    for (uint32_t b0 = 0; b0 < batch;) {
+        const int bg = (batch - b0 >= 4) ? 4 : 1;
+        uint32_t nst;
+        size_t smem;
+        int rc = q6k_launch_cfg(n_embd, bg, &nst, &smem);
+        if (rc) return rc;
+        p.nstages = nst;
+        p.hidden = hidden + (size_t)b0 * n_embd;
+        p.logits = nullptr;
+        p.ids = ids + b0;
+        p.slots = slots + b0;
+        p.batch_off = b0;
+        if (bg == 4)
+            WL_CUDA(launch(q6k_lmhead_kernel<4>, dim3(grid), dim3(Q6K_THREADS), smem, s, true, p));
+        else
+            WL_CUDA(launch(q6k_lmhead_kernel<1>, dim3(grid), dim3(Q6K_THREADS), smem, s, true, p));
+        b0 += (uint32_t)bg;
+        ++*launches;
+    }
     return WL_OK;
 }
 
@@ -1417,6 +1514,171 @@ int wl_dev_i2s_gemm_f32(const uint8_t *packed, float w_scale, uint32_t in_dim, u
         L.act_scale = scale + t;
         if ((rc = launch_i2s(L, s, true))) return rc;
     }
+    return WL_OK;
+}
+
+// ------------------------------------------------------------ tensor parallel
+int wl_tp_create(int rank, int world, size_t sym_bytes, wl_tp_group **group,
+                 uint8_t *handle_out) {
+    if (!group || !handle_out) return fail(WL_ERR_INVALID_ARGUMENT, "NULL argument");
+    *group = nullptr;
+    if (world < 1 || world > TP_MAX_WORLD || rank < 0 || rank >= world)
+        return fail(WL_ERR_INVALID_ARGUMENT, "rank %d / world %d (world must be 1..%d)", rank,
+                    world, TP_MAX_WORLD);
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(c.mu);
+    int rc = ensure_init(c);
+    if (rc) return rc;
+    auto *g = new wl_tp_group();
+    g->device = c.device;
+    g->rank = rank;
+    g->world = world;
+    g->bytes = TP_HEADER_BYTES + ((sym_bytes + 255) & ~(size_t)255);
+    cudaError_t e = cudaMalloc(&g->local, g->bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(g->local, 0, g->bytes, c.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, g->local);
+    if (e != cudaSuccess) {
+        if (g->local) cudaFree(g->local);
+        delete g;
+        return fail(WL_ERR_COMM, "symmetric block: %s", cudaGetErrorString(e));
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == WL_TP_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle_out, &h, WL_TP_HANDLE_BYTES);
+    *group = g;
+    return WL_OK;
+}
+
+int wl_tp_connect(wl_tp_group *g, const uint8_t *handles) {
+    if (!g || !handles) return fail(WL_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (g->connected) return WL_OK;
+    cudaSetDevice(g->device);
+    for (int r = 0; r < g->world; ++r) {
+        if (r == g->rank) {
+            g->peers[r] = g->local;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + (size_t)r * WL_TP_HANDLE_BYTES, WL_TP_HANDLE_BYTES);
+        void *ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return fail(WL_ERR_COMM, "opening rank %d's block: %s", r, cudaGetErrorString(e));
+        g->peers[r] = (uint8_t *)ptr;
+    }
+    g->connected = true;
+    return WL_OK;
+}
+
+void *wl_tp_buffer(wl_tp_group *g, size_t offset) {
+    if (!g || TP_HEADER_BYTES + offset >= g->bytes) return nullptr;
+    return g->local + TP_HEADER_BYTES + offset;
+}
+
+int wl_tp_destroy(wl_tp_group *g) {
+    if (!g) return WL_OK;
+    cudaSetDevice(g->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < g->world; ++r)
+        if (r != g->rank && g->peers[r]) cudaIpcCloseMemHandle(g->peers[r]);
+    if (g->local) cudaFree(g->local);
+    delete g;
+    return WL_OK;
+}
+
+int wl_tp_wait(wl_tp_group *g, void *stream) {
+    TpParams tp;
+    int rc = tp_params(g, 0, &tp);
+    if (rc) return rc;
+    if (g->arrivals == 0) return WL_OK;
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    tp_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(tp, g->arrivals, status);
+    WL_CUDA(cudaGetLastError());
+    return WL_OK;
+}
+
+int wl_tp_i2s_matvec_fused_f32(wl_tp_group *g, const wl_i2s_dev_weight *weights,
+                               const uint32_t *row_offsets, uint32_t n_weights, uint32_t in_dim,
+                               const float *x, int wait_for_input, void *stream) {
+    if (!weights || !row_offsets || n_weights == 0 || n_weights > WL_I2S_MAX_FUSED)
+        return fail(WL_ERR_INVALID_ARGUMENT, "n_weights must be 1..%d", WL_I2S_MAX_FUSED);
+    if (in_dim == 0 || in_dim % 128 || in_dim > I2S_FUSE_Q_MAX_K)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128 <= %u", in_dim,
+                    I2S_FUSE_Q_MAX_K);
+    if (!x || !aligned16(x)) return fail(WL_ERR_INVALID_ARGUMENT, "x NULL or misaligned");
+    TpParams tp;
+    int rc = tp_params(g, wait_for_input ? g->arrivals : 0u, &tp);
+    if (rc) return rc;
+    for (uint32_t j = 0; j < n_weights; ++j) {
+        if (!aligned16(weights[j].packed))
+            return fail(WL_ERR_INVALID_ARGUMENT, "weight %u not 16-byte aligned", j);
+        if (!std::isfinite(weights[j].w_scale))
+            return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale for weight %u", j);
+        if ((rc = check_sym_range(g, weights[j].y, (size_t)row_offsets[j] + weights[j].out_dim)))
+            return rc;
+        if (weights[j].acc) return fail(WL_ERR_INVALID_ARGUMENT, "acc is not gathered; pass NULL");
+    }
+    I2sLaunch L;
+    L.w = weights;
+    L.nw = n_weights;
+    L.K = in_dim;
+    L.x = x;
+    L.tp = &tp;
+    L.row_offs = row_offsets;
+    if ((rc = launch_i2s(L, (cudaStream_t)stream, true))) return rc;
+    g->arrivals += 1;
+    return WL_OK;
+}
+
+int wl_tp_i2s_stream_run(wl_tp_group *g, wl_i2s_stream_plan *plan, void *stream) {
+    if (!plan) return fail(WL_ERR_INVALID_ARGUMENT, "plan is NULL");
+    TpParams tp;
+    int rc = tp_params(g, 0, &tp);
+    if (rc) return rc;
+    if (plan->y_lo < (uintptr_t)(g->local + TP_HEADER_BYTES) ||
+        plan->y_hi > (uintptr_t)(g->local + g->bytes))
+        return fail(WL_ERR_INVALID_ARGUMENT, "stream plan outputs are not in the group's block");
+    cudaStream_t s = (cudaStream_t)stream;
+    WL_CUDA(launch(quantize_jobs_kernel, dim3(plan->n_quant), dim3(QUANT_THREADS), 0, s, true,
+                   (const QuantJob *)plan->d_qjobs));
+    I2sStreamParams p;
+    p.ops = plan->d_ops;
+    p.maps = plan->d_maps;
+    p.n_ops = plan->n_ops;
+    p.cta_blocks = plan->d_cta_blocks;
+    p.status = plan->status;
+    p.tp = tp;
+    WL_CUDA(launch(kStream[plan->c3 ? 1 : 0], dim3(plan->grid), dim3(STREAM_THREADS),
+                   STREAM_SMEM, s, true, p));
+    g->arrivals += 1;
+    return WL_OK;
+}
+
+int wl_tp_q6k_lm_head_greedy(wl_tp_group *g, const uint8_t *packed_shard, uint32_t n_embd,
+                             uint32_t vocab_shard, uint32_t row_offset, const float *hidden,
+                             uint32_t batch, uint32_t *ids, void *scratch, void *stream) {
+    if (n_embd == 0 || n_embd % 256) return fail(WL_ERR_GGUF_PARSE, "Q6_K row length %u", n_embd);
+    if (batch == 0 || batch > TP_MAX_BATCH)
+        return fail(WL_ERR_INVALID_ARGUMENT, "batch must be 1..%u", TP_MAX_BATCH);
+    if (!ids || !hidden || !aligned16(packed_shard) || !scratch || ((uintptr_t)scratch & 7u))
+        return fail(WL_ERR_INVALID_ARGUMENT, "NULL or misaligned pointer");
+    TpParams tp;
+    int rc = tp_params(g, 0, &tp);
+    if (rc) return rc;
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    cudaStream_t s = (cudaStream_t)stream;
+    // every rank launches the same batch groups, so arrivals stay in step
+    uint32_t launches = 0;
+    if ((rc = launch_q6k_tp(packed_shard, n_embd, vocab_shard, row_offset, hidden, batch, ids,
+                            scratch, s, &tp, g->lm_calls & 1u, &launches)))
+        return rc;
+    g->arrivals += launches;
+    q6k_tp_finalize_kernel<<<1, 64, 0, s>>>(tp, g->arrivals, g->lm_calls & 1u, batch, ids, status);
+    g->lm_calls += 1;
+    WL_CUDA(cudaGetLastError());
     return WL_OK;
 }
 
