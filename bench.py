@@ -24,9 +24,15 @@ weights before that wait) -- the latency-bound batch-1 decode figure.
 linear_matvec_f32 is called), host->device copy of each input and
 device->host copy of each output inside the timed region.
 
-Multi-GPU (torchrun, N > 1): every rank runs its own copy of the sweep (a
-replica; independent decode streams), no collective on the data path;
-value = N x bytes / max-over-ranks time ("scaling": "weak").
+Multi-GPU (torchrun, N > 1): tensor parallel, as the reference's model is
+split across the GPUs of one box: every BitLinear's output rows are divided
+among the ranks (64-row units) and the kernels store each output row into
+every rank's symmetric block over NVLink (an all-gather fused into the
+matvec); the lm-head is split by vocab rows with an in-kernel (max, index)
+reduction.  The total work per step is fixed ("scaling": "strong"); value =
+the whole model's bytes / max-over-ranks step time.  When a rank's share of
+the weights is under twice L2, several distinct weight copies are cycled step
+to step so that no step reads its weights from L2.
 
 `--impl reference` times the reference's x86 kernel (the oracle port of
 bitlinear_i2s_matvec_f32_sse2_i8, single-threaded like the reference's x86
@@ -134,32 +140,132 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ GPU arm
-def make_i2s_weights(torch, dev, rng: np.random.Generator):
-    """All 210 BitNet-2B BitLinear weights, generated on the device (seeded)."""
-    from project_willamette_b200.synth import _BYTE_LUT
-    lut = torch.from_numpy(_BYTE_LUT).to(dev)
-    g = torch.Generator(device=dev)
-    g.manual_seed(int(rng.integers(0, 2**62)))
-    layers = []
-    for _ in range(LAYERS):
-        groups = []
-        for in_dim, outs in GROUPS:
+L2_BYTES = 126 * 1024 * 1024
+
+
+def copies_for(per_copy_bytes: int) -> int:
+    """Distinct weight copies cycled step to step so that no step finds its
+    weights in L2: one copy when it alone is twice L2, else enough copies that
+    at least 1.5x L2 of other weights is read between two reads of one copy."""
+    if per_copy_bytes >= 2 * L2_BYTES:
+        return 1
+    return 1 + -(-int(1.5 * L2_BYTES) // max(per_copy_bytes, 1))
+
+
+class Sweep:
+    """This rank's share of the 210 BitNet-2B BitLinears.
+
+    Every rank draws the same full weights from one seed and keeps its row
+    slice (64-row units, tp.shard_rows); at N = 1 the slice is the whole
+    weight.  Inputs x (one per launch group) are shared by all copies and
+    ranks; outputs y are full-length vectors, in the symmetric block at N > 1
+    (the kernels gather them on every rank)."""
+
+    def __init__(self, torch, dev, world, rank, tpg):
+        from project_willamette_b200.synth import _BYTE_LUT
+        from project_willamette_b200.tp import shard_rows
+        self.torch, self.dev, self.world, self.rank = torch, dev, world, rank
+        lut = torch.from_numpy(_BYTE_LUT).to(dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(SEED)
+        rng = np.random.default_rng(SEED)
+        self.rank_bytes = 0  # this rank's algorithmic bytes per step
+        per_copy = 0
+        layout = []
+        for _ in range(LAYERS):
+            for in_dim, outs in GROUPS:
+                for n in outs:
+                    r0, cnt = shard_rows(n, world, rank, 64)
+                    layout.append((in_dim, n, r0, cnt))
+                    per_copy += cnt * in_dim // 4
+        self.copies = copies_for(per_copy)
+        # inputs: one contiguous buffer (one host->device copy per step in e2e)
+        n_x = LAYERS * sum(k for k, _ in GROUPS)
+        self.X = torch.randn(n_x, device=dev, generator=g, dtype=torch.float32)
+        # outputs: one contiguous run of full-length vectors
+        n_y = LAYERS * sum(sum(ns) for _, ns in GROUPS)
+        if tpg is None:
+            self.Y = torch.empty(n_y, device=dev, dtype=torch.float32)
+            y_base = self.Y.data_ptr()
+        else:
+            self.Y = None
+            y_base = tpg.view(0, n_y).ptr
+        self.y_base, self.n_y = y_base, n_y
+        self.dummy = torch.zeros(64, dtype=torch.uint8, device=dev)
+        self.weights = []  # [copy][op] = (packed tensor or None, scale)
+        for c in range(self.copies):
             ws = []
-            for n in outs:
+            for in_dim, n, r0, cnt in layout:
                 raw = torch.randint(0, 256, (n * in_dim // 4,), dtype=torch.uint8, device=dev,
                                     generator=g)
-                ws.append((lut[raw.long()], float(np.float32(rng.uniform(0.01, 0.1))), n))
-            x = torch.randn(in_dim, device=dev, generator=g, dtype=torch.float32)
-            groups.append((in_dim, ws, x))
-        layers.append(groups)
-    return layers
+                rb = in_dim // 4
+                part = lut[raw[r0 * rb:(r0 + cnt) * rb].long()].contiguous() if cnt else None
+                ws.append((part, float(np.float32(rng.uniform(0.01, 0.1)))))
+                del raw
+            self.weights.append(ws)
+        # op table: (op index, in_dim, n, r0, cnt, x ptr, y ptr) per launch group
+        self.groups = []
+        xo = yo = 0
+        oi = 0
+        for _ in range(LAYERS):
+            for in_dim, outs in GROUPS:
+                gops = []
+                for n in outs:
+                    _, _, r0, cnt = layout[oi]
+                    gops.append((oi, in_dim, n, r0, cnt, self.X.data_ptr() + 4 * xo,
+                                 y_base + 4 * yo))
+                    self.rank_bytes += cnt * in_dim // 4 + 4 + 4 * cnt
+                    oi += 1
+                    yo += n
+                self.rank_bytes += 4 * in_dim
+                self.groups.append(gops)
+                xo += in_dim
+        self.ops = [o for grp in self.groups for o in grp]
+
+    def packed_ptr(self, c, oi):
+        p = self.weights[c][oi][0]
+        return p.data_ptr() if p is not None else self.dummy.data_ptr()
+
+    def stream_ops(self, c):
+        from project_willamette_b200 import _abi
+        arr = (_abi.WlI2sStreamOp * len(self.ops))()
+        for i, (oi, in_dim, n, r0, cnt, xp, yp) in enumerate(self.ops):
+            arr[i].packed, arr[i].w_scale = self.packed_ptr(c, oi), self.weights[c][oi][1]
+            arr[i].in_dim, arr[i].out_dim = in_dim, cnt
+            arr[i].x, arr[i].y, arr[i].acc, arr[i].flags, arr[i].row_off = xp, yp, None, 0, r0
+        return arr
+
+    def chain(self, L, ck, stream):
+        """Decode-order launch groups over copy 0: QKV(h) -> O(q) -> gate/up(o)
+        -> down(gate) -> next layer's QKV(down); each consumes the previous
+        group's (gathered) output."""
+        from project_willamette_b200 import _abi
+        found = self.torch.zeros(1, dtype=self.torch.int32, device=self.dev)
+        out = []
+        prev_y = self.groups[0][0][5]  # the first group's own x
+        for gops in self.groups:
+            arr = (_abi.WlI2sDevWeight * len(gops))()
+            offs = (C.c_uint32 * len(gops))()
+            for i, (oi, in_dim, n, r0, cnt, xp, yp) in enumerate(gops):
+                pp = self.packed_ptr(0, oi)
+                flags = _abi.WL_I2S_NO_CODE3
+                if cnt:
+                    ck(L.wl_dev_i2s_scan_code3(pp, cnt * in_dim // 4, found.data_ptr(), stream))
+                    self.torch.cuda.synchronize()
+                    flags = 0 if int(found.item()) else _abi.WL_I2S_NO_CODE3
+                arr[i].packed, arr[i].w_scale, arr[i].out_dim = pp, self.weights[0][oi][1], cnt
+                arr[i].y, arr[i].acc, arr[i].flags = yp, None, flags
+                offs[i] = r0
+            in_dim = gops[0][1]
+            out.append((in_dim, prev_y, arr, offs, len(gops)))
+            prev_y = gops[0][6]  # the group's first output feeds the next group
+        return out
 
 
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
     import project_willamette_b200 as wl
-    from project_willamette_b200 import _abi
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -178,43 +284,37 @@ def run_gpu(args) -> None:
         if rc:
             raise RuntimeError(L.wl_last_error().decode())
 
-    rng = np.random.default_rng(SEED + rank)
-    layers = make_i2s_weights(torch, dev, rng)
+    tpg = None
+    if world > 1:
+        from project_willamette_b200.tp import TPGroup
+        tpg = TPGroup(rank, world, 8 << 20, device=local)
+    sw = Sweep(torch, dev, world, rank, tpg)
     stream = torch.cuda.Stream(device=dev)
-    found = torch.zeros(1, dtype=torch.int32, device=dev)
 
-    # Per launch group: a fused-input weight array (decode-order chain) and the
-    # same weights as stream ops (persistent streaming launch).
-    groups, sops, outs = [], [], []
-    for lgroups in layers:
-        for in_dim, ws, x in lgroups:
-            arr = (_abi.WlI2sDevWeight * len(ws))()
-            for i, (packed, s, n) in enumerate(ws):
-                ck(L.wl_dev_i2s_scan_code3(packed.data_ptr(), packed.numel(), found.data_ptr(),
-                                           stream.cuda_stream))
-                torch.cuda.synchronize()
-                y = torch.empty(n, dtype=torch.float32, device=dev)
-                outs.append(y)
-                arr[i].packed, arr[i].w_scale, arr[i].out_dim = packed.data_ptr(), s, n
-                arr[i].y, arr[i].acc = y.data_ptr(), None
-                arr[i].flags = 0 if int(found.item()) else _abi.WL_I2S_NO_CODE3
-                op = _abi.WlI2sStreamOp()
-                op.packed, op.w_scale, op.in_dim, op.out_dim = packed.data_ptr(), s, in_dim, n
-                op.x, op.y, op.acc, op.flags = x.data_ptr(), y.data_ptr(), None, 0
-                sops.append(op)
-            groups.append((in_dim, x, arr, len(ws)))
-    ops_arr = (_abi.WlI2sStreamOp * len(sops))(*sops)
-    plan = C.c_void_p()
-    ck(L.wl_i2s_stream_plan_create(ops_arr, len(sops), C.byref(plan)))
+    plans = []
+    for c in range(sw.copies):
+        arr = sw.stream_ops(c)
+        plan = C.c_void_p()
+        ck(L.wl_i2s_stream_plan_create(arr, len(sw.ops), C.byref(plan)))
+        plans.append(plan)
+    chain = sw.chain(L, ck, stream.cuda_stream)
 
-    def stream_step(h: int) -> int:
-        ck(L.wl_dev_i2s_stream_run(plan, h))
-        return 2
+    def stream_step(c):
+        def fn(h):
+            if tpg is None:
+                ck(L.wl_dev_i2s_stream_run(plans[c], h))
+            else:
+                ck(L.wl_tp_i2s_stream_run(tpg._g, plans[c], h))
+            return 2
+        return fn
 
-    def chain_step(h: int) -> int:
-        for in_dim, x, arr, nw in groups:
-            ck(L.wl_dev_i2s_matvec_fused_f32(arr, nw, in_dim, x.data_ptr(), h))
-        return len(groups)
+    def chain_step(h):
+        for in_dim, xp, arr, offs, nw in chain:
+            if tpg is None:
+                ck(L.wl_dev_i2s_matvec_fused_f32(arr, nw, in_dim, xp, h))
+            else:
+                ck(L.wl_tp_i2s_matvec_fused_f32(tpg._g, arr, offs, nw, in_dim, xp, 1, h))
+        return len(chain)
 
     def capture(fn):
         with torch.cuda.stream(stream):
@@ -225,10 +325,17 @@ def run_gpu(args) -> None:
                 fn(torch.cuda.current_stream().cuda_stream)
         return g, n
 
-    def timed(g, steps, clocks=None):
+    def max_over_ranks(v):
+        if world > 1:
+            t = torch.tensor([v], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            v = float(t.item())
+        return v
+
+    def timed(graphs, steps, clocks=None):
         with torch.cuda.stream(stream):
-            for _ in range(max(args.warmup, 3)):
-                g.replay()
+            for i in range(max(args.warmup, 3)):
+                graphs[i % len(graphs)].replay()
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
@@ -237,85 +344,84 @@ def run_gpu(args) -> None:
             ctx = clocks if clocks is not None else _Null()
             with ctx:
                 e0.record(stream)
-                for _ in range(steps):
-                    g.replay()
+                for i in range(steps):
+                    graphs[i % len(graphs)].replay()
                 e1.record(stream)
                 torch.cuda.synchronize()
             ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(ms)
 
-    g_stream, launches_per_step = capture(stream_step)
+    caps = [capture(stream_step(c)) for c in range(sw.copies)]
+    g_streams = [g for g, _ in caps]
+    launches_per_step = caps[0][1]
     g_chain, chain_launches = capture(chain_step)
     clk = ClockSampler(local)
-    ms_total = timed(g_stream, args.steps, clk)
+    ms_total = timed(g_streams, args.steps, clk)
     chain_steps = max(1, args.steps // 4)
-    ms_chain = timed(g_chain, chain_steps)
-
-    # Isolated per-launch duration of the per-op kernel (events around each
-    # launch of one eager decode-order step; no overlap between launches).
-    iso = []
-    with torch.cuda.stream(stream):
-        for in_dim, x, arr, nw in groups:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            ck(L.wl_dev_i2s_matvec_fused_f32(arr, nw, in_dim, x.data_ptr(), stream.cuda_stream))
-            b.record(stream)
-            iso.append((a, b, sum(algorithmic_bytes(in_dim, arr[i].out_dim) for i in range(nw))))
-        torch.cuda.synchronize()
-    iso_ms = sum(a.elapsed_time(b) for a, b, _ in iso)
-    iso_bytes = sum(nb for _, _, nb in iso)
+    ms_chain = timed([g_chain], chain_steps)
+    status = C.c_uint32(0)
+    ck(L.wl_device_status(C.byref(status)))
+    if status.value:
+        raise RuntimeError(f"device status {status.value:#x} after the timed runs")
 
     bytes_step = sweep_bytes()
     ms_step = ms_total / args.steps
-    value = world * bytes_step / (ms_step * 1e-3) / 1e9
-    achieved = bytes_step / (ms_step * 1e-3) / 1e9  # one stream launch per step
+    value = bytes_step / (ms_step * 1e-3) / 1e9          # whole job: every weight once per step
+    achieved = sw.rank_bytes / (ms_step * 1e-3) / 1e9   # this rank's stream launch
     ms_chain_step = ms_chain / chain_steps
     pk = peaks()
 
-    # ---- lm-head (Q6_K 128256 x 2560, batch 1 and 64) and prefill GEMM (config 3)
-    lm = lm_head_bench(torch, dev, L, stream, rng, reps=max(20, min(args.steps, 200)))
-    gemm = gemm_bench(torch, dev, L, stream, rng)
-
-    # ---- e2e through the host-buffer C ABI
-    e2e = e2e_bench(torch, layers, wl, rng, steps=max(1, min(args.steps, 20)))
-    if world > 1:
-        t = torch.tensor([e2e["seconds_per_step"]], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e["seconds_per_step"] = float(t.item())
-    e2e_value = world * bytes_step / e2e["seconds_per_step"] / 1e9
+    # ---- lm-head (Q6_K 128256 x 2560, batch 1 and 64; vocab-sharded at N > 1)
+    lm = lm_head_bench(torch, dev, L, stream, world, rank, tpg, max_over_ranks,
+                       reps=max(20, min(args.steps, 200)))
+    # ---- prefill GEMM (config 3, single GPU)
+    gemm = (gemm_bench(torch, dev, L, stream, np.random.default_rng(SEED + 3))
+            if world == 1 else None)
+    # ---- e2e
+    if world == 1:
+        e2e = e2e_bench(torch, sw, wl, np.random.default_rng(SEED + 5),
+                        steps=max(1, min(args.steps, 20)))
+    else:
+        e2e = e2e_tp_bench(torch, sw, stream, g_streams[0], rank,
+                           steps=max(3, min(args.steps, 50)))
+    e2e["seconds_per_step"] = max_over_ranks(e2e["seconds_per_step"])
+    e2e_value = bytes_step / e2e["seconds_per_step"] / 1e9
 
     cpu = None
     if rank == 0 and world == 1:
         cpu = cpu_baseline(seconds=args.cpu_seconds)
 
     if rank == 0:
+        par = "single" if world == 1 else f"tp{world} (row-split BitLinears, gathered in-kernel)"
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "int8xternary->i32", "data": "synthetic (seeded; BASELINE distributions)",
             "config": {"workload": WORKLOAD, "layers": LAYERS, "d_model": D_MODEL, "d_ff": D_FF,
                        "kv_dim": D_KV, "matvecs_per_step": LAYERS * 7,
                        "bytes_per_step": bytes_step, "batch": 1,
-                       "mode": "sustained: 210 independent matvecs, one persistent launch",
-                       "l2": "inputs larger than L2 (521 MB of distinct weights per step)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single"},
+                       "mode": "sustained: 210 independent matvecs, one persistent launch per GPU",
+                       "l2": (f"inputs larger than L2: {sw.copies} weight cop"
+                              f"{'y' if sw.copies == 1 else 'ies'} of "
+                              f"{sw.rank_bytes / 1e6:.0f} MB per GPU cycled step to step"),
+                       "parallelism": par},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                         "traffic": TRAFFIC_PER_STEP_BYTES,
-                         "peak_source": pk["source"], "kernel": "i2s_stream_kernel"},
+                         "traffic": TRAFFIC_PER_STEP_BYTES if world == 1 else None,
+                         "peak_source": pk["source"], "kernel": "i2s_stream_kernel",
+                         "algorithmic_bytes_per_launch": sw.rank_bytes},
             "decode_chain": {
-                "gbs": round(world * bytes_step / (ms_chain_step * 1e-3) / 1e9, 2),
+                "gbs": round(bytes_step / (ms_chain_step * 1e-3) / 1e9, 2),
                 "ms_per_step": round(ms_chain_step, 5), "launches_per_step": chain_launches,
-                "note": "decode order: 120 dependent fused quantise+matvec kernels (PDL)",
-                "isolated_launch_gbs": round(iso_bytes / (iso_ms * 1e-3) / 1e9, 2)},
+                "note": ("decode order: 120 dependent fused quantise+matvec kernels, each "
+                         "consuming the previous group's output" +
+                         (" gathered from every rank (in-kernel wait)" if world > 1 else
+                          " (PDL)"))},
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT,
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                    "api": "wl_bitlinear_i2s_matvec_f32 (host buffers, one call per BitLinear)"},
+                    "api": e2e["api"]},
             "gpu_launches": launches_per_step * args.steps,
             "lm_head": lm,
             "prefill_gemm": gemm,
@@ -324,10 +430,12 @@ def run_gpu(args) -> None:
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    del g_stream, g_chain
-    L.wl_i2s_stream_plan_destroy(plan)
+    del g_streams, g_chain, caps
+    for plan in plans:
+        L.wl_i2s_stream_plan_destroy(plan)
     if world > 1:
         dist.barrier()
+        tpg.close()
         dist.destroy_process_group()
 
 
@@ -339,64 +447,73 @@ class _Null:
         return False
 
 
-# Measured DRAM traffic of the sweep per step (ncu, see profiles/); None until
-# captured.
-TRAFFIC_PER_STEP_BYTES = None
+# DRAM traffic of one i2s_stream_kernel launch of the 1-GPU sweep (ncu
+# dram__bytes_read.sum + dram__bytes_write.sum = 535,326,464 + 5,324,800;
+# profiles/i2s_stream_kernel_bitnet2b_sweep.md).
+TRAFFIC_PER_STEP_BYTES = 540651264
 
 
-def lm_head_bench(torch, dev, L, stream, rng, reps: int) -> dict:
-    """Q6_K tied lm-head + greedy argmax, 128256 x 2560, batch 1 (config 4)."""
+def lm_head_bench(torch, dev, L, stream, world, rank, tpg, max_over_ranks, reps: int) -> dict:
+    """Q6_K tied lm-head + greedy argmax, 128256 x 2560, batch 1 and 64
+    (config 4); at N > 1 each rank holds a vocab shard and the ids come from
+    the in-kernel (max, index) reduction."""
     from project_willamette_b200 import synth
-    raw = torch.from_numpy(synth.q6k_rows(rng, D_MODEL, VOCAB)).to(dev)
-    packed = torch.empty(L.wl_q6k_packed_bytes(D_MODEL, VOCAB), dtype=torch.uint8, device=dev)
-    assert L.wl_dev_q6k_repack(raw.data_ptr(), D_MODEL, VOCAB, packed.data_ptr(),
+    from project_willamette_b200.tp import shard_rows
+    v0, nv = shard_rows(VOCAB, world, rank)
+    rng = np.random.default_rng(SEED + 4)
+    raw_all = synth.q6k_rows(rng, D_MODEL, VOCAB)
+    rb = D_MODEL // 256 * 210
+    raw = torch.from_numpy(raw_all[v0 * rb:(v0 + nv) * rb]).to(dev)
+    del raw_all
+    packed = torch.empty(max(L.wl_q6k_packed_bytes(D_MODEL, nv), 16), dtype=torch.uint8,
+                         device=dev)
+    assert L.wl_dev_q6k_repack(raw.data_ptr(), D_MODEL, nv, packed.data_ptr(),
                                stream.cuda_stream) == 0
     del raw
-    h = torch.randn(D_MODEL, device=dev)
-    ids = torch.zeros(1, dtype=torch.int32, device=dev)
-    scratch = torch.zeros(L.wl_q6k_scratch_bytes(1), dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 4)
     s = stream.cuda_stream
+    out = {"vocab": VOCAB, "vocab_per_gpu": nv, "exact_logits": True,
+           "algorithmic_bytes": 269337600 + 4 * D_MODEL + 4}
 
-    def once():
-        rc = L.wl_dev_q6k_lm_head(packed.data_ptr(), D_MODEL, VOCAB, h.data_ptr(), 1, None,
-                                  ids.data_ptr(), scratch.data_ptr(), s)
-        if rc:
-            raise RuntimeError(L.wl_last_error().decode())
+    def run(batch, n):
+        H = torch.randn(batch, D_MODEL, device=dev, generator=g)
+        ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        scratch = torch.zeros(L.wl_q6k_scratch_bytes(batch), dtype=torch.uint8, device=dev)
 
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            once()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
-            once()
-        b.record(stream)
-        torch.cuda.synchronize()
-    us = a.elapsed_time(b) * 1e3 / reps
-    alg = 269337600 + 4 * D_MODEL + 4
-    # batch 64 (config 4), same exact arithmetic
-    H = torch.randn(64, D_MODEL, device=dev)
-    ids64 = torch.zeros(64, dtype=torch.int32, device=dev)
-    scratch64 = torch.zeros(L.wl_q6k_scratch_bytes(64), dtype=torch.uint8, device=dev)
-    with torch.cuda.stream(stream):
-        def once64():
-            rc = L.wl_dev_q6k_lm_head(packed.data_ptr(), D_MODEL, VOCAB, H.data_ptr(), 64, None,
-                                      ids64.data_ptr(), scratch64.data_ptr(), s)
+        def once():
+            if tpg is None:
+                rc = L.wl_dev_q6k_lm_head(packed.data_ptr(), D_MODEL, nv, H.data_ptr(), batch,
+                                          None, ids.data_ptr(), scratch.data_ptr(), s)
+            else:
+                rc = L.wl_tp_q6k_lm_head_greedy(tpg._g, packed.data_ptr(), D_MODEL, nv, v0,
+                                                H.data_ptr(), batch, ids.data_ptr(),
+                                                scratch.data_ptr(), s)
             if rc:
                 raise RuntimeError(L.wl_last_error().decode())
-        once64()
-        torch.cuda.synchronize()
-        a.record(stream)
-        for _ in range(5):
-            once64()
-        b.record(stream)
-        torch.cuda.synchronize()
-    us64 = a.elapsed_time(b) * 1e3 / 5
-    return {"us_per_call": round(us, 2), "gbs": round(alg / (us * 1e-6) / 1e9, 1),
-            "algorithmic_bytes": alg, "vocab": VOCAB, "batch": 1, "exact_logits": True,
-            "batch64_us_per_call": round(us64, 1),
-            "batch64_gflops": round(2 * 64 * D_MODEL * VOCAB / (us64 * 1e-6) / 1e9, 1)}
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                once()
+            torch.cuda.synchronize()
+            if world > 1:
+                import torch.distributed as dist
+                dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(n):
+                once()
+            b.record(stream)
+            torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b) * 1e3 / n)
+
+    us = run(1, reps)
+    us64 = run(64, 5)
+    out.update({"us_per_call": round(us, 2), "batch": 1,
+                "gbs": round(out["algorithmic_bytes"] / (us * 1e-6) / 1e9, 1),
+                "batch64_us_per_call": round(us64, 1),
+                "batch64_gflops": round(2 * 64 * D_MODEL * VOCAB / (us64 * 1e-6) / 1e9, 1)})
+    return out
 
 
 def int8_peak_tops() -> dict:
@@ -452,17 +569,16 @@ def gemm_bench(torch, dev, L, stream, rng) -> dict:
             "cases": rows}
 
 
-def e2e_bench(torch, layers, wl, rng, steps: int) -> dict:
-    """The 210 matvecs through the host-buffer drop-in entry point."""
+def e2e_bench(torch, sw, wl, rng, steps: int) -> dict:
+    """The 210 matvecs through the host-buffer drop-in entry point (one call
+    per BitLinear, as the reference's linear_matvec_f32 is called)."""
     calls = []
-    for groups in layers:
-        for in_dim, ws, _ in groups:
-            for packed, s, n in ws:
-                host = packed.cpu().numpy()
-                t = wl.TensorView.i2s("w", in_dim, n, host, s)
-                x = rng.standard_normal(in_dim).astype(np.float32)
-                y = np.empty(n, np.float32)
-                calls.append((t, x, y))
+    for (oi, in_dim, n, r0, cnt, xp, yp) in sw.ops:
+        host = sw.weights[0][oi][0].cpu().numpy()
+        t = wl.TensorView.i2s("w", in_dim, n, host, sw.weights[0][oi][1])
+        x = rng.standard_normal(in_dim).astype(np.float32)
+        y = np.empty(n, np.float32)
+        calls.append((t, x, y))
     h2d = sum(c[1].nbytes for c in calls)
     d2h = sum(c[2].nbytes for c in calls)
     for t, x, y in calls:  # first use uploads and caches the weights
@@ -473,7 +589,40 @@ def e2e_bench(torch, layers, wl, rng, steps: int) -> dict:
             wl.bitlinear_i2s_matvec_f32(t, x, y)
     dt = (time.perf_counter() - t0) / steps
     wl.release_weights()
-    return {"seconds_per_step": dt, "h2d": h2d, "d2h": d2h}
+    return {"seconds_per_step": dt, "h2d": h2d, "d2h": d2h,
+            "api": "wl_bitlinear_i2s_matvec_f32 (host buffers, one call per BitLinear)"}
+
+
+def e2e_tp_bench(torch, sw, stream, graph, rank, steps: int) -> dict:
+    """Tensor parallel end to end: every rank copies all inputs from pinned
+    host memory, runs its stream plan (gathering every output on every rank),
+    and rank 0 reads the gathered outputs back; wall clock per step, max over
+    ranks."""
+    import torch.distributed as dist
+    from project_willamette_b200.tp import SymView
+    xh = torch.randn(sw.X.numel(), dtype=torch.float32).pin_memory()
+    yh = torch.empty(sw.n_y, dtype=torch.float32).pin_memory()
+    ydev = torch.as_tensor(SymView(sw.y_base, (sw.n_y,), "<f4", None), device=sw.dev)
+    world = dist.get_world_size()
+
+    def step():
+        with torch.cuda.stream(stream):
+            sw.X.copy_(xh, non_blocking=True)
+            graph.replay()
+            if rank == 0:
+                yh.copy_(ydev, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        step()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    return {"seconds_per_step": dt, "h2d": world * xh.numel() * 4, "d2h": yh.numel() * 4,
+            "api": "wl_tp_i2s_stream_run (pinned host inputs copied on every rank; "
+                   "gathered outputs read back on rank 0)"}
 
 
 # ------------------------------------------------------------------ CPU arms
@@ -547,7 +696,8 @@ def run_reference(args) -> None:
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "int8xternary->i32",
         "data": "synthetic (seeded; BASELINE distributions)",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "d_model": D_MODEL, "d_ff": D_FF,

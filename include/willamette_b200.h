@@ -245,7 +245,9 @@ int wl_dev_i2s_matvec_f32_noalloc(const uint8_t *packed, float w_scale, uint32_t
  * symmetric block over NVLink (CUDA IPC) and signal arrival counters there
  * (system-scope release/acquire); the consumer's kernel waits, bounded, on
  * its own memory.  Every rank must issue the same sequence of wl_tp_* calls.
- * Setup: wl_tp_create on every rank, exchange the WL_TP_HANDLE_BYTES handles
+ * Wait targets and key-slot sets are read on the device (from this rank's own
+ * counters), so a sequence of wl_tp_* launches can be captured in a CUDA graph
+ * and replayed.  Setup: wl_tp_create on every rank, exchange the WL_TP_HANDLE_BYTES handles
  * (any host channel), wl_tp_connect with all world handles in rank order. */
 #define WL_TP_HANDLE_BYTES 64
 typedef struct wl_tp_group wl_tp_group;

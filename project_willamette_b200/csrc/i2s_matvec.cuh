@@ -333,9 +333,9 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();  // the input comes from the previous kernel
-    if (p.tp.world && p.tp.wait_target) {
+    if (p.tp.world && p.tp.wait) {
         // the input is a vector all ranks gathered into this rank's block
-        if (tid == 0 && !tp_wait(p.tp, p.tp.wait_target)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
+        if (tid == 0 && !tp_wait(p.tp)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
         __syncthreads();
     }
 

@@ -68,7 +68,6 @@ struct Q6kParams {
     uint32_t *status;
     uint32_t row_offset;        // vocab shard: global id of local row 0
     uint32_t batch_off;         // first batch row of this launch (key slots)
-    uint32_t key_set;           // which of the two key-slot sets this call uses
     TpParams tp;                // world 0: single GPU (ids written here)
 };
 
@@ -77,32 +76,45 @@ struct Q6kParams {
 constexpr uint32_t TP_KEYS_OFF = 1024;
 constexpr uint32_t TP_MAX_BATCH = 64;
 // Key slots: [set 0..1][source rank][batch row].  Successive lm-head calls
-// alternate sets, so a rank that runs ahead into the next call cannot
-// overwrite keys a slower rank has not reduced yet (it can only get one call
-// ahead: its next finalize waits for the slower rank's lm-head arrivals).
+// alternate sets (the parity of this rank's lm-head call counter, bumped by
+// the finalize kernel), so a rank that runs ahead into the next call cannot
+// overwrite keys a slower rank has not reduced yet: it can only get one call
+// ahead, since its next finalize waits for the slower rank's arrivals.
 static_assert(TP_KEYS_OFF + 2 * TP_MAX_WORLD * TP_MAX_BATCH * 8 <= TP_HEADER_BYTES, "key slots");
 __device__ __forceinline__ unsigned long long *tp_key_slot(uint8_t *base, uint32_t set, int src,
                                                            uint32_t b) {
     return reinterpret_cast<unsigned long long *>(base + TP_KEYS_OFF) +
            (set * TP_MAX_WORLD + src) * TP_MAX_BATCH + b;
 }
+__device__ __forceinline__ uint32_t tp_key_set(const TpParams &tp) {
+    return *reinterpret_cast<volatile uint32_t *>(tp.local_base + TP_LMCALL_OFF) & 1u;
+}
 
-// After every rank's lm-head shard: wait for all keys, reduce, decode ids.
-__global__ void q6k_tp_finalize_kernel(const TpParams tp, uint32_t target, uint32_t key_set,
-                                       uint32_t batch, uint32_t *ids, uint32_t *status) {
-    __shared__ uint32_t ok;
+// After every rank's lm-head shard: wait for all keys, reduce, decode ids,
+// then advance this rank's lm-head call counter (selects the next key set).
+__global__ void q6k_tp_finalize_kernel(const TpParams tp, uint32_t batch, uint32_t *ids,
+                                       uint32_t *status) {
+    __shared__ uint32_t ok, set;
     if (threadIdx.x == 0) {
-        ok = tp_wait(tp, target) ? 1u : 0u;
+        set = tp_key_set(tp);
+        ok = tp_wait(tp) ? 1u : 0u;
         if (!ok) atomicOr(status, WL_DEV_ERR_PEER_TIMEOUT);
     }
     __syncthreads();
     for (uint32_t b = threadIdx.x; b < batch; b += blockDim.x) {
         unsigned long long best = 0ull;
         for (int s = 0; s < tp.world; ++s) {
-            const unsigned long long k = *(volatile unsigned long long *)tp_key_slot(tp.local_base, key_set, s, b);
+            const unsigned long long k =
+                *(volatile unsigned long long *)tp_key_slot(tp.local_base, set, s, b);
             best = best > k ? best : k;
         }
         ids[b] = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        volatile uint32_t *calls =
+            reinterpret_cast<volatile uint32_t *>(tp.local_base + TP_LMCALL_OFF);
+        *calls = *calls + 1u;
     }
 }
 
@@ -339,8 +351,9 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
         __threadfence();
         const unsigned long long k = atomicExch(&p.slots[tid], 0ull);
         if (p.tp.world) {
+            const uint32_t set = tp_key_set(p.tp);
             for (int r = 0; r < p.tp.world; ++r)
-                *tp_key_slot(p.tp.peer_base[r], p.key_set, p.tp.rank, p.batch_off + tid) = k;
+                *tp_key_slot(p.tp.peer_base[r], set, p.tp.rank, p.batch_off + tid) = k;
         } else {
             p.ids[tid] = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
         }

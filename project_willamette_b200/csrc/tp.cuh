@@ -10,9 +10,12 @@
 //    every rank's block (its own included), then, after a system-scope fence,
 //    adds 1 to its rank's arrival counter in every rank's block;
 //  * a kernel that consumes a gathered vector first waits (bounded, on its
-//    own memory) until every rank's counter has reached the number of CTAs
-//    that rank has launched so far -- every store of every rank is then
-//    visible.
+//    own memory) until every rank's counter has caught up with this rank's
+//    own -- every rank has then finished every exchange op this rank has
+//    finished, and all their stores are visible.  The target is read on the
+//    device (this rank's own counter, complete because the previous kernel on
+//    the stream has finished), so launches can be captured in a CUDA graph
+//    and replayed without host bookkeeping.
 // No TMA copy of any kind touches peer memory; peers are reached with plain
 // stores and atomics only.
 #pragma once
@@ -25,9 +28,11 @@ namespace wl {
 
 constexpr int TP_MAX_WORLD = 8;
 // Symmetric block header: [0, 32) arrival counters (one per source rank),
-// [256, 260) this rank's CTA-done counter, [1024, 9216) argmax key slots.
+// [256, 260) this rank's CTA-done counter, [260, 264) its lm-head call
+// counter, [1024, 9216) argmax key slots.
 constexpr uint32_t TP_HEADER_BYTES = 16384;
 constexpr uint32_t TP_DONE_OFF = 256;
+constexpr uint32_t TP_LMCALL_OFF = 260;
 constexpr uint32_t WL_DEV_ERR_PEER_TIMEOUT = 2u;
 
 struct TpParams {
@@ -35,7 +40,7 @@ struct TpParams {
     int rank;
     uint8_t *local_base;                // this rank's symmetric block
     uint8_t *peer_base[TP_MAX_WORLD];   // every rank's block as mapped here
-    uint32_t wait_target;               // 0: no wait; else every counter must reach it
+    uint32_t wait;                      // wait for every rank before reading inputs
 };
 
 // The symmetric block starts with one arrival counter per source rank.
@@ -85,9 +90,11 @@ __device__ __forceinline__ void tp_arrive(const TpParams &tp) {
     }
 }
 
-// Called by one thread: wait (bounded) until every rank's counter in this
-// rank's block reaches target.  Returns false on timeout.
-__device__ __forceinline__ bool tp_wait(const TpParams &tp, uint32_t target) {
+// Called by one thread once the previous kernel on the stream has finished:
+// wait (bounded) until every rank's counter in this rank's block has reached
+// this rank's own.  Returns false on timeout.
+__device__ __forceinline__ bool tp_wait(const TpParams &tp) {
+    const uint32_t target = ld_acquire_sys(tp_counter(tp.local_base, tp.rank));
     const uint64_t t0 = globaltimer_ns();
     for (int s = 0; s < tp.world; ++s) {
         const uint32_t *c = tp_counter(tp.local_base, s);
@@ -100,8 +107,8 @@ __device__ __forceinline__ bool tp_wait(const TpParams &tp, uint32_t target) {
 
 // Stand-alone wait (one thread): used between steps and before a consumer
 // that is not itself a library kernel.
-__global__ void tp_wait_kernel(const TpParams tp, uint32_t target, uint32_t *status) {
-    if (threadIdx.x == 0 && !tp_wait(tp, target)) atomicOr(status, WL_DEV_ERR_PEER_TIMEOUT);
+__global__ void tp_wait_kernel(const TpParams tp, uint32_t *status) {
+    if (threadIdx.x == 0 && !tp_wait(tp)) atomicOr(status, WL_DEV_ERR_PEER_TIMEOUT);
 }
 
 }  // namespace wl

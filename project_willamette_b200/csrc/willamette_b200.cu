@@ -1014,13 +1014,11 @@ struct wl_tp_group {
     size_t bytes = 0;
     uint8_t *peers[TP_MAX_WORLD] = {};
     bool connected = false;
-    uint32_t arrivals = 0;  // arrivals each rank has signalled so far (equal on all ranks)
-    uint32_t lm_calls = 0;  // lm-head calls so far (selects the key-slot set)
 };
 
 namespace {
 
-int tp_params(wl_tp_group *g, uint32_t wait_target, TpParams *tp) {
+int tp_params(wl_tp_group *g, bool wait, TpParams *tp) {
     if (!g) return fail(WL_ERR_INVALID_ARGUMENT, "group is NULL");
     if (!g->connected) return fail(WL_ERR_COMM, "group is not connected (wl_tp_connect)");
     memset(tp, 0, sizeof *tp);
@@ -1028,7 +1026,7 @@ int tp_params(wl_tp_group *g, uint32_t wait_target, TpParams *tp) {
     tp->rank = g->rank;
     tp->local_base = g->local;
     for (int r = 0; r < g->world; ++r) tp->peer_base[r] = g->peers[r];
-    tp->wait_target = wait_target;
+    tp->wait = wait ? 1u : 0u;
     return WL_OK;
 }
 
@@ -1045,7 +1043,7 @@ int check_sym_range(wl_tp_group *g, const float *y, size_t n_floats) {
 
 int launch_q6k_tp(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, uint32_t row_offset,
                   const float *hidden, uint32_t batch, uint32_t *ids, void *scratch,
-                  cudaStream_t s, const TpParams *tp, uint32_t key_set, uint32_t *launches) {
+                  cudaStream_t s, const TpParams *tp) {
     uint32_t *status = status_ptr();
     if (!status) return WL_ERR_NO_DEVICE;
     unsigned long long *slots = reinterpret_cast<unsigned long long *>(scratch);
@@ -1062,10 +1060,8 @@ int launch_q6k_tp(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, uint32
     p.counter = counter;
     p.status = status;
     p.row_offset = row_offset;
-    p.key_set = key_set;
     p.tp = *tp;
     const uint32_t grid = (v + p.rows_per_cta - 1) / p.rows_per_cta;
-    *launches = 0;
     for (uint32_t b0 = 0; b0 < batch;) {
         const int bg = (batch - b0 >= 4) ? 4 : 1;
         uint32_t nst;
@@ -1083,7 +1079,6 @@ int launch_q6k_tp(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, uint32
         else
             WL_CUDA(launch(q6k_lmhead_kernel<1>, dim3(grid), dim3(Q6K_THREADS), smem, s, true, p));
         b0 += (uint32_t)bg;
-        ++*launches;
     }
     return WL_OK;
 }
@@ -1589,12 +1584,11 @@ int wl_tp_destroy(wl_tp_group *g) {
 
 int wl_tp_wait(wl_tp_group *g, void *stream) {
     TpParams tp;
-    int rc = tp_params(g, 0, &tp);
+    int rc = tp_params(g, true, &tp);
     if (rc) return rc;
-    if (g->arrivals == 0) return WL_OK;
     uint32_t *status = status_ptr();
     if (!status) return WL_ERR_NO_DEVICE;
-    tp_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(tp, g->arrivals, status);
+    tp_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(tp, status);
     WL_CUDA(cudaGetLastError());
     return WL_OK;
 }
@@ -1609,7 +1603,7 @@ int wl_tp_i2s_matvec_fused_f32(wl_tp_group *g, const wl_i2s_dev_weight *weights,
                     I2S_FUSE_Q_MAX_K);
     if (!x || !aligned16(x)) return fail(WL_ERR_INVALID_ARGUMENT, "x NULL or misaligned");
     TpParams tp;
-    int rc = tp_params(g, wait_for_input ? g->arrivals : 0u, &tp);
+    int rc = tp_params(g, wait_for_input != 0, &tp);
     if (rc) return rc;
     for (uint32_t j = 0; j < n_weights; ++j) {
         if (!aligned16(weights[j].packed))
@@ -1627,15 +1621,13 @@ int wl_tp_i2s_matvec_fused_f32(wl_tp_group *g, const wl_i2s_dev_weight *weights,
     L.x = x;
     L.tp = &tp;
     L.row_offs = row_offsets;
-    if ((rc = launch_i2s(L, (cudaStream_t)stream, true))) return rc;
-    g->arrivals += 1;
-    return WL_OK;
+    return launch_i2s(L, (cudaStream_t)stream, true);
 }
 
 int wl_tp_i2s_stream_run(wl_tp_group *g, wl_i2s_stream_plan *plan, void *stream) {
     if (!plan) return fail(WL_ERR_INVALID_ARGUMENT, "plan is NULL");
     TpParams tp;
-    int rc = tp_params(g, 0, &tp);
+    int rc = tp_params(g, false, &tp);
     if (rc) return rc;
     if (plan->y_lo < (uintptr_t)(g->local + TP_HEADER_BYTES) ||
         plan->y_hi > (uintptr_t)(g->local + g->bytes))
@@ -1652,7 +1644,6 @@ int wl_tp_i2s_stream_run(wl_tp_group *g, wl_i2s_stream_plan *plan, void *stream)
     p.tp = tp;
     WL_CUDA(launch(kStream[plan->c3 ? 1 : 0], dim3(plan->grid), dim3(STREAM_THREADS),
                    STREAM_SMEM, s, true, p));
-    g->arrivals += 1;
     return WL_OK;
 }
 
@@ -1665,19 +1656,16 @@ int wl_tp_q6k_lm_head_greedy(wl_tp_group *g, const uint8_t *packed_shard, uint32
     if (!ids || !hidden || !aligned16(packed_shard) || !scratch || ((uintptr_t)scratch & 7u))
         return fail(WL_ERR_INVALID_ARGUMENT, "NULL or misaligned pointer");
     TpParams tp;
-    int rc = tp_params(g, 0, &tp);
+    int rc = tp_params(g, false, &tp);
     if (rc) return rc;
     uint32_t *status = status_ptr();
     if (!status) return WL_ERR_NO_DEVICE;
     cudaStream_t s = (cudaStream_t)stream;
     // every rank launches the same batch groups, so arrivals stay in step
-    uint32_t launches = 0;
     if ((rc = launch_q6k_tp(packed_shard, n_embd, vocab_shard, row_offset, hidden, batch, ids,
-                            scratch, s, &tp, g->lm_calls & 1u, &launches)))
+                            scratch, s, &tp)))
         return rc;
-    g->arrivals += launches;
-    q6k_tp_finalize_kernel<<<1, 64, 0, s>>>(tp, g->arrivals, g->lm_calls & 1u, batch, ids, status);
-    g->lm_calls += 1;
+    q6k_tp_finalize_kernel<<<1, 64, 0, s>>>(tp, batch, ids, status);
     WL_CUDA(cudaGetLastError());
     return WL_OK;
 }

@@ -182,6 +182,47 @@ def _worker(rank, world, port, q):
                 assert ids.cpu().tolist() == want, (it, hi, ids.cpu().tolist(), want)
             flags = ctypes.c_uint32(0)
             assert L.wl_device_status(ctypes.byref(flags)) == 0 and flags.value == 0, flags.value
+
+        # The same chain and head captured once in a CUDA graph and replayed
+        # with fresh inputs: wait targets and key sets are read on the device,
+        # so replays need no host bookkeeping.
+        side = torch.cuda.Stream(device=dev)
+        graph = torch.cuda.CUDAGraph()
+        dist.barrier()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                h = torch.cuda.current_stream().cuda_stream
+                g.i2s_matvec([(sA[j][2], A[j][1], sA[j][1], yA[j].ptr, sA[j][3])
+                              for j in range(3)], [sA[j][0] for j in range(3)], 2560,
+                             x0d.data_ptr(), True, h)
+                g.i2s_matvec([(sB[j][2], B[j][1], sB[j][1], yB[j].ptr, sB[j][3])
+                              for j in range(2)], [sB[j][0] for j in range(2)], 2560,
+                             yA[0].ptr, True, h)
+                g.i2s_matvec([(sC[2], C_[1], sC[1], yC.ptr, sC[3])], [sC[0]], 6912, yB[0].ptr,
+                             True, h)
+                g.lm_head_greedy(shards[0][0].data_ptr(), n_embd, nv, v0, Hd.data_ptr(), batch,
+                                 ids.data_ptr(), scratch.data_ptr(), h)
+                g.wait(h)
+        grng = np.random.default_rng(555)  # same on every rank
+        for rep in range(3):
+            xr = synth.activations(grng, 2560)
+            Hr = synth.activations(grng, batch, n_embd)
+            x0d.copy_(torch.from_numpy(xr))
+            Hd.copy_(torch.from_numpy(Hr))
+            torch.cuda.synchronize()
+            dist.barrier()  # every rank's inputs are in place before any replay
+            graph.replay()
+            torch.cuda.synchronize()
+            ra = oracle.i2s_matvec_sse2_i8(A[0][0], A[0][1], 2560, 2560, xr)[0]
+            rb = oracle.i2s_matvec_sse2_i8(B[0][0], B[0][1], 2560, 6912, ra)[0]
+            rc = oracle.i2s_matvec_sse2_i8(C_[0], C_[1], 6912, 2560, rb)[0]
+            assert np.array_equal(read(yC).view(np.uint32), rc.view(np.uint32)), ("graph", rep)
+            want = [oracle.argmax(oracle.compute_logits(Hr[b], heads[0], 14, n_embd, vocab,
+                                                        n_threads=0)) for b in range(batch)]
+            assert ids.cpu().tolist() == want, ("graph ids", rep)
+        flags = ctypes.c_uint32(0)
+        assert L.wl_device_status(ctypes.byref(flags)) == 0 and flags.value == 0, flags.value
+        del graph
         dist.barrier()
         L.wl_i2s_stream_plan_destroy(plan)
         g.close()
