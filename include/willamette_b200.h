@@ -280,6 +280,52 @@ int wl_tp_q6k_lm_head_greedy(wl_tp_group *group, const uint8_t *packed_shard, ui
                              uint32_t vocab_shard, uint32_t row_offset, const float *hidden,
                              uint32_t batch, uint32_t *ids, void *scratch, void *stream);
 
+/* ------------------------------------------------ BitNet b1.58 decode engine
+ * Device-resident single-token forward with the reference's i8 KV cache and
+ * greedy generation: forward_with_cache (src/model/cached_forward.rs:206-504)
+ * and greedy_generate_with_cache (src/model/generate.rs:111-190) for the
+ * BitNetSubNorm variant (RMSNorm, NEOX RoPE, GQA attention, attn_sub_norm,
+ * relu^2 * up, ffn_sub_norm, tied Q6_K embedding / lm-head).  Weights are
+ * copied to the device at create time; the caller keeps no device memory.
+ * A decode step (lm-head, argmax, next forward) is replayed from a CUDA graph
+ * and reads the token and position on the device. */
+typedef struct {
+    uint32_t n_layers, n_embd, n_heads, n_kv_heads, head_dim, n_ff, vocab, n_rot, max_seq;
+    float eps, freq_base;
+} wl_bitnet_config;
+
+typedef struct {
+    const uint8_t *const *w;   /* n_layers * 7 host I2_S packed: q, k, v, o, gate, up, down */
+    const float *w_scale;      /* n_layers * 7 per-tensor scales */
+    const float *norms;        /* per layer: attn_norm[E], attn_sub_norm[E], ffn_norm[E],
+                                  ffn_sub_norm[n_ff] */
+    const float *output_norm;  /* E */
+    const uint8_t *token_embd; /* vocab Q6_K rows (GGUF layout), tied lm-head */
+} wl_bitnet_weights;
+
+typedef struct wl_bitnet wl_bitnet;
+int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *weights,
+                     wl_bitnet **out);
+int wl_bitnet_destroy(wl_bitnet *model);
+/* Empty the KV cache (position 0). */
+int wl_bitnet_reset(wl_bitnet *model);
+uint32_t wl_bitnet_position(const wl_bitnet *model);
+/* forward_with_cache (cached_forward.rs:131-149): position must equal the
+ * cache position; out_hidden (host, n_embd, may be NULL) = output_norm(hidden). */
+int wl_bitnet_forward(wl_bitnet *model, uint32_t token, uint32_t position, float *out_hidden);
+/* Forward each token in order from the current position (the prompt loop of
+ * generate.rs:147-160). */
+int wl_bitnet_prefill(wl_bitnet *model, const uint32_t *tokens, uint32_t n);
+/* The decode loop of generate.rs:165-187 from the last forward's hidden:
+ * n_new greedy ids (host); out_hiddens (host, n_new x n_embd, optional): the
+ * hidden each id was chosen from; device_ms (optional): device time of the
+ * loop (CUDA events on the engine's stream). */
+int wl_bitnet_decode(wl_bitnet *model, uint32_t n_new, uint32_t *out_ids, float *out_hiddens,
+                     float *device_ms);
+/* greedy_generate_with_cache: reset, prefill, decode. */
+int wl_bitnet_generate(wl_bitnet *model, const uint32_t *prompt, uint32_t n_prompt,
+                       uint32_t n_new, uint32_t *out_ids, float *out_hiddens);
+
 /* Q6_K lm-head.  The raw GGUF rows (vocab x n_embd/256 x 210 bytes) are
  * repacked once into the device layout (wl_q6k_packed_bytes bytes). */
 size_t wl_q6k_packed_bytes(uint32_t n_embd, uint32_t vocab);

@@ -241,3 +241,115 @@ def argmax(logits):
     logits = _f32(logits)
     r = lib().or_argmax(_p(logits, _f32p), logits.size)
     return None if r < 0 else int(r)
+
+
+# ------------------------------------------------------------ decode step
+class OrBitnetConfig(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("n_layers", "n_embd", "n_heads", "n_kv_heads",
+                                          "head_dim", "n_ff", "vocab", "n_rot", "max_seq")] + \
+               [("eps", C.c_float), ("freq_base", C.c_float)]
+
+
+class OrBitnetWeights(C.Structure):
+    _fields_ = [("w", C.POINTER(_u8p)), ("w_scale", _f32p), ("norms", _f32p),
+                ("output_norm", _f32p), ("token_embd", _u8p)]
+
+
+class OrKvCache(C.Structure):
+    _fields_ = [("k_q", _i8p), ("v_q", _i8p), ("k_s", _f32p), ("v_s", _f32p), ("pos", _u32)]
+
+
+def _bitnet_prototypes(L):
+    L.or_bitnet_forward.argtypes = [C.POINTER(OrBitnetConfig), C.POINTER(OrBitnetWeights),
+                                    C.POINTER(OrKvCache), _u32, _u32, _f32p, C.c_int]
+    L.or_bitnet_generate.argtypes = [C.POINTER(OrBitnetConfig), C.POINTER(OrBitnetWeights),
+                                     C.POINTER(OrKvCache), C.POINTER(_u32), _u32, _u32,
+                                     C.POINTER(_u32), _f32p, C.c_int]
+    L.or_rms_norm.argtypes = [_f32p, _f32p, C.c_float, _f32p, _u32]
+    L.or_rope_neox.argtypes = [_f32p, _u32, _u32, C.c_float]
+    L.or_softmax_inplace.argtypes = [_f32p, _u32]
+    L.or_kv_quantise.argtypes = [_f32p, _u32, _i8p, _f32p]
+    for n in ("or_rms_norm", "or_rope_neox", "or_softmax_inplace", "or_kv_quantise"):
+        getattr(L, n).restype = None
+
+
+def _blib():
+    L = lib()
+    if not getattr(L, "_bitnet_ready", False):
+        _bitnet_prototypes(L)
+        L._bitnet_ready = True
+    return L
+
+
+def rms_norm(x, w, eps: float) -> np.ndarray:
+    x, w = _f32(x), _f32(w)
+    out = np.zeros(x.size, np.float32)
+    _blib().or_rms_norm(_p(x, _f32p), _p(w, _f32p), eps, _p(out, _f32p), x.size)
+    return out
+
+
+def rope_neox(x, n_rot: int, position: int, freq_base: float) -> np.ndarray:
+    x = _f32(x).copy()
+    _blib().or_rope_neox(_p(x, _f32p), n_rot, position, freq_base)
+    return x
+
+
+def softmax(x) -> np.ndarray:
+    x = _f32(x).copy()
+    _blib().or_softmax_inplace(_p(x, _f32p), x.size)
+    return x
+
+
+def kv_quantise(x) -> tuple[np.ndarray, float]:
+    x = _f32(x)
+    q = np.zeros(x.size, np.int8)
+    s = C.c_float(0.0)
+    _blib().or_kv_quantise(_p(x, _f32p), x.size, _p(q, _i8p), C.byref(s))
+    return q, float(s.value)
+
+
+class BitnetOracle:
+    """The reference's cached forward + greedy generation on a model dict
+    (see project_willamette_b200.synth.bitnet_model)."""
+
+    def __init__(self, model: dict):
+        self.m = model
+        c = model["config"]
+        self.cfg = OrBitnetConfig(**{k: c[k] for k in (
+            "n_layers", "n_embd", "n_heads", "n_kv_heads", "head_dim", "n_ff", "vocab", "n_rot",
+            "max_seq", "eps", "freq_base")})
+        ws = model["w"]
+        self._wp = (_u8p * len(ws))(*[_p(a, _u8p) for a in ws])
+        self.weights = OrBitnetWeights(self._wp, _p(model["w_scale"], _f32p),
+                                       _p(model["norms"], _f32p), _p(model["output_norm"], _f32p),
+                                       _p(model["token_embd"], _u8p))
+        kv = c["n_kv_heads"] * c["head_dim"]
+        n = c["n_layers"] * c["max_seq"]
+        self.kq = np.zeros(n * kv, np.int8)
+        self.vq = np.zeros(n * kv, np.int8)
+        self.ks = np.zeros(n, np.float32)
+        self.vs = np.zeros(n, np.float32)
+        self.kv = OrKvCache(_p(self.kq, _i8p), _p(self.vq, _i8p), _p(self.ks, _f32p),
+                            _p(self.vs, _f32p), 0)
+
+    def reset(self):
+        self.kv.pos = 0
+
+    def forward(self, token: int, position: int, n_threads: int = 0) -> np.ndarray:
+        out = np.zeros(self.cfg.n_embd, np.float32)
+        _check(_blib().or_bitnet_forward(C.byref(self.cfg), C.byref(self.weights),
+                                         C.byref(self.kv), token, position, _p(out, _f32p),
+                                         n_threads or os.cpu_count()), "bitnet_forward")
+        return out
+
+    def generate(self, prompt, n_new: int, n_threads: int = 0, hiddens: bool = False):
+        self.reset()
+        pr = np.ascontiguousarray(prompt, dtype=np.uint32)
+        ids = np.zeros(max(n_new, 1), np.uint32)
+        hs = np.zeros((max(n_new, 1), self.cfg.n_embd), np.float32) if hiddens else None
+        _check(_blib().or_bitnet_generate(
+            C.byref(self.cfg), C.byref(self.weights), C.byref(self.kv),
+            pr.ctypes.data_as(C.POINTER(_u32)), pr.size, n_new,
+            ids.ctypes.data_as(C.POINTER(_u32)), _p(hs, _f32p) if hs is not None else None,
+            n_threads or os.cpu_count()), "bitnet_generate")
+        return (ids[:n_new], hs[:n_new]) if hiddens else ids[:n_new]

@@ -119,6 +119,49 @@ int or_compute_logits(const float *hidden, uint32_t n_embd,
 /* src/model/lm_head.rs:161-174.  Returns -1 for an empty slice. */
 int64_t or_argmax(const float *logits, size_t n);
 
+/* ---- single-token decode step with the i8 KV cache (bitnet_forward.c) ----
+ * BitNet b1.58 (ForwardVariant::BitNetSubNorm): RMSNorm, Q/K/V BitLinears,
+ * NEOX RoPE, KV append (per-token absmax i8), attention, attn_sub_norm, O,
+ * residual, ffn_norm, gate/up, relu^2 * up, ffn_sub_norm, down, residual;
+ * output_norm after the last layer (src/model/cached_forward.rs:206-504). */
+typedef struct {
+    uint32_t n_layers, n_embd, n_heads, n_kv_heads, head_dim, n_ff, vocab, n_rot, max_seq;
+    float eps, freq_base;
+} or_bitnet_config;
+
+typedef struct {
+    const uint8_t *const *w;  /* n_layers * 7 packed I2_S: q, k, v, o, gate, up, down */
+    const float *w_scale;     /* n_layers * 7 */
+    const float *norms;       /* per layer: attn_norm[E], attn_sub_norm[E], ffn_norm[E],
+                                 ffn_sub_norm[F] */
+    const float *output_norm; /* E */
+    const uint8_t *token_embd; /* vocab Q6_K rows (tied embedding / lm-head) */
+} or_bitnet_weights;
+
+typedef struct { /* src/model/kv_cache.rs layout, one slab per layer */
+    int8_t *k_q, *v_q; /* n_layers * max_seq * kv_dim */
+    float *k_s, *v_s;  /* n_layers * max_seq */
+    uint32_t pos;
+} or_kv_cache;
+
+/* primitives.rs:227-254 */
+void or_rms_norm(const float *x, const float *w, float eps, float *out, uint32_t n);
+/* primitives.rs:283-345, RopeType::Neox on one head (head_dim >= n_rot) */
+void or_rope_neox(float *x, uint32_t n_rot, uint32_t position, float freq_base);
+/* attention.rs:45-73 */
+void or_softmax_inplace(float *x, uint32_t n);
+/* kv_cache.rs:245-259 (one token's K or V) */
+void or_kv_quantise(const float *x, uint32_t n, int8_t *q, float *scale);
+/* forward_with_cache (cached_forward.rs:206-259): out = output_norm(hidden). */
+int or_bitnet_forward(const or_bitnet_config *c, const or_bitnet_weights *w, or_kv_cache *kv,
+                      uint32_t token, uint32_t position, float *out, int n_threads);
+/* greedy_generate_with_cache (generate.rs:111-190): prefill the prompt token by
+ * token, then n_new greedy ids.  hiddens (optional, n_new x E): the final
+ * hidden each id was chosen from. */
+int or_bitnet_generate(const or_bitnet_config *c, const or_bitnet_weights *w, or_kv_cache *kv,
+                       const uint32_t *prompt, uint32_t n_prompt, uint32_t n_new,
+                       uint32_t *out_ids, float *hiddens, int n_threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,6 +70,18 @@ class WlI2sStreamOp(C.Structure):
 
 WL_TP_HANDLE_BYTES = 64
 
+
+class WlBitnetConfig(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("n_layers", "n_embd", "n_heads", "n_kv_heads",
+                                          "head_dim", "n_ff", "vocab", "n_rot", "max_seq")] + \
+               [("eps", C.c_float), ("freq_base", C.c_float)]
+
+
+class WlBitnetWeights(C.Structure):
+    _fields_ = [("w", C.POINTER(C.c_void_p)), ("w_scale", C.POINTER(C.c_float)),
+                ("norms", C.POINTER(C.c_float)), ("output_norm", C.POINTER(C.c_float)),
+                ("token_embd", C.c_void_p)]
+
 _vp = C.c_void_p
 _sz = C.c_size_t
 _u32 = C.c_uint32
@@ -110,6 +122,15 @@ PROTOTYPES = {
     "wl_q8_0_packed_bytes": ([_u32, _u32], _sz),
     "wl_dev_q8_0_repack": ([_vp, _u32, _u32, _vp, _vp], _i),
     "wl_dev_q8_0_matvec": ([_vp, _u32, _u32, _vp, _vp, _vp], _i),
+    "wl_bitnet_create": ([C.POINTER(WlBitnetConfig), C.POINTER(WlBitnetWeights), C.POINTER(_vp)],
+                         _i),
+    "wl_bitnet_destroy": ([_vp], _i),
+    "wl_bitnet_reset": ([_vp], _i),
+    "wl_bitnet_position": ([_vp], _u32),
+    "wl_bitnet_forward": ([_vp, _u32, _u32, _fp], _i),
+    "wl_bitnet_prefill": ([_vp, C.POINTER(_u32), _u32], _i),
+    "wl_bitnet_decode": ([_vp, _u32, C.POINTER(_u32), _fp, _fp], _i),
+    "wl_bitnet_generate": ([_vp, C.POINTER(_u32), _u32, _u32, C.POINTER(_u32), _fp], _i),
     "wl_tp_create": ([_i, _i, _sz, C.POINTER(_vp), C.POINTER(C.c_uint8)], _i),
     "wl_tp_connect": ([_vp, C.POINTER(C.c_uint8)], _i),
     "wl_tp_buffer": ([_vp, _sz], _vp),

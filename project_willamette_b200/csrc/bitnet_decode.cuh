@@ -1,0 +1,281 @@
+// bitnet_decode.cuh -- the non-BitLinear kernels of the device-resident
+// BitNet b1.58 decode step (embedding, attention with the i8 KV cache, final
+// norm).  The BitLinears run through i2s_matvec_kernel, whose CTAs apply the
+// RMSNorm (and relu^2 * up for the down projection) to their input before
+// quantising it, and whose epilogue adds the residual in place.
+//
+// Reference step: forward_with_cache_progress_into / forward_one_layer /
+// scaled_dot_product_attention_into / apply_ffn_block
+// (src/model/cached_forward.rs:206-504); primitives: rms_norm_f32
+// (primitives.rs:227-254), apply_rope_f32 NEOX (:283-345), softmax_inplace
+// (attention.rs:45-73), KVCache append / read_into (kv_cache.rs:154-259).
+//
+// The step reads the token and the position from device memory, so a whole
+// step (and greedy decode: lm-head -> token -> next step) is replayed from a
+// CUDA graph without host round trips.
+//
+// Numerics: the per-element arithmetic is the reference's, IEEE
+// round-to-nearest, no FMA contraction; RoPE cos/sin come from a table the
+// host fills with the C library's powf/sinf/cosf exactly as the reference
+// computes them.  Sums (RMSNorm, attention dot products, softmax, the V
+// weighted sum) run as parallel trees instead of the reference's sequential
+// loops, and exp is evaluated in double and rounded to f32, so hidden states
+// agree to rounding level, not bit for bit.
+#pragma once
+
+#include <cstdint>
+
+#include "q6k_lmhead.cuh"
+#include "wl_ptx.cuh"
+
+namespace wl {
+
+constexpr uint32_t WL_DEV_ERR_NONFINITE = 4u;  // non-finite hidden after a layer
+constexpr uint32_t WL_DEV_ERR_POSITION = 8u;   // KV cache full
+constexpr int ATTN_THREADS = 256;
+
+// ---------------------------------------------------------------------------
+// Block-wide reductions (deterministic: fixed shuffle tree, then warps in order).
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = red[0];
+    for (uint32_t w = 1; w < blockDim.x / 32; ++w) t = __fadd_rn(t, red[w]);
+    return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = red[0];
+    for (uint32_t w = 1; w < blockDim.x / 32; ++w) t = fmaxf(t, red[w]);
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// Embedding: the token's row of the tied Q6_K table (repacked lm-head
+// layout, q6k_lmhead.cuh), dequantised w = (d * sc) * q (q6_k.rs:25-69).
+// One CTA per 256-value super-block, one thread per value.  CTA 0 also
+// appends the token to the generated-id list when `ids` is set.
+struct EmbedParams {
+    const uint8_t *packed;  // repacked Q6_K rows
+    uint32_t nb, row_stride;
+    const uint32_t *token;
+    float *hidden;
+    uint32_t *ids;          // optional: ids[*step] = token, ++*step
+    uint32_t *step;
+};
+
+__global__ void __launch_bounds__(256) embed_q6k_kernel(const __grid_constant__ EmbedParams p) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t tok = *p.token;
+    const uint32_t b = blockIdx.x, t = threadIdx.x;
+    const uint8_t *row = p.packed + (size_t)tok * p.row_stride;
+    const uint8_t *ql = row + b * 128u, *qh = row + p.nb * 128u + b * 64u;
+    const int8_t *sc = reinterpret_cast<const int8_t *>(row + p.nb * 192u + b * 16u);
+    const uint16_t dbits = *reinterpret_cast<const uint16_t *>(row + p.nb * 208u + b * 2u);
+    // value t of the block: half h, quarter a, lane l (q6_k.rs:25-57)
+    const uint32_t h = t >> 7, a = (t >> 5) & 3u, l = t & 31u;
+    const uint8_t lb = ql[h * 64u + l + ((a & 1u) ? 32u : 0u)];
+    const uint32_t lo = (a & 2u) ? (lb >> 4) : (lb & 0x0Fu);
+    const uint32_t hi = (qh[h * 32u + l] >> (2u * a)) & 3u;
+    const int q = (int)(lo | (hi << 4)) - 32;
+    const float d = f16_bits_to_f32(dbits);
+    const float w = __fmul_rn(__fmul_rn(d, (float)sc[h * 8u + (l >> 4) + 2u * a]), (float)q);
+    p.hidden[b * 256u + t] = w;
+    if (p.ids && b == 0 && t == 0) {
+        p.ids[*p.step] = tok;
+        *p.step += 1u;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Final RMSNorm (one CTA), then the position advances: the step is done.
+struct OutNormParams {
+    const float *hidden;
+    const float *w;
+    float *out;
+    uint32_t n;
+    float eps;
+    uint32_t *pos;
+};
+
+__global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ OutNormParams p) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
+        ss = __fadd_rn(ss, __fmul_rn(p.hidden[i], p.hidden[i]));
+    const float sum_sq = block_sum(ss, red);
+    const float mean = __fdiv_rn(sum_sq, (float)p.n);
+    const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+    for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
+        p.out[i] = __fmul_rn(__fmul_rn(p.hidden[i], rsqrt), p.w[i]);
+    __syncthreads();
+    if (threadIdx.x == 0) *p.pos += 1u;
+}
+
+// ---------------------------------------------------------------------------
+// Attention for one decode position: one CTA per query head.
+//  1. NEOX RoPE on every K head (all CTAs, redundantly) and on this CTA's Q
+//     head, from the host-filled (cos, sin) table.
+//  2. Per-token absmax i8 quantisation of K and V (kv_cache.rs:245-259);
+//     CTA 0 appends them to the cache, every CTA keeps its own copy for the
+//     current position (no cross-CTA dependency inside the kernel).
+//  3. scores[p] = (q . k_p) * scale over the cache (k_p = (f32)q8 * s_p),
+//     softmax (attention.rs:45-73), out = sum_p w_p * v_p.
+struct AttnParams {
+    const float *q, *k, *v;  // this step's projections: E, KV, KV
+    float *att;              // E
+    int8_t *k_cache, *v_cache;  // this layer: [max_seq][KV]
+    float *k_scale, *v_scale;   // this layer: [max_seq]
+    const float2 *rope;         // [max_seq][n_rot / 2] (cos, sin)
+    const uint32_t *pos;
+    uint32_t n_kv_heads, head_dim, n_rot, max_seq, group;
+    float scale;
+    uint32_t *status;
+};
+
+__device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, int8_t *q,
+                                                  float *scale_out, float *red) {
+    float m = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
+    const float absmax = block_max(m, red);
+    const bool zero = absmax == 0.0f || !isfinite(absmax);
+    const float inv = zero ? 0.0f : __fdiv_rn(127.0f, absmax);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        int qi = 0;
+        if (!zero) {
+            const float r = roundf(__fmul_rn(x[i], inv));
+            qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+        }
+        q[i] = (int8_t)qi;
+    }
+    if (threadIdx.x == 0) *scale_out = zero ? 0.0f : __fdiv_rn(absmax, 127.0f);
+}
+
+__global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float red[32];
+    __shared__ float s_ks, s_vs;
+    const uint32_t HD = p.head_dim, KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
+    const uint32_t h = blockIdx.x, kvh = h / p.group, tid = threadIdx.x;
+    float *ks = reinterpret_cast<float *>(smem);  // KV: rotated k
+    float *vs = ks + KV;                          // KV: v
+    float *qh = vs + KV;                          // HD: rotated q of this head
+    float *obuf = qh + HD;                        // ATTN_THREADS: partial outputs
+    float *scores = obuf + ATTN_THREADS;          // max_seq
+    int8_t *kq = reinterpret_cast<int8_t *>(scores + p.max_seq);  // KV
+    int8_t *vq = kq + KV;                                          // KV
+
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t pos = *p.pos;
+    if (pos >= p.max_seq) {
+        if (tid == 0) atomicOr(p.status, WL_DEV_ERR_POSITION);
+        return;
+    }
+    for (uint32_t i = tid; i < KV; i += blockDim.x) {
+        ks[i] = p.k[i];
+        vs[i] = p.v[i];
+    }
+    for (uint32_t i = tid; i < HD; i += blockDim.x) qh[i] = p.q[h * HD + i];
+    __syncthreads();
+    const float2 *cs = p.rope + (size_t)pos * half;
+    for (uint32_t i = tid; i < p.n_kv_heads * half; i += blockDim.x) {
+        const uint32_t hk = i / half, j = i % half;
+        float *x = ks + hk * HD;
+        const float a = x[j], b = x[j + half], c = cs[j].x, s = cs[j].y;
+        x[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        x[j + half] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+    for (uint32_t j = tid; j < half; j += blockDim.x) {
+        const float a = qh[j], b = qh[j + half], c = cs[j].x, s = cs[j].y;
+        qh[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        qh[j + half] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+    __syncthreads();
+    kv_quantise_block(ks, KV, kq, &s_ks, red);
+    kv_quantise_block(vs, KV, vq, &s_vs, red);
+    __syncthreads();
+    if (h == 0) {
+        for (uint32_t i = tid; i < KV; i += blockDim.x) {
+            p.k_cache[(size_t)pos * KV + i] = kq[i];
+            p.v_cache[(size_t)pos * KV + i] = vq[i];
+        }
+        if (tid == 0) {
+            p.k_scale[pos] = s_ks;
+            p.v_scale[pos] = s_vs;
+        }
+    }
+
+    // scores: warp per position, HD/32 consecutive dims per lane
+    const uint32_t warp = tid >> 5, lane = tid & 31u, nwarps = blockDim.x >> 5;
+    const uint32_t per = HD / 32u;
+    float qreg[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qreg[e] = (uint32_t)e < per ? qh[lane * per + e] : 0.0f;
+    for (uint32_t t = warp; t <= pos; t += nwarps) {
+        const int8_t *kr = t == pos ? kq + kvh * HD : p.k_cache + (size_t)t * KV + kvh * HD;
+        const float sk = t == pos ? s_ks : p.k_scale[t];
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            if ((uint32_t)e < per)
+                d = __fadd_rn(d, __fmul_rn(qreg[e], __fmul_rn((float)kr[lane * per + e], sk)));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, off));
+        if (lane == 0) scores[t] = __fmul_rn(d, p.scale);
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (uint32_t t = tid; t <= pos; t += blockDim.x) m = fmaxf(m, scores[t]);
+    const float mx = block_max(m, red);
+    if (!isfinite(mx)) {  // all -inf, or NaN / +inf present: zeros
+        for (uint32_t t = tid; t <= pos; t += blockDim.x) scores[t] = 0.0f;
+    } else {
+        float sum = 0.0f;
+        for (uint32_t t = tid; t <= pos; t += blockDim.x) {
+            const float e = (float)exp((double)__fsub_rn(scores[t], mx));
+            scores[t] = e;
+            sum = __fadd_rn(sum, e);
+        }
+        const float total = block_sum(sum, red);
+        if (total > 0.0f) {
+            const float inv = __fdiv_rn(1.0f, total);
+            for (uint32_t t = tid; t <= pos; t += blockDim.x) scores[t] = __fmul_rn(scores[t], inv);
+        }
+    }
+    __syncthreads();
+    // out[d] = sum_p w_p * ((f32)v8[p][d] * s_p): groups of HD threads split p
+    const uint32_t groups = blockDim.x / HD, d = tid % HD, g = tid / HD;
+    float acc = 0.0f;
+    if (g < groups) {
+        for (uint32_t t = g; t <= pos; t += groups) {
+            const int8_t vv = t == pos ? vq[kvh * HD + d] : p.v_cache[(size_t)t * KV + kvh * HD + d];
+            const float sv = t == pos ? s_vs : p.v_scale[t];
+            acc = __fadd_rn(acc, __fmul_rn(scores[t], __fmul_rn((float)vv, sv)));
+        }
+    }
+    obuf[tid] = acc;
+    __syncthreads();
+    if (tid < HD) {
+        float o = obuf[tid];
+        for (uint32_t gg = 1; gg < groups; ++gg) o = __fadd_rn(o, obuf[gg * HD + tid]);
+        p.att[h * HD + tid] = o;
+    }
+}
+
+inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq) {
+    return (size_t)(2 * kv + hd + ATTN_THREADS + max_seq) * 4u + 2u * kv + 16u;
+}
+
+}  // namespace wl

@@ -65,7 +65,17 @@ struct I2sMatvecParams {
     float *scale_out;       // FUSE_Q: optional activation scale (CTA 0)
     uint32_t *status;
     TpParams tp;            // world 0: single GPU
+    // Decode-step fusions (FUSE_Q only): the CTA transforms its input before
+    // quantising it, and the epilogue can add the output into y in place.
+    uint32_t pre;           // I2S_PRE_NONE / I2S_PRE_RMSNORM / I2S_PRE_RELU2_RMSNORM
+    const float *norm_w;    // RMSNorm weight, K floats
+    const float *x2;        // I2S_PRE_RELU2_RMSNORM: the up projection, K floats
+    float eps;
+    uint32_t residual;      // y[r] = y[r] + out (reference residual add)
+    uint32_t finite_flag;   // status bit set when a residual sum is not finite
 };
+
+constexpr uint32_t I2S_PRE_NONE = 0, I2S_PRE_RMSNORM = 1, I2S_PRE_RELU2_RMSNORM = 2;
 
 // ---------------------------------------------------------------------------
 // Kernel 1: per-row absmax quantisation (bitlinear_sse2.rs:285-304).
@@ -259,6 +269,52 @@ __device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint3
     return max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
 }
 
+// Decode-step input transform, by the whole CTA into xs (every CTA computes
+// the same values in the same order):
+//   I2S_PRE_RMSNORM:       xs = rms_norm(x, w)            (primitives.rs:227-254)
+//   I2S_PRE_RELU2_RMSNORM: xs = rms_norm(relu(x)^2 * x2, w) (ffn.rs:37-65, then
+//                          the ffn_sub_norm of cached_forward.rs:480-494)
+// rms_norm: mean = sum(v*v) / K, rsqrt = 1 / sqrt(mean + eps),
+// out = (v * rsqrt) * w, IEEE round-to-nearest (the sum as a tree).
+__device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t K, float *xs,
+                                              float *red) {
+    const uint32_t tid = threadIdx.x, nthr = blockDim.x;
+    float ss = 0.0f;
+    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
+        float4 v = *reinterpret_cast<const float4 *>(p.x + i);
+        if (p.pre == I2S_PRE_RELU2_RMSNORM) {
+            const float4 u = *reinterpret_cast<const float4 *>(p.x2 + i);
+            const float r0 = v.x > 0.0f ? v.x : 0.0f, r1 = v.y > 0.0f ? v.y : 0.0f;
+            const float r2 = v.z > 0.0f ? v.z : 0.0f, r3 = v.w > 0.0f ? v.w : 0.0f;
+            v.x = __fmul_rn(__fmul_rn(r0, r0), u.x);
+            v.y = __fmul_rn(__fmul_rn(r1, r1), u.y);
+            v.z = __fmul_rn(__fmul_rn(r2, r2), u.z);
+            v.w = __fmul_rn(__fmul_rn(r3, r3), u.w);
+        }
+        *reinterpret_cast<float4 *>(xs + i) = v;
+        ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                                     __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float sum_sq = red[0];
+    for (uint32_t w = 1; w < nthr / 32; ++w) sum_sq = __fadd_rn(sum_sq, red[w]);
+    const float mean = __fdiv_rn(sum_sq, (float)K);
+    const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
+        float4 v = *reinterpret_cast<const float4 *>(xs + i);
+        const float4 w = *reinterpret_cast<const float4 *>(p.norm_w + i);
+        v.x = __fmul_rn(__fmul_rn(v.x, rsqrt), w.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, rsqrt), w.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, rsqrt), w.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, rsqrt), w.w);
+        *reinterpret_cast<float4 *>(xs + i) = v;
+    }
+    __syncthreads();  // red is reused by the quantiser; xs is complete
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 2: per-op matvec (one BitLinear, or several sharing one input).
 
@@ -344,7 +400,12 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     if constexpr (FUSE_Q) {
         float *xs = reinterpret_cast<float *>(smem + nst * stage_bytes);
         int8_t *qs = reinterpret_cast<int8_t *>(xs + K);
-        act_scale = cta_quantize(p.x, K, xs, qs, red);
+        if (p.pre != I2S_PRE_NONE) {
+            cta_pre_input(p, K, xs, red);
+            act_scale = cta_quantize(xs, K, xs, qs, red);
+        } else {
+            act_scale = cta_quantize(p.x, K, xs, qs, red);
+        }
         if (blockIdx.x == 0) {
             if (p.q_out)
                 for (uint32_t i = tid * 16; i < K; i += I2S_THREADS * 16)
@@ -443,6 +504,11 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             const float yv = __fmul_rn(combined, __int2float_rn(dot));
             if (p.tp.world) {
                 tp_store_all(p.tp, job.y + job.row_off + local, yv);
+            } else if (p.residual) {
+                float *dst = job.y + job.row_off + local;
+                const float nv = __fadd_rn(*dst, yv);
+                *dst = nv;
+                if (p.finite_flag && !isfinite(nv)) atomicOr(p.status, p.finite_flag);
             } else {
                 job.y[job.row_off + local] = yv;
             }

@@ -18,6 +18,7 @@
 
 #include "../../include/willamette_b200.h"
 #include "argmax.cuh"
+#include "bitnet_decode.cuh"
 #include "i2s_matvec.cuh"
 #include "i2s_stream.cuh"
 #include "i2s_gemm.cuh"
@@ -127,7 +128,7 @@ int configure_kernels() {
                             (const void *)i2s_gemm_kernel<256>,
                             (const void *)kStream[0], (const void *)kStream[1],
                             (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<4>,
-                            (const void *)q8_0_matvec_kernel};
+                            (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel};
     for (const void *k : others)
         WL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      WL_MAX_DYN_SMEM));
@@ -261,6 +262,11 @@ struct I2sLaunch {
     float *scale_out = nullptr;
     const TpParams *tp = nullptr;      // tensor-parallel exchange, or null
     const uint32_t *row_offs = nullptr;  // per weight (tensor parallel)
+    // decode-step fusions (fused-input kernels only)
+    uint32_t pre = I2S_PRE_NONE;
+    const float *norm_w = nullptr, *x2 = nullptr;
+    float eps = 0.0f;
+    uint32_t residual = 0, finite_flag = 0;
 };
 
 bool weights_may_have_code3(const wl_i2s_dev_weight *w, uint32_t nw) {
@@ -294,6 +300,12 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     p.scale_out = L.scale_out;
     p.status = status;
     if (L.tp) p.tp = *L.tp;
+    p.pre = L.pre;
+    p.norm_w = L.norm_w;
+    p.x2 = L.x2;
+    p.eps = L.eps;
+    p.residual = L.residual;
+    p.finite_flag = L.finite_flag;
     const bool fuse = L.x != nullptr;
     int lpr = 32;
     const int shape = i2s_shape_index(K, &lpr);
@@ -1085,6 +1097,246 @@ int launch_q6k_tp(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, uint32
 
 }  // namespace
 
+// ------------------------------------------------------- BitNet decode engine
+// Device-resident single-token forward with the reference's i8 KV cache
+// (cached_forward.rs:206-504) and greedy generation (generate.rs:111-190).
+struct wl_bitnet {
+    wl_bitnet_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    uint8_t *wblock = nullptr;             // every packed I2_S weight
+    std::vector<wl_i2s_dev_weight> mats;   // n_layers * 7 (y set per use)
+    float *norms = nullptr, *out_norm = nullptr;
+    uint8_t *q6k = nullptr;                // repacked tied embedding / lm-head
+    float2 *rope = nullptr;
+    int8_t *kq = nullptr, *vq = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    float *hidden = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+          *gate = nullptr, *up = nullptr, *final_h = nullptr;
+    uint32_t *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_ids = nullptr;
+    uint32_t ids_cap = 0;
+    void *lm_scratch = nullptr;
+    uint32_t *h_pinned = nullptr;          // token staging
+    uint32_t pos = 0;                      // host mirror of the cache position
+    bool have_hidden = false;              // final_h holds a forward's output
+    cudaGraphExec_t g_forward = nullptr, g_step = nullptr, g_last = nullptr;
+};
+
+namespace {
+
+constexpr int BN_MATS = 7;  // q, k, v, o, gate, up, down
+
+uint32_t bn_kv(const wl_bitnet_config &c) { return c.n_kv_heads * c.head_dim; }
+
+int bn_validate(const wl_bitnet_config *c) {
+    if (!c) return fail(WL_ERR_INVALID_ARGUMENT, "config is NULL");
+    const uint32_t E = c->n_embd, F = c->n_ff, HD = c->head_dim;
+    if (!c->n_layers || !E || !F || !HD || !c->n_heads || !c->n_kv_heads || !c->vocab ||
+        !c->max_seq)
+        return fail(WL_ERR_GGUF_PARSE, "bitnet config: zero dimension");
+    if (E % 256 || E > I2S_FUSE_Q_MAX_K)
+        return fail(WL_ERR_GGUF_PARSE, "embedding_length %u must be a multiple of 256 <= %u", E,
+                    I2S_FUSE_Q_MAX_K);
+    if (F % 128 || F > I2S_FUSE_Q_MAX_K)
+        return fail(WL_ERR_GGUF_PARSE, "feed_forward_length %u must be a multiple of 128 <= %u",
+                    F, I2S_FUSE_Q_MAX_K);
+    if (c->n_heads * HD != E || c->n_heads % c->n_kv_heads)
+        return fail(WL_ERR_GGUF_PARSE, "heads %u x head_dim %u vs embedding %u / kv heads %u",
+                    c->n_heads, HD, E, c->n_kv_heads);
+    if (HD % 32 || HD > 256 || (bn_kv(*c)) % 128)
+        return fail(WL_ERR_GGUF_PARSE, "head_dim %u must be a multiple of 32 <= 256 and kv_dim a "
+                    "multiple of 128", HD);
+    if (!c->n_rot || c->n_rot % 2 || c->n_rot > HD)
+        return fail(WL_ERR_GGUF_PARSE, "rope_dimension_count %u", c->n_rot);
+    if (attn_smem_bytes(bn_kv(*c), HD, c->max_seq) > (size_t)WL_MAX_DYN_SMEM)
+        return fail(WL_ERR_INVALID_ARGUMENT, "max_seq %u too long for the attention kernel",
+                    c->max_seq);
+    if (!std::isfinite(c->eps) || !std::isfinite(c->freq_base))
+        return fail(WL_ERR_GGUF_PARSE, "non-finite eps / rope base");
+    return WL_OK;
+}
+
+// The reference's RoPE angles (primitives.rs:316-340): theta = pos *
+// freq_base^(-2j / n_rot) in f32 with the C library's powf, then sinf/cosf.
+void bn_rope_table(const wl_bitnet_config &c, std::vector<float2> &t) {
+    const uint32_t half = c.n_rot / 2;
+    t.resize((size_t)c.max_seq * half);
+    const float n_rot_f = (float)c.n_rot;
+    for (uint32_t p = 0; p < c.max_seq; ++p) {
+        const float pos = (float)p;
+        for (uint32_t j = 0; j < half; ++j) {
+            const float exponent = -2.0f * (float)j / n_rot_f;
+            const float theta = pos * powf(c.freq_base, exponent);
+            t[(size_t)p * half + j] = make_float2(cosf(theta), sinf(theta));
+        }
+    }
+}
+
+int bn_matvec(wl_bitnet *m, uint32_t l, int first, int count, uint32_t K, const float *x,
+              float *const *ys, uint32_t pre, const float *norm_w, const float *x2,
+              uint32_t residual, uint32_t finite_flag, cudaStream_t s) {
+    wl_i2s_dev_weight w[3];
+    for (int j = 0; j < count; ++j) {
+        w[j] = m->mats[(size_t)l * BN_MATS + first + j];
+        w[j].y = ys[j];
+        w[j].acc = nullptr;
+    }
+    I2sLaunch L;
+    L.w = w;
+    L.nw = (uint32_t)count;
+    L.K = K;
+    L.x = x;
+    L.pre = pre;
+    L.norm_w = norm_w;
+    L.x2 = x2;
+    L.eps = m->cfg.eps;
+    L.residual = residual;
+    L.finite_flag = finite_flag;
+    return launch_i2s(L, s, true);
+}
+
+// One token: embedding (of *d_token; appended to d_ids when commit), every
+// layer, output norm; the device position advances by one.
+int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
+    const wl_bitnet_config &c = m->cfg;
+    const uint32_t E = c.n_embd, F = c.n_ff, KV = bn_kv(c), nb = E / 256u;
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    EmbedParams ep;
+    ep.packed = m->q6k;
+    ep.nb = nb;
+    ep.row_stride = q6k_row_stride(nb);
+    ep.token = m->d_token;
+    ep.hidden = m->hidden;
+    ep.ids = commit ? m->d_ids : nullptr;
+    ep.step = m->d_step;
+    WL_CUDA(launch(embed_q6k_kernel, dim3(nb), dim3(256), 0, s, true, ep));
+    const size_t attn_smem = attn_smem_bytes(KV, c.head_dim, c.max_seq);
+    const float scale = 1.0f / sqrtf((float)c.head_dim);  // attention_scale, primitives.rs:354
+    int rc;
+    for (uint32_t l = 0; l < c.n_layers; ++l) {
+        const float *nrm = m->norms + (size_t)l * (3 * E + F);
+        float *qkv[3] = {m->q, m->k, m->v};
+        if ((rc = bn_matvec(m, l, 0, 3, E, m->hidden, qkv, I2S_PRE_RMSNORM, nrm, nullptr, 0, 0, s)))
+            return rc;
+        AttnParams ap;
+        ap.q = m->q;
+        ap.k = m->k;
+        ap.v = m->v;
+        ap.att = m->att;
+        ap.k_cache = m->kq + (size_t)l * c.max_seq * KV;
+        ap.v_cache = m->vq + (size_t)l * c.max_seq * KV;
+        ap.k_scale = m->ks + (size_t)l * c.max_seq;
+        ap.v_scale = m->vs + (size_t)l * c.max_seq;
+        ap.rope = m->rope;
+        ap.pos = m->d_pos;
+        ap.n_kv_heads = c.n_kv_heads;
+        ap.head_dim = c.head_dim;
+        ap.n_rot = c.n_rot;
+        ap.max_seq = c.max_seq;
+        ap.group = c.n_heads / c.n_kv_heads;
+        ap.scale = scale;
+        ap.status = status;
+        WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads), dim3(ATTN_THREADS), attn_smem, s, true,
+                       ap));
+        float *o[1] = {m->hidden};
+        if ((rc = bn_matvec(m, l, 3, 1, E, m->att, o, I2S_PRE_RMSNORM, nrm + E, nullptr, 1, 0, s)))
+            return rc;
+        float *gu[2] = {m->gate, m->up};
+        if ((rc = bn_matvec(m, l, 4, 2, E, m->hidden, gu, I2S_PRE_RMSNORM, nrm + 2 * E, nullptr, 0,
+                            0, s)))
+            return rc;
+        if ((rc = bn_matvec(m, l, 6, 1, F, m->gate, o, I2S_PRE_RELU2_RMSNORM, nrm + 3 * E, m->up, 1,
+                            WL_DEV_ERR_NONFINITE, s)))
+            return rc;
+    }
+    OutNormParams op;
+    op.hidden = m->hidden;
+    op.w = m->out_norm;
+    op.out = m->final_h;
+    op.n = E;
+    op.eps = c.eps;
+    op.pos = m->d_pos;
+    WL_CUDA(launch(out_norm_kernel, dim3(1), dim3(256), 0, s, true, op));
+    return WL_OK;
+}
+
+// Greedy head on final_h -> *d_token (lm_head.rs:29-108 + :161-174).
+int bn_enqueue_head(wl_bitnet *m, cudaStream_t s) {
+    return launch_q6k(m->q6k, m->cfg.n_embd, m->cfg.vocab, m->final_h, 1, nullptr, m->d_token,
+                      m->lm_scratch, s, true);
+}
+
+int bn_capture(wl_bitnet *m, int which, cudaGraphExec_t *out) {
+    cudaGraph_t g = nullptr;
+    WL_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = WL_OK;
+    if (which == 0) {
+        rc = bn_enqueue_forward(m, m->stream, false);
+    } else if (which == 1) {
+        rc = bn_enqueue_head(m, m->stream);
+        if (!rc) rc = bn_enqueue_forward(m, m->stream, true);
+    } else {
+        rc = bn_enqueue_head(m, m->stream);
+        if (!rc) {
+            // commit the last id without running its forward: the embedding
+            // kernel appends it (writing hidden, which nothing reads next)
+            EmbedParams ep;
+            const uint32_t nb = m->cfg.n_embd / 256u;
+            ep.packed = m->q6k;
+            ep.nb = nb;
+            ep.row_stride = q6k_row_stride(nb);
+            ep.token = m->d_token;
+            ep.hidden = m->hidden;
+            ep.ids = m->d_ids;
+            ep.step = m->d_step;
+            if (launch(embed_q6k_kernel, dim3(nb), dim3(256), 0, m->stream, true, ep) !=
+                cudaSuccess)
+                rc = fail(WL_ERR_CUDA, "embedding launch failed");
+        }
+    }
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(WL_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(WL_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    return WL_OK;
+}
+
+// Device status after a synchronised run: a non-finite hidden is the
+// reference's GgufParse error (cached_forward.rs:507-517).
+int bn_check_status(wl_bitnet *m) {
+    Ctx &c = ctx();
+    WL_CUDA(cudaStreamSynchronize(m->stream));
+    uint32_t f = 0;
+    WL_CUDA(cudaMemcpy(&f, c.d_status, 4, cudaMemcpyDeviceToHost));
+    if (!f) return WL_OK;
+    WL_CUDA(cudaMemset(c.d_status, 0, 4));
+    if (f & WL_DEV_ERR_NONFINITE)
+        return fail(WL_ERR_GGUF_PARSE, "forward_with_cache: non-finite hidden after a layer");
+    if (f & WL_DEV_ERR_POSITION) return fail(WL_ERR_GGUF_PARSE, "KV cache is full");
+    return fail(WL_ERR_DEVICE_TIMEOUT, "device status %#x", f);
+}
+
+int bn_forward_token(wl_bitnet *m, uint32_t token) {
+    *m->h_pinned = token;
+    WL_CUDA(cudaMemcpyAsync(m->d_token, m->h_pinned, 4, cudaMemcpyHostToDevice, m->stream));
+    if (!m->g_forward) {
+        int rc = bn_capture(m, 0, &m->g_forward);
+        if (rc) return rc;
+    }
+    WL_CUDA(cudaGraphLaunch(m->g_forward, m->stream));
+    m->pos += 1;
+    m->have_hidden = true;
+    return WL_OK;
+}
+
+}  // namespace
+
 // ===================================================================== C ABI
 extern "C" {
 
@@ -1668,6 +1920,250 @@ int wl_tp_q6k_lm_head_greedy(wl_tp_group *g, const uint8_t *packed_shard, uint32
     q6k_tp_finalize_kernel<<<1, 64, 0, s>>>(tp, batch, ids, status);
     WL_CUDA(cudaGetLastError());
     return WL_OK;
+}
+
+// ------------------------------------------------------- BitNet decode engine
+int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_bitnet **out) {
+    if (!out) return fail(WL_ERR_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    int rc = bn_validate(cfg);
+    if (rc) return rc;
+    if (!w || !w->w || !w->w_scale || !w->norms || !w->output_norm || !w->token_embd)
+        return fail(WL_ERR_INVALID_ARGUMENT, "weights: NULL pointer");
+    const wl_bitnet_config c = *cfg;
+    const uint32_t E = c.n_embd, F = c.n_ff, KV = bn_kv(c);
+    const uint32_t outs[BN_MATS] = {E, KV, KV, E, F, F, E};
+    const uint32_t ins[BN_MATS] = {E, E, E, E, E, E, F};
+    for (uint32_t i = 0; i < c.n_layers * BN_MATS; ++i)
+        if (!w->w[i] || !std::isfinite(w->w_scale[i]))
+            return fail(WL_ERR_GGUF_PARSE, "layer %u tensor %u: missing data or non-finite scale",
+                        i / BN_MATS, i % BN_MATS);
+    Ctx &cx = ctx();
+    std::lock_guard<std::mutex> lk(cx.mu);
+    if ((rc = ensure_init(cx))) return rc;
+    auto *m = new wl_bitnet();
+    m->cfg = c;
+    m->device = cx.device;
+    auto cleanup = [&](int code) {
+        wl_bitnet_destroy(m);
+        return code;
+    };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return cleanup(fail(WL_ERR_CUDA, "stream"));
+    // packed I2_S weights, 256-byte aligned each
+    size_t total = 0;
+    std::vector<size_t> off(c.n_layers * BN_MATS);
+    for (uint32_t i = 0; i < c.n_layers * BN_MATS; ++i) {
+        off[i] = total;
+        total += ((size_t)ins[i % BN_MATS] / 4 * outs[i % BN_MATS] + 255) & ~(size_t)255;
+    }
+    const size_t nrm = (size_t)c.n_layers * (3 * E + F);
+    const size_t q6_raw = (size_t)c.vocab * (E / 256) * 210;
+    const size_t q6_packed = (size_t)c.vocab * q6k_row_stride(E / 256);
+    const size_t kv_bytes = (size_t)c.n_layers * c.max_seq * KV;
+    const size_t kvs = (size_t)c.n_layers * c.max_seq;
+    m->ids_cap = 1u << 16;
+    void *p = nullptr;
+#define BN_ALLOC(ptr, bytes)                                                         \
+    do {                                                                             \
+        if (cudaMalloc(&p, (bytes)) != cudaSuccess)                                  \
+            return cleanup(fail(WL_ERR_CUDA, "out of device memory (%s)", #ptr));    \
+        ptr = reinterpret_cast<decltype(ptr)>(p);                                    \
+    } while (0)
+    BN_ALLOC(m->wblock, total);
+    BN_ALLOC(m->norms, nrm * 4);
+    BN_ALLOC(m->out_norm, (size_t)E * 4);
+    BN_ALLOC(m->q6k, q6_packed);
+    BN_ALLOC(m->rope, (size_t)c.max_seq * (c.n_rot / 2) * sizeof(float2));
+    BN_ALLOC(m->kq, kv_bytes);
+    BN_ALLOC(m->vq, kv_bytes);
+    BN_ALLOC(m->ks, kvs * 4);
+    BN_ALLOC(m->vs, kvs * 4);
+    BN_ALLOC(m->hidden, (size_t)E * 4);
+    BN_ALLOC(m->q, (size_t)E * 4);
+    BN_ALLOC(m->k, (size_t)KV * 4);
+    BN_ALLOC(m->v, (size_t)KV * 4);
+    BN_ALLOC(m->att, (size_t)E * 4);
+    BN_ALLOC(m->gate, (size_t)F * 4);
+    BN_ALLOC(m->up, (size_t)F * 4);
+    BN_ALLOC(m->final_h, (size_t)E * 4);
+    BN_ALLOC(m->d_token, 16);
+    BN_ALLOC(m->d_pos, 16);
+    BN_ALLOC(m->d_step, 16);
+    BN_ALLOC(m->d_ids, (size_t)m->ids_cap * 4);
+    BN_ALLOC(m->lm_scratch, 256);
+#undef BN_ALLOC
+    if (cudaMallocHost(&p, 64) != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "pinned"));
+    m->h_pinned = (uint32_t *)p;
+    cudaStream_t s = m->stream;
+    uint8_t *q6raw = nullptr;
+    if (cudaMalloc(&q6raw, q6_raw) != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "q6k staging"));
+    cudaError_t e = cudaMemcpyAsync(q6raw, w->token_embd, q6_raw, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        q6k_repack_kernel<<<1024, 256, 0, s>>>(q6raw, E / 256, c.vocab, m->q6k);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(q6raw);
+    if (e != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "embedding upload: %s", cudaGetErrorString(e)));
+    std::vector<float2> rope;
+    bn_rope_table(c, rope);
+    m->mats.resize((size_t)c.n_layers * BN_MATS);
+    uint32_t *found = cx.d_status + 8;
+    for (uint32_t i = 0; i < c.n_layers * BN_MATS && e == cudaSuccess; ++i) {
+        const uint32_t K = ins[i % BN_MATS], N = outs[i % BN_MATS];
+        const size_t bytes = (size_t)K / 4 * N;
+        uint8_t *dst = m->wblock + off[i];
+        e = cudaMemcpyAsync(dst, w->w[i], bytes, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(found, 0, 4, s);
+        if (e == cudaSuccess) {
+            const size_t n16 = bytes / 16;
+            i2s_scan_code3_kernel<<<(unsigned)std::min<size_t>((n16 + 255) / 256, 2048), 256, 0, s>>>(
+                (const uint4 *)dst, n16, found);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaMemcpyAsync(m->h_pinned, found, 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        wl_i2s_dev_weight &mw = m->mats[i];
+        mw.packed = dst;
+        mw.w_scale = w->w_scale[i];
+        mw.out_dim = N;
+        mw.y = nullptr;
+        mw.acc = nullptr;
+        mw.flags = *m->h_pinned ? 0u : WL_I2S_NO_CODE3;
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->norms, w->norms, nrm * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->out_norm, w->output_norm, (size_t)E * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->rope, rope.data(), rope.size() * sizeof(float2),
+                            cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->lm_scratch, 0, 256, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->d_pos, 0, 16, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->d_step, 0, 16, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e)));
+    *out = m;
+    return WL_OK;
+}
+
+int wl_bitnet_destroy(wl_bitnet *m) {
+    if (!m) return WL_OK;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->g_forward) cudaGraphExecDestroy(m->g_forward);
+    if (m->g_step) cudaGraphExecDestroy(m->g_step);
+    if (m->g_last) cudaGraphExecDestroy(m->g_last);
+    void *bufs[] = {m->wblock, m->norms, m->out_norm, m->q6k, m->rope, m->kq, m->vq, m->ks,
+                    m->vs, m->hidden, m->q, m->k, m->v, m->att, m->gate, m->up, m->final_h,
+                    m->d_token, m->d_pos, m->d_step, m->d_ids, m->lm_scratch};
+    for (void *b : bufs)
+        if (b) cudaFree(b);
+    if (m->h_pinned) cudaFreeHost(m->h_pinned);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return WL_OK;
+}
+
+int wl_bitnet_reset(wl_bitnet *m) {
+    if (!m) return fail(WL_ERR_INVALID_ARGUMENT, "model is NULL");
+    cudaSetDevice(m->device);
+    WL_CUDA(cudaMemsetAsync(m->d_pos, 0, 4, m->stream));
+    WL_CUDA(cudaStreamSynchronize(m->stream));
+    m->pos = 0;
+    m->have_hidden = false;
+    return WL_OK;
+}
+
+uint32_t wl_bitnet_position(const wl_bitnet *m) { return m ? m->pos : 0u; }
+
+int wl_bitnet_forward(wl_bitnet *m, uint32_t token, uint32_t position, float *out_hidden) {
+    if (!m) return fail(WL_ERR_INVALID_ARGUMENT, "model is NULL");
+    if (m->pos != position)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "forward_with_cache: cache.position()=%u != position=%u; tokens must be "
+                    "processed in order", m->pos, position);
+    if (position >= m->cfg.max_seq) return fail(WL_ERR_GGUF_PARSE, "KV cache is full");
+    if (token >= m->cfg.vocab)
+        return fail(WL_ERR_GGUF_PARSE, "forward_with_cache: token_id %u out of vocab range %u",
+                    token, m->cfg.vocab);
+    cudaSetDevice(m->device);
+    int rc = bn_forward_token(m, token);
+    if (rc) return rc;
+    if ((rc = bn_check_status(m))) return rc;
+    if (out_hidden)
+        WL_CUDA(cudaMemcpy(out_hidden, m->final_h, (size_t)m->cfg.n_embd * 4, cudaMemcpyDeviceToHost));
+    return WL_OK;
+}
+
+int wl_bitnet_prefill(wl_bitnet *m, const uint32_t *tokens, uint32_t n) {
+    if (!m || (!tokens && n)) return fail(WL_ERR_INVALID_ARGUMENT, "NULL argument");
+    if ((uint64_t)m->pos + n > m->cfg.max_seq) return fail(WL_ERR_GGUF_PARSE, "KV cache is full");
+    for (uint32_t i = 0; i < n; ++i)
+        if (tokens[i] >= m->cfg.vocab)
+            return fail(WL_ERR_GGUF_PARSE, "prompt token %u (idx %u) out of vocab range %u",
+                        tokens[i], i, m->cfg.vocab);
+    cudaSetDevice(m->device);
+    for (uint32_t i = 0; i < n; ++i) {
+        int rc = bn_forward_token(m, tokens[i]);
+        if (rc) return rc;
+        // the token staging word is reused: wait for its copy before the next
+        WL_CUDA(cudaStreamSynchronize(m->stream));
+    }
+    return bn_check_status(m);
+}
+
+int wl_bitnet_decode(wl_bitnet *m, uint32_t n_new, uint32_t *out_ids, float *out_hiddens,
+                     float *device_ms) {
+    if (!m || (!out_ids && n_new)) return fail(WL_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (!m->have_hidden) return fail(WL_ERR_INVALID_ARGUMENT, "decode needs a prefilled prompt");
+    if (n_new == 0) return WL_OK;
+    if (n_new > m->ids_cap) return fail(WL_ERR_INVALID_ARGUMENT, "n_new > %u", m->ids_cap);
+    if ((uint64_t)m->pos + n_new - 1 > m->cfg.max_seq)
+        return fail(WL_ERR_GGUF_PARSE, "KV cache is full");
+    cudaSetDevice(m->device);
+    int rc;
+    if (!m->g_step && (rc = bn_capture(m, 1, &m->g_step))) return rc;
+    if (!m->g_last && (rc = bn_capture(m, 2, &m->g_last))) return rc;
+    const uint32_t E = m->cfg.n_embd;
+    WL_CUDA(cudaMemsetAsync(m->d_step, 0, 4, m->stream));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (device_ms) {
+        WL_CUDA(cudaEventCreate(&e0));
+        WL_CUDA(cudaEventCreate(&e1));
+        WL_CUDA(cudaEventRecord(e0, m->stream));
+    }
+    for (uint32_t step = 0; step < n_new; ++step) {
+        if (out_hiddens)  // the hidden this step's id is chosen from
+            WL_CUDA(cudaMemcpyAsync(out_hiddens + (size_t)step * E, m->final_h, (size_t)E * 4,
+                                    cudaMemcpyDeviceToHost, m->stream));
+        WL_CUDA(cudaGraphLaunch(step + 1 < n_new ? m->g_step : m->g_last, m->stream));
+    }
+    if (device_ms) {
+        WL_CUDA(cudaEventRecord(e1, m->stream));
+        WL_CUDA(cudaEventSynchronize(e1));
+        cudaEventElapsedTime(device_ms, e0, e1);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    m->pos += n_new - 1;
+    if ((rc = bn_check_status(m))) return rc;
+    WL_CUDA(cudaMemcpy(out_ids, m->d_ids, (size_t)n_new * 4, cudaMemcpyDeviceToHost));
+    return WL_OK;
+}
+
+int wl_bitnet_generate(wl_bitnet *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_new,
+                       uint32_t *out_ids, float *out_hiddens) {
+    if (!m) return fail(WL_ERR_INVALID_ARGUMENT, "model is NULL");
+    if (n_prompt == 0 || !prompt)
+        return fail(WL_ERR_GGUF_PARSE, "greedy_generate_with_cache: prompt_ids must not be empty");
+    if ((uint64_t)n_prompt + n_new > m->cfg.max_seq)
+        return fail(WL_ERR_GGUF_PARSE, "prompt %u + %u new tokens exceed the cache (%u)", n_prompt,
+                    n_new, m->cfg.max_seq);
+    int rc = wl_bitnet_reset(m);
+    if (!rc) rc = wl_bitnet_prefill(m, prompt, n_prompt);
+    if (!rc) rc = wl_bitnet_decode(m, n_new, out_ids, out_hiddens, nullptr);
+    return rc;
 }
 
 }  // extern "C"

@@ -77,3 +77,32 @@ BITNET_2B_LAYER = [
 BITNET_2B_LAYERS = 30
 BITNET_2B_VOCAB = 128256
 BITNET_2B_EMBD = 2560
+
+
+def bitnet_model(rng: np.random.Generator, n_layers: int = 30, n_embd: int = 2560,
+                 n_heads: int = 20, n_kv_heads: int = 5, head_dim: int = 128, n_ff: int = 6912,
+                 vocab: int = 128256, max_seq: int = 1024, eps: float = 1e-5,
+                 freq_base: float = 500000.0) -> dict:
+    """A random BitNet-b1.58-shaped model (BASELINE config 2 distributions):
+    every linear I2_S with P(0)=0.5 and a U[0.01, 0.1] scale, norm weights
+    U[0.5, 1.5], tied Q6_K embedding / lm-head (config 4 distributions).
+    Defaults are the 2B shapes."""
+    kv = n_kv_heads * head_dim
+    shapes = [(n_embd, n_embd), (n_embd, kv), (n_embd, kv), (n_embd, n_embd), (n_embd, n_ff),
+              (n_embd, n_ff), (n_ff, n_embd)]
+    w, sc = [], []
+    for _ in range(n_layers):
+        for k, n in shapes:
+            w.append(i2s_packed(rng, k, n))
+            sc.append(i2s_scale(rng))
+    norms = rng.uniform(0.5, 1.5, size=n_layers * (3 * n_embd + n_ff)).astype(np.float32)
+    return {
+        "config": dict(n_layers=n_layers, n_embd=n_embd, n_heads=n_heads, n_kv_heads=n_kv_heads,
+                       head_dim=head_dim, n_ff=n_ff, vocab=vocab, n_rot=head_dim,
+                       max_seq=max_seq, eps=eps, freq_base=freq_base),
+        "w": w,
+        "w_scale": np.asarray(sc, np.float32),
+        "norms": norms,
+        "output_norm": rng.uniform(0.5, 1.5, size=n_embd).astype(np.float32),
+        "token_embd": q6k_rows(rng, n_embd, vocab),
+    }
