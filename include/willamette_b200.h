@@ -292,6 +292,10 @@ int wl_tp_q6k_lm_head_greedy(wl_tp_group *group, const uint8_t *packed_shard, ui
 typedef struct {
     uint32_t n_layers, n_embd, n_heads, n_kv_heads, head_dim, n_ff, vocab, n_rot, max_seq;
     float eps, freq_base;
+    /* 0: sums (RMSNorm, softmax, attention-weighted V) as parallel trees;
+     * 1: every sum in the reference's sequential order (slower).  Either way
+     * the per-element arithmetic is the reference's. */
+    uint32_t exact;
 } wl_bitnet_config;
 
 typedef struct {

@@ -74,7 +74,7 @@ WL_TP_HANDLE_BYTES = 64
 class WlBitnetConfig(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("n_layers", "n_embd", "n_heads", "n_kv_heads",
                                           "head_dim", "n_ff", "vocab", "n_rot", "max_seq")] + \
-               [("eps", C.c_float), ("freq_base", C.c_float)]
+               [("eps", C.c_float), ("freq_base", C.c_float), ("exact", C.c_uint32)]
 
 
 class WlBitnetWeights(C.Structure):

@@ -34,11 +34,11 @@ def _fp(a: Optional[np.ndarray]):
 
 
 class BitNet:
-    def __init__(self, model: dict, device: int = 0):
+    def __init__(self, model: dict, device: int = 0, exact: bool = False):
         L = lib()
         _check(L.wl_init(device))
         c = model["config"]
-        self.cfg = WlBitnetConfig(**{k: c[k] for k in _CFG_KEYS})
+        self.cfg = WlBitnetConfig(**{k: c[k] for k in _CFG_KEYS}, exact=int(exact))
         self.n_embd = c["n_embd"]
         ws = [np.ascontiguousarray(a, np.uint8) for a in model["w"]]
         self._keep = [ws, np.ascontiguousarray(model["w_scale"], np.float32),

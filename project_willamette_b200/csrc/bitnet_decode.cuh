@@ -105,16 +105,28 @@ struct OutNormParams {
     uint32_t n;
     float eps;
     uint32_t *pos;
+    uint32_t exact;  // sequential sum of squares (the reference's order)
 };
 
 __global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ OutNormParams p) {
     __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
-    float ss = 0.0f;
-    for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
-        ss = __fadd_rn(ss, __fmul_rn(p.hidden[i], p.hidden[i]));
-    const float sum_sq = block_sum(ss, red);
+    float sum_sq;
+    if (p.exact) {
+        if (threadIdx.x == 0) {
+            float t = 0.0f;
+            for (uint32_t i = 0; i < p.n; ++i) t = __fadd_rn(t, __fmul_rn(p.hidden[i], p.hidden[i]));
+            red[0] = t;
+        }
+        __syncthreads();
+        sum_sq = red[0];
+    } else {
+        float ss = 0.0f;
+        for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
+            ss = __fadd_rn(ss, __fmul_rn(p.hidden[i], p.hidden[i]));
+        sum_sq = block_sum(ss, red);
+    }
     const float mean = __fdiv_rn(sum_sq, (float)p.n);
     const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
     for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
@@ -124,14 +136,19 @@ __global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ O
 }
 
 // ---------------------------------------------------------------------------
-// Attention for one decode position: one CTA per query head.
-//  1. NEOX RoPE on every K head (all CTAs, redundantly) and on this CTA's Q
+// Attention for one decode position, split over positions (grid: heads x
+// splits; the last CTA of a head combines the splits).
+//  1. NEOX RoPE on every K head (every CTA, redundantly) and on this CTA's Q
 //     head, from the host-filled (cos, sin) table.
 //  2. Per-token absmax i8 quantisation of K and V (kv_cache.rs:245-259);
-//     CTA 0 appends them to the cache, every CTA keeps its own copy for the
-//     current position (no cross-CTA dependency inside the kernel).
-//  3. scores[p] = (q . k_p) * scale over the cache (k_p = (f32)q8 * s_p),
-//     softmax (attention.rs:45-73), out = sum_p w_p * v_p.
+//     CTA (0, 0) appends them to the cache, every CTA keeps its own copy for
+//     the current position (no cross-CTA dependency on the new entry).
+//  3. scores[t] = (q . k_t) * scale, k_t = (f32)k8 * s_t, one thread per
+//     position summing over the head in the reference's order (bit-exact
+//     scores); per split: local max m, e = exp(s - m), l = sum e,
+//     o = sum e * v_t.  Combine: M = max m, w = e * exp(m - M) / sum(l *
+//     exp(m - M)) -- the reference's softmax (attention.rs:45-73) up to
+//     rounding; a non-finite maximum gives zeros, as there.
 struct AttnParams {
     const float *q, *k, *v;  // this step's projections: E, KV, KV
     float *att;              // E
@@ -139,9 +156,12 @@ struct AttnParams {
     float *k_scale, *v_scale;   // this layer: [max_seq]
     const float2 *rope;         // [max_seq][n_rot / 2] (cos, sin)
     const uint32_t *pos;
-    uint32_t n_kv_heads, head_dim, n_rot, max_seq, group;
+    uint32_t n_kv_heads, head_dim, n_rot, max_seq, group, splits;
     float scale;
+    float *partial;             // [n_heads][splits][2 + head_dim]
+    uint32_t *counters;         // [n_heads], zero between launches
     uint32_t *status;
+    uint32_t exact;             // splits == 1: softmax and V sums in the reference's order
 };
 
 __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, int8_t *q,
@@ -162,18 +182,25 @@ __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, in
     if (threadIdx.x == 0) *scale_out = zero ? 0.0f : __fdiv_rn(absmax, 127.0f);
 }
 
+__device__ __forceinline__ float exp_f32(float x) {
+    return (float)exp((double)x);  // exp rounded once to f32
+}
+
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_constant__ AttnParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[32];
     __shared__ float s_ks, s_vs;
+    __shared__ uint32_t s_last;
     const uint32_t HD = p.head_dim, KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
-    const uint32_t h = blockIdx.x, kvh = h / p.group, tid = threadIdx.x;
+    const uint32_t h = blockIdx.x, sp = blockIdx.y, kvh = h / p.group, tid = threadIdx.x;
+    // scores rounded to 4 floats so the int8 rows after them stay 16-byte aligned
+    const uint32_t chunk_max = ((p.max_seq + p.splits - 1) / p.splits + 3u) & ~3u;
     float *ks = reinterpret_cast<float *>(smem);  // KV: rotated k
     float *vs = ks + KV;                          // KV: v
     float *qh = vs + KV;                          // HD: rotated q of this head
     float *obuf = qh + HD;                        // ATTN_THREADS: partial outputs
-    float *scores = obuf + ATTN_THREADS;          // max_seq
-    int8_t *kq = reinterpret_cast<int8_t *>(scores + p.max_seq);  // KV
+    float *scores = obuf + ATTN_THREADS;          // chunk_max
+    int8_t *kq = reinterpret_cast<int8_t *>(scores + chunk_max);  // KV
     int8_t *vq = kq + KV;                                          // KV
 
     pdl_launch_dependents();
@@ -206,7 +233,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     kv_quantise_block(ks, KV, kq, &s_ks, red);
     kv_quantise_block(vs, KV, vq, &s_vs, red);
     __syncthreads();
-    if (h == 0) {
+    if (h == 0 && sp == 0) {
         for (uint32_t i = tid; i < KV; i += blockDim.x) {
             p.k_cache[(size_t)pos * KV + i] = kq[i];
             p.v_cache[(size_t)pos * KV + i] = vq[i];
@@ -216,66 +243,135 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
             p.v_scale[pos] = s_vs;
         }
     }
-
-    // scores: warp per position, HD/32 consecutive dims per lane
-    const uint32_t warp = tid >> 5, lane = tid & 31u, nwarps = blockDim.x >> 5;
-    const uint32_t per = HD / 32u;
-    float qreg[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qreg[e] = (uint32_t)e < per ? qh[lane * per + e] : 0.0f;
-    for (uint32_t t = warp; t <= pos; t += nwarps) {
+    // this split's positions [t0, t1)
+    const uint32_t n = pos + 1u, chunk = (n + p.splits - 1u) / p.splits;
+    const uint32_t t0 = min(n, sp * chunk), t1 = min(n, t0 + chunk), cnt = t1 - t0;
+    for (uint32_t i = tid; i < cnt; i += blockDim.x) {
+        const uint32_t t = t0 + i;
         const int8_t *kr = t == pos ? kq + kvh * HD : p.k_cache + (size_t)t * KV + kvh * HD;
         const float sk = t == pos ? s_ks : p.k_scale[t];
         float d = 0.0f;
+        for (uint32_t c = 0; c < HD; c += 16u) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(kr + c);
+            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-            if ((uint32_t)e < per)
-                d = __fadd_rn(d, __fmul_rn(qreg[e], __fmul_rn((float)kr[lane * per + e], sk)));
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, off));
-        if (lane == 0) scores[t] = __fmul_rn(d, p.scale);
+            for (int e = 0; e < 16; ++e) {
+                const float kv8 = (float)(int8_t)(wv[e >> 2] >> (8 * (e & 3)));
+                d = __fadd_rn(d, __fmul_rn(qh[c + e], __fmul_rn(kv8, sk)));
+            }
+        }
+        scores[i] = __fmul_rn(d, p.scale);
     }
     __syncthreads();
+    if (p.exact) {
+        // softmax_inplace (attention.rs:45-73) and out_h[d] += w * v_h[d]
+        // (cached_forward.rs:441-449) in the reference's sequential order.
+        __shared__ float s_inv, s_max;
+        __shared__ uint32_t s_norm;
+        if (tid == 0) {
+            float mxs = -INFINITY;
+            for (uint32_t i = 0; i < cnt; ++i)
+                if (scores[i] > mxs) mxs = scores[i];
+            s_max = mxs;
+        }
+        __syncthreads();
+        const float mxs = s_max;
+        if (!isfinite(mxs)) {
+            for (uint32_t i = tid; i < cnt; i += blockDim.x) scores[i] = 0.0f;
+        } else {
+            for (uint32_t i = tid; i < cnt; i += blockDim.x)
+                scores[i] = exp_f32(__fsub_rn(scores[i], mxs));
+            __syncthreads();
+            if (tid == 0) {
+                float sum = 0.0f;
+                for (uint32_t i = 0; i < cnt; ++i) sum = __fadd_rn(sum, scores[i]);
+                s_norm = sum > 0.0f ? 1u : 0u;
+                s_inv = s_norm ? __fdiv_rn(1.0f, sum) : 1.0f;
+            }
+            __syncthreads();
+            if (s_norm)
+                for (uint32_t i = tid; i < cnt; i += blockDim.x) scores[i] = __fmul_rn(scores[i], s_inv);
+        }
+        __syncthreads();
+        if (tid < HD) {
+            float o = 0.0f;
+            for (uint32_t i = 0; i < cnt; ++i) {
+                const uint32_t t = t0 + i;
+                const int8_t vv = t == pos ? vq[kvh * HD + tid] : p.v_cache[(size_t)t * KV + kvh * HD + tid];
+                const float sv = t == pos ? s_vs : p.v_scale[t];
+                o = __fadd_rn(o, __fmul_rn(scores[i], __fmul_rn((float)vv, sv)));
+            }
+            p.att[h * HD + tid] = o;
+        }
+        return;
+    }
     float m = -INFINITY;
-    for (uint32_t t = tid; t <= pos; t += blockDim.x) m = fmaxf(m, scores[t]);
+    for (uint32_t i = tid; i < cnt; i += blockDim.x) m = fmaxf(m, scores[i]);
     const float mx = block_max(m, red);
-    if (!isfinite(mx)) {  // all -inf, or NaN / +inf present: zeros
-        for (uint32_t t = tid; t <= pos; t += blockDim.x) scores[t] = 0.0f;
-    } else {
-        float sum = 0.0f;
-        for (uint32_t t = tid; t <= pos; t += blockDim.x) {
-            const float e = (float)exp((double)__fsub_rn(scores[t], mx));
-            scores[t] = e;
-            sum = __fadd_rn(sum, e);
-        }
-        const float total = block_sum(sum, red);
-        if (total > 0.0f) {
-            const float inv = __fdiv_rn(1.0f, total);
-            for (uint32_t t = tid; t <= pos; t += blockDim.x) scores[t] = __fmul_rn(scores[t], inv);
+    float lsum = 0.0f;
+    const bool finite = isfinite(mx);
+    if (finite) {
+        for (uint32_t i = tid; i < cnt; i += blockDim.x) {
+            const float e = exp_f32(__fsub_rn(scores[i], mx));
+            scores[i] = e;
+            lsum = __fadd_rn(lsum, e);
         }
     }
+    const float l = block_sum(lsum, red);
     __syncthreads();
-    // out[d] = sum_p w_p * ((f32)v8[p][d] * s_p): groups of HD threads split p
     const uint32_t groups = blockDim.x / HD, d = tid % HD, g = tid / HD;
     float acc = 0.0f;
-    if (g < groups) {
-        for (uint32_t t = g; t <= pos; t += groups) {
+    if (finite && g < groups) {
+        for (uint32_t i = g; i < cnt; i += groups) {
+            const uint32_t t = t0 + i;
             const int8_t vv = t == pos ? vq[kvh * HD + d] : p.v_cache[(size_t)t * KV + kvh * HD + d];
             const float sv = t == pos ? s_vs : p.v_scale[t];
-            acc = __fadd_rn(acc, __fmul_rn(scores[t], __fmul_rn((float)vv, sv)));
+            acc = __fadd_rn(acc, __fmul_rn(scores[i], __fmul_rn((float)vv, sv)));
         }
     }
     obuf[tid] = acc;
     __syncthreads();
+    float *part = p.partial + ((size_t)h * p.splits + sp) * (2u + HD);
     if (tid < HD) {
         float o = obuf[tid];
         for (uint32_t gg = 1; gg < groups; ++gg) o = __fadd_rn(o, obuf[gg * HD + tid]);
-        p.att[h * HD + tid] = o;
+        part[2 + tid] = o;
     }
+    if (tid == 0) {
+        part[0] = mx;
+        part[1] = l;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(p.counters + h, 1u) == p.splits - 1u ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float *base = p.partial + (size_t)h * p.splits * (2u + HD);
+    float M = -INFINITY;
+    for (uint32_t s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, __ldcg(base + s2 * (2u + HD)));
+    if (tid < HD) {
+        float out = 0.0f;
+        if (isfinite(M)) {
+            float L = 0.0f, O = 0.0f;
+            for (uint32_t s2 = 0; s2 < p.splits; ++s2) {
+                const float *ps = base + s2 * (2u + HD);
+                const float ms = __ldcg(ps);
+                if (!(ms > -INFINITY)) continue;  // empty split
+                const float f = exp_f32(__fsub_rn(ms, M));
+                L = __fadd_rn(L, __fmul_rn(__ldcg(ps + 1), f));
+                O = __fadd_rn(O, __fmul_rn(__ldcg(ps + 2 + tid), f));
+            }
+            out = L > 0.0f ? __fmul_rn(O, __fdiv_rn(1.0f, L)) : O;
+        }
+        p.att[h * HD + tid] = out;
+    }
+    if (tid == 0) p.counters[h] = 0u;  // re-arm for the next launch
 }
 
-inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq) {
-    return (size_t)(2 * kv + hd + ATTN_THREADS + max_seq) * 4u + 2u * kv + 16u;
+inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq, uint32_t splits) {
+    const uint32_t chunk = ((max_seq + splits - 1) / splits + 3u) & ~3u;
+    return (size_t)(2 * kv + hd + ATTN_THREADS + chunk) * 4u + 2u * kv + 16u;
 }
 
 }  // namespace wl

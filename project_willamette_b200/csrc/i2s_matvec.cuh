@@ -73,6 +73,7 @@ struct I2sMatvecParams {
     float eps;
     uint32_t residual;      // y[r] = y[r] + out (reference residual add)
     uint32_t finite_flag;   // status bit set when a residual sum is not finite
+    uint32_t exact_norm;    // sum of squares in the reference's sequential order
 };
 
 constexpr uint32_t I2S_PRE_NONE = 0, I2S_PRE_RMSNORM = 1, I2S_PRE_RELU2_RMSNORM = 2;
@@ -295,12 +296,26 @@ __device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t
         ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
                                      __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
     }
+    float sum_sq;
+    if (p.exact_norm) {
+        // the reference's loop: sum_sq += x[i] * x[i], i = 0, 1, ... (one thread)
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.0f;
+            for (uint32_t i = 0; i < K; ++i) t = __fadd_rn(t, __fmul_rn(xs[i], xs[i]));
+            red[0] = t;
+        }
+        __syncthreads();
+        sum_sq = red[0];
+    } else {
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    float sum_sq = red[0];
-    for (uint32_t w = 1; w < nthr / 32; ++w) sum_sq = __fadd_rn(sum_sq, red[w]);
+        for (int off = 16; off > 0; off >>= 1)
+            ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        sum_sq = red[0];
+        for (uint32_t w = 1; w < nthr / 32; ++w) sum_sq = __fadd_rn(sum_sq, red[w]);
+    }
     const float mean = __fdiv_rn(sum_sq, (float)K);
     const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
     for (uint32_t i = tid * 4; i < K; i += nthr * 4) {

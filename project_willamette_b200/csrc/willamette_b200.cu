@@ -266,7 +266,7 @@ struct I2sLaunch {
     uint32_t pre = I2S_PRE_NONE;
     const float *norm_w = nullptr, *x2 = nullptr;
     float eps = 0.0f;
-    uint32_t residual = 0, finite_flag = 0;
+    uint32_t residual = 0, finite_flag = 0, exact_norm = 0;
 };
 
 bool weights_may_have_code3(const wl_i2s_dev_weight *w, uint32_t nw) {
@@ -306,6 +306,7 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     p.eps = L.eps;
     p.residual = L.residual;
     p.finite_flag = L.finite_flag;
+    p.exact_norm = L.exact_norm;
     const bool fuse = L.x != nullptr;
     int lpr = 32;
     const int shape = i2s_shape_index(K, &lpr);
@@ -1115,6 +1116,9 @@ struct wl_bitnet {
           *gate = nullptr, *up = nullptr, *final_h = nullptr;
     uint32_t *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_ids = nullptr;
     uint32_t ids_cap = 0;
+    uint32_t splits = 1;                   // attention CTAs per head
+    float *attn_partial = nullptr;
+    uint32_t *attn_counters = nullptr;
     void *lm_scratch = nullptr;
     uint32_t *h_pinned = nullptr;          // token staging
     uint32_t pos = 0;                      // host mirror of the cache position
@@ -1148,7 +1152,7 @@ int bn_validate(const wl_bitnet_config *c) {
                     "multiple of 128", HD);
     if (!c->n_rot || c->n_rot % 2 || c->n_rot > HD)
         return fail(WL_ERR_GGUF_PARSE, "rope_dimension_count %u", c->n_rot);
-    if (attn_smem_bytes(bn_kv(*c), HD, c->max_seq) > (size_t)WL_MAX_DYN_SMEM)
+    if (attn_smem_bytes(bn_kv(*c), HD, c->max_seq, 1) > (size_t)WL_MAX_DYN_SMEM)
         return fail(WL_ERR_INVALID_ARGUMENT, "max_seq %u too long for the attention kernel",
                     c->max_seq);
     if (!std::isfinite(c->eps) || !std::isfinite(c->freq_base))
@@ -1192,6 +1196,7 @@ int bn_matvec(wl_bitnet *m, uint32_t l, int first, int count, uint32_t K, const 
     L.eps = m->cfg.eps;
     L.residual = residual;
     L.finite_flag = finite_flag;
+    L.exact_norm = m->cfg.exact;
     return launch_i2s(L, s, true);
 }
 
@@ -1211,7 +1216,7 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
     ep.ids = commit ? m->d_ids : nullptr;
     ep.step = m->d_step;
     WL_CUDA(launch(embed_q6k_kernel, dim3(nb), dim3(256), 0, s, true, ep));
-    const size_t attn_smem = attn_smem_bytes(KV, c.head_dim, c.max_seq);
+    const size_t attn_smem = attn_smem_bytes(KV, c.head_dim, c.max_seq, m->splits);
     const float scale = 1.0f / sqrtf((float)c.head_dim);  // attention_scale, primitives.rs:354
     int rc;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
@@ -1236,9 +1241,13 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
         ap.max_seq = c.max_seq;
         ap.group = c.n_heads / c.n_kv_heads;
         ap.scale = scale;
+        ap.splits = m->splits;
+        ap.partial = m->attn_partial;
+        ap.counters = m->attn_counters;
         ap.status = status;
-        WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads), dim3(ATTN_THREADS), attn_smem, s, true,
-                       ap));
+        ap.exact = c.exact;
+        WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits), dim3(ATTN_THREADS),
+                       attn_smem, s, true, ap));
         float *o[1] = {m->hidden};
         if ((rc = bn_matvec(m, l, 3, 1, E, m->att, o, I2S_PRE_RMSNORM, nrm + E, nullptr, 1, 0, s)))
             return rc;
@@ -1257,6 +1266,7 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
     op.n = E;
     op.eps = c.eps;
     op.pos = m->d_pos;
+    op.exact = c.exact;
     WL_CUDA(launch(out_norm_kernel, dim3(1), dim3(256), 0, s, true, op));
     return WL_OK;
 }
@@ -1992,6 +2002,14 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
     BN_ALLOC(m->d_step, 16);
     BN_ALLOC(m->d_ids, (size_t)m->ids_cap * 4);
     BN_ALLOC(m->lm_scratch, 256);
+    // attention splits: about 2 CTAs per SM over all heads, at least 32
+    // positions per split
+    m->splits = c.exact ? 1u
+                        : std::max<uint32_t>(1u, std::min<uint32_t>((c.max_seq + 31) / 32,
+                                                                    (uint32_t)(2 * cx.sm_count) /
+                                                                        c.n_heads));
+    BN_ALLOC(m->attn_partial, (size_t)c.n_heads * m->splits * (2 + c.head_dim) * 4);
+    BN_ALLOC(m->attn_counters, (size_t)c.n_heads * 4);
 #undef BN_ALLOC
     if (cudaMallocHost(&p, 64) != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "pinned"));
     m->h_pinned = (uint32_t *)p;
@@ -2039,6 +2057,7 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
         e = cudaMemcpyAsync(m->rope, rope.data(), rope.size() * sizeof(float2),
                             cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(m->lm_scratch, 0, 256, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->attn_counters, 0, (size_t)c.n_heads * 4, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(m->d_pos, 0, 16, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(m->d_step, 0, 16, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
@@ -2056,7 +2075,8 @@ int wl_bitnet_destroy(wl_bitnet *m) {
     if (m->g_last) cudaGraphExecDestroy(m->g_last);
     void *bufs[] = {m->wblock, m->norms, m->out_norm, m->q6k, m->rope, m->kq, m->vq, m->ks,
                     m->vs, m->hidden, m->q, m->k, m->v, m->att, m->gate, m->up, m->final_h,
-                    m->d_token, m->d_pos, m->d_step, m->d_ids, m->lm_scratch};
+                    m->d_token, m->d_pos, m->d_step, m->d_ids, m->lm_scratch,
+                    m->attn_partial, m->attn_counters};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
