@@ -374,6 +374,8 @@ def run_gpu(args) -> None:
     # ---- lm-head (Q6_K 128256 x 2560, batch 1 and 64; vocab-sharded at N > 1)
     lm = lm_head_bench(torch, dev, L, stream, world, rank, tpg, max_over_ranks,
                        reps=max(20, min(args.steps, 200)))
+    # ---- BitNet-2B greedy decode (config 2, single GPU)
+    decode = decode_bench() if world == 1 else None
     # ---- prefill GEMM (config 3, single GPU)
     gemm = (gemm_bench(torch, dev, L, stream, np.random.default_rng(SEED + 3))
             if world == 1 else None)
@@ -424,6 +426,7 @@ def run_gpu(args) -> None:
                     "api": e2e["api"]},
             "gpu_launches": launches_per_step * args.steps,
             "lm_head": lm,
+            "decode": decode,
             "prefill_gemm": gemm,
             "clocks": clk.summary(),
         }
@@ -513,6 +516,53 @@ def lm_head_bench(torch, dev, L, stream, world, rank, tpg, max_over_ranks, reps:
                 "gbs": round(out["algorithmic_bytes"] / (us * 1e-6) / 1e9, 1),
                 "batch64_us_per_call": round(us64, 1),
                 "batch64_gflops": round(2 * 64 * D_MODEL * VOCAB / (us64 * 1e-6) / 1e9, 1)})
+    return out
+
+
+def decode_bench(reps: int = 3) -> dict:
+    """BitNet-2B-shaped greedy decode on the device-resident
+    decode step -- KV cache prefilled to 512 positions (the reference's prompt
+    loop, one forward per token), then 128 greedy tokens, device time of the
+    128-token loop (CUDA events), median of `reps` runs.  Fast mode (parallel
+    sums) is the timed one; exact mode (the reference's sequential sums,
+    bit-identical hidden states) is timed once beside it."""
+    from project_willamette_b200 import synth
+    from project_willamette_b200.bitnet import BitNet
+    n_prompt, n_new = 512, 128
+    m = synth.bitnet_model(np.random.default_rng(SEED + 7), max_seq=n_prompt + n_new)
+    rng = np.random.default_rng(SEED + 8)
+    prompts = [rng.integers(0, VOCAB, n_prompt) for _ in range(reps)]
+    c = m["config"]
+    kv = c["n_kv_heads"] * c["head_dim"]
+    # bytes one decode step must read: every I2_S weight, the Q6_K lm-head, the
+    # i8 KV cache of the average context (+ its scales), norm weights
+    i2s = LAYERS * sum(k // 4 * n for k, ns in GROUPS for n in ns)
+    avg_ctx = n_prompt + (n_new - 1) / 2.0
+    kv_bytes = LAYERS * 2 * avg_ctx * (kv + 4)
+    norms = 4 * (m["norms"].size + m["output_norm"].size)
+    step_bytes = i2s + 269337600 + kv_bytes + norms
+    out = {"config": "bitnet2b: 30 layers, d 2560, 20/5 heads x 128, d_ff 6912, vocab 128256 "
+                     "(Q6_K tied), KV i8 per-token absmax (the reference's layout)",
+           "prompt": n_prompt, "new_tokens": n_new}
+    for exact in (False, True):
+        g = BitNet(m, exact=exact)
+        times, walls = [], []
+        for r in range(reps if not exact else 1):
+            g.reset()
+            g.prefill(prompts[r])
+            t0 = time.perf_counter()
+            ids, ms = g.decode(n_new, timed=True)
+            walls.append(time.perf_counter() - t0)
+            times.append(ms)
+        g.close()
+        ms = statistics.median(times)
+        key = "exact" if exact else "fast"
+        out[key] = {"tok_s": round(n_new / (ms * 1e-3), 1), "ms_per_token": round(ms / n_new, 4),
+                    "e2e_tok_s": round(n_new / statistics.median(walls), 1)}
+        if not exact:
+            gbs = step_bytes / (ms / n_new * 1e-3) / 1e9
+            out[key].update({"bytes_per_token": int(step_bytes), "gbs": round(gbs, 1),
+                             "hbm_frac": round(gbs / peaks()["hbm_gbs"], 4)})
     return out
 
 

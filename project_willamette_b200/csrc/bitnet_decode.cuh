@@ -193,15 +193,18 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     __shared__ uint32_t s_last;
     const uint32_t HD = p.head_dim, KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
     const uint32_t h = blockIdx.x, sp = blockIdx.y, kvh = h / p.group, tid = threadIdx.x;
-    // scores rounded to 4 floats so the int8 rows after them stay 16-byte aligned
+    // float regions rounded to 4 floats so the int8 rows after them stay 16-byte aligned
     const uint32_t chunk_max = ((p.max_seq + p.splits - 1) / p.splits + 3u) & ~3u;
     float *ks = reinterpret_cast<float *>(smem);  // KV: rotated k
     float *vs = ks + KV;                          // KV: v
     float *qh = vs + KV;                          // HD: rotated q of this head
     float *obuf = qh + HD;                        // ATTN_THREADS: partial outputs
     float *scores = obuf + ATTN_THREADS;          // chunk_max
-    int8_t *kq = reinterpret_cast<int8_t *>(scores + chunk_max);  // KV
-    int8_t *vq = kq + KV;                                          // KV
+    float *vsc = scores + chunk_max;              // chunk_max: V scales of the split
+    float2 *rope = reinterpret_cast<float2 *>(vsc + chunk_max);  // half (rounded to 2)
+    float *comb = reinterpret_cast<float *>(rope + ((half + 1u) & ~1u));  // splits*(2+HD)
+    int8_t *kq = reinterpret_cast<int8_t *>(comb + ((p.splits * (2u + HD) + 3u) & ~3u));  // KV
+    int8_t *vq = kq + KV;                                                                 // KV
 
     pdl_launch_dependents();
     pdl_wait();
@@ -210,22 +213,24 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
         if (tid == 0) atomicOr(p.status, WL_DEV_ERR_POSITION);
         return;
     }
+    // one round of independent loads: k, v, this head's q, the RoPE row
+    const float2 *cs = p.rope + (size_t)pos * half;
     for (uint32_t i = tid; i < KV; i += blockDim.x) {
         ks[i] = p.k[i];
         vs[i] = p.v[i];
     }
     for (uint32_t i = tid; i < HD; i += blockDim.x) qh[i] = p.q[h * HD + i];
+    for (uint32_t j = tid; j < half; j += blockDim.x) rope[j] = cs[j];
     __syncthreads();
-    const float2 *cs = p.rope + (size_t)pos * half;
     for (uint32_t i = tid; i < p.n_kv_heads * half; i += blockDim.x) {
         const uint32_t hk = i / half, j = i % half;
         float *x = ks + hk * HD;
-        const float a = x[j], b = x[j + half], c = cs[j].x, s = cs[j].y;
+        const float a = x[j], b = x[j + half], c = rope[j].x, s = rope[j].y;
         x[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
         x[j + half] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
     }
     for (uint32_t j = tid; j < half; j += blockDim.x) {
-        const float a = qh[j], b = qh[j + half], c = cs[j].x, s = cs[j].y;
+        const float a = qh[j], b = qh[j + half], c = rope[j].x, s = rope[j].y;
         qh[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
         qh[j + half] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
     }
@@ -246,18 +251,26 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     // this split's positions [t0, t1)
     const uint32_t n = pos + 1u, chunk = (n + p.splits - 1u) / p.splits;
     const uint32_t t0 = min(n, sp * chunk), t1 = min(n, t0 + chunk), cnt = t1 - t0;
+    // scores: one thread per position, the head's row loaded whole first
+    // (one memory round trip), then summed in the reference's order
     for (uint32_t i = tid; i < cnt; i += blockDim.x) {
         const uint32_t t = t0 + i;
         const int8_t *kr = t == pos ? kq + kvh * HD : p.k_cache + (size_t)t * KV + kvh * HD;
         const float sk = t == pos ? s_ks : p.k_scale[t];
+        vsc[i] = t == pos ? s_vs : p.v_scale[t];
+        uint4 w[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+            if ((uint32_t)c * 16u < HD) w[c] = *reinterpret_cast<const uint4 *>(kr + c * 16);
         float d = 0.0f;
-        for (uint32_t c = 0; c < HD; c += 16u) {
-            const uint4 w = *reinterpret_cast<const uint4 *>(kr + c);
-            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            if ((uint32_t)c * 16u >= HD) break;
+            const uint32_t wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const float kv8 = (float)(int8_t)(wv[e >> 2] >> (8 * (e & 3)));
-                d = __fadd_rn(d, __fmul_rn(qh[c + e], __fmul_rn(kv8, sk)));
+                d = __fadd_rn(d, __fmul_rn(qh[c * 16 + e], __fmul_rn(kv8, sk)));
             }
         }
         scores[i] = __fmul_rn(d, p.scale);
@@ -298,8 +311,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
             for (uint32_t i = 0; i < cnt; ++i) {
                 const uint32_t t = t0 + i;
                 const int8_t vv = t == pos ? vq[kvh * HD + tid] : p.v_cache[(size_t)t * KV + kvh * HD + tid];
-                const float sv = t == pos ? s_vs : p.v_scale[t];
-                o = __fadd_rn(o, __fmul_rn(scores[i], __fmul_rn((float)vv, sv)));
+                o = __fadd_rn(o, __fmul_rn(scores[i], __fmul_rn((float)vv, vsc[i])));
             }
             p.att[h * HD + tid] = o;
         }
@@ -319,14 +331,25 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     }
     const float l = block_sum(lsum, red);
     __syncthreads();
+    // out[d] = sum_i e_i * ((f32)v8 * s): groups of HD threads split the
+    // positions; 8 independent row loads per round trip
     const uint32_t groups = blockDim.x / HD, d = tid % HD, g = tid / HD;
     float acc = 0.0f;
     if (finite && g < groups) {
-        for (uint32_t i = g; i < cnt; i += groups) {
-            const uint32_t t = t0 + i;
-            const int8_t vv = t == pos ? vq[kvh * HD + d] : p.v_cache[(size_t)t * KV + kvh * HD + d];
-            const float sv = t == pos ? s_vs : p.v_scale[t];
-            acc = __fadd_rn(acc, __fmul_rn(scores[i], __fmul_rn((float)vv, sv)));
+        const int8_t *vbase = p.v_cache + (size_t)kvh * HD + d;
+        for (uint32_t i0 = g; i0 < cnt; i0 += 8u * groups) {
+            int8_t vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t i = i0 + (uint32_t)u * groups;
+                const uint32_t t = t0 + i;
+                vv[u] = i >= cnt ? (int8_t)0 : (t == pos ? vq[kvh * HD + d] : vbase[(size_t)t * KV]);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t i = i0 + (uint32_t)u * groups;
+                if (i < cnt) acc = __fadd_rn(acc, __fmul_rn(scores[i], __fmul_rn((float)vv[u], vsc[i])));
+            }
         }
     }
     obuf[tid] = acc;
@@ -347,20 +370,22 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // last CTA of the head: stage every split's partial, then combine
     const float *base = p.partial + (size_t)h * p.splits * (2u + HD);
+    for (uint32_t i = tid; i < p.splits * (2u + HD); i += blockDim.x) comb[i] = __ldcg(base + i);
+    __syncthreads();
     float M = -INFINITY;
-    for (uint32_t s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, __ldcg(base + s2 * (2u + HD)));
+    for (uint32_t s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, comb[s2 * (2u + HD)]);
     if (tid < HD) {
         float out = 0.0f;
         if (isfinite(M)) {
             float L = 0.0f, O = 0.0f;
             for (uint32_t s2 = 0; s2 < p.splits; ++s2) {
-                const float *ps = base + s2 * (2u + HD);
-                const float ms = __ldcg(ps);
-                if (!(ms > -INFINITY)) continue;  // empty split
-                const float f = exp_f32(__fsub_rn(ms, M));
-                L = __fadd_rn(L, __fmul_rn(__ldcg(ps + 1), f));
-                O = __fadd_rn(O, __fmul_rn(__ldcg(ps + 2 + tid), f));
+                const float *ps = comb + s2 * (2u + HD);
+                if (!(ps[0] > -INFINITY)) continue;  // empty split
+                const float f = exp_f32(__fsub_rn(ps[0], M));
+                L = __fadd_rn(L, __fmul_rn(ps[1], f));
+                O = __fadd_rn(O, __fmul_rn(ps[2 + tid], f));
             }
             out = L > 0.0f ? __fmul_rn(O, __fdiv_rn(1.0f, L)) : O;
         }
@@ -371,7 +396,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
 
 inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq, uint32_t splits) {
     const uint32_t chunk = ((max_seq + splits - 1) / splits + 3u) & ~3u;
-    return (size_t)(2 * kv + hd + ATTN_THREADS + chunk) * 4u + 2u * kv + 16u;
+    const uint32_t half2 = ((hd / 2u + 1u) & ~1u) * 2u;  // float2 RoPE row, in floats
+    const uint32_t comb = (splits * (2u + hd) + 3u) & ~3u;
+    return (size_t)(2 * kv + hd + ATTN_THREADS + 2 * chunk + half2 + comb) * 4u + 2u * kv + 16u;
 }
 
 }  // namespace wl
