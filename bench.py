@@ -519,6 +519,10 @@ def lm_head_bench(torch, dev, L, stream, world, rank, tpg, max_over_ranks, reps:
     return out
 
 
+def key_fast(exact: bool, persistent: bool) -> bool:
+    return not exact and not persistent
+
+
 def decode_bench(reps: int = 3) -> dict:
     """BitNet-2B-shaped greedy decode on the device-resident
     decode step -- KV cache prefilled to 512 positions (the reference's prompt
@@ -544,10 +548,10 @@ def decode_bench(reps: int = 3) -> dict:
     out = {"config": "bitnet2b: 30 layers, d 2560, 20/5 heads x 128, d_ff 6912, vocab 128256 "
                      "(Q6_K tied), KV i8 per-token absmax (the reference's layout)",
            "prompt": n_prompt, "new_tokens": n_new}
-    for exact in (False, True):
-        g = BitNet(m, exact=exact)
+    for exact, persistent in ((False, False), (True, False), (False, True)):
+        g = BitNet(m, exact=exact, persistent=persistent)
         times, walls = [], []
-        for r in range(reps if not exact else 1):
+        for r in range(reps if key_fast(exact, persistent) else 1):
             g.reset()
             g.prefill(prompts[r])
             t0 = time.perf_counter()
@@ -556,10 +560,10 @@ def decode_bench(reps: int = 3) -> dict:
             times.append(ms)
         g.close()
         ms = statistics.median(times)
-        key = "exact" if exact else "fast"
+        key = "exact" if exact else ("fast_persistent" if persistent else "fast")
         out[key] = {"tok_s": round(n_new / (ms * 1e-3), 1), "ms_per_token": round(ms / n_new, 4),
                     "e2e_tok_s": round(n_new / statistics.median(walls), 1)}
-        if not exact:
+        if key_fast(exact, persistent):
             gbs = step_bytes / (ms / n_new * 1e-3) / 1e9
             out[key].update({"bytes_per_token": int(step_bytes), "gbs": round(gbs, 1),
                              "hbm_frac": round(gbs / peaks()["hbm_gbs"], 4)})

@@ -296,6 +296,11 @@ typedef struct {
      * 1: every sum in the reference's sequential order (slower).  Either way
      * the per-element arithmetic is the reference's. */
     uint32_t exact;
+    /* 0: one kernel per operation (PDL chain, the faster engine today);
+     * 1: the whole forward as one persistent cooperative kernel (grid
+     * barriers between phases, weights prefetched into shared memory).
+     * Same arithmetic. */
+    uint32_t persistent;
 } wl_bitnet_config;
 
 typedef struct {
@@ -314,6 +319,9 @@ int wl_bitnet_destroy(wl_bitnet *model);
 /* Empty the KV cache (position 0). */
 int wl_bitnet_reset(wl_bitnet *model);
 uint32_t wl_bitnet_position(const wl_bitnet *model);
+/* 1 when the forward runs as the persistent kernel (it needs one CTA's shared
+ * memory on every SM), 0 when it runs per operation. */
+int wl_bitnet_uses_persistent_kernel(const wl_bitnet *model);
 /* forward_with_cache (cached_forward.rs:131-149): position must equal the
  * cache position; out_hidden (host, n_embd, may be NULL) = output_norm(hidden). */
 int wl_bitnet_forward(wl_bitnet *model, uint32_t token, uint32_t position, float *out_hidden);

@@ -74,7 +74,8 @@ WL_TP_HANDLE_BYTES = 64
 class WlBitnetConfig(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("n_layers", "n_embd", "n_heads", "n_kv_heads",
                                           "head_dim", "n_ff", "vocab", "n_rot", "max_seq")] + \
-               [("eps", C.c_float), ("freq_base", C.c_float), ("exact", C.c_uint32)]
+               [("eps", C.c_float), ("freq_base", C.c_float), ("exact", C.c_uint32),
+                ("persistent", C.c_uint32)]
 
 
 class WlBitnetWeights(C.Structure):
@@ -127,6 +128,7 @@ PROTOTYPES = {
     "wl_bitnet_destroy": ([_vp], _i),
     "wl_bitnet_reset": ([_vp], _i),
     "wl_bitnet_position": ([_vp], _u32),
+    "wl_bitnet_uses_persistent_kernel": ([_vp], _i),
     "wl_bitnet_forward": ([_vp, _u32, _u32, _fp], _i),
     "wl_bitnet_prefill": ([_vp, C.POINTER(_u32), _u32], _i),
     "wl_bitnet_decode": ([_vp, _u32, C.POINTER(_u32), _fp, _fp], _i),

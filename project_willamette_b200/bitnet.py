@@ -34,11 +34,13 @@ def _fp(a: Optional[np.ndarray]):
 
 
 class BitNet:
-    def __init__(self, model: dict, device: int = 0, exact: bool = False):
+    def __init__(self, model: dict, device: int = 0, exact: bool = False,
+                 persistent: bool = False):
         L = lib()
         _check(L.wl_init(device))
         c = model["config"]
-        self.cfg = WlBitnetConfig(**{k: c[k] for k in _CFG_KEYS}, exact=int(exact))
+        self.cfg = WlBitnetConfig(**{k: c[k] for k in _CFG_KEYS}, exact=int(exact),
+                                  persistent=int(persistent))
         self.n_embd = c["n_embd"]
         ws = [np.ascontiguousarray(a, np.uint8) for a in model["w"]]
         self._keep = [ws, np.ascontiguousarray(model["w_scale"], np.float32),
@@ -51,6 +53,10 @@ class BitNet:
         self._h = C.c_void_p()
         _check(L.wl_bitnet_create(C.byref(self.cfg), C.byref(w), C.byref(self._h)))
         self._keep = None  # the library holds device copies
+
+    @property
+    def persistent(self) -> bool:
+        return bool(lib().wl_bitnet_uses_persistent_kernel(self._h))
 
     @property
     def position(self) -> int:

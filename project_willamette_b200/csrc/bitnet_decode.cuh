@@ -158,7 +158,7 @@ struct AttnParams {
     const uint32_t *pos;
     uint32_t n_kv_heads, head_dim, n_rot, max_seq, group, splits;
     float scale;
-    float *partial;             // [n_heads][splits][2 + head_dim]
+    float *partial;             // [n_heads][splits][head_dim + 4]: o, max, sum
     uint32_t *counters;         // [n_heads], zero between launches
     uint32_t *status;
     uint32_t exact;             // splits == 1: softmax and V sums in the reference's order
@@ -354,15 +354,15 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     }
     obuf[tid] = acc;
     __syncthreads();
-    float *part = p.partial + ((size_t)h * p.splits + sp) * (2u + HD);
+    float *part = p.partial + ((size_t)h * p.splits + sp) * (HD + 4u);  // o[HD], max, sum
     if (tid < HD) {
         float o = obuf[tid];
         for (uint32_t gg = 1; gg < groups; ++gg) o = __fadd_rn(o, obuf[gg * HD + tid]);
-        part[2 + tid] = o;
+        part[tid] = o;
     }
     if (tid == 0) {
-        part[0] = mx;
-        part[1] = l;
+        part[HD] = mx;
+        part[HD + 1] = l;
     }
     __threadfence();
     __syncthreads();
@@ -370,26 +370,59 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // last CTA of the head: stage every split's partial, then combine
-    const float *base = p.partial + (size_t)h * p.splits * (2u + HD);
-    for (uint32_t i = tid; i < p.splits * (2u + HD); i += blockDim.x) comb[i] = __ldcg(base + i);
-    __syncthreads();
-    float M = -INFINITY;
-    for (uint32_t s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, comb[s2 * (2u + HD)]);
-    if (tid < HD) {
-        float out = 0.0f;
-        if (isfinite(M)) {
-            float L = 0.0f, O = 0.0f;
-            for (uint32_t s2 = 0; s2 < p.splits; ++s2) {
-                const float *ps = comb + s2 * (2u + HD);
-                if (!(ps[0] > -INFINITY)) continue;  // empty split
-                const float f = exp_f32(__fsub_rn(ps[0], M));
-                L = __fadd_rn(L, __fmul_rn(ps[1], f));
-                O = __fadd_rn(O, __fmul_rn(ps[2 + tid], f));
-            }
-            out = L > 0.0f ? __fmul_rn(O, __fdiv_rn(1.0f, L)) : O;
+    // last CTA of the head: warp 0 reduces the splits' maxima and sums and
+    // keeps the factors exp(m - M) in comb; then HD/4 threads combine the o
+    // rows with float4 loads, eight splits per round of loads.
+    const uint32_t S = p.splits, RS = HD + 4u;
+    const float *base = p.partial + (size_t)h * S * RS;
+    if (tid < 32) {
+        float M = -INFINITY;
+        for (uint32_t s2 = tid; s2 < S; s2 += 32u) M = fmaxf(M, __ldcg(base + s2 * RS + HD));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        const bool fin = isfinite(M);
+        float L = 0.0f;
+        for (uint32_t s2 = tid; s2 < S; s2 += 32u) {
+            const float ms = __ldcg(base + s2 * RS + HD), ls = __ldcg(base + s2 * RS + HD + 1);
+            const float f = (fin && ms > -INFINITY) ? exp_f32(__fsub_rn(ms, M)) : 0.0f;
+            comb[s2] = f;
+            L = __fadd_rn(L, __fmul_rn(ls, f));
         }
-        p.att[h * HD + tid] = out;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) L = __fadd_rn(L, __shfl_xor_sync(0xffffffffu, L, off));
+        if (tid == 0) {
+            red[0] = !fin ? 2.0f : (L > 0.0f ? 1.0f : 0.0f);
+            red[1] = L > 0.0f ? __fdiv_rn(1.0f, L) : 1.0f;
+        }
+    }
+    __syncthreads();
+    const float mode = red[0], inv = red[1];
+    for (uint32_t c = tid; c < HD / 4u; c += blockDim.x) {
+        float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (uint32_t s0 = 0; s0 < S; s0 += 8u) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (s0 + u < S) v[u] = __ldcg(reinterpret_cast<const float4 *>(base + (s0 + u) * RS) + c);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (s0 + u < S) {
+                    const float f = comb[s0 + u];
+                    O.x = __fadd_rn(O.x, __fmul_rn(v[u].x, f));
+                    O.y = __fadd_rn(O.y, __fmul_rn(v[u].y, f));
+                    O.z = __fadd_rn(O.z, __fmul_rn(v[u].z, f));
+                    O.w = __fadd_rn(O.w, __fmul_rn(v[u].w, f));
+                }
+        }
+        if (mode == 2.0f) {
+            O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        } else if (mode == 1.0f) {
+            O.x = __fmul_rn(O.x, inv);
+            O.y = __fmul_rn(O.y, inv);
+            O.z = __fmul_rn(O.z, inv);
+            O.w = __fmul_rn(O.w, inv);
+        }
+        reinterpret_cast<float4 *>(p.att + h * HD)[c] = O;
     }
     if (tid == 0) p.counters[h] = 0u;  // re-arm for the next launch
 }

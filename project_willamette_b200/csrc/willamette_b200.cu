@@ -19,6 +19,7 @@
 #include "../../include/willamette_b200.h"
 #include "argmax.cuh"
 #include "bitnet_decode.cuh"
+#include "bitnet_mega.cuh"
 #include "i2s_matvec.cuh"
 #include "i2s_stream.cuh"
 #include "i2s_gemm.cuh"
@@ -128,7 +129,9 @@ int configure_kernels() {
                             (const void *)i2s_gemm_kernel<256>,
                             (const void *)kStream[0], (const void *)kStream[1],
                             (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<4>,
-                            (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel};
+                            (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel,
+                            (const void *)bitnet_mega_kernel<false>,
+                            (const void *)bitnet_mega_kernel<true>};
     for (const void *k : others)
         WL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      WL_MAX_DYN_SMEM));
@@ -1116,9 +1119,17 @@ struct wl_bitnet {
           *gate = nullptr, *up = nullptr, *final_h = nullptr;
     uint32_t *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_ids = nullptr;
     uint32_t ids_cap = 0;
-    uint32_t splits = 1;                   // attention CTAs per head
+    uint32_t splits = 1;                   // attention CTAs per head (per-op path)
     float *attn_partial = nullptr;
     uint32_t *attn_counters = nullptr;
+    // persistent whole-forward kernel
+    bool mega = false, mega_c3 = false;
+    uint32_t mega_grid = 0, mega_splits = 1;
+    size_t mega_smem = 0;
+    MegaParams mp{};
+    MegaLayer *d_layers = nullptr;
+    void *mega_state = nullptr;             // arrivals (u64), launches, abort
+    float *att_g = nullptr;                 // exact-mode attention output
     void *lm_scratch = nullptr;
     uint32_t *h_pinned = nullptr;          // token staging
     uint32_t pos = 0;                      // host mirror of the cache position
@@ -1202,7 +1213,116 @@ int bn_matvec(wl_bitnet *m, uint32_t l, int first, int count, uint32_t K, const 
 
 // One token: embedding (of *d_token; appended to d_ids when commit), every
 // layer, output norm; the device position advances by one.
+// Shared-memory layout and parameters of the persistent kernel; it runs when
+// one CTA fits on every SM (cooperative launch), else the per-op kernels do.
+int bn_setup_mega(wl_bitnet *m) {
+    const wl_bitnet_config &c = m->cfg;
+    const uint32_t E = c.n_embd, F = c.n_ff, KV = bn_kv(c), HD = c.head_dim, G = m->mega_grid;
+    auto up = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
+    const size_t rpc_qkv = (E + 2 * KV + G - 1) / G, rpc_gu = (2 * F + G - 1) / G,
+                 rpc_e = (E + G - 1) / G;
+    const size_t size_a = up(std::max(rpc_qkv, rpc_gu) * (E / 4), 1024);
+    const size_t size_b = up(rpc_e * std::max(E / 4, F / 4), 1024);
+    const size_t xq = up((size_t)std::max(E, F) * 4, 16) + up(std::max(E, F), 16);
+    const uint32_t S = m->mega_splits, half = c.n_rot / 2;
+    const size_t chunk = ((c.max_seq + S - 1) / S + 3) & ~3u;
+    const size_t attn = (2 * KV + HD + MEGA_THREADS + 2 * chunk) * 4 + ((half + 1) & ~1u) * 8 +
+                        2 * KV;
+    const size_t region = up(std::max(xq, attn), 16);
+    const size_t cmb = up(mega_cmb_floats(c.n_heads, S) * 4, 16);
+    MegaParams &p = m->mp;
+    p.buf_a = 0;
+    p.norm_a = (uint32_t)size_a;
+    p.buf_b = p.norm_a + (uint32_t)up((size_t)E * 4, 128);
+    p.norm_b = p.buf_b + (uint32_t)size_b;
+    p.xs_off = p.norm_b + (uint32_t)up((size_t)std::max(E, F) * 4, 128);
+    p.qs_off = p.xs_off + (uint32_t)up((size_t)std::max(E, F) * 4, 16);
+    p.att_off = p.xs_off;
+    p.cmb_off = p.xs_off + (uint32_t)region;
+    p.hloc_off = p.cmb_off + (uint32_t)cmb;
+    m->mega_smem = p.hloc_off + up(rpc_e * 4, 16);
+    if (m->mega_smem > (size_t)WL_MAX_DYN_SMEM) return WL_OK;  // per-op kernels
+    bool c3 = false;
+    for (auto &w : m->mats) c3 |= !(w.flags & WL_I2S_NO_CODE3);
+    const void *k = c3 ? (const void *)bitnet_mega_kernel<true> : (const void *)bitnet_mega_kernel<false>;
+    int per_sm = 0;
+    WL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, MEGA_THREADS, m->mega_smem));
+    if (per_sm < 1) return WL_OK;
+    std::vector<MegaLayer> hl(c.n_layers);
+    for (uint32_t l = 0; l < c.n_layers; ++l) {
+        for (int j = 0; j < BN_MATS; ++j) {
+            hl[l].w[j] = m->mats[(size_t)l * BN_MATS + j].packed;
+            hl[l].scale[j] = m->mats[(size_t)l * BN_MATS + j].w_scale;
+        }
+        hl[l].norm = m->norms + (size_t)l * (3 * E + F);
+    }
+    WL_CUDA(cudaMalloc(&m->d_layers, hl.size() * sizeof(MegaLayer)));
+    WL_CUDA(cudaMemcpy(m->d_layers, hl.data(), hl.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
+    WL_CUDA(cudaMemset(m->mega_state, 0, 64));
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    p.layers = m->d_layers;
+    p.n_layers = c.n_layers;
+    p.E = E;
+    p.F = F;
+    p.KV = KV;
+    p.HD = HD;
+    p.n_heads = c.n_heads;
+    p.group = c.n_heads / c.n_kv_heads;
+    p.n_rot = c.n_rot;
+    p.max_seq = c.max_seq;
+    p.splits = S;
+    p.eps = c.eps;
+    p.scale = 1.0f / sqrtf((float)HD);  // attention_scale, primitives.rs:354
+    p.exact = c.exact;
+    p.q6k = m->q6k;
+    p.nb = E / 256u;
+    p.q6k_stride = q6k_row_stride(E / 256u);
+    p.token = m->d_token;
+    p.ids = nullptr;
+    p.step = m->d_step;
+    p.hidden = m->hidden;
+    p.qkv = m->q;
+    p.gu = m->gate;
+    p.att = m->att_g;
+    p.final_h = m->final_h;
+    p.partial = m->attn_partial;
+    p.out_norm = m->out_norm;
+    p.kq = m->kq;
+    p.vq = m->vq;
+    p.ks = m->ks;
+    p.vs = m->vs;
+    p.rope = m->rope;
+    p.pos = m->d_pos;
+    p.arrivals = reinterpret_cast<unsigned long long *>(m->mega_state);
+    p.launches = reinterpret_cast<uint32_t *>(m->mega_state) + 2;
+    p.abort = reinterpret_cast<uint32_t *>(m->mega_state) + 3;
+    p.status = status;
+    m->mega_c3 = c3;
+    m->mega = true;
+    return WL_OK;
+}
+
+int bn_enqueue_mega(wl_bitnet *m, cudaStream_t s, bool commit) {
+    MegaParams p = m->mp;
+    p.ids = commit ? m->d_ids : nullptr;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m->mega_grid);
+    cfg.blockDim = dim3(MEGA_THREADS);
+    cfg.dynamicSmemBytes = m->mega_smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (m->mega_c3) WL_CUDA(cudaLaunchKernelEx(&cfg, bitnet_mega_kernel<true>, p));
+    else WL_CUDA(cudaLaunchKernelEx(&cfg, bitnet_mega_kernel<false>, p));
+    return WL_OK;
+}
+
 int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
+    if (m->mega) return bn_enqueue_mega(m, s, commit);
     const wl_bitnet_config &c = m->cfg;
     const uint32_t E = c.n_embd, F = c.n_ff, KV = bn_kv(c), nb = E / 256u;
     uint32_t *status = status_ptr();
@@ -1326,6 +1446,8 @@ int bn_check_status(wl_bitnet *m) {
     WL_CUDA(cudaMemcpy(&f, c.d_status, 4, cudaMemcpyDeviceToHost));
     if (!f) return WL_OK;
     WL_CUDA(cudaMemset(c.d_status, 0, 4));
+    if ((f & WL_DEV_ERR_MEGA) && m->mega_state)  // the grid stopped early: re-arm its barriers
+        WL_CUDA(cudaMemset(m->mega_state, 0, 64));
     if (f & WL_DEV_ERR_NONFINITE)
         return fail(WL_ERR_GGUF_PARSE, "forward_with_cache: non-finite hidden after a layer");
     if (f & WL_DEV_ERR_POSITION) return fail(WL_ERR_GGUF_PARSE, "KV cache is full");
@@ -1990,12 +2112,14 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
     BN_ALLOC(m->ks, kvs * 4);
     BN_ALLOC(m->vs, kvs * 4);
     BN_ALLOC(m->hidden, (size_t)E * 4);
-    BN_ALLOC(m->q, (size_t)E * 4);
-    BN_ALLOC(m->k, (size_t)KV * 4);
-    BN_ALLOC(m->v, (size_t)KV * 4);
+    BN_ALLOC(m->q, (size_t)(E + 2 * KV) * 4);  // q | k | v, contiguous
+    m->k = m->q + E;
+    m->v = m->k + KV;
     BN_ALLOC(m->att, (size_t)E * 4);
-    BN_ALLOC(m->gate, (size_t)F * 4);
-    BN_ALLOC(m->up, (size_t)F * 4);
+    BN_ALLOC(m->gate, (size_t)2 * F * 4);       // gate | up, contiguous
+    m->up = m->gate + F;
+    BN_ALLOC(m->att_g, (size_t)E * 4);
+    BN_ALLOC(m->mega_state, 64);
     BN_ALLOC(m->final_h, (size_t)E * 4);
     BN_ALLOC(m->d_token, 16);
     BN_ALLOC(m->d_pos, 16);
@@ -2008,7 +2132,10 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
                         : std::max<uint32_t>(1u, std::min<uint32_t>((c.max_seq + 31) / 32,
                                                                     (uint32_t)(2 * cx.sm_count) /
                                                                         c.n_heads));
-    BN_ALLOC(m->attn_partial, (size_t)c.n_heads * m->splits * (2 + c.head_dim) * 4);
+    m->mega_grid = (uint32_t)cx.sm_count;
+    m->mega_splits = c.exact ? 1u : std::max<uint32_t>(1u, m->mega_grid / c.n_heads);
+    BN_ALLOC(m->attn_partial, (size_t)c.n_heads * std::max(m->splits, m->mega_splits) *
+                                  (4 + c.head_dim) * 4);
     BN_ALLOC(m->attn_counters, (size_t)c.n_heads * 4);
 #undef BN_ALLOC
     if (cudaMallocHost(&p, 64) != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "pinned"));
@@ -2062,6 +2189,7 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
     if (e == cudaSuccess) e = cudaMemsetAsync(m->d_step, 0, 16, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e)));
+    if (c.persistent && (rc = bn_setup_mega(m))) return cleanup(rc);
     *out = m;
     return WL_OK;
 }
@@ -2074,7 +2202,8 @@ int wl_bitnet_destroy(wl_bitnet *m) {
     if (m->g_step) cudaGraphExecDestroy(m->g_step);
     if (m->g_last) cudaGraphExecDestroy(m->g_last);
     void *bufs[] = {m->wblock, m->norms, m->out_norm, m->q6k, m->rope, m->kq, m->vq, m->ks,
-                    m->vs, m->hidden, m->q, m->k, m->v, m->att, m->gate, m->up, m->final_h,
+                    m->vs, m->hidden, m->q, m->att, m->gate, m->final_h, m->att_g,
+                    m->mega_state, m->d_layers,
                     m->d_token, m->d_pos, m->d_step, m->d_ids, m->lm_scratch,
                     m->attn_partial, m->attn_counters};
     for (void *b : bufs)
@@ -2096,6 +2225,9 @@ int wl_bitnet_reset(wl_bitnet *m) {
 }
 
 uint32_t wl_bitnet_position(const wl_bitnet *m) { return m ? m->pos : 0u; }
+
+int wl_bitnet_uses_persistent_kernel(const wl_bitnet *m) { return m && m->mega ? 1 : 0; }
+
 
 int wl_bitnet_forward(wl_bitnet *m, uint32_t token, uint32_t position, float *out_hidden) {
     if (!m) return fail(WL_ERR_INVALID_ARGUMENT, "model is NULL");

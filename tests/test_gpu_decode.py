@@ -56,16 +56,19 @@ CASES = {
 }
 
 
+@pytest.mark.parametrize("persistent", [False, True])
 @pytest.mark.parametrize("exact", [False, True])
 @pytest.mark.parametrize("name", list(CASES))
-def test_decode_matches_oracle(name, exact):
+def test_decode_matches_oracle(name, exact, persistent):
+    """Both engines: the per-op chain and the persistent whole-forward kernel."""
     from project_willamette_b200.bitnet import BitNet
     m = _model(100 + list(CASES).index(name), **CASES[name])
     rng = np.random.default_rng(1)
     n_prompt = m["config"]["max_seq"] // 2
     prompt = rng.integers(0, m["config"]["vocab"], n_prompt)
     o = oracle.BitnetOracle(m)
-    g = BitNet(m, exact=exact)
+    g = BitNet(m, exact=exact, persistent=persistent)
+    assert g.persistent == persistent
     check = _check_exact if exact else _check_errs
     try:
         errs = []
@@ -120,14 +123,16 @@ def bitnet2b():
 
 
 @pytest.mark.parametrize("exact", [True, False])
-def test_decode_bitnet2b_shapes(bitnet2b, exact):
+@pytest.mark.parametrize("persistent", [False, True])
+def test_decode_bitnet2b_shapes(bitnet2b, exact, persistent):
     """BASELINE config 2 shapes (30 layers, 2560, 20/5 heads, 6912, vocab
     128256), a short prompt and a few greedy tokens.  Fast mode at 30 layers
     accumulates re-quantisation flips in the hidden state (see the module
     docstring), so only its ids are held to the reference there."""
     from project_willamette_b200.bitnet import BitNet
     m, prompt, want_ids, want_h = bitnet2b
-    g = BitNet(m, exact=exact)
+    g = BitNet(m, exact=exact, persistent=persistent)
+    assert g.persistent == persistent
     try:
         got_ids, got_h = g.generate(prompt, 6, hiddens=True)
         assert got_ids.tolist() == want_ids.tolist()
