@@ -191,6 +191,20 @@ size_t wl_i2s_gemm_workspace_bytes(uint32_t m, uint32_t in_dim);
 int wl_dev_i2s_gemm_f32(const uint8_t *packed, float w_scale, uint32_t in_dim, uint32_t out_dim,
                         uint32_t m, const float *x, float *y, int32_t *acc, void *workspace,
                         uint32_t flags, void *stream);
+/* Weights expanded once to int8 ternary values (t = code - 1, code 0b11 -> 0;
+ * bitlinear.rs:43-50) in natural element order, out_dim x in_dim bytes -- 4x
+ * the packed size, kept resident for prefill.  The GEMM over them is a
+ * warp-specialised persistent tcgen05 kernel (TMA producer warp, MMA warp,
+ * epilogue warps, double-buffered tensor-memory accumulators) and has no
+ * code-0b11 restriction.  Same result as wl_dev_i2s_gemm_f32 (the reference's
+ * per-token matvec, bit for bit). */
+size_t wl_i2s_expanded_bytes(uint32_t in_dim, uint32_t out_dim);
+int wl_dev_i2s_expand(const uint8_t *packed, uint32_t in_dim, uint32_t out_dim, int8_t *ternary,
+                      void *stream);
+/* workspace: wl_i2s_gemm_workspace_bytes(m, in_dim) bytes, 16-byte aligned. */
+int wl_dev_i2s_gemm_s8_f32(const int8_t *ternary, float w_scale, uint32_t in_dim,
+                           uint32_t out_dim, uint32_t m, const float *x, float *y, int32_t *acc,
+                           void *workspace, void *stream);
 
 /* *found (device u32) = 1 if the packed tensor contains a 0b11 code, else 0. */
 int wl_dev_i2s_scan_code3(const uint8_t *packed, size_t bytes, uint32_t *found, void *stream);

@@ -112,6 +112,9 @@ PROTOTYPES = {
     "wl_dev_i2s_scan_code3": ([_vp, _sz, _vp, _vp], _i),
     "wl_i2s_gemm_workspace_bytes": ([_u32, _u32], _sz),
     "wl_dev_i2s_gemm_f32": ([_vp, C.c_float, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u32, _vp], _i),
+    "wl_i2s_expanded_bytes": ([_u32, _u32], _sz),
+    "wl_dev_i2s_expand": ([_vp, _u32, _u32, _vp, _vp], _i),
+    "wl_dev_i2s_gemm_s8_f32": ([_vp, C.c_float, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp], _i),
     "wl_i2s_stream_plan_create": ([C.POINTER(WlI2sStreamOp), _u32, C.POINTER(_vp)], _i),
     "wl_dev_i2s_stream_run": ([_vp, _vp], _i),
     "wl_i2s_stream_plan_destroy": ([_vp], _i),

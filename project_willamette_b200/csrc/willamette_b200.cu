@@ -23,6 +23,7 @@
 #include "i2s_matvec.cuh"
 #include "i2s_stream.cuh"
 #include "i2s_gemm.cuh"
+#include "i2s_gemm_ws.cuh"
 #include "q6k_lmhead.cuh"
 #include "q8_0.cuh"
 
@@ -131,7 +132,10 @@ int configure_kernels() {
                             (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<4>,
                             (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel,
                             (const void *)bitnet_mega_kernel<false>,
-                            (const void *)bitnet_mega_kernel<true>};
+                            (const void *)bitnet_mega_kernel<true>,
+                            (const void *)i2s_gemm_ws_kernel<64>,
+                            (const void *)i2s_gemm_ws_kernel<128>,
+                            (const void *)i2s_gemm_ws_kernel<256>};
     for (const void *k : others)
         WL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      WL_MAX_DYN_SMEM));
@@ -891,6 +895,55 @@ int launch_i2s_gemm(const uint8_t *packed, float w_scale, uint32_t K, uint32_t N
         WL_CUDA(launch(i2s_gemm_kernel<128>, grid, dim3(GEMM_THREADS), GemmSmem<128>::DYN, s, pdl, p));
     else
         WL_CUDA(launch(i2s_gemm_kernel<64>, grid, dim3(GEMM_THREADS), GemmSmem<64>::DYN, s, pdl, p));
+    return WL_OK;
+}
+
+// Y[m][n] from pre-quantised activations q [m][K] and int8 ternary weights
+// t [N][K] (i2s_expand_kernel): the warp-specialised persistent GEMM.
+int launch_i2s_gemm_s8(const int8_t *t, float w_scale, uint32_t K, uint32_t N, uint32_t M,
+                       const int8_t *q, const float *act_scale, float *y, int32_t *acc,
+                       cudaStream_t s, bool pdl, uint32_t *status) {
+    if (M == 0 || N == 0) return WL_OK;
+    EncodeTiledFn enc;
+    int rc = get_encode_tiled(&enc);
+    if (rc) return rc;
+    const uint32_t mt = (M + GEMM_BM - 1) / GEMM_BM;
+    const uint32_t sms = (uint32_t)sm_count_for_launch();
+    // widest tile that still gives every SM work
+    int bn = 256;
+    if ((uint64_t)mt * ((N + 255) / 256) < sms) bn = 128;
+    if (bn == 128 && (uint64_t)mt * ((N + 127) / 128) < sms) bn = 64;
+    I2sGemmWsParams p;
+    memset(&p, 0, sizeof p);
+    if ((rc = encode_2d(enc, &p.a_map, q, K, M, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    if ((rc = encode_2d(enc, &p.b_map, t, K, N, GEMM_BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    p.act_scale = act_scale;
+    p.w_scale = w_scale;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.y = y;
+    p.acc = acc;
+    p.status = status;
+    const uint32_t tiles = mt * ((N + bn - 1) / bn);
+    const dim3 grid(std::min(tiles, sms));
+    if (bn == 256)
+        WL_CUDA(launch(i2s_gemm_ws_kernel<256>, grid, dim3(WS_THREADS), WsSmem<256>::DYN, s, pdl, p));
+    else if (bn == 128)
+        WL_CUDA(launch(i2s_gemm_ws_kernel<128>, grid, dim3(WS_THREADS), WsSmem<128>::DYN, s, pdl, p));
+    else
+        WL_CUDA(launch(i2s_gemm_ws_kernel<64>, grid, dim3(WS_THREADS), WsSmem<64>::DYN, s, pdl, p));
+    return WL_OK;
+}
+
+int launch_i2s_expand(const uint8_t *packed, uint32_t K, uint32_t N, int8_t *out, cudaStream_t s) {
+    const size_t blocks = (size_t)N * (K / 128u);
+    if (!blocks) return WL_OK;
+    const uint32_t grid = (uint32_t)std::min<size_t>((blocks + 255) / 256, 4u * 1184u);
+    i2s_expand_kernel<<<grid, 256, 0, s>>>(packed, blocks, out);
+    WL_CUDA(cudaGetLastError());
     return WL_OK;
 }
 
@@ -1894,6 +1947,43 @@ int wl_dev_i2s_gemm_f32(const uint8_t *packed, float w_scale, uint32_t in_dim, u
         if ((rc = launch_i2s(L, s, true))) return rc;
     }
     return WL_OK;
+}
+
+size_t wl_i2s_expanded_bytes(uint32_t in_dim, uint32_t out_dim) {
+    return (size_t)in_dim * out_dim;
+}
+
+int wl_dev_i2s_expand(const uint8_t *packed, uint32_t in_dim, uint32_t out_dim, int8_t *ternary,
+                      void *stream) {
+    if (in_dim == 0 || in_dim % 128 || in_dim > WL_I2S_MAX_IN_DIM)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128 <= %u", in_dim,
+                    WL_I2S_MAX_IN_DIM);
+    if (!packed || !ternary || !aligned16(packed) || !aligned16(ternary))
+        return fail(WL_ERR_INVALID_ARGUMENT, "NULL or misaligned pointer");
+    if (!status_ptr()) return WL_ERR_NO_DEVICE;
+    return launch_i2s_expand(packed, in_dim, out_dim, ternary, (cudaStream_t)stream);
+}
+
+int wl_dev_i2s_gemm_s8_f32(const int8_t *ternary, float w_scale, uint32_t in_dim,
+                           uint32_t out_dim, uint32_t m, const float *x, float *y, int32_t *acc,
+                           void *workspace, void *stream) {
+    if (in_dim == 0 || in_dim % 128 || in_dim > WL_I2S_MAX_IN_DIM)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128 <= %u", in_dim,
+                    WL_I2S_MAX_IN_DIM);
+    if (!std::isfinite(w_scale)) return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale");
+    if (!ternary || !x || !y || !workspace || !aligned16(ternary) || !aligned16(x) ||
+        !aligned16(workspace))
+        return fail(WL_ERR_INVALID_ARGUMENT, "NULL or misaligned pointer");
+    if (m == 0 || out_dim == 0) return WL_OK;
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    cudaStream_t s = (cudaStream_t)stream;
+    int8_t *q = (int8_t *)workspace;
+    float *scale = (float *)((uint8_t *)workspace + (size_t)m * in_dim);
+    int rc;
+    if ((rc = launch_quantize(x, in_dim, m, q, scale, s, true))) return rc;
+    return launch_i2s_gemm_s8(ternary, w_scale, in_dim, out_dim, m, q, scale, y, acc, s, true,
+                              status);
 }
 
 // ------------------------------------------------------------ tensor parallel
