@@ -40,13 +40,16 @@ struct WsSmem {
     static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK;  // 16 KB
     static constexpr uint32_t B_BYTES = BN * GEMM_BK;
     static constexpr uint32_t STAGE = A_BYTES + B_BYTES;
-    static constexpr uint32_t TOTAL = WS_STAGES * STAGE;
+    static constexpr uint32_t OUT = 4u * 32u * 32u * 4u;  // one 32 x 32 f32 box per epilogue warp
+    static constexpr uint32_t TOTAL = WS_STAGES * STAGE + OUT;
     static constexpr size_t DYN = TOTAL + 1024;  // + alignment slack
 };
 
 struct I2sGemmWsParams {
     CUtensorMap a_map;  // int8 activations [M][K], box {128 B, 128 rows}, 128B swizzle
     CUtensorMap b_map;  // int8 ternary weights [N][K], box {128 B, BN rows}, 128B swizzle
+    CUtensorMap y_map;  // f32 output [M][N], box {32, 32}, 128B swizzle (when use_tma_store)
+    uint32_t use_tma_store;
     const float *act_scale;  // [M]
     float w_scale;
     uint32_t M, N, K;
@@ -62,7 +65,22 @@ __device__ __forceinline__ uint32_t umma_idesc_s8s8() {
            ((uint32_t)(GEMM_BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mbar_arrive_cnt(uint64_t *bar) { mbar_arrive(bar); }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, uint32_t x,
+                                             uint32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+        "r"(smem_u32(src)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until the bulk stores of all but the newest N groups have read their
+// shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 
 template <int BN>
 __global__ void __launch_bounds__(WS_THREADS, 1)
@@ -102,7 +120,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
     const uint32_t tmem = tmem_base_s;
 
     pdl_launch_dependents();
-    pdl_wait();  // the quantised activations come from the previous kernel
+    // Only A (the quantised activations) and act_scale come from the previous
+    // kernel: the producer requests the first stages' weights before waiting
+    // for it, the epilogue waits before reading act_scale.
 
     auto abort_now = [&]() {
         atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
@@ -113,15 +133,30 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
             uint32_t it = 0;
+            // weights of the first stages before the dependency wait
+            const uint32_t pre = blockIdx.x < tiles ? min(nkb, (uint32_t)WS_STAGES) : 0u;
+            {
+                const uint32_t n0 = (blockIdx.x / MT) * BN;
+                for (uint32_t kb = 0; kb < pre; ++kb) {
+                    uint8_t *st = smem + kb * L::STAGE;
+                    mbar_arrive_expect_tx(&full[kb], L::STAGE);
+                    tma_load_2d_plain(st + L::A_BYTES, &p.b_map, kb * GEMM_BK, n0, &full[kb]);
+                }
+            }
+            pdl_wait();
             for (uint32_t t = blockIdx.x; t < tiles && !aborted(); t += gridDim.x) {
                 const uint32_t m0 = (t % MT) * GEMM_BM, n0 = (t / MT) * BN;
                 for (uint32_t kb = 0; kb < nkb; ++kb, ++it) {
                     const uint32_t s = it % WS_STAGES;
+                    uint8_t *st = smem + s * L::STAGE;
+                    if (it < pre) {  // weights already requested
+                        tma_load_2d_plain(st, &p.a_map, kb * GEMM_BK, m0, &full[s]);
+                        continue;
+                    }
                     if (it >= WS_STAGES && !mbar_wait(&empty[s], ((it / WS_STAGES) - 1u) & 1u)) {
                         abort_now();
                         break;
                     }
-                    uint8_t *st = smem + s * L::STAGE;
                     mbar_arrive_expect_tx(&full[s], L::STAGE);
                     tma_load_2d_plain(st, &p.a_map, kb * GEMM_BK, m0, &full[s]);
                     tma_load_2d_plain(st + L::A_BYTES, &p.b_map, kb * GEMM_BK, n0, &full[s]);
@@ -175,6 +210,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
         }
     } else {
         // epilogue warps 2..5: TMEM lanes 32*(warp % 4) .. +31
+        pdl_wait();  // act_scale comes from the previous kernel
         const uint32_t lb = 32u * (warp & 3u);
         uint32_t local = 0;
         for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
@@ -190,10 +226,41 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
             const bool mvalid = m < p.M;
             const float combined = mvalid ? __fmul_rn(p.w_scale, p.act_scale[m]) : 0.0f;
             float *yrow = p.y + (size_t)m * p.N;
+            // this warp's 32 x 32 f32 staging box (128-byte swizzle: row r's
+            // 16-byte chunk c at c ^ (r & 7))
+            uint8_t *box = smem + WS_STAGES * L::STAGE + (warp & 3u) * 4096u;
 #pragma unroll 1
             for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem + (lb << 16) + a * (uint32_t)BN + c0, r);
+                if (p.use_tma_store) {
+                    if (m0 + lb < p.M && n0 + c0 < p.N) {
+                        if (lane == 0) bulk_wait_group_read<0>();  // the box is free again
+                        __syncwarp();
+#pragma unroll
+                        for (uint32_t c = 0; c < 8; ++c) {
+                            float4 v;
+                            v.x = __fmul_rn(combined, __int2float_rn((int32_t)r[4 * c]));
+                            v.y = __fmul_rn(combined, __int2float_rn((int32_t)r[4 * c + 1]));
+                            v.z = __fmul_rn(combined, __int2float_rn((int32_t)r[4 * c + 2]));
+                            v.w = __fmul_rn(combined, __int2float_rn((int32_t)r[4 * c + 3]));
+                            *reinterpret_cast<float4 *>(box + lane * 128u + ((c ^ (lane & 7u)) << 4)) = v;
+                        }
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&p.y_map, box, n0 + c0, m0 + lb);
+                            bulk_commit_group();
+                        }
+                    }
+                    if (p.acc && mvalid) {
+                        int32_t *arow = p.acc + (size_t)m * p.N;
+#pragma unroll
+                        for (uint32_t i = 0; i < 32; ++i)
+                            if (n0 + c0 + i < p.N) arow[n0 + c0 + i] = (int32_t)r[i];
+                    }
+                    continue;
+                }
                 if (mvalid) {
                     const uint32_t nb = n0 + c0;
                     if (nb + 32u <= p.N && (p.N & 3u) == 0u) {
@@ -224,6 +291,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[a]);  // accumulator a may be overwritten
         }
+        if (lane == 0) bulk_wait_group_read<0>();  // stores have read the staging boxes
     }
     tc_fence_before();
     __syncthreads();

@@ -909,16 +909,36 @@ int launch_i2s_gemm_s8(const int8_t *t, float w_scale, uint32_t K, uint32_t N, u
     if (rc) return rc;
     const uint32_t mt = (M + GEMM_BM - 1) / GEMM_BM;
     const uint32_t sms = (uint32_t)sm_count_for_launch();
-    // widest tile that still gives every SM work
+    // Tile width by estimated time: waves of persistent tiles x per-tile cost
+    // (mainloop ~ BN columns, plus a fixed share for the epilogue and fill).
     int bn = 256;
-    if ((uint64_t)mt * ((N + 255) / 256) < sms) bn = 128;
-    if (bn == 128 && (uint64_t)mt * ((N + 127) / 128) < sms) bn = 64;
+    uint64_t best = ~0ull;
+    for (int cand : {256, 128, 64}) {
+        const uint64_t tiles = (uint64_t)mt * ((N + cand - 1) / cand);
+        const uint64_t cost = ((tiles + sms - 1) / sms) * (uint64_t)(cand + 128);
+        if (cost < best) {
+            best = cost;
+            bn = cand;
+        }
+    }
     I2sGemmWsParams p;
     memset(&p, 0, sizeof p);
     if ((rc = encode_2d(enc, &p.a_map, q, K, M, GEMM_BK, GEMM_BM, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
     if ((rc = encode_2d(enc, &p.b_map, t, K, N, GEMM_BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
+    // output boxes by TMA store when rows are 16-byte multiples
+    if ((N % 4u) == 0 && aligned16(y)) {
+        const cuuint64_t dims[2] = {N, M};
+        const cuuint64_t strides[1] = {(cuuint64_t)N * 4u};
+        const cuuint32_t box[2] = {32, 32};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc(&p.y_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)y, dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(WL_ERR_CUDA, "cuTensorMapEncodeTiled (y) failed (%d)", (int)r);
+        p.use_tma_store = 1;
+    }
     p.act_scale = act_scale;
     p.w_scale = w_scale;
     p.M = M;
