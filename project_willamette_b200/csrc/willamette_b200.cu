@@ -70,6 +70,7 @@ struct CachedWeight {
     size_t bytes = 0;
     bool bad_scale = false;  // Q8_0: some block scale is not finite
     bool has_code3 = true;   // I2_S: some 2-bit code is 0b11 (scanned on upload)
+    int8_t *ternary = nullptr;  // I2_S: int8 ternary copy for prefill, made on first use
 };
 
 using CacheKey = std::tuple<const void *, size_t, uint32_t, uint64_t, uint64_t>;
@@ -100,6 +101,11 @@ constexpr size_t I2S_GEMM_MIN_TOKENS = 16;
 int launch_i2s_gemm(const uint8_t *packed, float w_scale, uint32_t K, uint32_t N, uint32_t M,
                     const int8_t *q, const float *act_scale, const int32_t *rowsum, float *y,
                     int32_t *acc, cudaStream_t s, bool pdl, uint32_t *status);
+
+int launch_i2s_gemm_s8(const int8_t *t, float w_scale, uint32_t K, uint32_t N, uint32_t M,
+                       const int8_t *q, const float *act_scale, float *y, int32_t *acc,
+                       cudaStream_t s, bool pdl, uint32_t *status);
+int launch_i2s_expand(const uint8_t *packed, uint32_t K, uint32_t N, int8_t *out, cudaStream_t s);
 
 using I2sKernel = void (*)(I2sMatvecParams);
 using I2sStreamKernel = void (*)(I2sStreamParams);
@@ -609,19 +615,26 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
     uint8_t *pin = (uint8_t *)c.pinned;
     memcpy(pin, input, xin);
     WL_CUDA(cudaMemcpyAsync(c.x.p, pin, xin, cudaMemcpyHostToDevice, c.stream));
-    // Prefill of many tokens on code-3-free weights: one tensor-core GEMM.
-    const bool gemm = m >= I2S_GEMM_MIN_TOKENS && !cw->has_code3 && m <= 0x7FFFFFFFu;
+    // Prefill of many tokens: one tensor-core GEMM over the weight's int8
+    // ternary copy (expanded once, kept with the cached upload; 4x the packed
+    // bytes -- the memory-for-speed trade a 180 GB device affords).
+    const bool gemm = m >= I2S_GEMM_MIN_TOKENS && m <= 0x7FFFFFFFu;
     const bool fuse = !gemm && K <= I2S_FUSE_Q_MAX_K;
     if (gemm) {
-        if ((rc = grow(c.rowsum, m * 4))) return rc;
+        if (!cw->ternary) {
+            void *tp = nullptr;
+            WL_CUDA(cudaMalloc(&tp, (size_t)K * N));
+            cw->ternary = (int8_t *)tp;
+            if ((rc = launch_i2s_expand((const uint8_t *)cw->dptr, K, N, cw->ternary, c.stream)))
+                return rc;
+        }
         if ((rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m, (int8_t *)c.q.p,
-                                  (float *)c.scale.p, c.stream, false, (int32_t *)c.rowsum.p)))
+                                  (float *)c.scale.p, c.stream, false)))
             return rc;
-        if ((rc = launch_i2s_gemm((const uint8_t *)cw->dptr, w_scale, K, N, (uint32_t)m,
-                                  (const int8_t *)c.q.p, (const float *)c.scale.p,
-                                  (const int32_t *)c.rowsum.p, (float *)c.y.p,
-                                  acc_out ? (int32_t *)c.acc.p : nullptr, c.stream, true,
-                                  c.d_status)))
+        if ((rc = launch_i2s_gemm_s8(cw->ternary, w_scale, K, N, (uint32_t)m,
+                                     (const int8_t *)c.q.p, (const float *)c.scale.p,
+                                     (float *)c.y.p, acc_out ? (int32_t *)c.acc.p : nullptr,
+                                     c.stream, true, c.d_status)))
             return rc;
         m = 0;  // no per-token launches below
     } else if (!fuse && (rc = launch_quantize((const float *)c.x.p, K, (uint32_t)m,
@@ -1562,7 +1575,10 @@ int wl_init(int device) {
 int wl_release_weights(void) {
     Ctx &c = ctx();
     std::lock_guard<std::mutex> g(c.mu);
-    for (auto &kv : c.cache) cudaFree(kv.second.dptr);
+    for (auto &kv : c.cache) {
+        cudaFree(kv.second.dptr);
+        if (kv.second.ternary) cudaFree(kv.second.ternary);
+    }
     c.cache.clear();
     return WL_OK;
 }
