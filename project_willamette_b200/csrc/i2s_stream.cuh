@@ -5,10 +5,13 @@
 //  * every op's weight is cut into 32-row blocks; the blocks of all ops form
 //    one list, and each CTA (one per SM) owns a contiguous, byte-balanced
 //    range of it;
-//  * each of the 8 warps of a CTA takes every 8th block of that range and
+//  * each of the 12 warps of a CTA takes every 12th block of that range and
 //    streams it as 64-row x 128-byte boxes with 2-D TMA tensor copies
-//    (cp.async.bulk.tensor, 128-byte swizzle) through its own 3-stage
-//    shared-memory ring -- lane l owns rows l and l+32 of the box, so there
+//    (cp.async.bulk.tensor, 128-byte swizzle) through its own 2-stage
+//    shared-memory ring (12 x 2 beat 8 x 3 and 6-7 x 4 with the same bytes
+//    in flight: the consumer warps, not the copies, set the pace, and a pure
+//    TMA stream of these boxes runs at about 7 TB/s) -- lane l owns rows l
+//    and l+32 of the box, so there
 //    are no cross-lane reductions, and the swizzle makes the 32 lanes' 16-byte
 //    reads (one per row) hit distinct banks;
 //  * activations (quantised beforehand by quantize_jobs_kernel, one CTA per
@@ -29,9 +32,9 @@
 
 namespace wl {
 
-constexpr int STREAM_WARPS = 8;
+constexpr int STREAM_WARPS = 12;
 constexpr int STREAM_THREADS = STREAM_WARPS * 32;
-constexpr int STREAM_WSTAGES = 3;            // TMA boxes in flight per warp
+constexpr int STREAM_WSTAGES = 2;            // TMA boxes in flight per warp
 constexpr int STREAM_RPL = 2;                // rows per lane: activations loaded once per 2 rows
 constexpr uint32_t STREAM_BOX_ROWS = 32 * STREAM_RPL;
 constexpr uint32_t STREAM_BOX_BYTES = 128;   // 8 weight slots of 16 bytes
