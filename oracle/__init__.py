@@ -247,7 +247,8 @@ def argmax(logits):
 class OrBitnetConfig(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("n_layers", "n_embd", "n_heads", "n_kv_heads",
                                           "head_dim", "n_ff", "vocab", "n_rot", "max_seq")] + \
-               [("eps", C.c_float), ("freq_base", C.c_float)]
+               [("eps", C.c_float), ("freq_base", C.c_float), ("variant", _u32),
+                ("linear_type", _u32), ("embd_type", _u32)]
 
 
 class OrBitnetWeights(C.Structure):
@@ -267,9 +268,12 @@ def _bitnet_prototypes(L):
                                      C.POINTER(_u32), _f32p, C.c_int]
     L.or_rms_norm.argtypes = [_f32p, _f32p, C.c_float, _f32p, _u32]
     L.or_rope_neox.argtypes = [_f32p, _u32, _u32, C.c_float]
+    L.or_rope_norm.argtypes = [_f32p, _u32, _u32, C.c_float]
+    L.or_silu_inplace.argtypes = [_f32p, _u32]
     L.or_softmax_inplace.argtypes = [_f32p, _u32]
     L.or_kv_quantise.argtypes = [_f32p, _u32, _i8p, _f32p]
-    for n in ("or_rms_norm", "or_rope_neox", "or_softmax_inplace", "or_kv_quantise"):
+    for n in ("or_rms_norm", "or_rope_neox", "or_rope_norm", "or_silu_inplace",
+              "or_softmax_inplace", "or_kv_quantise"):
         getattr(L, n).restype = None
 
 
@@ -291,6 +295,18 @@ def rms_norm(x, w, eps: float) -> np.ndarray:
 def rope_neox(x, n_rot: int, position: int, freq_base: float) -> np.ndarray:
     x = _f32(x).copy()
     _blib().or_rope_neox(_p(x, _f32p), n_rot, position, freq_base)
+    return x
+
+
+def rope_norm(x, n_rot: int, position: int, freq_base: float) -> np.ndarray:
+    x = _f32(x).copy()
+    _blib().or_rope_norm(_p(x, _f32p), n_rot, position, freq_base)
+    return x
+
+
+def silu(x) -> np.ndarray:
+    x = _f32(x).copy()
+    _blib().or_silu_inplace(_p(x, _f32p), x.size)
     return x
 
 
@@ -317,7 +333,8 @@ class BitnetOracle:
         c = model["config"]
         self.cfg = OrBitnetConfig(**{k: c[k] for k in (
             "n_layers", "n_embd", "n_heads", "n_kv_heads", "head_dim", "n_ff", "vocab", "n_rot",
-            "max_seq", "eps", "freq_base")})
+            "max_seq", "eps", "freq_base")}, variant=c.get("variant", 0),
+            linear_type=c.get("linear_type", 0), embd_type=c.get("embd_type", 14))
         ws = model["w"]
         self._wp = (_u8p * len(ws))(*[_p(a, _u8p) for a in ws])
         self.weights = OrBitnetWeights(self._wp, _p(model["w_scale"], _f32p),

@@ -15,8 +15,12 @@
  *   attention_scale       src/model/primitives.rs:354-357
  *   softmax_inplace       src/model/attention.rs:45-73
  *   KVCache append / read src/model/kv_cache.rs:154-219, :245-259
- *   relu_square / elementwise_mul  src/model/ffn.rs:37-65
- *   embedding_gather (Q6_K row)    src/model/primitives.rs:120-190
+ *   relu_square / silu / elementwise_mul  src/model/ffn.rs:37-65
+ *   embedding_gather (Q6_K / Q8_0 row)    src/model/primitives.rs:120-190
+ * Two forward variants (cached_forward.rs:373-504, ForwardVariant):
+ * BitNetSubNorm (attn / ffn sub-norms, relu^2, NEOX RoPE) and VanillaLlama
+ * (no sub-norms, SiLU, Norm RoPE pairs (2j, 2j+1)), the latter with Q8_0
+ * linears (q8_0_matvec_f32, linear.rs:171-224) for the SmolLM shapes.
  * BitLinears go through or_i2s_matvec_sse2_i8 (the x86 default), split into
  * row chunks over OpenMP threads: each chunk quantises the same x the same
  * way and rows are independent, so the result equals one serial call.
@@ -51,6 +55,24 @@ void or_rope_neox(float *x, uint32_t n_rot, uint32_t position, float freq_base) 
         x[j] = a * cos_t - b * sin_t;
         x[j + half] = a * sin_t + b * cos_t;
     }
+}
+
+void or_rope_norm(float *x, uint32_t n_rot, uint32_t position, float freq_base) {
+    const uint32_t half = n_rot / 2;
+    const float pos = (float)position;
+    const float n_rot_f = (float)n_rot;
+    for (uint32_t j = 0; j < half; ++j) {
+        const float exponent = -2.0f * (float)j / n_rot_f;
+        const float theta = pos * powf(freq_base, exponent);
+        const float sin_t = sinf(theta), cos_t = cosf(theta);
+        const float a = x[2 * j], b = x[2 * j + 1];
+        x[2 * j] = a * cos_t - b * sin_t;
+        x[2 * j + 1] = a * sin_t + b * cos_t;
+    }
+}
+
+void or_silu_inplace(float *x, uint32_t n) {
+    for (uint32_t i = 0; i < n; ++i) x[i] /= 1.0f + expf(-x[i]);
 }
 
 void or_softmax_inplace(float *x, uint32_t n) {
@@ -109,6 +131,16 @@ static int bitlinear(const uint8_t *packed, float w_scale, uint32_t in_dim, uint
     return rc ? -1 : 0;
 }
 
+/* linear_matvec_f32 (linear.rs:11-25): I2_S -> the sse2_i8 kernel, Q8_0 ->
+ * q8_0_matvec_f32 (linear.rs:171-224, rows independent). */
+static int linear(const or_bitnet_config *c, const uint8_t *w, float w_scale, uint32_t in_dim,
+                  uint32_t out_dim, const float *x, float *y, int n_threads) {
+    if (c->linear_type == 8)
+        return or_q8_0_matvec(w, (size_t)out_dim * (in_dim / 32) * 34, in_dim, out_dim, x, y,
+                              n_threads) ? -1 : 0;
+    return bitlinear(w, w_scale, in_dim, out_dim, x, y, n_threads);
+}
+
 static int check_finite(const float *x, uint32_t n) {
     for (uint32_t i = 0; i < n; ++i)
         if (!isfinite(x[i])) return -1;
@@ -125,7 +157,8 @@ int or_bitnet_forward(const or_bitnet_config *c, const or_bitnet_weights *w, or_
         return -1;
     if (kv->pos != position || position >= c->max_seq || token >= c->vocab) return -2;
     const uint32_t group = c->n_heads / c->n_kv_heads;
-    const size_t q6_row = (size_t)E / 256 * 210;
+    const int llama = c->variant == 1;
+    const size_t emb_row = c->embd_type == 8 ? (size_t)E / 32 * 34 : (size_t)E / 256 * 210;
     float *hidden = calloc(E, 4), *xn = calloc(E, 4), *q = calloc(E, 4), *k = calloc(KV, 4),
           *v = calloc(KV, 4), *att = calloc(E, 4), *sub = calloc(E, 4), *o = calloc(E, 4),
           *gate = calloc(F, 4), *up = calloc(F, 4), *fused = calloc(F, 4), *fn = calloc(F, 4),
@@ -136,8 +169,10 @@ int or_bitnet_forward(const or_bitnet_config *c, const or_bitnet_weights *w, or_
         rc = -3;
         goto done;
     }
-    /* embedding_gather: the token's Q6_K row, dequantised */
-    if (or_q6k_dequantize_row(w->token_embd + (size_t)token * q6_row, q6_row, hidden, E)) {
+    /* embedding_gather: the token's Q6_K / Q8_0 row, dequantised */
+    if ((c->embd_type == 8
+             ? or_q8_0_dequantize_row(w->token_embd + (size_t)token * emb_row, emb_row, hidden, E)
+             : or_q6k_dequantize_row(w->token_embd + (size_t)token * emb_row, emb_row, hidden, E))) {
         rc = -4;
         goto done;
     }
@@ -150,11 +185,13 @@ int or_bitnet_forward(const or_bitnet_config *c, const or_bitnet_weights *w, or_
         const float *ffn_sub_norm = attn_norm + 3 * E;
 
         or_rms_norm(hidden, attn_norm, c->eps, xn, E);
-        rc |= bitlinear(m[0], s[0], E, E, xn, q, n_threads);
-        rc |= bitlinear(m[1], s[1], E, KV, xn, k, n_threads);
-        rc |= bitlinear(m[2], s[2], E, KV, xn, v, n_threads);
-        for (uint32_t h = 0; h < c->n_heads; ++h) or_rope_neox(q + h * HD, c->n_rot, position, c->freq_base);
-        for (uint32_t h = 0; h < c->n_kv_heads; ++h) or_rope_neox(k + h * HD, c->n_rot, position, c->freq_base);
+        rc |= linear(c, m[0], s[0], E, E, xn, q, n_threads);
+        rc |= linear(c, m[1], s[1], E, KV, xn, k, n_threads);
+        rc |= linear(c, m[2], s[2], E, KV, xn, v, n_threads);
+        for (uint32_t h = 0; h < c->n_heads; ++h)
+            (llama ? or_rope_norm : or_rope_neox)(q + h * HD, c->n_rot, position, c->freq_base);
+        for (uint32_t h = 0; h < c->n_kv_heads; ++h)
+            (llama ? or_rope_norm : or_rope_neox)(k + h * HD, c->n_rot, position, c->freq_base);
         /* KVCache::append then read_into (dequantised f32 of every position) */
         int8_t *kq = kv->k_q + ((size_t)l * c->max_seq + position) * KV;
         int8_t *vq = kv->v_q + ((size_t)l * c->max_seq + position) * KV;
@@ -181,18 +218,23 @@ int or_bitnet_forward(const or_bitnet_config *c, const or_bitnet_weights *w, or_
                 for (uint32_t i = 0; i < HD; ++i) oh[i] += wgt * ((float)vp[i] * sv);
             }
         }
-        or_rms_norm(att, attn_sub_norm, c->eps, sub, E);
-        rc |= bitlinear(m[3], s[3], E, E, sub, o, n_threads);
+        if (!llama) or_rms_norm(att, attn_sub_norm, c->eps, sub, E);
+        rc |= linear(c, m[3], s[3], E, E, llama ? att : sub, o, n_threads);
         for (uint32_t i = 0; i < E; ++i) hidden[i] += o[i];
         or_rms_norm(hidden, ffn_norm, c->eps, xn, E);
-        rc |= bitlinear(m[4], s[4], E, F, xn, gate, n_threads);
-        rc |= bitlinear(m[5], s[5], E, F, xn, up, n_threads);
+        rc |= linear(c, m[4], s[4], E, F, xn, gate, n_threads);
+        rc |= linear(c, m[5], s[5], E, F, xn, up, n_threads);
+        if (llama) or_silu_inplace(gate, F);  /* silu (ffn.rs:45-49) */
         for (uint32_t i = 0; i < F; ++i) {
-            const float r = gate[i] > 0.0f ? gate[i] : 0.0f;
-            fused[i] = (r * r) * up[i];
+            float g = gate[i];
+            if (!llama) {  /* relu_square (ffn.rs:37-42) */
+                const float r = g > 0.0f ? g : 0.0f;
+                g = r * r;
+            }
+            fused[i] = g * up[i];
         }
-        or_rms_norm(fused, ffn_sub_norm, c->eps, fn, F);
-        rc |= bitlinear(m[6], s[6], F, E, fn, down, n_threads);
+        if (!llama) or_rms_norm(fused, ffn_sub_norm, c->eps, fn, F);
+        rc |= linear(c, m[6], s[6], F, E, llama ? fused : fn, down, n_threads);
         for (uint32_t i = 0; i < E; ++i) hidden[i] += down[i];
         if (rc) {
             rc = -5;
@@ -216,7 +258,8 @@ int or_bitnet_generate(const or_bitnet_config *c, const or_bitnet_weights *w, or
                        uint32_t *out_ids, float *hiddens, int n_threads) {
     if (n_prompt == 0) return -1;
     const uint32_t E = c->n_embd;
-    const size_t q6_len = (size_t)c->vocab * (E / 256) * 210;
+    const size_t emb_len = c->embd_type == 8 ? (size_t)c->vocab * (E / 32) * 34
+                                             : (size_t)c->vocab * (E / 256) * 210;
     float *h = calloc(E, 4), *logits = calloc(c->vocab, 4);
     int rc = 0;
     if (!h || !logits) {
@@ -228,7 +271,8 @@ int or_bitnet_generate(const or_bitnet_config *c, const or_bitnet_weights *w, or
         if ((rc = or_bitnet_forward(c, w, kv, prompt[i], pos++, h, n_threads))) goto done;
     for (uint32_t step = 0; step < n_new; ++step) {
         if (hiddens) memcpy(hiddens + (size_t)step * E, h, (size_t)E * 4);
-        if ((rc = or_compute_logits(h, E, w->token_embd, q6_len, 14, c->vocab, logits, n_threads)))
+        if ((rc = or_compute_logits(h, E, w->token_embd, emb_len, c->embd_type, c->vocab, logits,
+                                    n_threads)))
             goto done;
         const int64_t next = or_argmax(logits, c->vocab);
         out_ids[step] = (uint32_t)next;

@@ -127,6 +127,11 @@ int64_t or_argmax(const float *logits, size_t n);
 typedef struct {
     uint32_t n_layers, n_embd, n_heads, n_kv_heads, head_dim, n_ff, vocab, n_rot, max_seq;
     float eps, freq_base;
+    /* ForwardVariant: 0 = BitNetSubNorm (sub-norms, relu^2, NEOX RoPE),
+     * 1 = VanillaLlama (no sub-norms, SiLU, "normal" RoPE); cached_forward.rs:373-504 */
+    uint32_t variant;
+    uint32_t linear_type;  /* 0 = I2_S (w_scale used), 8 = Q8_0 */
+    uint32_t embd_type;    /* tied embedding / lm-head: 14 = Q6_K, 8 = Q8_0 */
 } or_bitnet_config;
 
 typedef struct {
@@ -148,6 +153,10 @@ typedef struct { /* src/model/kv_cache.rs layout, one slab per layer */
 void or_rms_norm(const float *x, const float *w, float eps, float *out, uint32_t n);
 /* primitives.rs:283-345, RopeType::Neox on one head (head_dim >= n_rot) */
 void or_rope_neox(float *x, uint32_t n_rot, uint32_t position, float freq_base);
+/* primitives.rs:316-327, RopeType::Norm (pairs 2j, 2j+1) */
+void or_rope_norm(float *x, uint32_t n_rot, uint32_t position, float freq_base);
+/* ffn.rs:45-49 */
+void or_silu_inplace(float *x, uint32_t n);
 /* attention.rs:45-73 */
 void or_softmax_inplace(float *x, uint32_t n);
 /* kv_cache.rs:245-259 (one token's K or V) */

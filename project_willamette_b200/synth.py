@@ -106,3 +106,31 @@ def bitnet_model(rng: np.random.Generator, n_layers: int = 30, n_embd: int = 256
         "output_norm": rng.uniform(0.5, 1.5, size=n_embd).astype(np.float32),
         "token_embd": q6k_rows(rng, n_embd, vocab),
     }
+
+
+def llama_q8_model(rng: np.random.Generator, n_layers: int = 30, n_embd: int = 576,
+                   n_heads: int = 9, n_kv_heads: int = 3, head_dim: int = 64, n_ff: int = 1536,
+                   vocab: int = 49152, max_seq: int = 1088, eps: float = 1e-5,
+                   freq_base: float = 10000.0) -> dict:
+    """A random SmolLM-135M-shaped Llama model: every
+    linear and the tied embedding / lm-head Q8_0 (int8 quants U[-127, 127],
+    f16 scale |N(0, 0.01)|), norm weights U[0.5, 1.5].  Defaults are the 135M
+    shapes.  The norms array keeps the per-layer layout of ``bitnet_model``
+    (attn_norm, attn_sub_norm, ffn_norm, ffn_sub_norm); the Llama forward
+    reads only attn_norm and ffn_norm."""
+    kv = n_kv_heads * head_dim
+    shapes = [(n_embd, n_embd), (n_embd, kv), (n_embd, kv), (n_embd, n_embd), (n_embd, n_ff),
+              (n_embd, n_ff), (n_ff, n_embd)]
+    w = [q8_0_rows(rng, k, n) for _ in range(n_layers) for k, n in shapes]
+    norms = rng.uniform(0.5, 1.5, size=n_layers * (3 * n_embd + n_ff)).astype(np.float32)
+    return {
+        "config": dict(n_layers=n_layers, n_embd=n_embd, n_heads=n_heads, n_kv_heads=n_kv_heads,
+                       head_dim=head_dim, n_ff=n_ff, vocab=vocab, n_rot=head_dim,
+                       max_seq=max_seq, eps=eps, freq_base=freq_base, variant=1,
+                       linear_type=8, embd_type=8),
+        "w": w,
+        "w_scale": np.ones(len(w), np.float32),
+        "norms": norms,
+        "output_norm": rng.uniform(0.5, 1.5, size=n_embd).astype(np.float32),
+        "token_embd": q8_0_rows(rng, n_embd, vocab),
+    }

@@ -103,3 +103,59 @@ def test_generate_matches_step_by_step_forward():
     assert np.array_equal(h, hs[0])
     logits = oracle.compute_logits(h, m["token_embd"], 14, 256, 300)
     assert ids[0] == oracle.argmax(logits)
+
+
+def test_silu_known_values():
+    # ffn.rs:157-164
+    v = oracle.silu([-1.0, 0.0, 1.0])
+    assert abs(v[0] + 0.26894143) < 1e-6 and v[1] == 0.0 and abs(v[2] - 0.7310586) < 1e-6
+
+
+def test_rope_norm_pairs_and_differs_from_neox():
+    # primitives.rs:549-566 and tests/primitives.rs:233-251
+    a = oracle.rope_norm([1.0, 0.0, 0.0, 0.0], 4, 1, 10000.0)
+    b = oracle.rope_neox([1.0, 0.0, 0.0, 0.0], 4, 1, 10000.0)
+    assert np.max(np.abs(a - b)) > 1e-6
+    x = (np.arange(128) * 0.01).astype(np.float32)
+    y = oracle.rope_norm(x, 128, 5, 500000.0)
+    assert np.max(np.abs(y - oracle.rope_neox(x, 128, 5, 500000.0))) > 1e-3
+    for j in range(64):  # the (2j, 2j+1) pair norms are kept
+        assert abs(x[2 * j] ** 2 + x[2 * j + 1] ** 2 - y[2 * j] ** 2 - y[2 * j + 1] ** 2) < 1e-5
+    assert np.all(np.abs(oracle.rope_norm(x, 128, 0, 10000.0) - x) < 1e-6)
+
+
+def _small_llama(seed=5, **kw):
+    args = dict(n_layers=2, n_embd=128, n_heads=2, n_kv_heads=1, n_ff=256, vocab=300,
+                max_seq=32)
+    args.update(kw)
+    return synth.llama_q8_model(np.random.default_rng(seed), **args)
+
+
+def test_llama_q8_forward_follows_its_primitives():
+    """The VanillaLlama variant with Q8_0 linears, checked against a numpy
+    composition of the pinned primitives (one layer, position 0, where the
+    attention output is V itself: softmax over one key is exactly 1), down to
+    the final output norm the forward returns."""
+    m = _small_llama(n_layers=1)
+    c = m["config"]
+    E, KV, F = c["n_embd"], c["n_kv_heads"] * c["head_dim"], c["n_ff"]
+    tok = 17
+    emb = oracle.q8_0_dequantize_row(m["token_embd"][tok * (E // 32) * 34:][:(E // 32) * 34], E)
+    nrm = m["norms"]
+    attn_norm, ffn_norm = nrm[:E], nrm[2 * E:3 * E]  # layer layout: attn, attn_sub, ffn, ffn_sub
+    w = m["w"]
+
+    def lin(i, x, n):
+        return oracle.q8_0_matvec(w[i], x.size, n, x)
+
+    xn = oracle.rms_norm(emb, attn_norm, c["eps"])
+    v = lin(2, xn, KV)
+    vq, vs = oracle.kv_quantise(v)
+    att = np.tile(vq.astype(np.float32) * np.float32(vs), c["n_heads"] // c["n_kv_heads"])
+    h = emb + lin(3, att, E)
+    xn = oracle.rms_norm(h, ffn_norm, c["eps"])
+    fused = oracle.silu(lin(4, xn, F)) * lin(5, xn, F)
+    h = h + lin(6, fused, E)
+    want = oracle.rms_norm(h, m["output_norm"], c["eps"])  # cached_forward.rs:248-257
+    got = oracle.BitnetOracle(m).forward(tok, 0)
+    assert np.array_equal(got, want)
