@@ -374,6 +374,54 @@ int wl_dev_q8_0_repack(const uint8_t *raw, uint32_t in_dim, uint32_t out_dim, ui
 int wl_dev_q8_0_matvec(const uint8_t *packed, uint32_t in_dim, uint32_t out_dim,
                        const float *x, float *y, void *stream);
 
+/* ------------------------------------- batched Q8_0 Llama decode engine
+ * n_seqs independent sequences decoded in lock step, one token per sequence
+ * per step, each with its own i8 KV cache and position.  Per sequence this
+ * is the reference's greedy_generate_with_cache (src/model/generate.rs:
+ * 111-190) over forward_with_cache (src/model/cached_forward.rs:206-504) in
+ * its VanillaLlama variant: RMSNorm, Norm RoPE (pairs 2j, 2j+1), GQA
+ * attention, no sub-norms, silu(gate) * up, every linear Q8_0
+ * (q8_0_matvec_f32, src/model/linear.rs:171-224) and a tied Q8_0 embedding /
+ * lm-head (compute_logits, src/model/lm_head.rs:103; argmax :161-174).
+ * The config's `exact` selects the reference's summation order everywhere
+ * (bit-exact linears); 0 contracts the Q8_0 products into FMAs and sums
+ * norms / softmax as trees.  `persistent` is ignored. */
+typedef struct {
+    const uint8_t *const *w;   /* n_layers * 7 GGUF Q8_0 rows (34-byte blocks):
+                                  q, k, v, o, gate, up, down */
+    const float *attn_norm;    /* n_layers * n_embd */
+    const float *ffn_norm;     /* n_layers * n_embd */
+    const float *output_norm;  /* n_embd */
+    const uint8_t *token_embd; /* vocab GGUF Q8_0 rows, tied lm-head */
+} wl_llama_weights;
+
+typedef struct wl_llama_batch wl_llama_batch;
+int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *weights,
+                          uint32_t n_seqs, wl_llama_batch **out);
+int wl_llama_batch_destroy(wl_llama_batch *batch);
+/* Empty every sequence's KV cache. */
+int wl_llama_batch_reset(wl_llama_batch *batch);
+uint32_t wl_llama_batch_position(const wl_llama_batch *batch, uint32_t seq);
+/* Attention CTAs per (head or KV head, sequence) the engine chose. */
+uint32_t wl_llama_batch_attention_splits(const wl_llama_batch *batch);
+/* Tokens each CTA of the batched Q8_0 linears covers (1, 4, 8 or 32; 0, the
+ * default: chosen per launch from the row tiles and the SM count).  A tuning
+ * knob; results do not depend on it. */
+int wl_llama_batch_set_tokens_per_cta(wl_llama_batch *batch, uint32_t tokens);
+/* Forward sequence b's tokens tokens[offsets[b] .. offsets[b+1]) from its
+ * current position (the prompt loop of generate.rs:147-160), all sequences in
+ * lock step; a sequence with no tokens idles. */
+int wl_llama_batch_prefill(wl_llama_batch *batch, const uint32_t *tokens, const uint32_t *offsets);
+/* n_new greedy steps for every sequence (each must have been prefilled):
+ * out_ids[step * n_seqs + b]; out_hiddens (optional, [n_new][n_seqs][n_embd]):
+ * the hiddens the ids were chosen from; device_ms (optional): device time of
+ * the loop. */
+int wl_llama_batch_decode(wl_llama_batch *batch, uint32_t n_new, uint32_t *out_ids,
+                          float *out_hiddens, float *device_ms);
+/* Reset, prefill every sequence's (non-empty) prompt, decode n_new. */
+int wl_llama_batch_generate(wl_llama_batch *batch, const uint32_t *tokens, const uint32_t *offsets,
+                            uint32_t n_new, uint32_t *out_ids, float *out_hiddens);
+
 #ifdef __cplusplus
 }
 #endif

@@ -83,6 +83,12 @@ class WlBitnetWeights(C.Structure):
                 ("norms", C.POINTER(C.c_float)), ("output_norm", C.POINTER(C.c_float)),
                 ("token_embd", C.c_void_p)]
 
+class WlLlamaWeights(C.Structure):
+    _fields_ = [("w", C.POINTER(C.c_void_p)), ("attn_norm", C.POINTER(C.c_float)),
+                ("ffn_norm", C.POINTER(C.c_float)), ("output_norm", C.POINTER(C.c_float)),
+                ("token_embd", C.c_void_p)]
+
+
 _vp = C.c_void_p
 _sz = C.c_size_t
 _u32 = C.c_uint32
@@ -136,6 +142,17 @@ PROTOTYPES = {
     "wl_bitnet_prefill": ([_vp, C.POINTER(_u32), _u32], _i),
     "wl_bitnet_decode": ([_vp, _u32, C.POINTER(_u32), _fp, _fp], _i),
     "wl_bitnet_generate": ([_vp, C.POINTER(_u32), _u32, _u32, C.POINTER(_u32), _fp], _i),
+    "wl_llama_batch_create": ([C.POINTER(WlBitnetConfig), C.POINTER(WlLlamaWeights), _u32,
+                               C.POINTER(_vp)], _i),
+    "wl_llama_batch_destroy": ([_vp], _i),
+    "wl_llama_batch_reset": ([_vp], _i),
+    "wl_llama_batch_position": ([_vp, _u32], _u32),
+    "wl_llama_batch_attention_splits": ([_vp], _u32),
+    "wl_llama_batch_set_tokens_per_cta": ([_vp, _u32], _i),
+    "wl_llama_batch_prefill": ([_vp, C.POINTER(_u32), C.POINTER(_u32)], _i),
+    "wl_llama_batch_decode": ([_vp, _u32, C.POINTER(_u32), _fp, _fp], _i),
+    "wl_llama_batch_generate": ([_vp, C.POINTER(_u32), C.POINTER(_u32), _u32, C.POINTER(_u32),
+                                 _fp], _i),
     "wl_tp_create": ([_i, _i, _sz, C.POINTER(_vp), C.POINTER(C.c_uint8)], _i),
     "wl_tp_connect": ([_vp, C.POINTER(C.c_uint8)], _i),
     "wl_tp_buffer": ([_vp, _sz], _vp),

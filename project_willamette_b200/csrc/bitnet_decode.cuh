@@ -137,9 +137,10 @@ __global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ O
 
 // ---------------------------------------------------------------------------
 // Attention for one decode position, split over positions (grid: heads x
-// splits; the last CTA of a head combines the splits).
-//  1. NEOX RoPE on every K head (every CTA, redundantly) and on this CTA's Q
-//     head, from the host-filled (cos, sin) table.
+// splits x sequences; the last CTA of a head combines the splits).
+//  1. RoPE (NEOX pairs for BitNet, Norm pairs for VanillaLlama,
+//     cached_forward.rs:505-509) on every K head (every CTA, redundantly) and
+//     on this CTA's Q head, from the host-filled (cos, sin) table.
 //  2. Per-token absmax i8 quantisation of K and V (kv_cache.rs:245-259);
 //     CTA (0, 0) appends them to the cache, every CTA keeps its own copy for
 //     the current position (no cross-CTA dependency on the new entry).
@@ -162,6 +163,14 @@ struct AttnParams {
     uint32_t *counters;         // [n_heads], zero between launches
     uint32_t *status;
     uint32_t exact;             // splits == 1: softmax and V sums in the reference's order
+    // Batched sequences (grid z): sequence z reads q / k / v at + z * qkv_stride,
+    // writes att + z * att_stride, its cache at + z * cache_stride (scales
+    // + z * scale_stride), its position pos[z], partials / counters of its own;
+    // a zero active[z] skips the sequence.  One sequence: zeros / null.
+    uint32_t qkv_stride, att_stride, scale_stride;
+    size_t cache_stride;
+    const uint32_t *active;
+    uint32_t rope_pairs;        // 0: NEOX (j, j + n_rot/2); 1: Norm (2j, 2j + 1)
 };
 
 __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, int8_t *q,
@@ -208,31 +217,45 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
 
     pdl_launch_dependents();
     pdl_wait();
-    const uint32_t pos = *p.pos;
+    const uint32_t z = blockIdx.z;
+    if (p.active && !p.active[z]) return;
+    const uint32_t pos = p.pos[z];
     if (pos >= p.max_seq) {
         if (tid == 0) atomicOr(p.status, WL_DEV_ERR_POSITION);
         return;
     }
+    const float *q_in = p.q + (size_t)z * p.qkv_stride, *k_in = p.k + (size_t)z * p.qkv_stride,
+                *v_in = p.v + (size_t)z * p.qkv_stride;
+    float *att = p.att + (size_t)z * p.att_stride;
+    int8_t *k_cache = p.k_cache + z * p.cache_stride, *v_cache = p.v_cache + z * p.cache_stride;
+    float *k_scale = p.k_scale + (size_t)z * p.scale_stride,
+          *v_scale = p.v_scale + (size_t)z * p.scale_stride;
+    float *partial = p.partial + (size_t)z * gridDim.x * p.splits * (HD + 4u);
+    uint32_t *counters = p.counters + (size_t)z * gridDim.x;
     // one round of independent loads: k, v, this head's q, the RoPE row
     const float2 *cs = p.rope + (size_t)pos * half;
     for (uint32_t i = tid; i < KV; i += blockDim.x) {
-        ks[i] = p.k[i];
-        vs[i] = p.v[i];
+        ks[i] = k_in[i];
+        vs[i] = v_in[i];
     }
-    for (uint32_t i = tid; i < HD; i += blockDim.x) qh[i] = p.q[h * HD + i];
+    for (uint32_t i = tid; i < HD; i += blockDim.x) qh[i] = q_in[h * HD + i];
     for (uint32_t j = tid; j < half; j += blockDim.x) rope[j] = cs[j];
     __syncthreads();
+    // pair (i0, i1) of rotation j: NEOX (j, j + half), Norm (2j, 2j + 1)
+    const uint32_t pstep = p.rope_pairs ? 2u : 1u, poff = p.rope_pairs ? 1u : half;
     for (uint32_t i = tid; i < p.n_kv_heads * half; i += blockDim.x) {
         const uint32_t hk = i / half, j = i % half;
         float *x = ks + hk * HD;
-        const float a = x[j], b = x[j + half], c = rope[j].x, s = rope[j].y;
-        x[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        x[j + half] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+        const uint32_t i0 = j * pstep, i1 = i0 + poff;
+        const float a = x[i0], b = x[i1], c = rope[j].x, s = rope[j].y;
+        x[i0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        x[i1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
     }
     for (uint32_t j = tid; j < half; j += blockDim.x) {
-        const float a = qh[j], b = qh[j + half], c = rope[j].x, s = rope[j].y;
-        qh[j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        qh[j + half] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+        const uint32_t i0 = j * pstep, i1 = i0 + poff;
+        const float a = qh[i0], b = qh[i1], c = rope[j].x, s = rope[j].y;
+        qh[i0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        qh[i1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
     }
     __syncthreads();
     kv_quantise_block(ks, KV, kq, &s_ks, red);
@@ -240,12 +263,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     __syncthreads();
     if (h == 0 && sp == 0) {
         for (uint32_t i = tid; i < KV; i += blockDim.x) {
-            p.k_cache[(size_t)pos * KV + i] = kq[i];
-            p.v_cache[(size_t)pos * KV + i] = vq[i];
+            k_cache[(size_t)pos * KV + i] = kq[i];
+            v_cache[(size_t)pos * KV + i] = vq[i];
         }
         if (tid == 0) {
-            p.k_scale[pos] = s_ks;
-            p.v_scale[pos] = s_vs;
+            k_scale[pos] = s_ks;
+            v_scale[pos] = s_vs;
         }
     }
     // this split's positions [t0, t1)
@@ -255,9 +278,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     // (one memory round trip), then summed in the reference's order
     for (uint32_t i = tid; i < cnt; i += blockDim.x) {
         const uint32_t t = t0 + i;
-        const int8_t *kr = t == pos ? kq + kvh * HD : p.k_cache + (size_t)t * KV + kvh * HD;
-        const float sk = t == pos ? s_ks : p.k_scale[t];
-        vsc[i] = t == pos ? s_vs : p.v_scale[t];
+        const int8_t *kr = t == pos ? kq + kvh * HD : k_cache + (size_t)t * KV + kvh * HD;
+        const float sk = t == pos ? s_ks : k_scale[t];
+        vsc[i] = t == pos ? s_vs : v_scale[t];
         uint4 w[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c)
@@ -310,10 +333,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
             float o = 0.0f;
             for (uint32_t i = 0; i < cnt; ++i) {
                 const uint32_t t = t0 + i;
-                const int8_t vv = t == pos ? vq[kvh * HD + tid] : p.v_cache[(size_t)t * KV + kvh * HD + tid];
+                const int8_t vv = t == pos ? vq[kvh * HD + tid] : v_cache[(size_t)t * KV + kvh * HD + tid];
                 o = __fadd_rn(o, __fmul_rn(scores[i], __fmul_rn((float)vv, vsc[i])));
             }
-            p.att[h * HD + tid] = o;
+            att[h * HD + tid] = o;
         }
         return;
     }
@@ -336,7 +359,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     const uint32_t groups = blockDim.x / HD, d = tid % HD, g = tid / HD;
     float acc = 0.0f;
     if (finite && g < groups) {
-        const int8_t *vbase = p.v_cache + (size_t)kvh * HD + d;
+        const int8_t *vbase = v_cache + (size_t)kvh * HD + d;
         for (uint32_t i0 = g; i0 < cnt; i0 += 8u * groups) {
             int8_t vv[8];
 #pragma unroll
@@ -354,7 +377,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     }
     obuf[tid] = acc;
     __syncthreads();
-    float *part = p.partial + ((size_t)h * p.splits + sp) * (HD + 4u);  // o[HD], max, sum
+    float *part = partial + ((size_t)h * p.splits + sp) * (HD + 4u);  // o[HD], max, sum
     if (tid < HD) {
         float o = obuf[tid];
         for (uint32_t gg = 1; gg < groups; ++gg) o = __fadd_rn(o, obuf[gg * HD + tid]);
@@ -366,7 +389,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(p.counters + h, 1u) == p.splits - 1u ? 1u : 0u;
+    if (tid == 0) s_last = atomicAdd(counters + h, 1u) == p.splits - 1u ? 1u : 0u;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
@@ -374,7 +397,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     // keeps the factors exp(m - M) in comb; then HD/4 threads combine the o
     // rows with float4 loads, eight splits per round of loads.
     const uint32_t S = p.splits, RS = HD + 4u;
-    const float *base = p.partial + (size_t)h * S * RS;
+    const float *base = partial + (size_t)h * S * RS;
     if (tid < 32) {
         float M = -INFINITY;
         for (uint32_t s2 = tid; s2 < S; s2 += 32u) M = fmaxf(M, __ldcg(base + s2 * RS + HD));
@@ -422,9 +445,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
             O.z = __fmul_rn(O.z, inv);
             O.w = __fmul_rn(O.w, inv);
         }
-        reinterpret_cast<float4 *>(p.att + h * HD)[c] = O;
+        reinterpret_cast<float4 *>(att + h * HD)[c] = O;
     }
-    if (tid == 0) p.counters[h] = 0u;  // re-arm for the next launch
+    if (tid == 0) counters[h] = 0u;  // re-arm for the next launch
 }
 
 inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq, uint32_t splits) {
