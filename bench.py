@@ -376,6 +376,8 @@ def run_gpu(args) -> None:
                        reps=max(20, min(args.steps, 200)))
     # ---- BitNet-2B greedy decode (config 2, single GPU)
     decode = decode_bench() if world == 1 else None
+    # ---- SmolLM-135M Q8_0 batched decode (config 5, single GPU)
+    smollm = smollm_bench() if world == 1 else None
     # ---- prefill GEMM (config 3, single GPU)
     gemm = (gemm_bench(torch, dev, L, stream, np.random.default_rng(SEED + 3))
             if world == 1 else None)
@@ -427,6 +429,7 @@ def run_gpu(args) -> None:
             "gpu_launches": launches_per_step * args.steps,
             "lm_head": lm,
             "decode": decode,
+            "smollm_batch_decode": smollm,
             "prefill_gemm": gemm,
             "clocks": clk.summary(),
         }
@@ -567,6 +570,64 @@ def decode_bench(reps: int = 3) -> dict:
             gbs = step_bytes / (ms / n_new * 1e-3) / 1e9
             out[key].update({"bytes_per_token": int(step_bytes), "gbs": round(gbs, 1),
                              "hbm_frac": round(gbs / peaks()["hbm_gbs"], 4)})
+    return out
+
+
+def smollm_bench(reps: int = 2) -> dict:
+    """SmolLM-135M-shaped Q8_0 batched decode -- 32
+    independent sequences, KV caches prefilled to seeded contexts U[64, 1024]
+    (the reference's prompt loop, all sequences in lock step), then 64 greedy
+    tokens each; device time of the 64-step loop (CUDA events), median of
+    `reps` runs.  Fast mode is the timed one; exact mode (bit-exact Q8_0
+    linears, sequential sums) is timed once beside it.  The oracle (all host
+    cores, the reference's per-sequence order) is timed on a short sample."""
+    from project_willamette_b200 import synth
+    from project_willamette_b200.llama import LlamaBatch
+    import oracle
+    n_seqs, n_new = 32, 64
+    m = synth.llama_q8_model(np.random.default_rng(SEED + 11))
+    c = m["config"]
+    rng = np.random.default_rng(SEED + 12)
+    ctx = rng.integers(64, 1025, n_seqs)
+    prompts = [rng.integers(0, c["vocab"], int(n)) for n in ctx]
+    E, F, kvd = c["n_embd"], c["n_ff"], c["n_kv_heads"] * c["head_dim"]
+    # bytes one decode step (32 tokens) must read: every Q8_0 linear and the
+    # lm-head once (34 bytes per 32 weights), each sequence's i8 KV cache of
+    # its average context (+ the two f32 scales per position and layer)
+    lin = c["n_layers"] * (E * (E + 2 * kvd + E + 2 * F) + F * E) // 32 * 34
+    lm = c["vocab"] * E // 32 * 34
+    avg_ctx = float(np.mean(ctx)) + (n_new - 1) / 2.0
+    kv_bytes = c["n_layers"] * n_seqs * avg_ctx * (2 * kvd + 8)
+    step_bytes = lin + lm + kv_bytes
+    out = {"config": "smollm135m: 30 layers, d 576, 9/3 heads x 64, d_ff 1536 (SiLU), vocab "
+                     "49152, every tensor Q8_0; 32 sequences, contexts U[64,1024] seeded, "
+                     "64 greedy tokens each; KV i8 per-token absmax (the reference's layout)",
+           "sequences": n_seqs, "new_tokens": n_new, "mean_context": float(np.mean(ctx)),
+           "bytes_per_step": int(step_bytes)}
+    for exact in (False, True):
+        g = LlamaBatch(m, n_seqs, exact=exact)
+        times, walls = [], []
+        for r in range(reps if not exact else 1):
+            g.reset()
+            g.prefill(prompts)
+            t0 = time.perf_counter()
+            ids, ms = g.decode(n_new, timed=True)
+            walls.append(time.perf_counter() - t0)
+            times.append(ms)
+        g.close()
+        ms = statistics.median(times)
+        gbs = step_bytes / (ms / n_new * 1e-3) / 1e9
+        out["exact" if exact else "fast"] = {
+            "tok_s": round(n_seqs * n_new / (ms * 1e-3), 1), "ms_per_step": round(ms / n_new, 4),
+            "e2e_tok_s": round(n_seqs * n_new / statistics.median(walls), 1),
+            "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks()["hbm_gbs"], 4)}
+    # the oracle: one sequence, 16 prompt tokens + 8 greedy ones (24 forwards)
+    o = oracle.BitnetOracle(m)
+    t0 = time.perf_counter()
+    o.generate(prompts[0][:16], 8)
+    dt = time.perf_counter() - t0
+    out["cpu_oracle"] = {"tok_s": round(24 / dt, 2), "cores": os.cpu_count(),
+                         "sample": "1 sequence: 16 prompt + 8 greedy forwards at the full shapes"}
     return out
 
 

@@ -16,16 +16,18 @@
 //     positions come from the cache, the current one from shared memory, so
 //     no CTA waits on another's append.
 //  3. Scores, one thread per position: the position's K head row (HD bytes)
-//     is loaded in one round and dotted with every q head of the group.
+//     is loaded in one round and dotted with every q head of the group (q
+//     read as float4 broadcasts).
 //  4. Softmax statistics per q head (max, sum of exp) in block reductions.
-//  5. V: a thread owns 16 dimensions of one position per round (one 16-byte
-//     load) and accumulates them for every q head; positions are reduced
-//     over lanes, then warps.
+//  5. V: each warp takes every 8th position, a lane owns HD/32 dimensions of
+//     the row (one coalesced row load per warp and position) and accumulates
+//     them for every q head; the 8 warps' sums meet in shared memory.
 //  6. splits > 1: unnormalised partials (o, max, sum) per split, the last
 //     CTA of the (sequence, KV head) combines them.
 // Sums run as trees and products are fused (the engine's fast mode); the
 // exact mode keeps attn_decode_kernel.  A non-finite score maximum gives a
-// zero output, as in the reference.
+// zero output, as in the reference.  Templated on head_dim and group so
+// every loop has a static trip count.
 #pragma once
 
 #include <cstdint>
@@ -53,12 +55,14 @@ inline size_t attn_gqa_smem_bytes(uint32_t kv, uint32_t hd, uint32_t group, uint
     return f * 4u + 2u * hd + 16u;              // + the current position's i8 K / V slice
 }
 
+template <uint32_t HD, uint32_t G>
 __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __grid_constant__ AttnParams p) {
+    static_assert((HD == 64 || HD == 128) && G >= 1 && G <= AB_MAX_GROUP, "shape");
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[AB_WARPS * 2 * AB_MAX_GROUP];
     __shared__ float s_sc[2];
     __shared__ uint32_t s_last;
-    const uint32_t HD = p.head_dim, KV = p.n_kv_heads * HD, half = p.n_rot / 2u, G = p.group;
+    const uint32_t KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
     const uint32_t kvh = blockIdx.x, z = blockIdx.y, sp = blockIdx.z, S = gridDim.z;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t chunk_max = ((p.max_seq + S - 1) / S + 3u) & ~3u;
@@ -163,150 +167,147 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
         const int8_t *kr = t == pos ? kq : k_cache + (size_t)t * KV + kvh * HD;
         const float sk = t == pos ? sk_cur : k_scale[t];
         vsc[i] = t == pos ? sv_cur : v_scale[t];
-        float d[AB_MAX_GROUP];
+        uint4 w[HD / 16];  // the whole head row in one round of loads
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) d[g] = 0.0f;
-        uint4 w[16];  // the whole head row in one round of loads (HD <= 256)
+        for (uint32_t c = 0; c < HD / 16; ++c) w[c] = *reinterpret_cast<const uint4 *>(kr + c * 16u);
+        float d[G];
 #pragma unroll
-        for (uint32_t c = 0; c < 16u; ++c)
-            if (c * 16u < HD) w[c] = *reinterpret_cast<const uint4 *>(kr + c * 16u);
+        for (uint32_t g = 0; g < G; ++g) d[g] = 0.0f;
 #pragma unroll
-        for (uint32_t c = 0; c < 16u; ++c) {
-            if (c * 16u >= HD) break;
+        for (uint32_t c = 0; c < HD / 16; ++c) {
             const uint32_t wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const float k8 = __fmul_rn((float)(int8_t)(wv[e >> 2] >> (8 * (e & 3))), sk);
+            for (uint32_t e4 = 0; e4 < 4; ++e4) {
+                float k8[4];
 #pragma unroll
-                for (uint32_t g = 0; g < AB_MAX_GROUP; ++g)
-                    if (g < G) d[g] = __fmaf_rn(qg[g * HD + c * 16u + e], k8, d[g]);
+                for (int e = 0; e < 4; ++e)
+                    k8[e] = __fmul_rn((float)(int8_t)(wv[e4] >> (8 * e)), sk);
+#pragma unroll
+                for (uint32_t g = 0; g < G; ++g) {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qg + g * HD + c * 16u + e4 * 4u);
+                    d[g] = __fmaf_rn(q4.x, k8[0], d[g]);
+                    d[g] = __fmaf_rn(q4.y, k8[1], d[g]);
+                    d[g] = __fmaf_rn(q4.z, k8[2], d[g]);
+                    d[g] = __fmaf_rn(q4.w, k8[3], d[g]);
+                }
             }
         }
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g)
-            if (g < G) scores[g * chunk_max + i] = __fmul_rn(d[g], p.scale);
+        for (uint32_t g = 0; g < G; ++g) scores[g * chunk_max + i] = __fmul_rn(d[g], p.scale);
     }
     __syncthreads();
     // 4. per-head max and sum of exp
-    float mx[AB_MAX_GROUP], sum[AB_MAX_GROUP];
+    float mx[G], sum[G];
     {
-        float m[AB_MAX_GROUP];
+        float m[G];
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) m[g] = -INFINITY;
+        for (uint32_t g = 0; g < G; ++g) m[g] = -INFINITY;
         for (uint32_t i = tid; i < cnt; i += AB_THREADS)
 #pragma unroll
-            for (uint32_t g = 0; g < AB_MAX_GROUP; ++g)
-                if (g < G) m[g] = fmaxf(m[g], scores[g * chunk_max + i]);
+            for (uint32_t g = 0; g < G; ++g)
+                m[g] = fmaxf(m[g], scores[g * chunk_max + i]);
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) {
+        for (uint32_t g = 0; g < G; ++g) {
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], off));
-            if (lane == 0) red[warp * AB_MAX_GROUP + g] = m[g];
+            if (lane == 0) red[warp * G + g] = m[g];
         }
         __syncthreads();
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) {
+        for (uint32_t g = 0; g < G; ++g) {
             float t = red[g];
-            for (uint32_t w = 1; w < AB_WARPS; ++w) t = fmaxf(t, red[w * AB_MAX_GROUP + g]);
+            for (uint32_t w = 1; w < AB_WARPS; ++w) t = fmaxf(t, red[w * G + g]);
             mx[g] = t;
         }
         __syncthreads();
-        float l[AB_MAX_GROUP];
+        float l[G];
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) l[g] = 0.0f;
+        for (uint32_t g = 0; g < G; ++g) l[g] = 0.0f;
         for (uint32_t i = tid; i < cnt; i += AB_THREADS)
 #pragma unroll
-            for (uint32_t g = 0; g < AB_MAX_GROUP; ++g)
-                if (g < G) {
+            for (uint32_t g = 0; g < G; ++g)
+                {
                     const float e = isfinite(mx[g]) ? expf(scores[g * chunk_max + i] - mx[g]) : 0.0f;
                     scores[g * chunk_max + i] = __fmul_rn(e, vsc[i]);  // the V scale folded in
                     l[g] += e;
                 }
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) {
+        for (uint32_t g = 0; g < G; ++g) {
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) l[g] += __shfl_xor_sync(0xffffffffu, l[g], off);
-            if (lane == 0) red[warp * AB_MAX_GROUP + g] = l[g];
+            if (lane == 0) red[warp * G + g] = l[g];
         }
         __syncthreads();
 #pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) {
+        for (uint32_t g = 0; g < G; ++g) {
             float t = red[g];
-            for (uint32_t w = 1; w < AB_WARPS; ++w) t += red[w * AB_MAX_GROUP + g];
+            for (uint32_t w = 1; w < AB_WARPS; ++w) t += red[w * G + g];
             sum[g] = t;
         }
     }
-    // 5. o[g][d] = sum_i w_i * v8[i][d]: thread = (position lane, 16-dim quad)
-    const uint32_t DQ = HD / 16u, PL = AB_THREADS / DQ;  // quads per row, positions per round
-    const uint32_t dq = tid % DQ, pl = tid / DQ;
-    float acc[AB_MAX_GROUP][16];
+    // 5. o[g][d] = sum_i w_i * v8[i][d]: warp = every 8th position, lane =
+    //    HD/32 dimensions (a 64-byte row of HD = 64 is one coalesced load)
+    constexpr uint32_t DL = HD / 32u;  // dimensions per lane
+    float acc[G][DL];
 #pragma unroll
-    for (uint32_t g = 0; g < AB_MAX_GROUP; ++g)
+    for (uint32_t g = 0; g < G; ++g)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) acc[g][e] = 0.0f;
-    for (uint32_t i0 = pl; i0 < cnt; i0 += 4u * PL) {
-        uint4 w[4];
+        for (uint32_t e = 0; e < DL; ++e) acc[g][e] = 0.0f;
+    for (uint32_t i0 = warp; i0 < cnt; i0 += 8u * AB_WARPS) {
+        uint32_t w[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint32_t i = i0 + (uint32_t)u * PL, t = t0 + i;
-            w[u] = make_uint4(0u, 0u, 0u, 0u);
-            if (i < cnt)
-                w[u] = *reinterpret_cast<const uint4 *>(t == pos ? vq + dq * 16u
-                                                                 : v_cache + (size_t)t * KV + kvh * HD + dq * 16u);
+        for (uint32_t u = 0; u < 8; ++u) {
+            const uint32_t i = i0 + u * AB_WARPS, t = t0 + i;
+            w[u] = 0u;
+            if (i < cnt) {
+                const int8_t *vr = t == pos ? vq : v_cache + (size_t)t * KV + kvh * HD;
+                if (DL == 4) w[u] = reinterpret_cast<const uint32_t *>(vr)[lane];
+                else w[u] = reinterpret_cast<const uint16_t *>(vr)[lane];
+            }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint32_t i = i0 + (uint32_t)u * PL;
+        for (uint32_t u = 0; u < 8; ++u) {
+            const uint32_t i = i0 + u * AB_WARPS;
             if (i >= cnt) break;
-            const uint32_t wv[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+            float v8[DL];
 #pragma unroll
-            for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) {
-                if (g >= G) break;
+            for (uint32_t e = 0; e < DL; ++e) v8[e] = (float)(int8_t)(w[u] >> (8 * e));
+#pragma unroll
+            for (uint32_t g = 0; g < G; ++g) {
                 const float wt = scores[g * chunk_max + i];
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    acc[g][e] = __fmaf_rn(wt, (float)(int8_t)(wv[e >> 2] >> (8 * (e & 3))), acc[g][e]);
+                for (uint32_t e = 0; e < DL; ++e) acc[g][e] = __fmaf_rn(wt, v8[e], acc[g][e]);
             }
         }
     }
-    // reduce over the position lanes of a warp (lanes with the same quad)
 #pragma unroll
-    for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) {
-        if (g >= G) break;
+    for (uint32_t g = 0; g < G; ++g)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            float v = acc[g][e];
-            for (uint32_t off = DQ; off < 32u; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            acc[g][e] = v;
-        }
-    }
-    if (lane < DQ) {
-#pragma unroll
-        for (uint32_t g = 0; g < AB_MAX_GROUP; ++g) {
-            if (g >= G) break;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) vpart[((size_t)warp * G + g) * HD + dq * 16u + e] = acc[g][e];
-        }
-    }
+        for (uint32_t e = 0; e < DL; ++e) vpart[((size_t)warp * G + g) * HD + lane * DL + e] = acc[g][e];
     __syncthreads();
     const uint32_t RS = HD + 4u;  // partial row: o[HD], max, sum
     float *part = p.partial + (((size_t)z * gridDim.x + kvh) * S + sp) * G * RS;
-    for (uint32_t i = tid; i < G * HD; i += AB_THREADS) {
-        const uint32_t g = i / HD, d = i % HD;
-        float o = 0.0f;
-        for (uint32_t w = 0; w < AB_WARPS; ++w) o += vpart[((size_t)w * G + g) * HD + d];
-        if (S == 1) {
-            const float L = sum[g];
-            o = !isfinite(mx[g]) ? 0.0f : (L > 0.0f ? __fdiv_rn(o, L) : o);
-            p.att[(size_t)z * p.att_stride + (kvh * G + g) * HD + d] = o;
-        } else {
-            part[g * RS + d] = o;
+#pragma unroll
+    for (uint32_t g = 0; g < G; ++g)
+        for (uint32_t d = tid; d < HD; d += AB_THREADS) {
+            float o = 0.0f;
+#pragma unroll
+            for (uint32_t w = 0; w < AB_WARPS; ++w) o += vpart[((size_t)w * G + g) * HD + d];
+            if (S == 1) {
+                const float L = sum[g];
+                o = !isfinite(mx[g]) ? 0.0f : (L > 0.0f ? __fdiv_rn(o, L) : o);
+                p.att[(size_t)z * p.att_stride + (kvh * G + g) * HD + d] = o;
+            } else {
+                part[g * RS + d] = o;
+            }
         }
-    }
     if (S == 1) return;
-    if (tid < G) {
-        part[tid * RS + HD] = mx[tid];
-        part[tid * RS + HD + 1] = sum[tid];
+    if (tid == 0) {
+#pragma unroll
+        for (uint32_t g = 0; g < G; ++g) {
+            part[g * RS + HD] = mx[g];
+            part[g * RS + HD + 1] = sum[g];
+        }
     }
     __threadfence();
     __syncthreads();

@@ -152,7 +152,14 @@ int configure_kernels() {
                             (const void *)q8_batch_kernel<4, true>,
                             (const void *)q8_batch_kernel<8, true>,
                             (const void *)q8_batch_kernel<32, true>,
-                            (const void *)attn_gqa_batch_kernel};
+                            (const void *)attn_gqa_batch_kernel<64, 1>,
+                            (const void *)attn_gqa_batch_kernel<64, 2>,
+                            (const void *)attn_gqa_batch_kernel<64, 3>,
+                            (const void *)attn_gqa_batch_kernel<64, 4>,
+                            (const void *)attn_gqa_batch_kernel<128, 1>,
+                            (const void *)attn_gqa_batch_kernel<128, 2>,
+                            (const void *)attn_gqa_batch_kernel<128, 3>,
+                            (const void *)attn_gqa_batch_kernel<128, 4>};
     for (const void *k : others)
         WL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      WL_MAX_DYN_SMEM));
@@ -2476,8 +2483,8 @@ struct wl_llama_batch {
     float *attn_norm = nullptr, *ffn_norm = nullptr, *out_norm = nullptr;
     uint8_t *emb = nullptr;                   // repacked tied embedding / lm-head
     float2 *rope = nullptr;
-    int8_t *kq = nullptr, *vq = nullptr;      // [seq][layer][max_seq][KV]
-    float *ks = nullptr, *vs = nullptr;       // [seq][layer][max_seq]
+    int8_t *kq = nullptr, *vq = nullptr;      // [layer][seq][max_seq][KV]
+    float *ks = nullptr, *vs = nullptr;       // [layer][seq][max_seq]
     float *hidden = nullptr, *qkv = nullptr, *att = nullptr, *fused = nullptr,
           *final_h = nullptr;
     uint32_t *d_tokens = nullptr, *d_active = nullptr, *d_ones = nullptr, *d_pos = nullptr,
@@ -2505,6 +2512,19 @@ const QbKernel kQb[2][4] = {
     {q8_batch_kernel<1, true>, q8_batch_kernel<4, true>, q8_batch_kernel<8, true>,
      q8_batch_kernel<32, true>}};
 constexpr uint32_t kQbTg[4] = {1, 4, 8, 32};
+
+using AttnKernel = void (*)(AttnParams);
+// fast-mode batched attention for head_dim 64 / 128 and 1..4 q heads per KV head
+AttnKernel gqa_attn_kernel(uint32_t hd, uint32_t group) {
+    static const AttnKernel k64[4] = {attn_gqa_batch_kernel<64, 1>, attn_gqa_batch_kernel<64, 2>,
+                                      attn_gqa_batch_kernel<64, 3>, attn_gqa_batch_kernel<64, 4>};
+    static const AttnKernel k128[4] = {attn_gqa_batch_kernel<128, 1>, attn_gqa_batch_kernel<128, 2>,
+                                       attn_gqa_batch_kernel<128, 3>, attn_gqa_batch_kernel<128, 4>};
+    if (group < 1 || group > AB_MAX_GROUP) return nullptr;
+    if (hd == 64) return k64[group - 1];
+    if (hd == 128) return k128[group - 1];
+    return nullptr;
+}
 
 int lb_validate(const wl_bitnet_config *c, uint32_t n_seqs) {
     if (!c) return fail(WL_ERR_INVALID_ARGUMENT, "config is NULL");
@@ -2628,7 +2648,9 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
         ap.k = m->qkv + E;
         ap.v = m->qkv + E + KV;
         ap.att = m->att;
-        const size_t cache_l = (size_t)l * c.max_seq;
+        // cache layout [layer][sequence][position][KV]: one layer's caches of
+        // every sequence are contiguous
+        const size_t cache_l = (size_t)l * S * c.max_seq;
         ap.k_cache = m->kq + cache_l * KV;
         ap.v_cache = m->vq + cache_l * KV;
         ap.k_scale = m->ks + cache_l;
@@ -2648,13 +2670,13 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
         ap.exact = c.exact;
         ap.qkv_stride = QS;
         ap.att_stride = E;
-        ap.scale_stride = c.n_layers * c.max_seq;
-        ap.cache_stride = (size_t)c.n_layers * c.max_seq * KV;
+        ap.scale_stride = c.max_seq;
+        ap.cache_stride = (size_t)c.max_seq * KV;
         ap.active = m->d_active;
         ap.rope_pairs = 1;  // RopeType::Norm for VanillaLlama (cached_forward.rs:505-509)
         if (m->gqa_attn) {
-            WL_CUDA(launch(attn_gqa_batch_kernel, dim3(c.n_kv_heads, S, m->splits), dim3(AB_THREADS),
-                           attn_smem, s, true, ap));
+            WL_CUDA(launch(gqa_attn_kernel(HD, c.n_heads / c.n_kv_heads), dim3(c.n_kv_heads, S, m->splits),
+                           dim3(AB_THREADS), attn_smem, s, true, ap));
         } else {
             WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits, S), dim3(ATTN_THREADS),
                            attn_smem, s, true, ap));
@@ -2787,9 +2809,9 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
     // for groups of up to 4 q heads, splits filling about two CTAs per SM.
     const uint32_t group = c.n_heads / c.n_kv_heads;
     m->splits = 1;
-    if (!c.exact && group <= AB_MAX_GROUP) {
-        uint32_t sp = std::max<uint32_t>(1u, (2u * (uint32_t)cx.sm_count + c.n_kv_heads * S - 1) /
-                                                 (c.n_kv_heads * S));
+    if (!c.exact && gqa_attn_kernel(c.head_dim, group)) {
+        // as many splits as keep every CTA resident at once (two per SM)
+        uint32_t sp = std::max<uint32_t>(1u, (2u * (uint32_t)cx.sm_count) / (c.n_kv_heads * S));
         sp = std::min<uint32_t>(sp, std::min<uint32_t>(64u / group, (c.max_seq + 63) / 64));
         sp = std::max<uint32_t>(sp, 1u);
         if (attn_gqa_smem_bytes(KV, c.head_dim, group, c.max_seq, sp) <= (size_t)WL_MAX_DYN_SMEM) {
