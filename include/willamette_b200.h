@@ -329,6 +329,19 @@ typedef struct {
 typedef struct wl_bitnet wl_bitnet;
 int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *weights,
                      wl_bitnet **out);
+/* Tensor-parallel engine, one per rank of a connected group (every rank
+ * passes the same config and full host weights): each BitLinear's output
+ * rows are split evenly over the ranks and gathered by the matvec kernels
+ * themselves (peer stores over NVLink, bounded in-kernel waits); norms,
+ * RoPE, attention and the KV cache are replicated; the lm-head is split by
+ * vocabulary rows and reduced with (max, lowest index) keys.  The engine
+ * places its gathered vectors at the start of the group's caller region,
+ * which must hold wl_bitnet_tp_sym_bytes(cfg) bytes and is the engine's
+ * while it lives.  Results equal the single-GPU engine's bit for bit.
+ * Every rank must make the same sequence of calls.  `persistent` must be 0. */
+int wl_bitnet_create_tp(const wl_bitnet_config *cfg, const wl_bitnet_weights *weights,
+                        wl_tp_group *group, wl_bitnet **out);
+size_t wl_bitnet_tp_sym_bytes(const wl_bitnet_config *cfg);
 int wl_bitnet_destroy(wl_bitnet *model);
 /* Empty the KV cache (position 0). */
 int wl_bitnet_reset(wl_bitnet *model);

@@ -134,6 +134,9 @@ PROTOTYPES = {
     "wl_dev_q8_0_matvec": ([_vp, _u32, _u32, _vp, _vp, _vp], _i),
     "wl_bitnet_create": ([C.POINTER(WlBitnetConfig), C.POINTER(WlBitnetWeights), C.POINTER(_vp)],
                          _i),
+    "wl_bitnet_create_tp": ([C.POINTER(WlBitnetConfig), C.POINTER(WlBitnetWeights), _vp,
+                             C.POINTER(_vp)], _i),
+    "wl_bitnet_tp_sym_bytes": ([C.POINTER(WlBitnetConfig)], _sz),
     "wl_bitnet_destroy": ([_vp], _i),
     "wl_bitnet_reset": ([_vp], _i),
     "wl_bitnet_position": ([_vp], _u32),

@@ -35,9 +35,12 @@ def _fp(a: Optional[np.ndarray]):
 
 class BitNet:
     def __init__(self, model: dict, device: int = 0, exact: bool = False,
-                 persistent: bool = False):
+                 persistent: bool = False, tp=None):
+        """tp: a connected ``tp.TPGroup`` (one per rank) for the tensor-parallel
+        engine; its symmetric region must hold ``BitNet.tp_sym_bytes(model)``."""
         L = lib()
-        _check(L.wl_init(device))
+        if tp is None:
+            _check(L.wl_init(device))
         c = model["config"]
         self.cfg = WlBitnetConfig(**{k: c[k] for k in _CFG_KEYS}, exact=int(exact),
                                   persistent=int(persistent))
@@ -51,8 +54,19 @@ class BitNet:
         w = WlBitnetWeights(ptrs, _fp(self._keep[1]), _fp(self._keep[2]), _fp(self._keep[3]),
                             self._keep[4].ctypes.data)
         self._h = C.c_void_p()
-        _check(L.wl_bitnet_create(C.byref(self.cfg), C.byref(w), C.byref(self._h)))
+        if tp is None:
+            _check(L.wl_bitnet_create(C.byref(self.cfg), C.byref(w), C.byref(self._h)))
+        else:
+            _check(L.wl_bitnet_create_tp(C.byref(self.cfg), C.byref(w), tp._g, C.byref(self._h)))
+        self._tp = tp  # the engine's gathered vectors live in the group's block
         self._keep = None  # the library holds device copies
+
+    @staticmethod
+    def tp_sym_bytes(model: dict) -> int:
+        """Symmetric-region bytes the tensor-parallel engine needs."""
+        c = model["config"]
+        cfg = WlBitnetConfig(**{k: c[k] for k in _CFG_KEYS}, exact=0, persistent=0)
+        return int(lib().wl_bitnet_tp_sym_bytes(C.byref(cfg)))
 
     @property
     def persistent(self) -> bool:

@@ -26,6 +26,7 @@
 #include <cstdint>
 
 #include "q6k_lmhead.cuh"
+#include "tp.cuh"
 #include "wl_ptx.cuh"
 
 namespace wl {
@@ -171,6 +172,9 @@ struct AttnParams {
     size_t cache_stride;
     const uint32_t *active;
     uint32_t rope_pairs;        // 0: NEOX (j, j + n_rot/2); 1: Norm (2j, 2j + 1)
+    // Tensor parallel: q / k / v were gathered from every rank's row slice;
+    // with tp.wait set, every CTA first waits (bounded) for every rank's stores.
+    TpParams tp;
 };
 
 __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, int8_t *q,
@@ -217,6 +221,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
 
     pdl_launch_dependents();
     pdl_wait();
+    if (p.tp.world && p.tp.wait) {
+        if (tid == 0 && !tp_wait(p.tp)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
+        __syncthreads();
+    }
     const uint32_t z = blockIdx.z;
     if (p.active && !p.active[z]) return;
     const uint32_t pos = p.pos[z];

@@ -518,7 +518,14 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             const float combined = __fmul_rn(job.w_scale, act_scale);
             const float yv = __fmul_rn(combined, __int2float_rn(dot));
             if (p.tp.world) {
-                tp_store_all(p.tp, job.y + job.row_off + local, yv);
+                // gathered output: every rank's replica of y gets the row
+                // (residual: this rank's replica + y, the same on every rank)
+                float v = yv;
+                if (p.residual) {
+                    v = __fadd_rn(job.y[job.row_off + local], yv);
+                    if (p.finite_flag && !isfinite(v)) atomicOr(p.status, p.finite_flag);
+                }
+                tp_store_all(p.tp, job.y + job.row_off + local, v);
             } else if (p.residual) {
                 float *dst = job.y + job.row_off + local;
                 const float nv = __fadd_rn(*dst, yv);

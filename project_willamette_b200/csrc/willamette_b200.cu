@@ -1239,6 +1239,13 @@ struct wl_bitnet {
     uint32_t pos = 0;                      // host mirror of the cache position
     bool have_hidden = false;              // final_h holds a forward's output
     cudaGraphExec_t g_forward = nullptr, g_step = nullptr, g_last = nullptr;
+    // tensor parallel (world > 1): this rank's row slice of every BitLinear,
+    // hidden / q|k|v / gate|up in the group's symmetric block (gathered by
+    // the matvec kernels), a vocab shard of the lm-head
+    wl_tp_group *tpg = nullptr;
+    TpParams tp{};
+    std::vector<uint32_t> row_offs;        // n_layers * 7: first global row of the slice
+    uint32_t vocab_off = 0, vocab_shard = 0;
 };
 
 namespace {
@@ -1291,9 +1298,11 @@ void bn_rope_table(const wl_bitnet_config &c, std::vector<float2> &t) {
     }
 }
 
+// Tensor parallel: this rank's row slices, outputs stored to every rank;
+// tp_wait: the input x was gathered, wait for every rank's stores first.
 int bn_matvec(wl_bitnet *m, uint32_t l, int first, int count, uint32_t K, const float *x,
               float *const *ys, uint32_t pre, const float *norm_w, const float *x2,
-              uint32_t residual, uint32_t finite_flag, cudaStream_t s) {
+              uint32_t residual, uint32_t finite_flag, cudaStream_t s, bool tp_wait = false) {
     wl_i2s_dev_weight w[3];
     for (int j = 0; j < count; ++j) {
         w[j] = m->mats[(size_t)l * BN_MATS + first + j];
@@ -1301,6 +1310,12 @@ int bn_matvec(wl_bitnet *m, uint32_t l, int first, int count, uint32_t K, const 
         w[j].acc = nullptr;
     }
     I2sLaunch L;
+    TpParams tp = m->tp;
+    if (m->tpg) {
+        tp.wait = tp_wait ? 1u : 0u;
+        L.tp = &tp;
+        L.row_offs = m->row_offs.data() + (size_t)l * BN_MATS + first;
+    }
     L.w = w;
     L.nw = (uint32_t)count;
     L.K = K;
@@ -1446,7 +1461,8 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
     for (uint32_t l = 0; l < c.n_layers; ++l) {
         const float *nrm = m->norms + (size_t)l * (3 * E + F);
         float *qkv[3] = {m->q, m->k, m->v};
-        if ((rc = bn_matvec(m, l, 0, 3, E, m->hidden, qkv, I2S_PRE_RMSNORM, nrm, nullptr, 0, 0, s)))
+        if ((rc = bn_matvec(m, l, 0, 3, E, m->hidden, qkv, I2S_PRE_RMSNORM, nrm, nullptr, 0, 0, s,
+                            true)))
             return rc;
         AttnParams ap{};  // one sequence: no batch strides, NEOX pairs
         ap.q = m->q;
@@ -1470,6 +1486,10 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
         ap.counters = m->attn_counters;
         ap.status = status;
         ap.exact = c.exact;
+        if (m->tpg) {  // q / k / v were gathered from every rank
+            ap.tp = m->tp;
+            ap.tp.wait = 1u;
+        }
         WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits), dim3(ATTN_THREADS),
                        attn_smem, s, true, ap));
         float *o[1] = {m->hidden};
@@ -1477,11 +1497,17 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
             return rc;
         float *gu[2] = {m->gate, m->up};
         if ((rc = bn_matvec(m, l, 4, 2, E, m->hidden, gu, I2S_PRE_RMSNORM, nrm + 2 * E, nullptr, 0,
-                            0, s)))
+                            0, s, true)))
             return rc;
         if ((rc = bn_matvec(m, l, 6, 1, F, m->gate, o, I2S_PRE_RELU2_RMSNORM, nrm + 3 * E, m->up, 1,
-                            WL_DEV_ERR_NONFINITE, s)))
+                            WL_DEV_ERR_NONFINITE, s, true)))
             return rc;
+    }
+    if (m->tpg) {  // the final hidden was gathered by the last down projection
+        TpParams tp = m->tp;
+        tp.wait = 1u;
+        tp_wait_kernel<<<1, 32, 0, s>>>(tp, status);
+        WL_CUDA(cudaGetLastError());
     }
     OutNormParams op;
     op.hidden = m->hidden;
@@ -1497,6 +1523,19 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
 
 // Greedy head on final_h -> *d_token (lm_head.rs:29-108 + :161-174).
 int bn_enqueue_head(wl_bitnet *m, cudaStream_t s) {
+    if (m->tpg) {  // this rank's vocab shard, keys reduced across ranks
+        uint32_t *status = status_ptr();
+        if (!status) return WL_ERR_NO_DEVICE;
+        TpParams tp = m->tp;
+        tp.wait = 0u;
+        const uint8_t *shard = m->q6k + (size_t)m->vocab_off * q6k_row_stride(m->cfg.n_embd / 256u);
+        int rc = launch_q6k_tp(shard, m->cfg.n_embd, m->vocab_shard, m->vocab_off, m->final_h, 1,
+                               m->d_token, m->lm_scratch, s, &tp);
+        if (rc) return rc;
+        q6k_tp_finalize_kernel<<<1, 64, 0, s>>>(tp, 1, m->d_token, status);
+        WL_CUDA(cudaGetLastError());
+        return WL_OK;
+    }
     return launch_q6k(m->q6k, m->cfg.n_embd, m->cfg.vocab, m->final_h, 1, nullptr, m->d_token,
                       m->lm_scratch, s, true);
 }
@@ -2199,11 +2238,44 @@ int wl_tp_q6k_lm_head_greedy(wl_tp_group *g, const uint8_t *packed_shard, uint32
 }
 
 // ------------------------------------------------------- BitNet decode engine
-int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_bitnet **out) {
+}  // extern "C"
+
+namespace {
+
+// Caller-region bytes of a tensor-parallel engine's symmetric buffers:
+// hidden (E), q | k | v (E + 2 KV), gate | up (2 F), each 256-byte aligned.
+size_t bn_sym_layout(const wl_bitnet_config &c, size_t *off_q, size_t *off_g) {
+    auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t E = c.n_embd, KV = bn_kv(c), F = c.n_ff;
+    *off_q = up(E * 4);
+    *off_g = *off_q + up((E + 2 * KV) * 4);
+    return *off_g + up(2 * F * 4);
+}
+
+int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_group *tpg,
+              wl_bitnet **out) {
     if (!out) return fail(WL_ERR_INVALID_ARGUMENT, "out is NULL");
     *out = nullptr;
     int rc = bn_validate(cfg);
     if (rc) return rc;
+    TpParams tpp{};
+    if (tpg) {
+        if ((rc = tp_params(tpg, false, &tpp))) return rc;
+        if (cfg->persistent)
+            return fail(WL_ERR_INVALID_ARGUMENT, "the persistent engine runs on one GPU only");
+        size_t oq, og;
+        const size_t need = bn_sym_layout(*cfg, &oq, &og);
+        if (TP_HEADER_BYTES + need > tpg->bytes)
+            return fail(WL_ERR_INVALID_ARGUMENT, "symmetric block too small: %zu bytes needed",
+                        need);
+        if (tpg->device != ctx().device)
+            return fail(WL_ERR_INVALID_ARGUMENT, "group is on device %d, library on %d", tpg->device,
+                        ctx().device);
+    }
+    const uint32_t world = tpg ? (uint32_t)tpg->world : 1u, rank = tpg ? (uint32_t)tpg->rank : 0u;
+    // rank's slice [lo, hi) of n rows
+    auto slice_lo = [&](uint32_t n) { return (uint32_t)((uint64_t)n * rank / world); };
+    auto slice_hi = [&](uint32_t n) { return (uint32_t)((uint64_t)n * (rank + 1) / world); };
     if (!w || !w->w || !w->w_scale || !w->norms || !w->output_norm || !w->token_embd)
         return fail(WL_ERR_INVALID_ARGUMENT, "weights: NULL pointer");
     const wl_bitnet_config c = *cfg;
@@ -2231,8 +2303,10 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
     std::vector<size_t> off(c.n_layers * BN_MATS);
     for (uint32_t i = 0; i < c.n_layers * BN_MATS; ++i) {
         off[i] = total;
-        total += ((size_t)ins[i % BN_MATS] / 4 * outs[i % BN_MATS] + 255) & ~(size_t)255;
+        const uint32_t N = outs[i % BN_MATS];
+        total += ((size_t)ins[i % BN_MATS] / 4 * (slice_hi(N) - slice_lo(N)) + 255) & ~(size_t)255;
     }
+    total = std::max<size_t>(total, 256);
     const size_t nrm = (size_t)c.n_layers * (3 * E + F);
     const size_t q6_raw = (size_t)c.vocab * (E / 256) * 210;
     const size_t q6_packed = (size_t)c.vocab * q6k_row_stride(E / 256);
@@ -2255,13 +2329,26 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
     BN_ALLOC(m->vq, kv_bytes);
     BN_ALLOC(m->ks, kvs * 4);
     BN_ALLOC(m->vs, kvs * 4);
-    BN_ALLOC(m->hidden, (size_t)E * 4);
-    BN_ALLOC(m->q, (size_t)(E + 2 * KV) * 4);  // q | k | v, contiguous
+    if (tpg) {  // gathered vectors live in the group's symmetric block
+        size_t oq, og;
+        bn_sym_layout(c, &oq, &og);
+        uint8_t *base = reinterpret_cast<uint8_t *>(wl_tp_buffer(tpg, 0));
+        m->tpg = tpg;
+        m->tp = tpp;
+        m->hidden = reinterpret_cast<float *>(base);
+        m->q = reinterpret_cast<float *>(base + oq);
+        m->gate = reinterpret_cast<float *>(base + og);
+    } else {
+        BN_ALLOC(m->hidden, (size_t)E * 4);
+        BN_ALLOC(m->q, (size_t)(E + 2 * KV) * 4);  // q | k | v, contiguous
+        BN_ALLOC(m->gate, (size_t)2 * F * 4);       // gate | up, contiguous
+    }
     m->k = m->q + E;
     m->v = m->k + KV;
     BN_ALLOC(m->att, (size_t)E * 4);
-    BN_ALLOC(m->gate, (size_t)2 * F * 4);       // gate | up, contiguous
     m->up = m->gate + F;
+    m->vocab_off = slice_lo(c.vocab);
+    m->vocab_shard = slice_hi(c.vocab) - m->vocab_off;
     BN_ALLOC(m->att_g, (size_t)E * 4);
     BN_ALLOC(m->mega_state, 64);
     BN_ALLOC(m->final_h, (size_t)E * 4);
@@ -2298,14 +2385,17 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
     std::vector<float2> rope;
     bn_rope_table(c, rope);
     m->mats.resize((size_t)c.n_layers * BN_MATS);
+    m->row_offs.resize((size_t)c.n_layers * BN_MATS);
     uint32_t *found = cx.d_status + 8;
     for (uint32_t i = 0; i < c.n_layers * BN_MATS && e == cudaSuccess; ++i) {
-        const uint32_t K = ins[i % BN_MATS], N = outs[i % BN_MATS];
+        const uint32_t K = ins[i % BN_MATS], N0 = outs[i % BN_MATS];
+        const uint32_t r0 = slice_lo(N0), N = slice_hi(N0) - r0;  // this rank's rows
+        m->row_offs[i] = r0;
         const size_t bytes = (size_t)K / 4 * N;
         uint8_t *dst = m->wblock + off[i];
-        e = cudaMemcpyAsync(dst, w->w[i], bytes, cudaMemcpyHostToDevice, s);
+        if (bytes) e = cudaMemcpyAsync(dst, w->w[i] + (size_t)r0 * (K / 4), bytes, cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess) e = cudaMemsetAsync(found, 0, 4, s);
-        if (e == cudaSuccess) {
+        if (e == cudaSuccess && bytes >= 16) {
             const size_t n16 = bytes / 16;
             i2s_scan_code3_kernel<<<(unsigned)std::min<size_t>((n16 + 255) / 256, 2048), 256, 0, s>>>(
                 (const uint4 *)dst, n16, found);
@@ -2338,6 +2428,26 @@ int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl
     return WL_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int wl_bitnet_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_bitnet **out) {
+    return bn_create(cfg, w, nullptr, out);
+}
+
+int wl_bitnet_create_tp(const wl_bitnet_config *cfg, const wl_bitnet_weights *w,
+                        wl_tp_group *group, wl_bitnet **out) {
+    if (!group) return fail(WL_ERR_INVALID_ARGUMENT, "group is NULL");
+    return bn_create(cfg, w, group, out);
+}
+
+size_t wl_bitnet_tp_sym_bytes(const wl_bitnet_config *cfg) {
+    if (!cfg) return 0;
+    size_t oq, og;
+    return bn_sym_layout(*cfg, &oq, &og);
+}
+
 int wl_bitnet_destroy(wl_bitnet *m) {
     if (!m) return WL_OK;
     cudaSetDevice(m->device);
@@ -2345,6 +2455,11 @@ int wl_bitnet_destroy(wl_bitnet *m) {
     if (m->g_forward) cudaGraphExecDestroy(m->g_forward);
     if (m->g_step) cudaGraphExecDestroy(m->g_step);
     if (m->g_last) cudaGraphExecDestroy(m->g_last);
+    if (m->tpg) {  // in the group's symmetric block, not ours
+        m->hidden = nullptr;
+        m->q = nullptr;
+        m->gate = nullptr;
+    }
     void *bufs[] = {m->wblock, m->norms, m->out_norm, m->q6k, m->rope, m->kq, m->vq, m->ks,
                     m->vs, m->hidden, m->q, m->att, m->gate, m->final_h, m->att_g,
                     m->mega_state, m->d_layers,
