@@ -34,6 +34,13 @@ the whole model's bytes / max-over-ranks step time.  When a rank's share of
 the weights is under twice L2, several distinct weight copies are cycled step
 to step so that no step reads its weights from L2.
 
+Beside the headline the line carries the decode engines: `decode` is
+BASELINE config 2 (BitNet-2B-shaped greedy decode, 512-token prompt, 128 new
+tokens; tensor parallel over the N GPUs at N > 1), `smollm_batch_decode` is
+config 5 (SmolLM-135M-shaped Q8_0 model, 32 sequences with contexts
+U[64, 1024], 64 new tokens each; 1 GPU), `lm_head` config 4 and
+`prefill_gemm` config 3.
+
 `--impl reference` times the reference's x86 kernel (the oracle port of
 bitlinear_i2s_matvec_f32_sse2_i8, single-threaded like the reference's x86
 I2_S path) on this host over a bounded sample of the same sweep.
@@ -375,7 +382,8 @@ def run_gpu(args) -> None:
     lm = lm_head_bench(torch, dev, L, stream, world, rank, tpg, max_over_ranks,
                        reps=max(20, min(args.steps, 200)))
     # ---- BitNet-2B greedy decode (config 2, single GPU)
-    decode = decode_bench() if world == 1 else None
+    decode = (decode_bench() if world == 1 else
+              decode_tp_bench(world, rank, max_over_ranks))
     # ---- SmolLM-135M Q8_0 batched decode (config 5, single GPU)
     smollm = smollm_bench() if world == 1 else None
     # ---- prefill GEMM (config 3, single GPU)
@@ -571,6 +579,40 @@ def decode_bench(reps: int = 3) -> dict:
             out[key].update({"bytes_per_token": int(step_bytes), "gbs": round(gbs, 1),
                              "hbm_frac": round(gbs / peaks()["hbm_gbs"], 4)})
     return out
+
+
+def decode_tp_bench(world: int, rank: int, max_over_ranks, reps: int = 2) -> dict:
+    """BASELINE config 2 on `world` GPUs: the tensor-parallel engine (every
+    BitLinear row-split and gathered in-kernel over NVLink, attention
+    replicated, vocab-sharded greedy head), same prompt / token counts as
+    the single-GPU run; device time of the 128-token loop, max over ranks,
+    median of `reps` runs (fast mode)."""
+    from project_willamette_b200 import synth
+    from project_willamette_b200.bitnet import BitNet
+    from project_willamette_b200.tp import TPGroup
+    n_prompt, n_new = 512, 128
+    m = synth.bitnet_model(np.random.default_rng(SEED + 7), max_seq=n_prompt + n_new)
+    rng = np.random.default_rng(SEED + 8)
+    prompts = [rng.integers(0, VOCAB, n_prompt) for _ in range(reps)]
+    g = TPGroup(rank, world, BitNet.tp_sym_bytes(m), device=rank)
+    eng = BitNet(m, tp=g)
+    times, walls = [], []
+    for r in range(reps):
+        eng.reset()
+        eng.prefill(prompts[r])
+        t0 = time.perf_counter()
+        ids, ms = eng.decode(n_new, timed=True)
+        walls.append(max_over_ranks(time.perf_counter() - t0))
+        times.append(max_over_ranks(ms))
+    eng.close()
+    g.close()
+    ms = statistics.median(times)
+    return {"config": "bitnet2b as the 1-GPU run, tensor parallel over "
+                      f"{world} GPUs (row-split BitLinears gathered in-kernel, replicated "
+                      "attention, vocab-sharded head)",
+            "prompt": n_prompt, "new_tokens": n_new,
+            "fast": {"tok_s": round(n_new / (ms * 1e-3), 1), "ms_per_token": round(ms / n_new, 4),
+                     "e2e_tok_s": round(n_new / statistics.median(walls), 1)}}
 
 
 def smollm_bench(reps: int = 2) -> dict:
