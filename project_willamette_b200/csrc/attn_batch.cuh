@@ -1,6 +1,7 @@
 // attn_batch.cuh -- decode attention for many independent sequences, one
-// CTA per (KV head, sequence, split) serving the KV head's whole group of
-// query heads (GQA), so every cached K / V row is read once per step.
+// CTA per (KV head, sequence, split of `chunk` positions) serving the KV
+// head's whole group of query heads (GQA), so every cached K / V row is read
+// once per step.
 //
 // Reference: scaled_dot_product_attention_into (src/model/cached_forward.rs:
 // 421-451), softmax_inplace (src/model/attention.rs:45-73), KVCache append /
@@ -15,9 +16,10 @@
 //     appends it to the cache (head 0 also the two scales).  Earlier
 //     positions come from the cache, the current one from shared memory, so
 //     no CTA waits on another's append.
-//  3. Scores, one thread per position: the position's K head row (HD bytes)
-//     is loaded in one round and dotted with every q head of the group (q
-//     read as float4 broadcasts).
+//  3. The split's cached K / V head rows and scales are requested (cp.async,
+//     one round) right after the dependency wait and land in shared memory
+//     while step 1 runs.  Scores, one thread per position: the position's K
+//     row dotted with every q head of the group (q read as float4 broadcasts).
 //  4. Softmax statistics per q head (max, sum of exp) in block reductions.
 //  5. V: each warp takes every 8th position, a lane owns HD/32 dimensions of
 //     the row (one coalesced row load per warp and position) and accumulates
@@ -41,18 +43,35 @@ constexpr uint32_t AB_MAX_GROUP = 4;  // q heads per KV head
 constexpr uint32_t AB_WARPS = AB_THREADS / 32;
 
 // dynamic shared memory of attn_gqa_batch_kernel
-inline size_t attn_gqa_smem_bytes(uint32_t kv, uint32_t hd, uint32_t group, uint32_t max_seq,
-                                  uint32_t splits) {
-    const uint32_t chunk = ((max_seq + splits - 1) / splits + 3u) & ~3u;
+inline size_t attn_gqa_smem_bytes(uint32_t kv, uint32_t hd, uint32_t group, uint32_t chunk_pos) {
+    const uint32_t chunk = (chunk_pos + 3u) & ~3u;
     const uint32_t half2 = ((hd / 2u + 1u) & ~1u) * 2u;
     size_t f = 2u * kv                          // k, v (rotated k)
                + group * hd                     // q heads
                + half2                          // RoPE row
                + (size_t)group * chunk          // scores / weights
-               + chunk                          // V scales
+               + 2u * chunk                     // K and V scales of the split's positions
                + (size_t)AB_WARPS * group * hd  // per-warp V partial sums
                + 4u * group + 64u;              // combine factors
-    return f * 4u + 2u * hd + 16u;              // + the current position's i8 K / V slice
+    return f * 4u + 2u * hd                     // + the current position's i8 K / V slice
+           + (size_t)chunk * (2u * hd + 16u)    // + the split's cached K (padded) / V rows
+           + 16u;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(void *smem_dst, const void *gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 template <uint32_t HD, uint32_t G>
@@ -63,19 +82,23 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     __shared__ float s_sc[2];
     __shared__ uint32_t s_last;
     const uint32_t KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
-    const uint32_t kvh = blockIdx.x, z = blockIdx.y, sp = blockIdx.z, S = gridDim.z;
+    const uint32_t kvh = blockIdx.x, z = blockIdx.y, sp = blockIdx.z;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    const uint32_t chunk_max = ((p.max_seq + S - 1) / S + 3u) & ~3u;
+    const uint32_t chunk_max = (p.chunk + 3u) & ~3u;
     float *ks = reinterpret_cast<float *>(smem);      // KV
     float *vs = ks + KV;                              // KV
     float *qg = vs + KV;                              // G * HD
     float2 *rope = reinterpret_cast<float2 *>(qg + G * HD);  // half (rounded to 2)
     float *scores = reinterpret_cast<float *>(rope + ((half + 1u) & ~1u));  // G * chunk_max
     float *vsc = scores + (size_t)G * chunk_max;      // chunk_max
-    float *vpart = vsc + chunk_max;                   // AB_WARPS * G * HD
+    float *ksc = vsc + chunk_max;                     // chunk_max
+    float *vpart = ksc + chunk_max;                   // AB_WARPS * G * HD
     float *stat = vpart + (size_t)AB_WARPS * G * HD;  // 4 * G + 64
     int8_t *kq = reinterpret_cast<int8_t *>(stat + 4u * G + 64u);  // HD
     int8_t *vq = kq + HD;                                          // HD
+    constexpr uint32_t KR = HD + 16u;                 // padded K row: conflict-free 16-byte reads
+    int8_t *ksm = vq + HD;                            // chunk_max * KR
+    int8_t *vsm = ksm + (size_t)chunk_max * KR;       // chunk_max * HD
 
     pdl_launch_dependents();
     pdl_wait();
@@ -90,6 +113,27 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     int8_t *k_cache = p.k_cache + z * p.cache_stride, *v_cache = p.v_cache + z * p.cache_stride;
     float *k_scale = p.k_scale + (size_t)z * p.scale_stride,
           *v_scale = p.v_scale + (size_t)z * p.scale_stride;
+    // this split's positions [t0, t1) (splits of p.chunk positions: long
+    // contexts take more CTAs, short ones fewer, so CTAs are equally long);
+    // the cached ones (< pos) are requested now and land in shared memory
+    // while the current position is prepared
+    const uint32_t n = pos + 1u, S = (n + p.chunk - 1u) / p.chunk;
+    if (sp >= S) return;
+    const uint32_t t0 = sp * p.chunk, t1 = min(n, t0 + p.chunk), cnt = t1 - t0;
+    const uint32_t nh = min(t1, pos) > t0 ? min(t1, pos) - t0 : 0u;  // cached positions
+    {
+        constexpr uint32_t U = HD / 16u;  // 16-byte units per row
+        for (uint32_t i = tid; i < nh * U; i += AB_THREADS) {
+            const uint32_t r = i / U, u = i % U;
+            const size_t src = (size_t)(t0 + r) * KV + kvh * HD + u * 16u;
+            cp_async16(ksm + (size_t)r * KR + u * 16u, k_cache + src);
+            cp_async16(vsm + (size_t)r * HD + u * 16u, v_cache + src);
+        }
+        for (uint32_t i = tid; i < nh; i += AB_THREADS) {
+            cp_async4(ksc + i, k_scale + t0 + i);
+            cp_async4(vsc + i, v_scale + t0 + i);
+        }
+    }
     const float2 *cs = p.rope + (size_t)pos * half;
     for (uint32_t i = tid; i < KV; i += AB_THREADS) {
         ks[i] = k_in[i];
@@ -158,15 +202,14 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
         __syncthreads();
     }
     const float sk_cur = s_sc[0], sv_cur = s_sc[1];
-    // this split's positions [t0, t1)
-    const uint32_t n = pos + 1u, chunk = (n + S - 1u) / S;
-    const uint32_t t0 = min(n, sp * chunk), t1 = min(n, t0 + chunk), cnt = t1 - t0;
+    cp_async_wait_all();
+    __syncthreads();
     // 3. scores (G heads) per position
     for (uint32_t i = tid; i < cnt; i += AB_THREADS) {
         const uint32_t t = t0 + i;
-        const int8_t *kr = t == pos ? kq : k_cache + (size_t)t * KV + kvh * HD;
-        const float sk = t == pos ? sk_cur : k_scale[t];
-        vsc[i] = t == pos ? sv_cur : v_scale[t];
+        const int8_t *kr = t == pos ? kq : ksm + (size_t)i * KR;
+        const float sk = t == pos ? sk_cur : ksc[i];
+        if (t == pos) vsc[i] = sv_cur;
         uint4 w[HD / 16];  // the whole head row in one round of loads
 #pragma unroll
         for (uint32_t c = 0; c < HD / 16; ++c) w[c] = *reinterpret_cast<const uint4 *>(kr + c * 16u);
@@ -260,7 +303,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
             const uint32_t i = i0 + u * AB_WARPS, t = t0 + i;
             w[u] = 0u;
             if (i < cnt) {
-                const int8_t *vr = t == pos ? vq : v_cache + (size_t)t * KV + kvh * HD;
+                const int8_t *vr = t == pos ? vq : vsm + (size_t)i * HD;
                 if (DL == 4) w[u] = reinterpret_cast<const uint32_t *>(vr)[lane];
                 else w[u] = reinterpret_cast<const uint16_t *>(vr)[lane];
             }
@@ -286,7 +329,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
         for (uint32_t e = 0; e < DL; ++e) vpart[((size_t)warp * G + g) * HD + lane * DL + e] = acc[g][e];
     __syncthreads();
     const uint32_t RS = HD + 4u;  // partial row: o[HD], max, sum
-    float *part = p.partial + (((size_t)z * gridDim.x + kvh) * S + sp) * G * RS;
+    float *part = p.partial + (((size_t)z * gridDim.x + kvh) * gridDim.z + sp) * G * RS;
 #pragma unroll
     for (uint32_t g = 0; g < G; ++g)
         for (uint32_t d = tid; d < HD; d += AB_THREADS) {
@@ -317,8 +360,8 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     if (!s_last) return;
     __threadfence();
     // combine: M = max m_s, f_s = exp(m_s - M), O = sum f_s o_s / sum f_s l_s
-    const float *base = p.partial + ((size_t)z * gridDim.x + kvh) * S * G * RS;
-    float *fac = stat;  // [S][G] combine factors (S * G <= 64 + 4G)
+    const float *base = p.partial + ((size_t)z * gridDim.x + kvh) * gridDim.z * G * RS;
+    float *fac = stat;  // [S][G] combine factors (S * G <= 64 + 4G, checked by the host)
     if (tid < G) {
         const uint32_t g = tid;
         float M = -INFINITY;

@@ -172,6 +172,8 @@ struct AttnParams {
     size_t cache_stride;
     const uint32_t *active;
     uint32_t rope_pairs;        // 0: NEOX (j, j + n_rot/2); 1: Norm (2j, 2j + 1)
+    uint32_t chunk;             // attn_gqa_batch_kernel: positions per split (grid z covers
+                                // max_seq); a sequence uses ceil((pos + 1) / chunk) splits
     // Tensor parallel: q / k / v were gathered from every rank's row slice;
     // with tp.wait set, every CTA first waits (bounded) for every rank's stores.
     TpParams tp;

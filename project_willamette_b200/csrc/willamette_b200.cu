@@ -2609,6 +2609,7 @@ struct wl_llama_batch {
     float *attn_partial = nullptr;
     uint32_t splits = 1, ids_cap_steps = 0;
     bool gqa_attn = false;                    // attn_gqa_batch_kernel (fast mode) or attn_decode_kernel
+    uint32_t attn_chunk = 0;                  // positions per attention CTA (gqa kernel)
     uint32_t fixed_tg = 0;                    // tokens per CTA of the linears, 0: chosen per launch
     std::vector<uint32_t> pos;                // host mirror of every position
     std::vector<uint8_t> have_hidden;
@@ -2748,7 +2749,7 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
     ep.cur_pos = m->d_cur_pos;
     WL_CUDA(launch(embed_q8_batch_kernel, dim3(S), dim3(256), 0, s, true, ep));
     const size_t attn_smem = m->gqa_attn ? attn_gqa_smem_bytes(KV, HD, c.n_heads / c.n_kv_heads,
-                                                               c.max_seq, m->splits)
+                                                               m->attn_chunk)
                                          : attn_smem_bytes(KV, HD, c.max_seq, m->splits);
     const float scale = 1.0f / sqrtf((float)HD);  // attention_scale (primitives.rs:354-357)
     int rc;
@@ -2789,6 +2790,7 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
         ap.cache_stride = (size_t)c.max_seq * KV;
         ap.active = m->d_active;
         ap.rope_pairs = 1;  // RopeType::Norm for VanillaLlama (cached_forward.rs:505-509)
+        ap.chunk = m->attn_chunk;
         if (m->gqa_attn) {
             WL_CUDA(launch(gqa_attn_kernel(HD, c.n_heads / c.n_kv_heads), dim3(c.n_kv_heads, S, m->splits),
                            dim3(AB_THREADS), attn_smem, s, true, ap));
@@ -2925,13 +2927,15 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
     const uint32_t group = c.n_heads / c.n_kv_heads;
     m->splits = 1;
     if (!c.exact && gqa_attn_kernel(c.head_dim, group)) {
-        // as many splits as keep every CTA resident at once (two per SM)
-        uint32_t sp = std::max<uint32_t>(1u, (2u * (uint32_t)cx.sm_count) / (c.n_kv_heads * S));
-        sp = std::min<uint32_t>(sp, std::min<uint32_t>(64u / group, (c.max_seq + 63) / 64));
-        sp = std::max<uint32_t>(sp, 1u);
-        if (attn_gqa_smem_bytes(KV, c.head_dim, group, c.max_seq, sp) <= (size_t)WL_MAX_DYN_SMEM) {
+        // splits of a fixed number of positions (a sequence uses as many as
+        // its context needs, so CTAs are equally long whatever the context
+        // mix); at most 64 / group of them (the combine's table)
+        uint32_t chunk = 256;
+        while ((c.max_seq + chunk - 1) / chunk > 64u / group) chunk *= 2;
+        if (attn_gqa_smem_bytes(KV, c.head_dim, group, chunk) <= (size_t)WL_MAX_DYN_SMEM) {
             m->gqa_attn = true;
-            m->splits = sp;
+            m->attn_chunk = chunk;
+            m->splits = (c.max_seq + chunk - 1) / chunk;
         }
     }
     if (!c.exact && !m->gqa_attn)
