@@ -56,6 +56,10 @@ struct Q8BatchParams {
     uint32_t K;         // multiple of 32
     uint32_t n_tokens;  // tokens of the launch (grid y covers them in groups)
     uint32_t rg;        // 32-row groups per job set (1, 2, 4, 8; paired: 1, 2, 4)
+    uint32_t stage_w;   // 1: the CTA's weight rows are bulk-copied to shared memory before
+                        // the dependency wait; 0: each lane reads its row from global memory
+                        // (the lm-head: no wait worth hiding, and its 256-row tiles would
+                        // not leave room for 32 tokens)
     const float *x;     // token t: x + t * x_stride (16-byte aligned rows)
     uint32_t x_stride;
     float *y;           // token t: y + t * y_stride
@@ -86,10 +90,11 @@ __device__ __forceinline__ void q8_word_to_f32(uint32_t word, float *f) {
                          8388736.0f);
 }
 
-// weight rows | x [TG][K] | block terms [nb][TG][rows] (phases > 1) | totals [TG][rows]
-inline size_t q8_batch_smem_bytes(uint32_t K, uint32_t tg, uint32_t rows, uint32_t phases) {
+// weight rows (when staged) | x [TG][K] | block terms [nb][TG][rows] (phases > 1) | totals [TG][rows]
+inline size_t q8_batch_smem_bytes(uint32_t K, uint32_t tg, uint32_t rows, uint32_t phases,
+                                  bool stage_w = true) {
     const size_t terms = phases > 1 ? (size_t)(K / 32u) * tg * rows : 0;
-    return (size_t)rows * q8_row_stride(K) +
+    return (stage_w ? (size_t)rows * q8_row_stride(K) : 0) +
            ((size_t)tg * K + terms + (size_t)tg * rows) * sizeof(float);
 }
 
@@ -114,7 +119,7 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
     const uint32_t t0 = blockIdx.y * TG;
     const uint32_t ntok = min((uint32_t)TG, p.n_tokens - t0);
     uint8_t *wsm = qbs;                                                // [R2][stride] weight rows
-    float *xs = reinterpret_cast<float *>(qbs + (size_t)R2 * stride);  // [TG][K]
+    float *xs = reinterpret_cast<float *>(qbs + (p.stage_w ? (size_t)R2 * stride : 0));  // [TG][K]
     float *terms = xs + (size_t)TG * K;                                // [nb][TG][R2] (P > 1)
     float *outs = terms + (P > 1 ? (size_t)nb * TG * R2 : 0);          // [TG][R2]
 
@@ -124,7 +129,9 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
     const uint32_t row = r0 + (g % p.rg) * 32u + lane;
     const bool row_ok = row < p.job[jj].n;
     const uint32_t rl = g * 32u + lane;
-    const uint8_t *rs = wsm + (size_t)rl * stride;  // this lane's row in shared memory
+    // this lane's row: in shared memory (staged) or in global memory
+    const uint8_t *rs = p.stage_w ? wsm + (size_t)rl * stride
+                                  : p.job[jj].w + (size_t)(row_ok ? row : 0u) * stride;
 
     if (tid == 0) {
         mbar_init(&s_bar[0], 1);
@@ -133,7 +140,7 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
     }
     __syncthreads();
     pdl_launch_dependents();
-    if (tid == 0) {  // the weights do not depend on earlier kernels: fetch them now
+    if (tid == 0 && p.stage_w) {  // the weights do not depend on earlier kernels: fetch them now
         const uint32_t sets = paired ? 2u : 1u;
         uint32_t bytes[2];
         uint32_t total = 0;
@@ -164,7 +171,7 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
         s_best[tid] = 0ull;
     }
     const bool got_x = mbar_wait(&s_bar[1], 0);
-    const bool got_w = mbar_wait(&s_bar[0], 0);
+    const bool got_w = !p.stage_w || mbar_wait(&s_bar[0], 0);
     if (!__syncthreads_and(got_x && got_w)) {
         if (tid == 0) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
         return;
@@ -198,9 +205,15 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
         uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
         uint32_t dbits = 0;
         if (row_ok) {
-            v0 = lds128(rs + 32u * b);
-            v1 = lds128(rs + 32u * b + 16u);
-            dbits = reinterpret_cast<const uint16_t *>(rs + K)[b];
+            if (p.stage_w) {
+                v0 = lds128(rs + 32u * b);
+                v1 = lds128(rs + 32u * b + 16u);
+                dbits = reinterpret_cast<const uint16_t *>(rs + K)[b];
+            } else {
+                v0 = __ldg(reinterpret_cast<const uint4 *>(rs + 32u * b));
+                v1 = __ldg(reinterpret_cast<const uint4 *>(rs + 32u * b + 16u));
+                dbits = __ldg(reinterpret_cast<const uint16_t *>(rs + K) + b);
+            }
         }
         float w[32];
         q8_word_to_f32(v0.x, w + 0);

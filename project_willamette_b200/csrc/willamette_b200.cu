@@ -2674,6 +2674,7 @@ int lb_q8(wl_llama_batch *m, const Q8BatchJob *jobs, uint32_t n_jobs, uint32_t K
     Q8BatchParams p{};
     const bool argmax = epi == QB_EPI_ARGMAX, paired = epi == QB_EPI_SILU_PAIR;
     p.rg = argmax ? 8u : 1u;
+    p.stage_w = argmax ? 0u : 1u;
     const uint32_t RT = 32u * p.rg, R2 = paired ? 2u * RT : RT;
     const uint32_t phases = QB_WARPS / (R2 / 32u);
     uint32_t tiles = 0;
@@ -2709,7 +2710,7 @@ int lb_q8(wl_llama_batch *m, const Q8BatchJob *jobs, uint32_t n_jobs, uint32_t K
     uint64_t best = ~0ull;
     for (int c = 0; c < 4; ++c) {
         const uint32_t tg = kQbTg[c];
-        const size_t sm = q8_batch_smem_bytes(K, tg, R2, phases);
+        const size_t sm = q8_batch_smem_bytes(K, tg, R2, phases, p.stage_w != 0);
         if (sm > (size_t)WL_MAX_DYN_SMEM) continue;
         if (m->fixed_tg) {
             if (tg == m->fixed_tg || ti < 0) ti = c;  // else the smallest feasible
@@ -2730,7 +2731,7 @@ int lb_q8(wl_llama_batch *m, const Q8BatchJob *jobs, uint32_t n_jobs, uint32_t K
     }
     if (ti < 0) return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for the batched Q8_0 kernel", K);
     const uint32_t tg = kQbTg[ti];
-    const size_t smem = q8_batch_smem_bytes(K, tg, R2, phases);
+    const size_t smem = q8_batch_smem_bytes(K, tg, R2, phases, p.stage_w != 0);
     WL_CUDA(launch(ks[ti], dim3(tiles, (m->n_seqs + tg - 1) / tg), dim3(QB_THREADS), smem, s, true, p));
     return WL_OK;
 }
