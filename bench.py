@@ -462,9 +462,9 @@ class _Null:
 
 
 # DRAM traffic of one i2s_stream_kernel launch of the 1-GPU sweep (ncu
-# dram__bytes_read.sum + dram__bytes_write.sum = 535,326,464 + 5,324,800;
+# dram__bytes_read.sum + dram__bytes_write.sum = 542,717,440 + 4,833,536;
 # profiles/i2s_stream_kernel_bitnet2b_sweep.md).
-TRAFFIC_PER_STEP_BYTES = 540651264
+TRAFFIC_PER_STEP_BYTES = 547550976
 
 
 def lm_head_bench(torch, dev, L, stream, world, rank, tpg, max_over_ranks, reps: int) -> dict:
