@@ -44,7 +44,12 @@ typedef enum wl_status {
     WL_ERR_CUDA = 5,                    /* CUDA runtime error */
     WL_ERR_NO_DEVICE = 6,               /* no sm_100 device visible */
     WL_ERR_DEVICE_TIMEOUT = 7,          /* a bounded device-side wait gave up */
-    WL_ERR_COMM = 8                     /* multi-GPU peer setup / exchange failure */
+    WL_ERR_COMM = 8,                    /* multi-GPU peer setup / exchange failure */
+    WL_ERR_INVALID_MAGIC = 9,           /* InvalidMagic(u32), error.rs:16 */
+    WL_ERR_UNSUPPORTED_VERSION = 10,    /* UnsupportedVersion(u32), error.rs:19 */
+    WL_ERR_UNSUPPORTED_ARCHITECTURE = 11, /* UnsupportedArchitecture(String), error.rs:22 */
+    WL_ERR_MISSING_METADATA = 12,       /* MissingMetadata(Vec<String>), error.rs:25 */
+    WL_ERR_TENSOR_OUT_OF_BOUNDS = 13    /* TensorOutOfBounds{..}, error.rs:40 */
 } wl_status;
 
 /* GGML type ids (src/gguf/types.rs:66-99). */
@@ -434,6 +439,50 @@ int wl_llama_batch_decode(wl_llama_batch *batch, uint32_t n_new, uint32_t *out_i
 /* Reset, prefill every sequence's (non-empty) prompt, decode n_new. */
 int wl_llama_batch_generate(wl_llama_batch *batch, const uint32_t *tokens, const uint32_t *offsets,
                             uint32_t n_new, uint32_t *out_ids, float *out_hiddens);
+
+/* ------------------------------------------------------------ GGUF models
+ * GgufFile::parse (src/gguf/reader.rs:120-415) over the caller's bytes -- the
+ * reference maps the file and parses the mapping; pass that mapping here.
+ * Zero-copy: tensor views point into `data`, which must outlive the handle.
+ * Errors: WL_ERR_INVALID_MAGIC, WL_ERR_UNSUPPORTED_VERSION,
+ * WL_ERR_TENSOR_OUT_OF_BOUNDS, else WL_ERR_GGUF_PARSE (same checks, same
+ * order as the reference).  Host code only: no GPU is touched. */
+typedef struct wl_gguf wl_gguf;
+int wl_gguf_open(const uint8_t *data, size_t len, wl_gguf **out);
+int wl_gguf_close(wl_gguf *gguf);
+uint32_t wl_gguf_version(const wl_gguf *gguf);
+uint64_t wl_gguf_alignment(const wl_gguf *gguf);
+uint64_t wl_gguf_tensor_count(const wl_gguf *gguf);
+/* Tensor i in directory order, or by name (WL_ERR_MISSING_METADATA if
+ * absent), as a view valid while the handle lives: data = the packed bytes
+ * (byte length of reader.rs:688-770), scale_data = the I2_S 32-byte trailing
+ * block (NULL for other types). */
+int wl_gguf_tensor(const wl_gguf *gguf, uint64_t index, wl_tensor_view *out);
+int wl_gguf_find_tensor(const wl_gguf *gguf, const char *name, wl_tensor_view *out);
+/* Metadata (GgufValue::as_u64 / as_f32 / as_str, reader.rs:46-90):
+ * WL_ERR_MISSING_METADATA when the key is absent or of another kind.
+ * wl_gguf_get_str's pointer lives as long as the handle. */
+int wl_gguf_get_u64(const wl_gguf *gguf, const char *key, uint64_t *out);
+int wl_gguf_get_f32(const wl_gguf *gguf, const char *key, float *out);
+int wl_gguf_get_str(const wl_gguf *gguf, const char *key, const char **out);
+/* Element count of an array value (0 if absent or not an array). */
+uint64_t wl_gguf_array_len(const wl_gguf *gguf, const char *key);
+/* ModelConfig::from_gguf_metadata (src/model/config.rs:61-260): the
+ * architecture (general.architecture: bitnet-b1.58 / bitnet-25 / bitnet ->
+ * variant 0, BitNetSubNorm; llama -> variant 1, VanillaLlama) and its
+ * dimensions into a wl_bitnet_config; max_seq = context_length. */
+int wl_gguf_model_config(const wl_gguf *gguf, wl_bitnet_config *cfg, uint32_t *variant);
+/* ModelGraph::from_gguf (src/model/graph.rs:95-240) straight to the device:
+ * the BitNet engine from a BitNet-family file (I2_S linears with their
+ * trailing scales, F32 norms, the tied embedding as Q6_K -- the reference's
+ * embedding-q6-k artifact; an F16 embedding is WL_ERR_NOT_IMPLEMENTED), or the
+ * batched Llama engine from a llama file (Q8_0 linears and tied Q8_0
+ * token_embd; other linear types or a separate output.weight are
+ * WL_ERR_NOT_IMPLEMENTED).  max_seq 0 = context_length. */
+int wl_bitnet_create_from_gguf(const wl_gguf *gguf, uint32_t max_seq, uint32_t exact,
+                               uint32_t persistent, wl_bitnet **out);
+int wl_llama_batch_create_from_gguf(const wl_gguf *gguf, uint32_t n_seqs, uint32_t max_seq,
+                                    uint32_t exact, wl_llama_batch **out);
 
 #ifdef __cplusplus
 }

@@ -63,6 +63,7 @@ class WillametteError(Exception):
     def __init__(self, status: int, message: str, raw_type: Optional[int] = None):
         self.status = WLStatus(status)
         self.raw_type = raw_type
+        self.message = message
         super().__init__(f"{self.status.name}: {message}")
 
 

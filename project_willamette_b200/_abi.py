@@ -25,6 +25,11 @@ class WLStatus(enum.IntEnum):
     NO_DEVICE = 6
     DEVICE_TIMEOUT = 7
     COMM = 8
+    INVALID_MAGIC = 9
+    UNSUPPORTED_VERSION = 10
+    UNSUPPORTED_ARCHITECTURE = 11
+    MISSING_METADATA = 12
+    TENSOR_OUT_OF_BOUNDS = 13
 
 
 class WlTensorView(C.Structure):
@@ -156,6 +161,20 @@ PROTOTYPES = {
     "wl_llama_batch_decode": ([_vp, _u32, C.POINTER(_u32), _fp, _fp], _i),
     "wl_llama_batch_generate": ([_vp, C.POINTER(_u32), C.POINTER(_u32), _u32, C.POINTER(_u32),
                                  _fp], _i),
+    "wl_gguf_open": ([_vp, _sz, C.POINTER(_vp)], _i),
+    "wl_gguf_close": ([_vp], _i),
+    "wl_gguf_version": ([_vp], _u32),
+    "wl_gguf_alignment": ([_vp], C.c_uint64),
+    "wl_gguf_tensor_count": ([_vp], C.c_uint64),
+    "wl_gguf_tensor": ([_vp, C.c_uint64, _tv], _i),
+    "wl_gguf_find_tensor": ([_vp, C.c_char_p, _tv], _i),
+    "wl_gguf_get_u64": ([_vp, C.c_char_p, C.POINTER(C.c_uint64)], _i),
+    "wl_gguf_get_f32": ([_vp, C.c_char_p, _fp], _i),
+    "wl_gguf_get_str": ([_vp, C.c_char_p, C.POINTER(C.c_char_p)], _i),
+    "wl_gguf_array_len": ([_vp, C.c_char_p], C.c_uint64),
+    "wl_gguf_model_config": ([_vp, C.POINTER(WlBitnetConfig), C.POINTER(_u32)], _i),
+    "wl_bitnet_create_from_gguf": ([_vp, _u32, _u32, _u32, C.POINTER(_vp)], _i),
+    "wl_llama_batch_create_from_gguf": ([_vp, _u32, _u32, _u32, C.POINTER(_vp)], _i),
     "wl_tp_create": ([_i, _i, _sz, C.POINTER(_vp), C.POINTER(C.c_uint8)], _i),
     "wl_tp_connect": ([_vp, C.POINTER(C.c_uint8)], _i),
     "wl_tp_buffer": ([_vp, _sz], _vp),

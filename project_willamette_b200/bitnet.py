@@ -61,6 +61,24 @@ class BitNet:
         self._tp = tp  # the engine's gathered vectors live in the group's block
         self._keep = None  # the library holds device copies
 
+    @classmethod
+    def from_gguf(cls, gguf_file, max_seq: int = 0, exact: bool = False,
+                  persistent: bool = False, device: int = 0) -> "BitNet":
+        """The engine straight from a parsed BitNet-family GGUF
+        (``gguf.GgufFile``): ModelGraph::from_gguf, src/model/graph.rs:95-240.
+        max_seq 0 = the file's context_length."""
+        L = lib()
+        _check(L.wl_init(device))
+        self = cls.__new__(cls)
+        cfg, _ = gguf_file.model_config()
+        self.cfg = WlBitnetConfig(**cfg, exact=int(exact), persistent=int(persistent))
+        self.n_embd = cfg["n_embd"]
+        self._tp = None
+        self._h = C.c_void_p()
+        _check(L.wl_bitnet_create_from_gguf(gguf_file._g, max_seq, int(exact), int(persistent),
+                                            C.byref(self._h)))
+        return self
+
     @staticmethod
     def tp_sym_bytes(model: dict) -> int:
         """Symmetric-region bytes the tensor-parallel engine needs."""

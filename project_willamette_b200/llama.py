@@ -57,6 +57,22 @@ class LlamaBatch:
         self._h = C.c_void_p()
         _check(L.wl_llama_batch_create(C.byref(self.cfg), C.byref(w), n_seqs, C.byref(self._h)))
 
+    @classmethod
+    def from_gguf(cls, gguf_file, n_seqs: int, max_seq: int = 0, exact: bool = False,
+                  device: int = 0) -> "LlamaBatch":
+        """The engine straight from a parsed llama GGUF (``gguf.GgufFile``,
+        Q8_0 linears and tied Q8_0 embedding).  max_seq 0 = context_length."""
+        L = lib()
+        _check(L.wl_init(device))
+        self = cls.__new__(cls)
+        cfg, _ = gguf_file.model_config()
+        self.cfg = WlBitnetConfig(**cfg, exact=int(exact), persistent=0)
+        self.n_embd, self.n_seqs = cfg["n_embd"], n_seqs
+        self._h = C.c_void_p()
+        _check(L.wl_llama_batch_create_from_gguf(gguf_file._g, n_seqs, max_seq, int(exact),
+                                                 C.byref(self._h)))
+        return self
+
     def position(self, seq: int) -> int:
         return int(lib().wl_llama_batch_position(self._h, seq))
 
