@@ -41,6 +41,7 @@ namespace wl {
 constexpr int AB_THREADS = 256;
 constexpr uint32_t AB_MAX_GROUP = 4;  // q heads per KV head
 constexpr uint32_t AB_WARPS = AB_THREADS / 32;
+constexpr uint32_t AB_COMBINE = 256;  // splits x group <= this (the combine's factor table)
 
 // dynamic shared memory of attn_gqa_batch_kernel
 inline size_t attn_gqa_smem_bytes(uint32_t kv, uint32_t hd, uint32_t group, uint32_t chunk_pos) {
@@ -52,7 +53,7 @@ inline size_t attn_gqa_smem_bytes(uint32_t kv, uint32_t hd, uint32_t group, uint
                + (size_t)group * chunk          // scores / weights
                + 2u * chunk                     // K and V scales of the split's positions
                + (size_t)AB_WARPS * group * hd  // per-warp V partial sums
-               + 4u * group + 64u;              // combine factors
+               + 4u * group + 2u * AB_COMBINE;  // combine factors and sums
     return f * 4u + 2u * hd                     // + the current position's i8 K / V slice
            + (size_t)chunk * (2u * hd + 16u)    // + the split's cached K (padded) / V rows
            + 16u;
@@ -93,8 +94,8 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     float *vsc = scores + (size_t)G * chunk_max;      // chunk_max
     float *ksc = vsc + chunk_max;                     // chunk_max
     float *vpart = ksc + chunk_max;                   // AB_WARPS * G * HD
-    float *stat = vpart + (size_t)AB_WARPS * G * HD;  // 4 * G + 64
-    int8_t *kq = reinterpret_cast<int8_t *>(stat + 4u * G + 64u);  // HD
+    float *stat = vpart + (size_t)AB_WARPS * G * HD;  // 4 * G + 2 * AB_COMBINE
+    int8_t *kq = reinterpret_cast<int8_t *>(stat + 4u * G + 2u * AB_COMBINE);  // HD
     int8_t *vq = kq + HD;                                          // HD
     constexpr uint32_t KR = HD + 16u;                 // padded K row: conflict-free 16-byte reads
     int8_t *ksm = vq + HD;                            // chunk_max * KR
@@ -102,6 +103,10 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
 
     pdl_launch_dependents();
     pdl_wait();
+    if (p.tp.world && p.tp.wait) {  // q / k / v were gathered from every rank
+        if (tid == 0 && !tp_wait(p.tp)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
+        __syncthreads();
+    }
     if (p.active && !p.active[z]) return;
     const uint32_t pos = p.pos[z];
     if (pos >= p.max_seq) {
@@ -359,19 +364,28 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // combine: M = max m_s, f_s = exp(m_s - M), O = sum f_s o_s / sum f_s l_s
+    // combine: M = max m_s, f_s = exp(m_s - M), O = sum f_s o_s / sum f_s l_s.
+    // Every split's (max, sum) pair arrives in one round of loads; the o rows
+    // in rounds of 16 independent loads per output (the splits' partials are
+    // L2-resident, so the rounds, not the bytes, set the time).
     const float *base = p.partial + ((size_t)z * gridDim.x + kvh) * gridDim.z * G * RS;
-    float *fac = stat;  // [S][G] combine factors (S * G <= 64 + 4G, checked by the host)
+    float *fac = stat;               // [S][G] maxima, then combine factors
+    float *lsm = stat + AB_COMBINE;  // [S][G] sums (S * G <= AB_COMBINE, checked by the host)
+    for (uint32_t i = tid; i < S * G; i += AB_THREADS) {
+        fac[i] = __ldcg(base + (size_t)i * RS + HD);
+        lsm[i] = __ldcg(base + (size_t)i * RS + HD + 1);
+    }
+    __syncthreads();
     if (tid < G) {
         const uint32_t g = tid;
         float M = -INFINITY;
-        for (uint32_t s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(base + ((size_t)s2 * G + g) * RS + HD));
+        for (uint32_t s2 = 0; s2 < S; ++s2) M = fmaxf(M, fac[s2 * G + g]);
         float L = 0.0f;
         for (uint32_t s2 = 0; s2 < S; ++s2) {
-            const float ms = __ldcg(base + ((size_t)s2 * G + g) * RS + HD);
+            const float ms = fac[s2 * G + g];
             const float f = (isfinite(M) && ms > -INFINITY) ? expf(ms - M) : 0.0f;
             fac[s2 * G + g] = f;
-            L += __ldcg(base + ((size_t)s2 * G + g) * RS + HD + 1) * f;
+            L += lsm[s2 * G + g] * f;
         }
         red[g] = !isfinite(M) ? 0.0f : (L > 0.0f ? __fdiv_rn(1.0f, L) : 1.0f);
     }
@@ -379,8 +393,15 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     for (uint32_t i = tid; i < G * HD; i += AB_THREADS) {
         const uint32_t g = i / HD, d = i % HD;
         float o = 0.0f;
-        for (uint32_t s2 = 0; s2 < S; ++s2)
-            o = __fmaf_rn(__ldcg(base + ((size_t)s2 * G + g) * RS + d), fac[s2 * G + g], o);
+        for (uint32_t s0 = 0; s0 < S; s0 += 16u) {
+            float v[16];
+#pragma unroll
+            for (uint32_t u = 0; u < 16u; ++u)
+                v[u] = s0 + u < S ? __ldcg(base + ((size_t)(s0 + u) * G + g) * RS + d) : 0.0f;
+#pragma unroll
+            for (uint32_t u = 0; u < 16u; ++u)
+                if (s0 + u < S) o = __fmaf_rn(v[u], fac[(s0 + u) * G + g], o);
+        }
         p.att[(size_t)z * p.att_stride + (kvh * G + g) * HD + d] = __fmul_rn(o, red[g]);
     }
     if (tid == 0) *ctr = 0u;  // re-arm for the next launch

@@ -1225,6 +1225,8 @@ struct wl_bitnet {
     uint32_t *d_token = nullptr, *d_pos = nullptr, *d_step = nullptr, *d_ids = nullptr;
     uint32_t ids_cap = 0;
     uint32_t splits = 1;                   // attention CTAs per head (per-op path)
+    bool gqa_attn = false;                 // fast mode: attn_gqa_batch_kernel (KV head x split CTAs)
+    uint32_t attn_chunk = 0;               // its positions per CTA
     float *attn_partial = nullptr;
     uint32_t *attn_counters = nullptr;
     // persistent whole-forward kernel
@@ -1252,6 +1254,20 @@ struct wl_bitnet {
 namespace {
 
 constexpr int BN_MATS = 7;  // q, k, v, o, gate, up, down
+
+using AttnKernel = void (*)(AttnParams);
+// fast-mode batched attention for head_dim 64 / 128 and 1..4 q heads per KV head
+AttnKernel gqa_attn_kernel(uint32_t hd, uint32_t group) {
+    static const AttnKernel k64[4] = {attn_gqa_batch_kernel<64, 1>, attn_gqa_batch_kernel<64, 2>,
+                                      attn_gqa_batch_kernel<64, 3>, attn_gqa_batch_kernel<64, 4>};
+    static const AttnKernel k128[4] = {attn_gqa_batch_kernel<128, 1>, attn_gqa_batch_kernel<128, 2>,
+                                       attn_gqa_batch_kernel<128, 3>, attn_gqa_batch_kernel<128, 4>};
+    if (group < 1 || group > AB_MAX_GROUP) return nullptr;
+    if (hd == 64) return k64[group - 1];
+    if (hd == 128) return k128[group - 1];
+    return nullptr;
+}
+
 
 uint32_t bn_kv(const wl_bitnet_config &c) { return c.n_kv_heads * c.head_dim; }
 
@@ -1456,7 +1472,9 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
     ep.ids = commit ? m->d_ids : nullptr;
     ep.step = m->d_step;
     WL_CUDA(launch(embed_q6k_kernel, dim3(nb), dim3(256), 0, s, true, ep));
-    const size_t attn_smem = attn_smem_bytes(KV, c.head_dim, c.max_seq, m->splits);
+    const uint32_t group = c.n_heads / c.n_kv_heads;
+    const size_t attn_smem = m->gqa_attn ? attn_gqa_smem_bytes(KV, c.head_dim, group, m->attn_chunk)
+                                         : attn_smem_bytes(KV, c.head_dim, c.max_seq, m->splits);
     const float scale = 1.0f / sqrtf((float)c.head_dim);  // attention_scale, primitives.rs:354
     int rc;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
@@ -1491,8 +1509,14 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
             ap.tp = m->tp;
             ap.tp.wait = 1u;
         }
-        WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits), dim3(ATTN_THREADS),
-                       attn_smem, s, true, ap));
+        if (m->gqa_attn) {
+            ap.chunk = m->attn_chunk;
+            WL_CUDA(launch(gqa_attn_kernel(c.head_dim, group), dim3(c.n_kv_heads, 1, m->splits),
+                           dim3(AB_THREADS), attn_smem, s, true, ap));
+        } else {
+            WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits), dim3(ATTN_THREADS),
+                           attn_smem, s, true, ap));
+        }
         float *o[1] = {m->hidden};
         if ((rc = bn_matvec(m, l, 3, 1, E, m->att, o, I2S_PRE_RMSNORM, nrm + E, nullptr, 1, 0, s)))
             return rc;
@@ -2364,6 +2388,21 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
                         : std::max<uint32_t>(1u, std::min<uint32_t>((c.max_seq + 31) / 32,
                                                                     (uint32_t)(2 * cx.sm_count) /
                                                                         c.n_heads));
+    {   // fast mode: one CTA per (KV head, split of `chunk` positions) for the
+        // whole query group, when the group and head size have a kernel
+        const uint32_t group = c.n_heads / c.n_kv_heads;
+        if (!c.exact && gqa_attn_kernel(c.head_dim, group)) {
+            uint32_t chunk = 32;  // about one CTA per SM at full context
+            while ((uint64_t)((c.max_seq + chunk - 1) / chunk) * c.n_kv_heads > (uint64_t)cx.sm_count ||
+                   (c.max_seq + chunk - 1) / chunk > AB_COMBINE / group)
+                chunk += 32;
+            if (attn_gqa_smem_bytes(KV, c.head_dim, group, chunk) <= (size_t)WL_MAX_DYN_SMEM) {
+                m->gqa_attn = true;
+                m->attn_chunk = chunk;
+                m->splits = (c.max_seq + chunk - 1) / chunk;
+            }
+        }
+    }
     m->mega_grid = (uint32_t)cx.sm_count;
     m->mega_splits = c.exact ? 1u : std::max<uint32_t>(1u, m->mega_grid / c.n_heads);
     BN_ALLOC(m->attn_partial, (size_t)c.n_heads * std::max(m->splits, m->mega_splits) *
@@ -2630,18 +2669,6 @@ const QbKernel kQb[2][4] = {
      q8_batch_kernel<32, true>}};
 constexpr uint32_t kQbTg[4] = {1, 4, 8, 32};
 
-using AttnKernel = void (*)(AttnParams);
-// fast-mode batched attention for head_dim 64 / 128 and 1..4 q heads per KV head
-AttnKernel gqa_attn_kernel(uint32_t hd, uint32_t group) {
-    static const AttnKernel k64[4] = {attn_gqa_batch_kernel<64, 1>, attn_gqa_batch_kernel<64, 2>,
-                                      attn_gqa_batch_kernel<64, 3>, attn_gqa_batch_kernel<64, 4>};
-    static const AttnKernel k128[4] = {attn_gqa_batch_kernel<128, 1>, attn_gqa_batch_kernel<128, 2>,
-                                       attn_gqa_batch_kernel<128, 3>, attn_gqa_batch_kernel<128, 4>};
-    if (group < 1 || group > AB_MAX_GROUP) return nullptr;
-    if (hd == 64) return k64[group - 1];
-    if (hd == 128) return k128[group - 1];
-    return nullptr;
-}
 
 int lb_validate(const wl_bitnet_config *c, uint32_t n_seqs) {
     if (!c) return fail(WL_ERR_INVALID_ARGUMENT, "config is NULL");
@@ -2931,9 +2958,9 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
     if (!c.exact && gqa_attn_kernel(c.head_dim, group)) {
         // splits of a fixed number of positions (a sequence uses as many as
         // its context needs, so CTAs are equally long whatever the context
-        // mix); at most 64 / group of them (the combine's table)
+        // mix); at most AB_COMBINE / group of them (the combine's table)
         uint32_t chunk = 256;
-        while ((c.max_seq + chunk - 1) / chunk > 64u / group) chunk *= 2;
+        while ((c.max_seq + chunk - 1) / chunk > AB_COMBINE / group) chunk *= 2;
         if (attn_gqa_smem_bytes(KV, c.head_dim, group, chunk) <= (size_t)WL_MAX_DYN_SMEM) {
             m->gqa_attn = true;
             m->attn_chunk = chunk;
