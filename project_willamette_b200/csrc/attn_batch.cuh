@@ -75,9 +75,17 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 template <uint32_t HD, uint32_t G>
 __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __grid_constant__ AttnParams p) {
     static_assert((HD == 64 || HD == 128) && G >= 1 && G <= AB_MAX_GROUP, "shape");
+    // (the host runs this kernel with n_rot % 4 == 0 and 16-byte aligned q / k / v rows)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[AB_WARPS * 2 * AB_MAX_GROUP];
     __shared__ float s_sc[2];
@@ -107,8 +115,8 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
         if (tid == 0 && !tp_wait(p.tp)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
         __syncthreads();
     }
+    const uint32_t pos = p.pos[z];  // (both loads in flight together)
     if (p.active && !p.active[z]) return;
-    const uint32_t pos = p.pos[z];
     if (pos >= p.max_seq) {
         if (tid == 0) atomicOr(p.status, WL_DEV_ERR_POSITION);
         return;
@@ -126,6 +134,17 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     if (sp >= S) return;
     const uint32_t t0 = sp * p.chunk, t1 = min(n, t0 + p.chunk), cnt = t1 - t0;
     const uint32_t nh = min(t1, pos) > t0 ? min(t1, pos) - t0 : 0u;  // cached positions
+    // one round of 16-byte async copies: this step's k, v, the group's q
+    // heads and the RoPE row (group 1), then the split's cached rows (group 2)
+    const float2 *cs = p.rope + (size_t)pos * half;
+    for (uint32_t i = tid; i < KV / 4u; i += AB_THREADS) {
+        cp_async16(ks + 4u * i, k_in + 4u * i);
+        cp_async16(vs + 4u * i, v_in + 4u * i);
+    }
+    for (uint32_t i = tid; i < G * HD / 4u; i += AB_THREADS)
+        cp_async16(qg + 4u * i, q_in + kvh * G * HD + 4u * i);
+    for (uint32_t j = tid; j < half / 2u; j += AB_THREADS) cp_async16(rope + 2u * j, cs + 2u * j);
+    cp_async_commit();
     {
         constexpr uint32_t U = HD / 16u;  // 16-byte units per row
         for (uint32_t i = tid; i < nh * U; i += AB_THREADS) {
@@ -139,13 +158,8 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
             cp_async4(vsc + i, v_scale + t0 + i);
         }
     }
-    const float2 *cs = p.rope + (size_t)pos * half;
-    for (uint32_t i = tid; i < KV; i += AB_THREADS) {
-        ks[i] = k_in[i];
-        vs[i] = v_in[i];
-    }
-    for (uint32_t i = tid; i < G * HD; i += AB_THREADS) qg[i] = q_in[kvh * G * HD + i];
-    for (uint32_t j = tid; j < half; j += AB_THREADS) rope[j] = cs[j];
+    cp_async_commit();
+    cp_async_wait_group<1>();  // group 1 has landed (group 2 may still be in flight)
     __syncthreads();
     const uint32_t pstep = p.rope_pairs ? 2u : 1u, poff = p.rope_pairs ? 1u : half;
     for (uint32_t i = tid; i < (p.n_kv_heads + G) * half; i += AB_THREADS) {

@@ -330,6 +330,114 @@ __device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t
     __syncthreads();  // red is reused by the quantiser; xs is complete
 }
 
+// Fast-mode input transform + quantisation with the input held in registers:
+// every global load of a thread is issued before any is used (one memory
+// round trip per CTA instead of one per 1024-element pass), the RMSNorm
+// weights were copied to `nw` (shared memory) before the dependency wait.
+// Same values, in the same per-thread order, as cta_pre_input (tree sums) +
+// cta_quantize.
+constexpr int I2S_PRE_V = (int)(I2S_FUSE_Q_MAX_K / (I2S_THREADS * 4u));  // float4 per thread
+
+__device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint32_t K,
+                                                  const float *nw, int8_t *qs, float *red) {
+    const uint32_t tid = threadIdx.x, nthr = blockDim.x;
+    const bool relu2 = p.pre == I2S_PRE_RELU2_RMSNORM;
+    float4 v[I2S_PRE_V];
+#pragma unroll
+    for (int k = 0; k < I2S_PRE_V; ++k) {
+        const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+        if (i < K) v[k] = *reinterpret_cast<const float4 *>(p.x + i);
+    }
+    if (relu2) {  // v = relu(x)^2 * up, the up vector in two halves (bounded registers)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 u[I2S_PRE_V / 2];
+#pragma unroll
+            for (int k = 0; k < I2S_PRE_V / 2; ++k) {
+                const uint32_t i = tid * 4u + (uint32_t)(h * (I2S_PRE_V / 2) + k) * nthr * 4u;
+                if (i < K) u[k] = *reinterpret_cast<const float4 *>(p.x2 + i);
+            }
+#pragma unroll
+            for (int k = 0; k < I2S_PRE_V / 2; ++k) {
+                const int kk = h * (I2S_PRE_V / 2) + k;
+                const uint32_t i = tid * 4u + (uint32_t)kk * nthr * 4u;
+                if (i < K) {
+                    float4 &x = v[kk];
+                    const float r0 = x.x > 0.0f ? x.x : 0.0f, r1 = x.y > 0.0f ? x.y : 0.0f;
+                    const float r2 = x.z > 0.0f ? x.z : 0.0f, r3 = x.w > 0.0f ? x.w : 0.0f;
+                    x.x = __fmul_rn(__fmul_rn(r0, r0), u[k].x);
+                    x.y = __fmul_rn(__fmul_rn(r1, r1), u[k].y);
+                    x.z = __fmul_rn(__fmul_rn(r2, r2), u[k].z);
+                    x.w = __fmul_rn(__fmul_rn(r3, r3), u[k].w);
+                }
+            }
+        }
+    }
+    if (p.pre != I2S_PRE_NONE) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < I2S_PRE_V; ++k) {
+            const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+            if (i < K)
+                ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v[k].x, v[k].x), __fmul_rn(v[k].y, v[k].y)),
+                                             __fadd_rn(__fmul_rn(v[k].z, v[k].z), __fmul_rn(v[k].w, v[k].w))));
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        float sum_sq = red[0];
+        for (uint32_t w = 1; w < nthr / 32; ++w) sum_sq = __fadd_rn(sum_sq, red[w]);
+        const float mean = __fdiv_rn(sum_sq, (float)K);
+        const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+#pragma unroll
+        for (int k = 0; k < I2S_PRE_V; ++k) {
+            const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+            if (i < K) {
+                const float4 w = *reinterpret_cast<const float4 *>(nw + i);
+                v[k].x = __fmul_rn(__fmul_rn(v[k].x, rsqrt), w.x);
+                v[k].y = __fmul_rn(__fmul_rn(v[k].y, rsqrt), w.y);
+                v[k].z = __fmul_rn(__fmul_rn(v[k].z, rsqrt), w.z);
+                v[k].w = __fmul_rn(__fmul_rn(v[k].w, rsqrt), w.w);
+            }
+        }
+        __syncthreads();  // red is reused below
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < I2S_PRE_V; ++k) {
+        const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+        if (i < K)
+            m = fmaxf(fmaxf(fmaxf(m, fabsf(v[k].x)), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w)));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    float max_abs = red[0];
+    for (uint32_t w = 1; w < nthr / 32; ++w) max_abs = fmaxf(max_abs, red[w]);
+    const float inv = max_abs == 0.0f ? 0.0f : __fdiv_rn(127.0f, max_abs);
+#pragma unroll
+    for (int k = 0; k < I2S_PRE_V; ++k) {
+        const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+        if (i < K) {
+            const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+            uint32_t packed = 0;
+            if (max_abs != 0.0f) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float r = roundf(__fmul_rn(e[c], inv));
+                    const int qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+                    packed |= (uint32_t)(qi & 0xFF) << (8 * c);
+                }
+            }
+            *reinterpret_cast<uint32_t *>(qs + i) = packed;
+        }
+    }
+    __syncthreads();
+    return max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 2: per-op matvec (one BitLinear, or several sharing one input).
 
@@ -401,6 +509,18 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             i2s_issue_chunk(p, c, r0, r1, RPI, row_bytes, smem + c * stage_bytes, &full_bar[c],
                             policy);
     }
+    // fast mode: the RMSNorm weights do not depend on earlier kernels either
+    const bool regs_pre = FUSE_Q && !(p.pre != I2S_PRE_NONE && p.exact_norm);
+    if constexpr (FUSE_Q) {
+        if (regs_pre && p.pre != I2S_PRE_NONE) {
+            float *nw = reinterpret_cast<float *>(smem + nst * stage_bytes);
+            for (uint32_t i = tid * 4u; i < K; i += I2S_THREADS * 4u)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(nw + i)),
+                             "l"(p.norm_w + i)
+                             : "memory");
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+    }
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();  // the input comes from the previous kernel
@@ -415,11 +535,15 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     if constexpr (FUSE_Q) {
         float *xs = reinterpret_cast<float *>(smem + nst * stage_bytes);
         int8_t *qs = reinterpret_cast<int8_t *>(xs + K);
-        if (p.pre != I2S_PRE_NONE) {
+        if (regs_pre) {
+            if (p.pre != I2S_PRE_NONE) {
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                __syncthreads();
+            }
+            act_scale = cta_prepare_regs(p, K, xs, qs, red);
+        } else {  // exact mode: the reference's sequential sum of squares
             cta_pre_input(p, K, xs, red);
             act_scale = cta_quantize(xs, K, xs, qs, red);
-        } else {
-            act_scale = cta_quantize(p.x, K, xs, qs, red);
         }
         if (blockIdx.x == 0) {
             if (p.q_out)

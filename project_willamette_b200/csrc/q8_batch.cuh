@@ -90,11 +90,12 @@ __device__ __forceinline__ void q8_word_to_f32(uint32_t word, float *f) {
                          8388736.0f);
 }
 
-// weight rows (when staged) | x [TG][K] | block terms [nb][TG][rows] (phases > 1) | totals [TG][rows]
+// weight rows (when staged) | RMSNorm weights [K] (when staged) | x [TG][K] |
+// block terms [nb][TG][rows] (phases > 1) | totals [TG][rows]
 inline size_t q8_batch_smem_bytes(uint32_t K, uint32_t tg, uint32_t rows, uint32_t phases,
-                                  bool stage_w = true) {
+                                  bool stage_w = true, bool norm = false) {
     const size_t terms = phases > 1 ? (size_t)(K / 32u) * tg * rows : 0;
-    return (stage_w ? (size_t)rows * q8_row_stride(K) : 0) +
+    return (stage_w ? (size_t)rows * q8_row_stride(K) + (norm ? (size_t)K * 4u : 0) : 0) +
            ((size_t)tg * K + terms + (size_t)tg * rows) * sizeof(float);
 }
 
@@ -119,7 +120,9 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
     const uint32_t t0 = blockIdx.y * TG;
     const uint32_t ntok = min((uint32_t)TG, p.n_tokens - t0);
     uint8_t *wsm = qbs;                                                // [R2][stride] weight rows
-    float *xs = reinterpret_cast<float *>(qbs + (p.stage_w ? (size_t)R2 * stride : 0));  // [TG][K]
+    const bool stage_nw = p.stage_w && p.pre == QB_PRE_RMSNORM;        // norm weights staged too
+    float *nws = reinterpret_cast<float *>(qbs + (p.stage_w ? (size_t)R2 * stride : 0));  // [K]
+    float *xs = nws + (stage_nw ? K : 0u);                             // [TG][K]
     float *terms = xs + (size_t)TG * K;                                // [nb][TG][R2] (P > 1)
     float *outs = terms + (P > 1 ? (size_t)nb * TG * R2 : 0);          // [TG][R2]
 
@@ -149,12 +152,13 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
             bytes[st] = min(RT, p.job[jx].n - r0) * stride;
             total += bytes[st];
         }
-        mbar_arrive_expect_tx(&s_bar[0], total);
+        mbar_arrive_expect_tx(&s_bar[0], total + (stage_nw ? K * 4u : 0u));
         for (uint32_t st = 0; st < sets; ++st) {
             const uint32_t jx = paired ? st : j;
             bulk_g2s(wsm + (size_t)st * RT * stride, p.job[jx].w + (size_t)r0 * stride, bytes[st],
                      &s_bar[0]);
         }
+        if (stage_nw) bulk_g2s(nws, p.norm_w, K * 4u, &s_bar[0]);
     }
     pdl_wait();
     if (tid == 0) {  // this group's activation rows
@@ -193,7 +197,8 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
             const float mean = __fdiv_rn(ss, (float)K);
             const float rsq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
             __syncwarp();
-            for (uint32_t i = lane; i < K; i += 32u) xt[i] = __fmul_rn(__fmul_rn(xt[i], rsq), p.norm_w[i]);
+            const float *nw = stage_nw ? nws : p.norm_w;
+            for (uint32_t i = lane; i < K; i += 32u) xt[i] = __fmul_rn(__fmul_rn(xt[i], rsq), nw[i]);
         }
         __syncthreads();
     }

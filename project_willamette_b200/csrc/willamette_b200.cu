@@ -2391,7 +2391,7 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
     {   // fast mode: one CTA per (KV head, split of `chunk` positions) for the
         // whole query group, when the group and head size have a kernel
         const uint32_t group = c.n_heads / c.n_kv_heads;
-        if (!c.exact && gqa_attn_kernel(c.head_dim, group)) {
+        if (!c.exact && gqa_attn_kernel(c.head_dim, group) && c.n_rot % 4 == 0) {
             uint32_t chunk = 32;  // about one CTA per SM at full context
             while ((uint64_t)((c.max_seq + chunk - 1) / chunk) * c.n_kv_heads > (uint64_t)cx.sm_count ||
                    (c.max_seq + chunk - 1) / chunk > AB_COMBINE / group)
@@ -2730,36 +2730,27 @@ int lb_q8(wl_llama_batch *m, const Q8BatchJob *jobs, uint32_t n_jobs, uint32_t K
     p.tokens = m->d_tokens;
     p.ids = ids;
     p.step = m->d_step;
-    // Tokens per CTA: the fixed choice when set and feasible, else the one with
-    // the least estimated time, waves x (TG + 2): a CTA's fixed cost (its
-    // weight copy, prologue, epilogue) is about two tokens' work.
+    // Tokens per CTA: the fixed choice when set and feasible, else the rule below.
     const QbKernel *ks = kQb[m->cfg.exact ? 0 : 1];
     int ti = -1;
-    uint64_t best = ~0ull;
     for (int c = 0; c < 4; ++c) {
         const uint32_t tg = kQbTg[c];
-        const size_t sm = q8_batch_smem_bytes(K, tg, R2, phases, p.stage_w != 0);
+        const size_t sm = q8_batch_smem_bytes(K, tg, R2, phases, p.stage_w != 0, pre == QB_PRE_RMSNORM);
         if (sm > (size_t)WL_MAX_DYN_SMEM) continue;
         if (m->fixed_tg) {
             if (tg == m->fixed_tg || ti < 0) ti = c;  // else the smallest feasible
             continue;
         }
         if (c > 0 && kQbTg[c - 1] >= m->n_seqs) break;  // a larger group only adds empty tokens
-        int occ = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ks[c], QB_THREADS, sm) != cudaSuccess ||
-            occ < 1)
-            occ = 1;
-        const uint64_t ctas = (uint64_t)tiles * ((m->n_seqs + tg - 1) / tg);
-        const uint64_t resident = (uint64_t)occ * (uint64_t)m->sm_count;
-        const uint64_t cost = (ctas + resident - 1) / resident * (tg + 2);
-        if (cost <= best) {
-            best = cost;
-            ti = c;
-        }
+        // measured on the SmolLM shapes (32 sequences): about 8 token groups
+        // (TG = sequences / 8) balance the per-CTA weight copy and conversion
+        // against the number of CTAs, for the layers and the lm-head alike;
+        // take the largest TG not above that
+        if (ti < 0 || tg <= std::max<uint32_t>(1u, (m->n_seqs + 7u) / 8u)) ti = c;
     }
     if (ti < 0) return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for the batched Q8_0 kernel", K);
     const uint32_t tg = kQbTg[ti];
-    const size_t smem = q8_batch_smem_bytes(K, tg, R2, phases, p.stage_w != 0);
+    const size_t smem = q8_batch_smem_bytes(K, tg, R2, phases, p.stage_w != 0, pre == QB_PRE_RMSNORM);
     WL_CUDA(launch(ks[ti], dim3(tiles, (m->n_seqs + tg - 1) / tg), dim3(QB_THREADS), smem, s, true, p));
     return WL_OK;
 }
@@ -2955,7 +2946,7 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
     // for groups of up to 4 q heads, splits filling about two CTAs per SM.
     const uint32_t group = c.n_heads / c.n_kv_heads;
     m->splits = 1;
-    if (!c.exact && gqa_attn_kernel(c.head_dim, group)) {
+    if (!c.exact && gqa_attn_kernel(c.head_dim, group) && c.n_rot % 4 == 0) {
         // splits of a fixed number of positions (a sequence uses as many as
         // its context needs, so CTAs are equally long whatever the context
         // mix); at most AB_COMBINE / group of them (the combine's table)
