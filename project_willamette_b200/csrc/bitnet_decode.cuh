@@ -130,8 +130,11 @@ __global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ O
     }
     const float mean = __fdiv_rn(sum_sq, (float)p.n);
     const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-    for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
-        p.out[i] = __fmul_rn(__fmul_rn(p.hidden[i], rsqrt), p.w[i]);
+    // distinct buffers: the loads of one pass need not wait for its stores
+    const float *__restrict__ h = p.hidden;
+    const float *__restrict__ w = p.w;
+    float *__restrict__ o = p.out;
+    for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(h[i], rsqrt), w[i]);
     __syncthreads();
     if (threadIdx.x == 0) *p.pos += 1u;
 }

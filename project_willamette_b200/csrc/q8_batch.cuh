@@ -375,8 +375,9 @@ __global__ void __launch_bounds__(256) out_norm_batch_kernel(const __grid_consta
     __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
-    const float *h = p.hidden + (size_t)blockIdx.x * p.n;
-    float *o = p.out + (size_t)blockIdx.x * p.n;
+    const float *__restrict__ h = p.hidden + (size_t)blockIdx.x * p.n;
+    float *__restrict__ o = p.out + (size_t)blockIdx.x * p.n;
+    const float *__restrict__ nw = p.w;
     float sum_sq;
     if (p.exact) {
         if (threadIdx.x == 0) {
@@ -393,7 +394,7 @@ __global__ void __launch_bounds__(256) out_norm_batch_kernel(const __grid_consta
     }
     const float mean = __fdiv_rn(sum_sq, (float)p.n);
     const float rsq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-    for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(h[i], rsq), p.w[i]);
+    for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(h[i], rsq), nw[i]);
 }
 
 }  // namespace wl
