@@ -16,7 +16,9 @@
 // chains with the same IEEE round-to-nearest operations (__fmul_rn /
 // __fadd_rn: no contraction), then the four threads of a row combine their
 // chains with the same tree.  The int->float conversion of q uses the
-// 2^23 magic-number construction, which is exact.
+// 2^23 magic-number construction, which is exact; it and q * (d * sc) run as
+// packed f32 pairs (two values per instruction), which round each lane as
+// the scalar operations do.
 //
 // Device layout (one-time repack, q6k_repack_kernel): each row becomes
 //   [ql: nb x 128][qh: nb x 64][sc: nb x 16][d: nb x 2][pad to 16 B]
@@ -271,27 +273,37 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
                         const uint32_t qhw[8] = {qhv0.x, qhv0.y, qhv0.z, qhv0.w,
                                                  qhv1.x, qhv1.y, qhv1.z, qhv1.w};
                         const uint32_t xbase = b * 256u + h * 128u + a * 32u;
+                        const float2 bias = make_float2(-8388640.0f, -8388640.0f);
 #pragma unroll
                         for (int m = 0; m < 8; ++m) {
                             const uint32_t u4 = ((qlw[m] >> ql_shift) & 0x0F0F0F0Fu) |
                                                 (((qhw[m] >> qh_shift) & 0x03030303u) << 4);
                             const float sc_f = m < 4 ? s0 : s1;
-                            float w[4];
+                            const float2 sc2 = make_float2(sc_f, sc_f);
+                            // (2^23 + u) - (2^23 + 32) = u - 32, exact; then q * (d * sc).
+                            // Packed pairs here only: no add follows these
+                            // multiplies, so nothing can be fused into an FMA.
+                            // The product with x and the chain add stay scalar
+                            // mul.rn / add.rn, which are never contracted.
+                            float2 w[2];
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const float qf = __fadd_rn(
-                                    __uint_as_float(__byte_perm(u4, 0x4B000000u, 0x7440 + k)),
-                                    -8388640.0f);  // (2^23 + u) - (2^23 + 32) = u - 32, exact
-                                w[k] = __fmul_rn(qf, sc_f);
+                            for (int j = 0; j < 2; ++j) {
+                                const float2 qf = f2_add_rn(
+                                    make_float2(
+                                        __uint_as_float(__byte_perm(u4, 0x4B000000u, 0x7440 + 2 * j)),
+                                        __uint_as_float(
+                                            __byte_perm(u4, 0x4B000000u, 0x7441 + 2 * j))),
+                                    bias);
+                                w[j] = f2_mul_rn(qf, sc2);
                             }
 #pragma unroll
                             for (int g = 0; g < BG; ++g) {
                                 const float4 xv = *reinterpret_cast<const float4 *>(
                                     xs + g * xs_len + q6k_xpad(xbase + 4u * m));
-                                acc[g][0] = __fadd_rn(acc[g][0], __fmul_rn(w[0], xv.x));
-                                acc[g][1] = __fadd_rn(acc[g][1], __fmul_rn(w[1], xv.y));
-                                acc[g][2] = __fadd_rn(acc[g][2], __fmul_rn(w[2], xv.z));
-                                acc[g][3] = __fadd_rn(acc[g][3], __fmul_rn(w[3], xv.w));
+                                acc[g][0] = __fadd_rn(acc[g][0], __fmul_rn(w[0].x, xv.x));
+                                acc[g][1] = __fadd_rn(acc[g][1], __fmul_rn(w[0].y, xv.y));
+                                acc[g][2] = __fadd_rn(acc[g][2], __fmul_rn(w[1].x, xv.z));
+                                acc[g][3] = __fadd_rn(acc[g][3], __fmul_rn(w[1].y, xv.w));
                             }
                         }
                     }

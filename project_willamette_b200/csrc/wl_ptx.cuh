@@ -118,4 +118,32 @@ __device__ __forceinline__ float4 lds128f(const void *p) {
     return v;
 }
 
+// Packed f32 pairs (sm_100a): one instruction, each lane rounded to nearest
+// as the scalar mul.rn / add.rn.  A packed multiply whose result feeds a
+// packed add can still be fused into one FMA by the assembler (one rounding
+// instead of two), so code that must keep two roundings uses these only where
+// no add consumes a product, and keeps scalar mul.rn / add.rn there.
+__device__ __forceinline__ float2 f2_mul_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{.reg .b64 a, b, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 d, a, b;\n\t"
+        "mov.b64 {%0, %1}, d;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 f2_add_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{.reg .b64 a, b, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "add.rn.f32x2 d, a, b;\n\t"
+        "mov.b64 {%0, %1}, d;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 }  // namespace wl

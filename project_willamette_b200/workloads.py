@@ -3,11 +3,14 @@ kernel family without the rest of ``bench.py``:
 
     python -m project_willamette_b200.workloads smollm_decode
     python -m project_willamette_b200.workloads bitnet_decode
+    python -m project_willamette_b200.workloads lm_head
 
 Each sets its model up (seeded as in ``bench.py``), prefills, and then runs
 two decode steps inside a CUDA profiler range (``cudaProfilerStart`` /
 ``Stop``), so ``ncu --profile-from-start off`` captures only the steady
-decode kernels.
+decode kernels.  ``lm_head`` repacks a 128256 x 2560 Q6_K matrix (config 4)
+and runs the greedy head at batch 1 (twice) and batch 4 (once) inside the
+range.
 """
 from __future__ import annotations
 
@@ -57,7 +60,50 @@ def bitnet_decode(steps: int = 2) -> float:
     return ms
 
 
-WORKLOADS = {"smollm_decode": smollm_decode, "bitnet_decode": bitnet_decode}
+def lm_head(calls: int = 2) -> float:
+    """BASELINE config 4: Q6_K tied lm-head + greedy argmax, 128256 x 2560;
+    `calls` batch-1 calls and one batch-4 call, device entry points on
+    device buffers.  Returns the batch-1 ms per call."""
+    import torch
+    from . import synth
+    from ._abi import lib
+    L = lib()
+    d_model, vocab = 2560, 128256
+    dev = torch.device("cuda:0")
+    raw = torch.from_numpy(synth.q6k_rows(np.random.default_rng(SEED + 4), d_model, vocab))
+    raw = raw.to(dev)
+    packed = torch.empty(L.wl_q6k_packed_bytes(d_model, vocab), dtype=torch.uint8, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    if L.wl_dev_q6k_repack(raw.data_ptr(), d_model, vocab, packed.data_ptr(), s):
+        raise RuntimeError(L.wl_last_error().decode())
+    del raw
+    H = torch.randn(4, d_model, device=dev, generator=torch.Generator(dev).manual_seed(SEED))
+    ids = torch.zeros(4, dtype=torch.int32, device=dev)
+    scratch = torch.zeros(L.wl_q6k_scratch_bytes(4), dtype=torch.uint8, device=dev)
+
+    def head(batch):
+        if L.wl_dev_q6k_lm_head(packed.data_ptr(), d_model, vocab, H.data_ptr(), batch, None,
+                                ids.data_ptr(), scratch.data_ptr(), s):
+            raise RuntimeError(L.wl_last_error().decode())
+
+    head(1)
+    torch.cuda.synchronize()
+
+    def run():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(calls):
+            head(1)
+        b.record()
+        head(4)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / calls
+
+    return _profiled(run)
+
+
+WORKLOADS = {"smollm_decode": smollm_decode, "bitnet_decode": bitnet_decode,
+             "lm_head": lm_head}
 
 if __name__ == "__main__":
     name = sys.argv[1] if len(sys.argv) > 1 else ""
