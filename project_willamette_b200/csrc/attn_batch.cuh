@@ -203,8 +203,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
             const float x = isv ? vs[kvh * HD + d] : ks[kvh * HD + d];
             int qi = 0;
             if (!(isv ? zv : zk)) {
-                const float r = roundf(__fmul_rn(x, isv ? iv : ik));
-                qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+                qi = quant_round_i8(__fmul_rn(x, isv ? iv : ik));
             }
             (isv ? vq : kq)[d] = (int8_t)qi;
             if (sp == 0) (isv ? v_cache : k_cache)[(size_t)pos * KV + kvh * HD + d] = (int8_t)qi;

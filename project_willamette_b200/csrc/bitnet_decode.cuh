@@ -192,8 +192,7 @@ __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, in
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
         int qi = 0;
         if (!zero) {
-            const float r = roundf(__fmul_rn(x[i], inv));
-            qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+            qi = quant_round_i8(__fmul_rn(x[i], inv));
         }
         q[i] = (int8_t)qi;
     }

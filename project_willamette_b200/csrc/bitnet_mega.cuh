@@ -257,8 +257,7 @@ __device__ __noinline__ float mega_norm_quantize(const MegaParams &p, float *xs,
     for (uint32_t i = tid; i < K; i += blockDim.x) {
         int qi = 0;
         if (max_abs != 0.0f) {
-            const float r = roundf(__fmul_rn(xs[i], inv));
-            qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+            qi = quant_round_i8(__fmul_rn(xs[i], inv));
         }
         qs[i] = (int8_t)qi;
     }

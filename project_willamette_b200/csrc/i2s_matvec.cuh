@@ -126,9 +126,7 @@ __global__ void __launch_bounds__(QUANT_THREADS)
         uint32_t packed = 0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            float r = roundf(__fmul_rn(e[k], inv));
-            int qi = 0;
-            if (!isnan(r)) qi = (int)fminf(fmaxf(r, -127.0f), 127.0f);
+            const int qi = quant_round_i8(__fmul_rn(e[k], inv));
             packed |= (uint32_t)(qi & 0xFF) << (8 * k);
         }
         *reinterpret_cast<uint32_t *>(qr + i) = packed;
@@ -234,10 +232,25 @@ __device__ __forceinline__ int32_t i2s_row_c3(const uint8_t *rp, const int8_t *q
     return corr;
 }
 
+// Warp-sum of a thread's share of the quantised activations, stored for the
+// CTA total (read after the quantiser's final barrier: cta_qsum).
+__device__ __forceinline__ void publish_qsum(int32_t qsum, int32_t *ared) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, off);
+    if ((threadIdx.x & 31) == 0) ared[threadIdx.x >> 5] = qsum;
+}
+__device__ __forceinline__ int32_t cta_qsum(const int32_t *ared) {
+    int32_t t = 0;
+#pragma unroll
+    for (int w = 0; w < I2S_WARPS; ++w) t += ared[w];
+    return t;
+}
+
 // Absmax quantisation of x[0..K) by the whole CTA into shared memory (same
-// IEEE steps as quantize_absmax_kernel).  Returns the activation scale.
+// IEEE steps as quantize_absmax_kernel).  Returns the activation scale; the
+// per-warp sums of the quantised values go to `ared`.
 __device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint32_t K, float *xs,
-                                              int8_t *qs, float *red) {
+                                              int8_t *qs, float *red, int32_t *ared) {
     const uint32_t tid = threadIdx.x, nthr = blockDim.x;
     float m = 0.0f;
     for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
@@ -252,6 +265,7 @@ __device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint3
     float max_abs = red[0];
     for (uint32_t w = 1; w < nthr / 32; ++w) max_abs = fmaxf(max_abs, red[w]);
     const float inv = max_abs == 0.0f ? 0.0f : __fdiv_rn(127.0f, max_abs);
+    int32_t qsum = 0;
     for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
         const float4 v = *reinterpret_cast<const float4 *>(xs + i);
         const float e[4] = {v.x, v.y, v.z, v.w};
@@ -259,13 +273,14 @@ __device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint3
         if (max_abs != 0.0f) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float r = roundf(__fmul_rn(e[k], inv));
-                const int qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+                const int qi = quant_round_i8(__fmul_rn(e[k], inv));
                 packed |= (uint32_t)(qi & 0xFF) << (8 * k);
             }
         }
         *reinterpret_cast<uint32_t *>(qs + i) = packed;
+        qsum = __dp4a((int)packed, 0x01010101, qsum);
     }
+    publish_qsum(qsum, ared);
     __syncthreads();
     return max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
 }
@@ -339,12 +354,18 @@ __device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t
 constexpr int I2S_PRE_V = (int)(I2S_FUSE_Q_MAX_K / (I2S_THREADS * 4u));  // float4 per thread
 
 __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint32_t K,
-                                                  const float *nw, int8_t *qs, float *red) {
+                                                  const float *nw, int8_t *qs, float *red,
+                                                  int32_t *ared) {
     const uint32_t tid = threadIdx.x, nthr = blockDim.x;
     const bool relu2 = p.pre == I2S_PRE_RELU2_RMSNORM;
+    // float4 slots this CTA's K needs: the unrolled loops leave at the first
+    // unused one (a warp-uniform branch) instead of issuing predicated-off
+    // work for every slot up to I2S_FUSE_Q_MAX_K.
+    const int kmax = (int)((K + nthr * 4u - 1u) / (nthr * 4u));
     float4 v[I2S_PRE_V];
 #pragma unroll
     for (int k = 0; k < I2S_PRE_V; ++k) {
+        if (k >= kmax) break;
         const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
         if (i < K) v[k] = *reinterpret_cast<const float4 *>(p.x + i);
     }
@@ -354,12 +375,14 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
             float4 u[I2S_PRE_V / 2];
 #pragma unroll
             for (int k = 0; k < I2S_PRE_V / 2; ++k) {
+                if (h * (I2S_PRE_V / 2) + k >= kmax) break;
                 const uint32_t i = tid * 4u + (uint32_t)(h * (I2S_PRE_V / 2) + k) * nthr * 4u;
                 if (i < K) u[k] = *reinterpret_cast<const float4 *>(p.x2 + i);
             }
 #pragma unroll
             for (int k = 0; k < I2S_PRE_V / 2; ++k) {
                 const int kk = h * (I2S_PRE_V / 2) + k;
+                if (kk >= kmax) break;
                 const uint32_t i = tid * 4u + (uint32_t)kk * nthr * 4u;
                 if (i < K) {
                     float4 &x = v[kk];
@@ -377,6 +400,7 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
         float ss = 0.0f;
 #pragma unroll
         for (int k = 0; k < I2S_PRE_V; ++k) {
+            if (k >= kmax) break;
             const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
             if (i < K)
                 ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v[k].x, v[k].x), __fmul_rn(v[k].y, v[k].y)),
@@ -392,6 +416,7 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
         const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
 #pragma unroll
         for (int k = 0; k < I2S_PRE_V; ++k) {
+            if (k >= kmax) break;
             const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
             if (i < K) {
                 const float4 w = *reinterpret_cast<const float4 *>(nw + i);
@@ -406,6 +431,7 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
     float m = 0.0f;
 #pragma unroll
     for (int k = 0; k < I2S_PRE_V; ++k) {
+        if (k >= kmax) break;
         const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
         if (i < K)
             m = fmaxf(fmaxf(fmaxf(m, fabsf(v[k].x)), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w)));
@@ -417,23 +443,24 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
     float max_abs = red[0];
     for (uint32_t w = 1; w < nthr / 32; ++w) max_abs = fmaxf(max_abs, red[w]);
     const float inv = max_abs == 0.0f ? 0.0f : __fdiv_rn(127.0f, max_abs);
+    int32_t qsum = 0;
 #pragma unroll
     for (int k = 0; k < I2S_PRE_V; ++k) {
+        if (k >= kmax) break;
         const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
         if (i < K) {
-            const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-            uint32_t packed = 0;
-            if (max_abs != 0.0f) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const float r = roundf(__fmul_rn(e[c], inv));
-                    const int qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
-                    packed |= (uint32_t)(qi & 0xFF) << (8 * c);
-                }
-            }
+            const uint32_t packed =
+                max_abs != 0.0f
+                    ? pack_i8x4(quant_round_i8(__fmul_rn(v[k].x, inv)),
+                                quant_round_i8(__fmul_rn(v[k].y, inv)),
+                                quant_round_i8(__fmul_rn(v[k].z, inv)),
+                                quant_round_i8(__fmul_rn(v[k].w, inv)))
+                    : 0u;
             *reinterpret_cast<uint32_t *>(qs + i) = packed;
+            qsum = __dp4a((int)packed, 0x01010101, qsum);
         }
     }
+    publish_qsum(qsum, ared);
     __syncthreads();
     return max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
 }
@@ -477,6 +504,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[I2S_MAX_STAGES];
     __shared__ float red[I2S_WARPS];
+    __shared__ int32_t ared[I2S_WARPS];
     constexpr int RPW = 32 / LPR;
     constexpr uint32_t RPI = I2S_WARPS * RPW;
 
@@ -540,10 +568,10 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
                 asm volatile("cp.async.wait_all;" ::: "memory");
                 __syncthreads();
             }
-            act_scale = cta_prepare_regs(p, K, xs, qs, red);
+            act_scale = cta_prepare_regs(p, K, xs, qs, red, ared);
         } else {  // exact mode: the reference's sequential sum of squares
             cta_pre_input(p, K, xs, red);
-            act_scale = cta_quantize(xs, K, xs, qs, red);
+            act_scale = cta_quantize(xs, K, xs, qs, red, ared);
         }
         if (blockIdx.x == 0) {
             if (p.q_out)
@@ -560,26 +588,34 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     const uint32_t s = lane % LPR;
     const uint32_t sub = lane / LPR;
     uint4 act[NP > 0 ? NP : 1][4];
+    // Sum of the quantised activations (the code-offset term): with FUSE_Q
+    // the quantiser produced the CTA total, subtracted once per row after the
+    // lane reduction; otherwise each lane sums the slots it owns.
     int32_t asum = 0;
+    if constexpr (FUSE_Q) asum = cta_qsum(ared);
     if constexpr (NP > 0) {
 #pragma unroll
         for (int i = 0; i < NP; ++i) {
             const uint32_t pp = s + LPR * i;
             if (pp < P) {
                 i2s_load_act(q, pp, act[i]);
+                if constexpr (!FUSE_Q) {
 #pragma unroll
-                for (int o = 0; o < 4; ++o) asum += sum_bytes(act[i][o]);
+                    for (int o = 0; o < 4; ++o) asum += sum_bytes(act[i][o]);
+                }
             } else {
 #pragma unroll
                 for (int o = 0; o < 4; ++o) act[i][o] = make_uint4(0, 0, 0, 0);
             }
         }
     } else {
-        for (uint32_t pp = s; pp < P; pp += LPR) {
-            uint4 a[4];
-            i2s_load_act(q, pp, a);
+        if constexpr (!FUSE_Q) {
+            for (uint32_t pp = s; pp < P; pp += LPR) {
+                uint4 a[4];
+                i2s_load_act(q, pp, a);
 #pragma unroll
-            for (int o = 0; o < 4; ++o) asum += sum_bytes(a[o]);
+                for (int o = 0; o < 4; ++o) asum += sum_bytes(a[o]);
+            }
         }
     }
 
@@ -617,12 +653,13 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
                 }
             }
         }
-        int32_t dot = i2s_acc_total(acc) - asum;
+        int32_t dot = i2s_acc_total(acc) - (FUSE_Q ? 0 : asum);
 #pragma unroll
         for (int off = LPR / 2; off > 0; off >>= 1) {
             dot += __shfl_xor_sync(0xffffffffu, dot, off);
             if constexpr (C3) c3 |= __shfl_xor_sync(0xffffffffu, c3, off);
         }
+        if constexpr (FUSE_Q) dot -= asum;
         if constexpr (C3) {
             if ((c3 & 0x55555555u) != 0u) {  // uniform across the LPR lanes of this row
                 int32_t corr = row < r1 ? i2s_row_c3(rp, q, s, LPR, P) : 0;

@@ -97,8 +97,7 @@ __global__ void __launch_bounds__(QUANT_THREADS)
         if (max_abs != 0.0f) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float r = roundf(__fmul_rn(e[k], inv));
-                const int qi = isnan(r) ? 0 : (int)fminf(fmaxf(r, -127.0f), 127.0f);
+                const int qi = quant_round_i8(__fmul_rn(e[k], inv));
                 packed |= (uint32_t)(qi & 0xFF) << (8 * k);
             }
         }

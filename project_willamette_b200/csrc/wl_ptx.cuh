@@ -118,6 +118,27 @@ __device__ __forceinline__ float4 lds128f(const void *p) {
     return v;
 }
 
+// Activation quantiser rounding: round(v) half away from zero, clamped to
+// [-127, 127], NaN -> 0 -- Rust's f32::round, then the clamp and saturating
+// `as i8` of the reference's absmax quantiser.  Exact, and without the slow
+// round/convert instructions: for a = min(|v|, 127), b = a + 0.5 rounded
+// toward zero has floor(b) = floor(a + 0.5) (every integer below 128 is a
+// float, so truncation cannot step over one), and b + 2^23 rounded toward
+// zero lies in [2^23, 2^23 + 128), where floats are the integers, so its
+// low bits are floor(b).
+__device__ __forceinline__ int quant_round_i8(float v) {
+    const float a = fminf(fabsf(v), 127.0f);
+    const int qa =
+        (int)(__float_as_uint(__fadd_rz(__fadd_rz(a, 0.5f), 8388608.0f)) - 0x4B000000u);
+    return v > 0.0f ? qa : (v < 0.0f ? -qa : 0);  // NaN fails both tests -> 0
+}
+
+// Four quantised values (low bytes of q0..q3) packed into one word, q0 lowest.
+__device__ __forceinline__ uint32_t pack_i8x4(int q0, int q1, int q2, int q3) {
+    return __byte_perm(__byte_perm((uint32_t)q0, (uint32_t)q1, 0x0040u),
+                       __byte_perm((uint32_t)q2, (uint32_t)q3, 0x0040u), 0x5410u);
+}
+
 // Packed f32 pairs (sm_100a): one instruction, each lane rounded to nearest
 // as the scalar mul.rn / add.rn.  A packed multiply whose result feeds a
 // packed add can still be fused into one FMA by the assembler (one rounding

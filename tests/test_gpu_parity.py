@@ -66,7 +66,8 @@ def test_i2s_fuzz_shapes(in_dim, out_dim):
     _check_i2s(*_i2s_case(rng, in_dim, out_dim, code3=0.02 if out_dim % 2 else 0.0))
 
 
-@pytest.mark.parametrize("kind", ["zeros", "outlier", "nan", "inf", "neg_zero", "tiny", "ties"])
+@pytest.mark.parametrize("kind", ["zeros", "outlier", "nan", "inf", "neg_zero", "tiny", "ties",
+                                  "round_edges"])
 def test_i2s_activation_edge_cases(kind):
     rng = np.random.default_rng(42)
     in_dim, out_dim = 768, 97
@@ -88,6 +89,15 @@ def test_i2s_activation_edge_cases(kind):
     elif kind == "ties":  # values landing exactly on .5 after scaling
         x = (np.arange(in_dim, dtype=np.float32) % 255 - 127) / np.float32(2.0)
         x[0] = 127.0
+    elif kind == "round_edges":
+        # max |x| = 127 makes the scale exactly 1, so each x is rounded as is:
+        # every k + 0.5 (k = 0..126) and its two float neighbours, both signs
+        h = np.arange(127, dtype=np.float32) + np.float32(0.5)
+        e = np.concatenate([np.nextafter(h, np.float32(0)), h, np.nextafter(h, np.float32(200))])
+        x = np.zeros(in_dim, np.float32)
+        x[0] = 127.0
+        x[1:1 + e.size] = e
+        x[1 + e.size:1 + 2 * e.size] = -e
     _check_i2s(*_i2s_case(rng, in_dim, out_dim, code3=0.01, x=x))
 
 
