@@ -496,8 +496,12 @@ __device__ __forceinline__ void i2s_issue_chunk(const I2sMatvecParams &p, uint32
 // are re-read from L1 per row (very large K).  FUSE_Q: the CTA quantises the
 // f32 input itself (no separate kernel, one dependency hop less).  C3: the
 // weights may contain code 0b11 (checked per row; the fast path otherwise).
-// At most 128 registers per thread, so the next op's CTA fits on the same SM
-// and its weight prefetch overlaps this op (programmatic dependent launch).
+// At most 128 registers per thread, so the next op's CTA fits on the same SM.
+// The programmatic-launch trigger comes after the row loop: the next op's
+// CTAs then arrive while this op's last rows finish and start their weight
+// copies there.  (Triggering at entry let them run their prologue beside this
+// op's whole pre-phase and row loop on the same SMs, which slowed this op's
+// slowest CTAs by 2-4 us: a BitNet decode token took 1631 instead of 1427 us.)
 template <int LPR, int NP, bool FUSE_Q, bool C3>
 __global__ void __launch_bounds__(I2S_THREADS, 2)
     i2s_matvec_kernel(const __grid_constant__ I2sMatvecParams p) {
@@ -550,7 +554,6 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         }
     }
     __syncthreads();
-    pdl_launch_dependents();
     pdl_wait();  // the input comes from the previous kernel
     if (p.tp.world && p.tp.wait) {
         // the input is a vector all ranks gathered into this rank's block
@@ -703,6 +706,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             i2s_issue_chunk(p, c + nst, r0, r1, RPI, row_bytes, smem + st * stage_bytes,
                             &full_bar[st], policy);
     }
+    pdl_launch_dependents();
     if (p.tp.world && tid == 0) tp_arrive(p.tp);  // after the loop's final barrier
 }
 
