@@ -48,7 +48,7 @@ inline size_t attn_gqa_smem_bytes(uint32_t kv, uint32_t hd, uint32_t group, uint
     const uint32_t chunk = (chunk_pos + 3u) & ~3u;
     const uint32_t half2 = ((hd / 2u + 1u) & ~1u) * 2u;
     size_t f = 2u * kv                          // k, v (rotated k)
-               + group * hd                     // q heads
+               + group * (hd + 4u)              // q heads (rows padded by 4 floats)
                + half2                          // RoPE row
                + (size_t)group * chunk          // scores / weights
                + 2u * chunk                     // K and V scales of the split's positions
@@ -96,8 +96,9 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     const uint32_t chunk_max = (p.chunk + 3u) & ~3u;
     float *ks = reinterpret_cast<float *>(smem);      // KV
     float *vs = ks + KV;                              // KV
-    float *qg = vs + KV;                              // G * HD
-    float2 *rope = reinterpret_cast<float2 *>(qg + G * HD);  // half (rounded to 2)
+    constexpr uint32_t QS = HD + 4u;                  // padded q row: the G heads on distinct banks
+    float *qg = vs + KV;                              // G * QS
+    float2 *rope = reinterpret_cast<float2 *>(qg + G * QS);  // half (rounded to 2)
     float *scores = reinterpret_cast<float *>(rope + ((half + 1u) & ~1u));  // G * chunk_max
     float *vsc = scores + (size_t)G * chunk_max;      // chunk_max
     float *ksc = vsc + chunk_max;                     // chunk_max
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
         cp_async16(vs + 4u * i, v_in + 4u * i);
     }
     for (uint32_t i = tid; i < G * HD / 4u; i += AB_THREADS)
-        cp_async16(qg + 4u * i, q_in + kvh * G * HD + 4u * i);
+        cp_async16(qg + (4u * i / HD) * QS + (4u * i) % HD, q_in + kvh * G * HD + 4u * i);
     for (uint32_t j = tid; j < half / 2u; j += AB_THREADS) cp_async16(rope + 2u * j, cs + 2u * j);
     cp_async_commit();
     {
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     const uint32_t pstep = p.rope_pairs ? 2u : 1u, poff = p.rope_pairs ? 1u : half;
     for (uint32_t i = tid; i < (p.n_kv_heads + G) * half; i += AB_THREADS) {
         const uint32_t hh = i / half, j = i % half;
-        float *x = hh < p.n_kv_heads ? ks + hh * HD : qg + (hh - p.n_kv_heads) * HD;
+        float *x = hh < p.n_kv_heads ? ks + hh * HD : qg + (hh - p.n_kv_heads) * QS;
         const uint32_t i0 = j * pstep, i1 = i0 + poff;
         const float a = x[i0], b = x[i1], c = rope[j].x, s = rope[j].y;
         x[i0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
@@ -222,39 +223,77 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     const float sk_cur = s_sc[0], sv_cur = s_sc[1];
     cp_async_wait_all();
     __syncthreads();
-    // 3. scores (G heads) per position
-    for (uint32_t i = tid; i < cnt; i += AB_THREADS) {
-        const uint32_t t = t0 + i;
-        const int8_t *kr = t == pos ? kq : ksm + (size_t)i * KR;
-        const float sk = t == pos ? sk_cur : ksc[i];
-        if (t == pos) vsc[i] = sv_cur;
-        uint4 w[HD / 16];  // the whole head row in one round of loads
+    // 3. scores.  Each head's dot runs over the dimensions in order.  Short
+    //    splits (positions x heads within one pass of the CTA) take one
+    //    thread per (position, head), the G threads of a position adjacent so
+    //    its K row is read once per warp, with the K bytes turned into floats
+    //    by the 2^23 construction, (2^23 + (b + 128)) - (2^23 + 128) = b
+    //    (exact, and cheaper than the convert instruction when few threads
+    //    are busy); longer splits one thread per position for all G heads,
+    //    each K row converted once.  Both give the same sums.
+    if (cnt * G <= AB_THREADS) {
+        if (tid < cnt * G) {
+            const uint32_t i = tid / G, g = tid % G;
+            const uint32_t t = t0 + i;
+            const int8_t *kr = t == pos ? kq : ksm + (size_t)i * KR;
+            const float sk = t == pos ? sk_cur : ksc[i];
+            if (t == pos && g == 0) vsc[i] = sv_cur;
+            const float *qh = qg + g * QS;
+            float d = 0.0f;
+#pragma unroll 2
+            for (uint32_t c = 0; c < HD / 16u; ++c) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(kr + c * 16u);
+                const uint32_t wv[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
+                                        w.w ^ 0x80808080u};
 #pragma unroll
-        for (uint32_t c = 0; c < HD / 16; ++c) w[c] = *reinterpret_cast<const uint4 *>(kr + c * 16u);
-        float d[G];
+                for (uint32_t e4 = 0; e4 < 4u; ++e4) {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qh + c * 16u + e4 * 4u);
+                    const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-        for (uint32_t g = 0; g < G; ++g) d[g] = 0.0f;
-#pragma unroll
-        for (uint32_t c = 0; c < HD / 16; ++c) {
-            const uint32_t wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
-#pragma unroll
-            for (uint32_t e4 = 0; e4 < 4; ++e4) {
-                float k8[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    k8[e] = __fmul_rn((float)(int8_t)(wv[e4] >> (8 * e)), sk);
-#pragma unroll
-                for (uint32_t g = 0; g < G; ++g) {
-                    const float4 q4 = *reinterpret_cast<const float4 *>(qg + g * HD + c * 16u + e4 * 4u);
-                    d[g] = __fmaf_rn(q4.x, k8[0], d[g]);
-                    d[g] = __fmaf_rn(q4.y, k8[1], d[g]);
-                    d[g] = __fmaf_rn(q4.z, k8[2], d[g]);
-                    d[g] = __fmaf_rn(q4.w, k8[3], d[g]);
+                    for (uint32_t e = 0; e < 4u; ++e) {
+                        const float k8 = __fmul_rn(
+                            __fsub_rn(__uint_as_float(__byte_perm(wv[e4], 0x4B000000u, 0x7440u + e)),
+                                      8388736.0f),
+                            sk);
+                        d = __fmaf_rn(qv[e], k8, d);
+                    }
                 }
             }
+            scores[g * chunk_max + i] = __fmul_rn(d, p.scale);
         }
+    } else {
+        for (uint32_t i = tid; i < cnt; i += AB_THREADS) {
+            const uint32_t t = t0 + i;
+            const int8_t *kr = t == pos ? kq : ksm + (size_t)i * KR;
+            const float sk = t == pos ? sk_cur : ksc[i];
+            if (t == pos) vsc[i] = sv_cur;
+            float d[G];
 #pragma unroll
-        for (uint32_t g = 0; g < G; ++g) scores[g * chunk_max + i] = __fmul_rn(d[g], p.scale);
+            for (uint32_t g = 0; g < G; ++g) d[g] = 0.0f;
+#pragma unroll
+            for (uint32_t c = 0; c < HD / 16u; ++c) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(kr + c * 16u);
+                const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (uint32_t e4 = 0; e4 < 4u; ++e4) {
+                    float k8[4];
+#pragma unroll
+                    for (uint32_t e = 0; e < 4u; ++e)
+                        k8[e] = __fmul_rn((float)(int8_t)(wv[e4] >> (8 * e)), sk);
+#pragma unroll
+                    for (uint32_t g = 0; g < G; ++g) {
+                        const float4 q4 =
+                            *reinterpret_cast<const float4 *>(qg + g * QS + c * 16u + e4 * 4u);
+                        d[g] = __fmaf_rn(q4.x, k8[0], d[g]);
+                        d[g] = __fmaf_rn(q4.y, k8[1], d[g]);
+                        d[g] = __fmaf_rn(q4.z, k8[2], d[g]);
+                        d[g] = __fmaf_rn(q4.w, k8[3], d[g]);
+                    }
+                }
+            }
+#pragma unroll
+            for (uint32_t g = 0; g < G; ++g) scores[g * chunk_max + i] = __fmul_rn(d[g], p.scale);
+        }
     }
     __syncthreads();
     // 4. per-head max and sum of exp
@@ -378,12 +417,23 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
     if (!s_last) return;
     __threadfence();
     // combine: M = max m_s, f_s = exp(m_s - M), O = sum f_s o_s / sum f_s l_s.
-    // Every split's (max, sum) pair arrives in one round of loads; the o rows
-    // in rounds of 16 independent loads per output (the splits' partials are
-    // L2-resident, so the rounds, not the bytes, set the time).
+    // Every split's (max, sum) pair and the first 16 splits' o values of this
+    // thread's outputs are requested in one round of loads (the partials are
+    // L2-resident, so the rounds, not the bytes, set the time); further
+    // splits follow in rounds of 16.
     const float *base = p.partial + ((size_t)z * gridDim.x + kvh) * gridDim.z * G * RS;
     float *fac = stat;               // [S][G] maxima, then combine factors
     float *lsm = stat + AB_COMBINE;  // [S][G] sums (S * G <= AB_COMBINE, checked by the host)
+    constexpr uint32_t OPT = (G * HD + AB_THREADS - 1u) / AB_THREADS;  // outputs per thread
+    float v0[OPT][16];
+#pragma unroll
+    for (uint32_t k = 0; k < OPT; ++k) {
+        const uint32_t i = tid + k * AB_THREADS;
+        const uint32_t g = i / HD, d = i % HD;
+#pragma unroll
+        for (uint32_t u = 0; u < 16u; ++u)
+            v0[k][u] = (i < G * HD && u < S) ? __ldcg(base + ((size_t)u * G + g) * RS + d) : 0.0f;
+    }
     for (uint32_t i = tid; i < S * G; i += AB_THREADS) {
         fac[i] = __ldcg(base + (size_t)i * RS + HD);
         lsm[i] = __ldcg(base + (size_t)i * RS + HD + 1);
@@ -403,10 +453,16 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
         red[g] = !isfinite(M) ? 0.0f : (L > 0.0f ? __fdiv_rn(1.0f, L) : 1.0f);
     }
     __syncthreads();
-    for (uint32_t i = tid; i < G * HD; i += AB_THREADS) {
+#pragma unroll
+    for (uint32_t k = 0; k < OPT; ++k) {
+        const uint32_t i = tid + k * AB_THREADS;
+        if (i >= G * HD) break;
         const uint32_t g = i / HD, d = i % HD;
         float o = 0.0f;
-        for (uint32_t s0 = 0; s0 < S; s0 += 16u) {
+#pragma unroll
+        for (uint32_t u = 0; u < 16u; ++u)
+            if (u < S) o = __fmaf_rn(v0[k][u], fac[u * G + g], o);
+        for (uint32_t s0 = 16u; s0 < S; s0 += 16u) {
             float v[16];
 #pragma unroll
             for (uint32_t u = 0; u < 16u; ++u)
