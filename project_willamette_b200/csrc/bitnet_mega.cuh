@@ -285,7 +285,7 @@ __device__ __noinline__ void mega_matvec_t(const MegaParams &p, const MegaSet &s
     for (int i = 0; i < NP; ++i) {
         const uint32_t pp = sl + LPR * i;
         if (pp < P) {
-            i2s_load_act(qs, pp, act[i]);
+            i2s_load_act<false>(qs, pp, 0u, act[i]);
 #pragma unroll
             for (int o = 0; o < 4; ++o) asum += sum_bytes(act[i][o]);
         } else {
@@ -320,7 +320,7 @@ __device__ __noinline__ void mega_matvec_t(const MegaParams &p, const MegaSet &s
         }
         if constexpr (C3) {
             if ((c3 & 0x55555555u) != 0u) {  // uniform across the row's lanes
-                int32_t corr = rl < R ? i2s_row_c3(rp, qs, sl, LPR, P) : 0;
+                int32_t corr = rl < R ? i2s_row_c3<false>(rp, qs, 0u, sl, LPR, P) : 0;
                 const uint32_t grp = __match_any_sync(__activemask(), rl);
 #pragma unroll
                 for (int off = LPR / 2; off > 0; off >>= 1) corr += __shfl_xor_sync(grp, corr, off);

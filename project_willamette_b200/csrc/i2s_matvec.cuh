@@ -209,21 +209,47 @@ __device__ __forceinline__ int32_t sum_bytes(uint4 v) {
     return __dp4a((int)v.w, 0x01010101, s);
 }
 
-// The four 16-byte activation vectors that line up with weight slot pp.
-__device__ __forceinline__ void i2s_load_act(const int8_t *q, uint32_t pp, uint4 (&a)[4]) {
-    const int8_t *base = q + (pp >> 1) * 128u + (pp & 1u) * 16u;
+// Shared-memory layout of the quantised activations in the fused kernels
+// (V = true): vector o (0..3) of weight slot pp -- the 16 activations that
+// line up with code bits 7:6 / 5:4 / 3:2 / 1:0 of the slot -- sits at
+// o * plane + pp * 16, plane = K/4 + 32 bytes.  The 8 lanes of a row read
+// vector o of 8 consecutive slots: 128 contiguous bytes, one wavefront per
+// quarter-warp.  (In the natural layout those 8 vectors lie at offsets
+// 0, 16, 128, 144, ...: a 4-way bank conflict in every quarter-warp, 16
+// wavefronts per 128-bit load, measured at about 1.3 us per matvec.)  The
+// 32-byte pad puts the 4 planes on different banks for the quantiser's stores.
+constexpr uint32_t I2S_QS_PAD = 128;  // bytes beyond K that the layout needs
+__host__ __device__ __forceinline__ uint32_t qs_plane(uint32_t K) { return K / 4u + 32u; }
+__device__ __forceinline__ uint32_t qs_index(uint32_t e, uint32_t plane) {
+    const uint32_t r = e & 127u;  // element e = 128 b + 32 o + 16 h + j, slot 2 b + h
+    return (r >> 5) * plane + ((e >> 7) * 2u + ((r >> 4) & 1u)) * 16u + (r & 15u);
+}
+
+// The four 16-byte activation vectors that line up with weight slot pp, from
+// the natural layout (V = false: element order) or the fused kernels' layout.
+template <bool V>
+__device__ __forceinline__ void i2s_load_act(const int8_t *q, uint32_t pp, uint32_t plane,
+                                             uint4 (&a)[4]) {
+    if constexpr (V) {
 #pragma unroll
-    for (int o = 0; o < 4; ++o) a[o] = *reinterpret_cast<const uint4 *>(base + 32 * o);
+        for (int o = 0; o < 4; ++o)
+            a[o] = *reinterpret_cast<const uint4 *>(q + o * plane + pp * 16u);
+    } else {
+        const int8_t *base = q + (pp >> 1) * 128u + (pp & 1u) * 16u;
+#pragma unroll
+        for (int o = 0; o < 4; ++o) a[o] = *reinterpret_cast<const uint4 *>(base + 32 * o);
+    }
 }
 
 // Correction for code-3 codes of one row (slots pp = s, s+stride, ... < P).
-__device__ __forceinline__ int32_t i2s_row_c3(const uint8_t *rp, const int8_t *q, uint32_t s,
-                                              uint32_t stride, uint32_t P) {
+template <bool V>
+__device__ __forceinline__ int32_t i2s_row_c3(const uint8_t *rp, const int8_t *q, uint32_t plane,
+                                              uint32_t s, uint32_t stride, uint32_t P) {
     int32_t corr = 0;
     for (uint32_t pp = s; pp < P; pp += stride) {
         const uint4 wv = *reinterpret_cast<const uint4 *>(rp + 16 * pp);
         uint4 a[4];
-        i2s_load_act(q, pp, a);
+        i2s_load_act<V>(q, pp, plane, a);
         corr = i2s_word_c3(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, corr);
         corr = i2s_word_c3(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, corr);
         corr = i2s_word_c3(wv.z, a[0].z, a[1].z, a[2].z, a[3].z, corr);
@@ -277,7 +303,7 @@ __device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint3
                 packed |= (uint32_t)(qi & 0xFF) << (8 * k);
             }
         }
-        *reinterpret_cast<uint32_t *>(qs + i) = packed;
+        *reinterpret_cast<uint32_t *>(qs + qs_index(i, qs_plane(K))) = packed;
         qsum = __dp4a((int)packed, 0x01010101, qsum);
     }
     publish_qsum(qsum, ared);
@@ -456,7 +482,7 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
                                 quant_round_i8(__fmul_rn(v[k].z, inv)),
                                 quant_round_i8(__fmul_rn(v[k].w, inv)))
                     : 0u;
-            *reinterpret_cast<uint32_t *>(qs + i) = packed;
+            *reinterpret_cast<uint32_t *>(qs + qs_index(i, qs_plane(K))) = packed;
             qsum = __dp4a((int)packed, 0x01010101, qsum);
         }
     }
@@ -579,7 +605,8 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         if (blockIdx.x == 0) {
             if (p.q_out)
                 for (uint32_t i = tid * 16; i < K; i += I2S_THREADS * 16)
-                    *reinterpret_cast<uint4 *>(p.q_out + i) = *reinterpret_cast<const uint4 *>(qs + i);
+                    *reinterpret_cast<uint4 *>(p.q_out + i) =
+                        *reinterpret_cast<const uint4 *>(qs + qs_index(i, qs_plane(K)));
             if (p.scale_out && tid == 0) *p.scale_out = act_scale;
         }
         q = qs;
@@ -590,6 +617,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
 
     const uint32_t s = lane % LPR;
     const uint32_t sub = lane / LPR;
+    const uint32_t plane = qs_plane(K);  // FUSE_Q: layout of the quantised activations
     uint4 act[NP > 0 ? NP : 1][4];
     // Sum of the quantised activations (the code-offset term): with FUSE_Q
     // the quantiser produced the CTA total, subtracted once per row after the
@@ -601,7 +629,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         for (int i = 0; i < NP; ++i) {
             const uint32_t pp = s + LPR * i;
             if (pp < P) {
-                i2s_load_act(q, pp, act[i]);
+                i2s_load_act<FUSE_Q>(q, pp, plane, act[i]);
                 if constexpr (!FUSE_Q) {
 #pragma unroll
                     for (int o = 0; o < 4; ++o) asum += sum_bytes(act[i][o]);
@@ -615,7 +643,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         if constexpr (!FUSE_Q) {
             for (uint32_t pp = s; pp < P; pp += LPR) {
                 uint4 a[4];
-                i2s_load_act(q, pp, a);
+                i2s_load_act<FUSE_Q>(q, pp, plane, a);
 #pragma unroll
                 for (int o = 0; o < 4; ++o) asum += sum_bytes(a[o]);
             }
@@ -651,7 +679,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             } else {
                 for (uint32_t pp = s; pp < P; pp += LPR) {
                     uint4 a[4];
-                    i2s_load_act(q, pp, a);
+                    i2s_load_act<FUSE_Q>(q, pp, plane, a);
                     i2s_slot<C3>(*reinterpret_cast<const uint4 *>(rp + 16 * pp), a, acc, c3);
                 }
             }
@@ -665,7 +693,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         if constexpr (FUSE_Q) dot -= asum;
         if constexpr (C3) {
             if ((c3 & 0x55555555u) != 0u) {  // uniform across the LPR lanes of this row
-                int32_t corr = row < r1 ? i2s_row_c3(rp, q, s, LPR, P) : 0;
+                int32_t corr = row < r1 ? i2s_row_c3<FUSE_Q>(rp, q, plane, s, LPR, P) : 0;
                 // Only the lanes of rows that took this branch participate.
                 const uint32_t grp = __match_any_sync(__activemask(), row_local);
 #pragma unroll

@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
                         const uint4 wv =
                             *reinterpret_cast<const uint4 *>(line + ((s ^ (lane & 7u)) << 4));
                         uint4 a[4];
-                        i2s_load_act(op.q, pp, a);
+                        i2s_load_act<false>(op.q, pp, 0u, a);
                         int32_t c = corr[r];
                         c = i2s_word_c3(wv.x, a[0].x, a[1].x, a[2].x, a[3].x, c);
                         c = i2s_word_c3(wv.y, a[0].y, a[1].y, a[2].y, a[3].y, c);
