@@ -74,6 +74,12 @@ struct I2sMatvecParams {
     uint32_t residual;      // y[r] = y[r] + out (reference residual add)
     uint32_t finite_flag;   // status bit set when a residual sum is not finite
     uint32_t exact_norm;    // sum of squares in the reference's sequential order
+    // FUSE_Q shared-memory staging, set by the host when it fits: the up
+    // vector of I2S_PRE_RELU2_RMSNORM (fast mode) and the residual rows this
+    // CTA adds into, both copied asynchronously right after the dependency
+    // wait so that their load latency overlaps the input transform.
+    uint32_t stage_up;
+    uint32_t stage_res;
 };
 
 constexpr uint32_t I2S_PRE_NONE = 0, I2S_PRE_RMSNORM = 1, I2S_PRE_RELU2_RMSNORM = 2;
@@ -381,7 +387,7 @@ constexpr int I2S_PRE_V = (int)(I2S_FUSE_Q_MAX_K / (I2S_THREADS * 4u));  // floa
 
 __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint32_t K,
                                                   const float *nw, int8_t *qs, float *red,
-                                                  int32_t *ared) {
+                                                  int32_t *ared, const float *us) {
     const uint32_t tid = threadIdx.x, nthr = blockDim.x;
     const bool relu2 = p.pre == I2S_PRE_RELU2_RMSNORM;
     // float4 slots this CTA's K needs: the unrolled loops leave at the first
@@ -395,7 +401,24 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
         const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
         if (i < K) v[k] = *reinterpret_cast<const float4 *>(p.x + i);
     }
-    if (relu2) {  // v = relu(x)^2 * up, the up vector in two halves (bounded registers)
+    if (relu2 && us) {  // v = relu(x)^2 * up, up copied to this thread's slots of `us`
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+#pragma unroll
+        for (int k = 0; k < I2S_PRE_V; ++k) {
+            if (k >= kmax) break;
+            const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+            if (i < K) {
+                const float4 u = *reinterpret_cast<const float4 *>(us + i);
+                float4 &x = v[k];
+                const float r0 = x.x > 0.0f ? x.x : 0.0f, r1 = x.y > 0.0f ? x.y : 0.0f;
+                const float r2 = x.z > 0.0f ? x.z : 0.0f, r3 = x.w > 0.0f ? x.w : 0.0f;
+                x.x = __fmul_rn(__fmul_rn(r0, r0), u.x);
+                x.y = __fmul_rn(__fmul_rn(r1, r1), u.y);
+                x.z = __fmul_rn(__fmul_rn(r2, r2), u.z);
+                x.w = __fmul_rn(__fmul_rn(r3, r3), u.w);
+            }
+        }
+    } else if (relu2) {  // the up vector in two halves (bounded registers)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             float4 u[I2S_PRE_V / 2];
@@ -592,12 +615,33 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     if constexpr (FUSE_Q) {
         float *xs = reinterpret_cast<float *>(smem + nst * stage_bytes);
         int8_t *qs = reinterpret_cast<int8_t *>(xs + K);
-        if (regs_pre) {
-            if (p.pre != I2S_PRE_NONE) {
-                asm volatile("cp.async.wait_all;" ::: "memory");
-                __syncthreads();
+        float *us = reinterpret_cast<float *>(qs + K + I2S_QS_PAD);  // K floats (stage_up)
+        float *ysm = us + (p.stage_up ? K : 0u);                      // this CTA's rows (stage_res)
+        if (regs_pre && p.pre != I2S_PRE_NONE) {
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            __syncthreads();
+        }
+        // Two copy groups, always both committed (possibly empty) so that
+        // "wait_group 1" means the first one has landed.
+        if (p.stage_up)
+            for (uint32_t i = tid * 4u; i < K; i += I2S_THREADS * 4u)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(us + i)),
+                             "l"(p.x2 + i)
+                             : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if (p.stage_res)
+            for (uint32_t j = tid; j < r1 - r0; j += I2S_THREADS) {
+                const uint32_t row = r0 + j;
+                int jb = 0;
+                while (jb + 1 < p.njobs && row >= p.jobs[jb + 1].row_begin) ++jb;
+                const I2sJob &job = p.jobs[jb];
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ysm + j)),
+                             "l"(job.y + job.row_off + (row - job.row_begin))
+                             : "memory");
             }
-            act_scale = cta_prepare_regs(p, K, xs, qs, red, ared);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if (regs_pre) {
+            act_scale = cta_prepare_regs(p, K, xs, qs, red, ared, p.stage_up ? us : nullptr);
         } else {  // exact mode: the reference's sequential sum of squares
             cta_pre_input(p, K, xs, red);
             act_scale = cta_quantize(xs, K, xs, qs, red, ared);
@@ -650,6 +694,13 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         }
     }
 
+    float *ysm = nullptr;  // staged residual rows (visible after the loop's first barrier)
+    if constexpr (FUSE_Q) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        if (p.stage_res)
+            ysm = reinterpret_cast<float *>(smem + nst * stage_bytes + (size_t)K * 5u + I2S_QS_PAD +
+                                            (p.stage_up ? (size_t)K * 4u : 0u));
+    }
     for (uint32_t c = 0; c < nchunks; ++c) {
         const uint32_t st = c % nst;
         const bool ok = mbar_wait(&full_bar[st], (c / nst) & 1u);
@@ -714,13 +765,13 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
                 // (residual: this rank's replica + y, the same on every rank)
                 float v = yv;
                 if (p.residual) {
-                    v = __fadd_rn(job.y[job.row_off + local], yv);
+                    v = __fadd_rn(ysm ? ysm[row - r0] : job.y[job.row_off + local], yv);
                     if (p.finite_flag && !isfinite(v)) atomicOr(p.status, p.finite_flag);
                 }
                 tp_store_all(p.tp, job.y + job.row_off + local, v);
             } else if (p.residual) {
                 float *dst = job.y + job.row_off + local;
-                const float nv = __fadd_rn(*dst, yv);
+                const float nv = __fadd_rn(ysm ? ysm[row - r0] : *dst, yv);
                 *dst = nv;
                 if (p.finite_flag && !isfinite(nv)) atomicOr(p.status, p.finite_flag);
             } else {

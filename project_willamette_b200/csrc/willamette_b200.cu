@@ -357,7 +357,16 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     nst = std::min<uint32_t>(nst, (uint32_t)I2S_MAX_STAGES);
     nst = std::min<uint32_t>(nst, nchunks);
     p.nstages = nst;
-    const size_t smem = (size_t)nst * stage_bytes + (fuse ? (size_t)K * 5u + I2S_QS_PAD : 0u);
+    size_t smem = (size_t)nst * stage_bytes + (fuse ? (size_t)K * 5u + I2S_QS_PAD : 0u);
+    if (fuse && L.pre == I2S_PRE_RELU2_RMSNORM && !L.exact_norm &&
+        smem + (size_t)K * 4u <= (size_t)WL_MAX_DYN_SMEM / 2) {
+        p.stage_up = 1;
+        smem += (size_t)K * 4u;
+    }
+    if (fuse && L.residual && smem + (size_t)p.rows_per_cta * 4u <= (size_t)WL_MAX_DYN_SMEM / 2) {
+        p.stage_res = 1;
+        smem += ((size_t)p.rows_per_cta * 4u + 15u) & ~(size_t)15u;
+    }
     if (smem > (size_t)WL_MAX_DYN_SMEM / 2)
         return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for one shared-memory stage", K);
     const uint32_t grid = std::max<uint32_t>(1u, (rows + p.rows_per_cta - 1) / p.rows_per_cta);
