@@ -409,13 +409,20 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
             part[g * RS + HD + 1] = sum[g];
         }
     }
-    __threadfence();
+    // Split hand-off: the barrier orders every thread's partial stores before
+    // thread 0's acquire-release count (release is cumulative over them); the
+    // last split's acquire, then the barrier, order its reads of the other
+    // splits' partials after their stores.  (One atomic round trip instead of
+    // a fence per thread plus the atomic.)
     __syncthreads();
     uint32_t *ctr = p.counters + (size_t)z * gridDim.x + kvh;
-    if (tid == 0) s_last = atomicAdd(ctr, 1u) == S - 1u ? 1u : 0u;
+    if (tid == 0) {
+        uint32_t old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+        s_last = old == S - 1u ? 1u : 0u;
+    }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     // combine: M = max m_s, f_s = exp(m_s - M), O = sum f_s o_s / sum f_s l_s.
     // Every split's (max, sum) pair and the first 16 splits' o values of this
     // thread's outputs are requested in one round of loads (the partials are
