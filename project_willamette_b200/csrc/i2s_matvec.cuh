@@ -558,6 +558,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     __shared__ __align__(8) uint64_t full_bar[I2S_MAX_STAGES];
     __shared__ float red[I2S_WARPS];
     __shared__ int32_t ared[I2S_WARPS];
+    __shared__ uint32_t s_bad;  // a warp's weight wait timed out (resident-chunk loop)
     constexpr int RPW = 32 / LPR;
     constexpr uint32_t RPI = I2S_WARPS * RPW;
 
@@ -583,6 +584,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     const uint64_t policy = l2_policy_evict_first();
 
     if (tid == 0) {
+        s_bad = 0;
         for (uint32_t s = 0; s < nst; ++s) mbar_init(&full_bar[s], 1);
         fence_mbar_init();
         const uint32_t pre = min(nchunks, nst);
@@ -701,10 +703,19 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             ysm = reinterpret_cast<float *>(smem + nst * stage_bytes + (size_t)K * 5u + I2S_QS_PAD +
                                             (p.stage_up ? (size_t)K * 4u : 0u));
     }
+    // Every chunk requested up front (no ring reuse): each warp waits for a
+    // chunk's weights itself and the loop needs no CTA barrier.  Otherwise
+    // the CTA waits together and refills a stage once all warps are done.
+    const bool resident = nchunks <= nst;
+    if (resident) __syncthreads();  // staged residual rows visible to every warp
     for (uint32_t c = 0; c < nchunks; ++c) {
         const uint32_t st = c % nst;
-        const bool ok = mbar_wait(&full_bar[st], (c / nst) & 1u);
-        if (!__syncthreads_and(ok)) {
+        if (resident) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[st], 0u))) {
+                if (lane == 0) atomicOr(&s_bad, 1u);
+                break;
+            }
+        } else if (!__syncthreads_and(mbar_wait(&full_bar[st], (c / nst) & 1u))) {
             if (tid == 0) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
             // Give the copies already in flight a bounded chance to land
             // before this CTA's shared memory is released.
@@ -779,11 +790,22 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             }
             if (job.acc) job.acc[job.row_off + local] = dot;
         }
-        // Every thread is done with stage st: refill it with chunk c + nst.
+        if (!resident) {
+            // Every thread is done with stage st: refill it with chunk c + nst.
+            __syncthreads();
+            if (tid == 0 && c + nst < nchunks)
+                i2s_issue_chunk(p, c + nst, r0, r1, RPI, row_bytes, smem + st * stage_bytes,
+                                &full_bar[st], policy);
+        }
+    }
+    if (resident) {
         __syncthreads();
-        if (tid == 0 && c + nst < nchunks)
-            i2s_issue_chunk(p, c + nst, r0, r1, RPI, row_bytes, smem + st * stage_bytes,
-                            &full_bar[st], policy);
+        if (s_bad && tid == 0) {
+            atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
+            // bounded waits for the copies still in flight before the CTA's
+            // shared memory is released
+            for (uint32_t k = 0; k < nchunks; ++k) (void)mbar_wait(&full_bar[k], 0u);
+        }
     }
     pdl_launch_dependents();
     if (p.tp.world && tid == 0) tp_arrive(p.tp);  // after the loop's final barrier
