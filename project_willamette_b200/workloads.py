@@ -4,13 +4,16 @@ kernel family without the rest of ``bench.py``:
     python -m project_willamette_b200.workloads smollm_decode
     python -m project_willamette_b200.workloads bitnet_decode
     python -m project_willamette_b200.workloads lm_head
+    python -m project_willamette_b200.workloads gemm_small
 
 Each sets its model up (seeded as in ``bench.py``), prefills, and then runs
 two decode steps inside a CUDA profiler range (``cudaProfilerStart`` /
 ``Stop``), so ``ncu --profile-from-start off`` captures only the steady
 decode kernels.  ``lm_head`` repacks a 128256 x 2560 Q6_K matrix (config 4)
 and runs the greedy head at batch 1 (twice) and batch 4 (once) inside the
-range.
+range.  ``gemm_small`` runs the prefill GEMM of config 3's smallest case
+(M 128, K 6912, N 2560: quantisation + warp-specialised tcgen05 GEMM over
+expanded int8 weights) twice inside the range.
 """
 from __future__ import annotations
 
@@ -102,8 +105,47 @@ def lm_head(calls: int = 2) -> float:
     return _profiled(run)
 
 
+def gemm_small(calls: int = 2) -> float:
+    """BASELINE config 3, M = 128 x (K 6912 -> N 2560): device entry points on
+    device buffers.  Returns ms per call."""
+    import torch
+    from . import synth
+    from ._abi import lib
+    L = lib()
+    M, K, N = 128, 6912, 2560
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(SEED + 3)
+    packed = torch.from_numpy(synth.i2s_packed(rng, K, N)).to(dev)
+    x = torch.randn(M, K, device=dev, generator=torch.Generator(dev).manual_seed(SEED))
+    y = torch.empty(M, N, device=dev)
+    ws = torch.empty(L.wl_i2s_gemm_workspace_bytes(M, K), dtype=torch.uint8, device=dev)
+    tern = torch.empty(L.wl_i2s_expanded_bytes(K, N), dtype=torch.int8, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    if L.wl_dev_i2s_expand(packed.data_ptr(), K, N, tern.data_ptr(), s):
+        raise RuntimeError(L.wl_last_error().decode())
+
+    def call():
+        if L.wl_dev_i2s_gemm_s8_f32(tern.data_ptr(), 0.05, K, N, M, x.data_ptr(), y.data_ptr(),
+                                    None, ws.data_ptr(), s):
+            raise RuntimeError(L.wl_last_error().decode())
+
+    call()
+    torch.cuda.synchronize()
+
+    def run():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(calls):
+            call()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / calls
+
+    return _profiled(run)
+
+
 WORKLOADS = {"smollm_decode": smollm_decode, "bitnet_decode": bitnet_decode,
-             "lm_head": lm_head}
+             "lm_head": lm_head, "gemm_small": gemm_small}
 
 if __name__ == "__main__":
     name = sys.argv[1] if len(sys.argv) > 1 else ""
