@@ -18,8 +18,10 @@
 //     no CTA waits on another's append.
 //  3. The split's cached K / V head rows and scales are requested (cp.async,
 //     one round) right after the dependency wait and land in shared memory
-//     while step 1 runs.  Scores, one thread per position: the position's K
-//     row dotted with every q head of the group (q read as float4 broadcasts).
+//     while step 1 runs.  Scores: one thread per (position, q head) when the
+//     split's positions x heads fit one pass of the CTA, else one thread per
+//     position for all G heads (q read as float4 broadcasts); each dot runs
+//     over the head dimensions in order either way.
 //  4. Softmax statistics per q head (max, sum of exp) in block reductions.
 //  5. V: each warp takes every 8th position, a lane owns HD/32 dimensions of
 //     the row (one coalesced row load per warp and position) and accumulates
