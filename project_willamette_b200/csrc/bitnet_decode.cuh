@@ -116,9 +116,7 @@ __global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ O
     float sum_sq;
     if (p.exact) {
         if (threadIdx.x == 0) {
-            float t = 0.0f;
-            for (uint32_t i = 0; i < p.n; ++i) t = __fadd_rn(t, __fmul_rn(p.hidden[i], p.hidden[i]));
-            red[0] = t;
+            red[0] = seq_sum_sq(p.hidden, p.n);
         }
         __syncthreads();
         sum_sq = red[0];

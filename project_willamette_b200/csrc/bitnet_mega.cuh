@@ -216,9 +216,7 @@ __device__ __noinline__ float mega_norm_quantize(const MegaParams &p, float *xs,
     __syncthreads();
     if (p.exact) {
         if (tid == 0) {
-            float t = 0.0f;
-            for (uint32_t i = 0; i < K; ++i) t = __fadd_rn(t, __fmul_rn(xs[i], xs[i]));
-            sh.s_scale = t;
+            sh.s_scale = seq_sum_sq(xs, K);
         }
         __syncthreads();
         sum_sq = sh.s_scale;
@@ -790,9 +788,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1)
         float sum_sq;
         if (p.exact) {
             if (tid == 0) {
-                float t = 0.0f;
-                for (uint32_t i = 0; i < p.E; ++i) t = __fadd_rn(t, __fmul_rn(xs[i], xs[i]));
-                sh.s_scale = t;
+                sh.s_scale = seq_sum_sq(xs, p.E);
             }
             __syncthreads();
             sum_sq = sh.s_scale;

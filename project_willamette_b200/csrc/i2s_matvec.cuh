@@ -348,9 +348,7 @@ __device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t
         // the reference's loop: sum_sq += x[i] * x[i], i = 0, 1, ... (one thread)
         __syncthreads();
         if (tid == 0) {
-            float t = 0.0f;
-            for (uint32_t i = 0; i < K; ++i) t = __fadd_rn(t, __fmul_rn(xs[i], xs[i]));
-            red[0] = t;
+            red[0] = seq_sum_sq(xs, K);
         }
         __syncthreads();
         sum_sq = red[0];

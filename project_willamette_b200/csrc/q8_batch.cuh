@@ -381,9 +381,7 @@ __global__ void __launch_bounds__(256) out_norm_batch_kernel(const __grid_consta
     float sum_sq;
     if (p.exact) {
         if (threadIdx.x == 0) {
-            float t = 0.0f;
-            for (uint32_t i = 0; i < p.n; ++i) t = __fadd_rn(t, __fmul_rn(h[i], h[i]));
-            red[0] = t;
+            red[0] = seq_sum_sq(h, p.n);
         }
         __syncthreads();
         sum_sq = red[0];

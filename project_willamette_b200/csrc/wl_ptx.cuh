@@ -118,6 +118,39 @@ __device__ __forceinline__ float4 lds128f(const void *p) {
     return v;
 }
 
+// Sum of x[i] * x[i] for i = 0, 1, ..., n - 1 in that order, one rounding per
+// product and per add (the reference's sequential RMSNorm loop, bit for bit),
+// with the loads and products of the next 32 elements issued ahead of the
+// dependent adds, so the loop runs at the add's latency.  x 16-byte aligned.
+__device__ __forceinline__ float seq_sum_sq(const float *x, uint32_t n) {
+    float t = 0.0f;
+    const uint32_t n4 = (n & ~31u) / 4u;  // float4s in whole groups of 32 elements
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    if (n4) {
+        float4 nxt[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) nxt[j] = x4[j];
+        for (uint32_t i = 0; i < n4; i += 8) {
+            float4 cur[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            if (i + 8 < n4) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) nxt[j] = x4[i + 8 + j];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                t = __fadd_rn(t, __fmul_rn(cur[j].x, cur[j].x));
+                t = __fadd_rn(t, __fmul_rn(cur[j].y, cur[j].y));
+                t = __fadd_rn(t, __fmul_rn(cur[j].z, cur[j].z));
+                t = __fadd_rn(t, __fmul_rn(cur[j].w, cur[j].w));
+            }
+        }
+    }
+    for (uint32_t i = n4 * 4u; i < n; ++i) t = __fadd_rn(t, __fmul_rn(x[i], x[i]));
+    return t;
+}
+
 // Activation quantiser rounding: round(v) half away from zero, clamped to
 // [-127, 127], NaN -> 0 -- Rust's f32::round, then the clamp and saturating
 // `as i8` of the reference's absmax quantiser.  Exact, and without the slow
