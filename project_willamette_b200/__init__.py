@@ -90,6 +90,12 @@ class TensorView:
                 sd = np.frombuffer(sd, np.uint8)
             self.scale_data = np.ascontiguousarray(sd).view(np.uint8).reshape(-1)
 
+    def __getstate__(self):
+        # the cached C struct (see _view) holds ctypes pointers: rebuilt on use
+        state = dict(self.__dict__)
+        state.pop("_cview", None)
+        return state
+
     @staticmethod
     def i2s(name: str, in_dim: int, out_dim: int, packed, scale: float) -> "TensorView":
         block = np.zeros(32, np.uint8)
@@ -105,7 +111,23 @@ _keepalive: dict = {}
 
 
 def _view(t: TensorView):
-    """Build the C struct for ``t``; returns (struct, objects to keep alive)."""
+    """The C struct for ``t``; returns (struct, objects to keep alive).  Built
+    once per TensorView and reused while its data, scale, shape, type and name
+    are unchanged (a per-call rebuild cost ~10 us, a quarter of a small
+    host-buffer matvec)."""
+    c = t.__dict__.get("_cview")
+    if (c is not None and c[0] is t.data and c[1] is t.scale_data and c[2] == tuple(t.shape)
+            and c[3] == t.ggml_type and c[4] == t.name):
+        if c[7] not in _keepalive:
+            _keepalive[c[7]] = t.data
+        return c[5], c[6]
+    v, keep, key = _build_view(t)
+    t.__dict__["_cview"] = (t.data, t.scale_data, tuple(t.shape), t.ggml_type, t.name, v, keep,
+                            key)
+    return v, keep
+
+
+def _build_view(t: TensorView):
     shape = (C.c_uint64 * len(t.shape))(*[int(s) for s in t.shape])
     name = t.name.encode()
     v = _abi.WlTensorView()
@@ -120,7 +142,7 @@ def _view(t: TensorView):
         v.scale_len = t.scale_data.size
     key = (t.data.ctypes.data, t.data.size, int(t.ggml_type), tuple(int(s) for s in t.shape))
     _keepalive[key] = t.data
-    return v, (shape, name)
+    return v, (shape, name), key
 
 
 def _check(rc: int) -> None:

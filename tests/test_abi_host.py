@@ -165,3 +165,25 @@ def test_stream_plan_validation_before_any_device_work():
     op.w_scale = float("nan")
     assert L.wl_i2s_stream_plan_create(ctypes.byref(op), 1, ctypes.byref(plan)) == WLStatus.GGUF_PARSE
     assert not plan.value
+
+
+def test_tensor_view_struct_cached_and_invalidated():
+    """The C struct of a TensorView is built once and rebuilt when the view
+    changes (data, shape, type or name); pickling drops the cached struct."""
+    import pickle
+    import project_willamette_b200 as wl_pkg
+    from project_willamette_b200 import synth
+    t = wl_pkg.TensorView.i2s("w", 256, 8, synth.i2s_packed(np.random.default_rng(5), 256, 8), 0.5)
+    v1, _ = wl_pkg._view(t)
+    v2, _ = wl_pkg._view(t)
+    assert v1 is v2 and v1.data_len == 256 // 4 * 8
+    t.shape = [256, 8]  # equal shape: still cached
+    assert wl_pkg._view(t)[0] is v1
+    t.name = "renamed"
+    v3, _ = wl_pkg._view(t)
+    assert v3 is not v1 and v3.name == b"renamed"
+    t.data = np.zeros(256 // 4 * 8, np.uint8)
+    v4, _ = wl_pkg._view(t)
+    assert v4 is not v3 and v4.data_len == 512
+    t2 = pickle.loads(pickle.dumps(t))
+    assert "_cview" not in t2.__dict__ and list(t2.shape) == [256, 8]
