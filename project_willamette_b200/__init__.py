@@ -175,14 +175,31 @@ def release_weights() -> None:
     _keepalive.clear()
 
 
+_matvec_fn = None
+
+
+def _matvec_entry():
+    """wl_bitlinear_i2s_matvec_f32 declared with address-sized arguments, so
+    a call passes the arrays' addresses as integers instead of building two
+    ctypes pointer objects (a few microseconds of a small call)."""
+    global _matvec_fn
+    if _matvec_fn is None:
+        L = lib()
+        f = type(L.wl_bitlinear_i2s_matvec_f32)(("wl_bitlinear_i2s_matvec_f32", L))
+        f.argtypes = [C.POINTER(_abi.WlTensorView), C.c_void_p, C.c_size_t, C.c_void_p,
+                      C.c_size_t]
+        f.restype = C.c_int
+        _matvec_fn = f
+    return _matvec_fn
+
+
 def bitlinear_i2s_matvec_f32(weight: TensorView, input, output: np.ndarray) -> None:
     """output = i2_scale * (W_ternary . input) via int8 activations
     (bitlinear.rs:67 -> bitlinear_sse2.rs:313).  Writes ``output`` in place."""
     x = _f32(input)
     y = _out(output, "output")
     v, keep = _view(weight)
-    _check(lib().wl_bitlinear_i2s_matvec_f32(C.byref(v), x.ctypes.data_as(_fp), x.size,
-                                             y.ctypes.data_as(_fp), y.size))
+    _check(_matvec_entry()(C.byref(v), x.ctypes.data, x.size, y.ctypes.data, y.size))
 
 
 def bitlinear_i2s_matvec_f32_dbg(weight: TensorView, input):

@@ -89,6 +89,9 @@ struct Ctx {
     void *pinned = nullptr;
     size_t pinned_cap = 0;
     DevBuf x, y, q, scale, acc, ids, scratch, rowsum;
+    // plain host-buffer matvec calls: [device status word, 16 B][y], so one
+    // copy returns both (zeroed on allocation; reset after a reported error)
+    DevBuf ys;
     std::map<CacheKey, CachedWeight> cache;
 };
 
@@ -648,6 +651,11 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
     // bytes -- the memory-for-speed trade a 180 GB device affords).
     const bool gemm = m >= I2S_GEMM_MIN_TOKENS && m <= 0x7FFFFFFFu;
     const bool fuse = !gemm && K <= I2S_FUSE_Q_MAX_K;
+    // no debug outputs: y and the status word come back in one copy
+    const bool plain = !gemm && !acc_out && !act_q_out && !act_scale_out;
+    if (plain && (rc = grow(c.ys, yout + 16))) return rc;
+    float *ydev = plain ? (float *)((uint8_t *)c.ys.p + 16) : (float *)c.y.p;
+    uint32_t *dstat = plain ? (uint32_t *)c.ys.p : c.d_status;
     if (gemm) {
         if (!cw->ternary) {
             void *tp = nullptr;
@@ -671,8 +679,8 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
         return rc;
     const size_t m_rows = gemm ? (yout / 4 / N) : m;
     for (size_t t = 0; t < m; ++t) {
-        wl_i2s_dev_weight dw = {(const uint8_t *)cw->dptr, w_scale, N, (float *)c.y.p + t * N,
-                                (int32_t *)c.acc.p + t * N,
+        wl_i2s_dev_weight dw = {(const uint8_t *)cw->dptr, w_scale, N, ydev + t * N,
+                                acc_out ? (int32_t *)c.acc.p + t * N : nullptr,
                                 cw->has_code3 ? 0u : WL_I2S_NO_CODE3};
         I2sLaunch L;
         L.w = &dw;
@@ -680,15 +688,30 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
         L.K = K;
         if (fuse) {
             L.x = (const float *)c.x.p + t * K;
-            L.q_out = (int8_t *)c.q.p + t * K;
-            L.scale_out = (float *)c.scale.p + t;
+            L.q_out = act_q_out ? (int8_t *)c.q.p + t * K : nullptr;
+            L.scale_out = act_scale_out ? (float *)c.scale.p + t : nullptr;
         } else {
             L.q = (const int8_t *)c.q.p + t * K;
             L.act_scale = (const float *)c.scale.p + t;
         }
-        if ((rc = launch_i2s(L, c.stream, t > 0 || !fuse))) return rc;
+        if ((rc = launch_i2s_with_status(L, c.stream, t > 0 || !fuse, dstat))) return rc;
     }
     m = m_rows;
+    if (plain) {
+        uint8_t *pys = pin + xin;  // [status][y]
+        WL_CUDA(cudaMemcpyAsync(pys, c.ys.p, yout + 16, cudaMemcpyDeviceToHost, c.stream));
+        cudaError_t e = cudaStreamSynchronize(c.stream);
+        if (e != cudaSuccess) return fail(WL_ERR_CUDA, "kernel execution: %s", cudaGetErrorString(e));
+        uint32_t f;
+        memcpy(&f, pys, 4);
+        if (f) {
+            WL_CUDA(cudaMemsetAsync(c.ys.p, 0, 4, c.stream));
+            WL_CUDA(cudaStreamSynchronize(c.stream));
+            return fail(WL_ERR_DEVICE_TIMEOUT, "a device-side wait timed out (flags 0x%x)", f);
+        }
+        memcpy(output, pys + 16, yout);
+        return WL_OK;
+    }
     uint8_t *py = pin + xin, *pacc = py + yout, *pq = pacc + yout, *ps = pq + m * (size_t)K;
     WL_CUDA(cudaMemcpyAsync(py, c.y.p, yout, cudaMemcpyDeviceToHost, c.stream));
     if (acc_out) WL_CUDA(cudaMemcpyAsync(pacc, c.acc.p, yout, cudaMemcpyDeviceToHost, c.stream));
