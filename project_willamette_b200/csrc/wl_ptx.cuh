@@ -110,14 +110,6 @@ __device__ __forceinline__ uint4 lds128(const void *p) {
     return v;
 }
 
-__device__ __forceinline__ float4 lds128f(const void *p) {
-    float4 v;
-    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(smem_u32(p)));
-    return v;
-}
-
 // Sum of x[i] * x[i] for i = 0, 1, ..., n - 1 in that order, one rounding per
 // product and per add (the reference's sequential RMSNorm loop, bit for bit),
 // with the loads and products of the next 32 elements issued ahead of the
