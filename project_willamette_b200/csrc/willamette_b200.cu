@@ -372,6 +372,11 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     }
     if (smem > (size_t)WL_MAX_DYN_SMEM / 2)
         return fail(WL_ERR_INVALID_ARGUMENT, "in_dim %u too large for one shared-memory stage", K);
+    // Decode-engine matvecs (fused input transform): ask for the kernel's
+    // whole shared-memory allowance so that two of this op's CTAs never share
+    // an SM (the block scheduler otherwise doubled some up while other SMs
+    // were left to the attention CTAs; token 1145 -> 1136 us at BitNet-2B).
+    if (fuse && L.pre != I2S_PRE_NONE) smem = (size_t)WL_MAX_DYN_SMEM / 2;
     const uint32_t grid = std::max<uint32_t>(1u, (rows + p.rows_per_cta - 1) / p.rows_per_cta);
     WL_CUDA(launch(k, dim3(grid), dim3(I2S_THREADS), smem, s, pdl, p));
     return WL_OK;
