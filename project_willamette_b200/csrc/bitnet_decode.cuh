@@ -312,16 +312,15 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     if (p.exact) {
         // softmax_inplace (attention.rs:45-73) and out_h[d] += w * v_h[d]
         // (cached_forward.rs:441-449) in the reference's sequential order.
-        __shared__ float s_inv, s_max;
+        // The maximum as a block reduction: the same value as the reference's
+        // strict-'>' scan (NaN never wins either way; +0 and -0 maxima give
+        // identical exponentials).  The sums below keep the reference's order,
+        // with their loads run ahead of the dependent adds.
+        __shared__ float s_inv;
         __shared__ uint32_t s_norm;
-        if (tid == 0) {
-            float mxs = -INFINITY;
-            for (uint32_t i = 0; i < cnt; ++i)
-                if (scores[i] > mxs) mxs = scores[i];
-            s_max = mxs;
-        }
-        __syncthreads();
-        const float mxs = s_max;
+        float mloc = -INFINITY;
+        for (uint32_t i = tid; i < cnt; i += blockDim.x) mloc = fmaxf(mloc, scores[i]);
+        const float mxs = block_max(mloc, red);
         if (!isfinite(mxs)) {
             for (uint32_t i = tid; i < cnt; i += blockDim.x) scores[i] = 0.0f;
         } else {
@@ -330,7 +329,21 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
             __syncthreads();
             if (tid == 0) {
                 float sum = 0.0f;
-                for (uint32_t i = 0; i < cnt; ++i) sum = __fadd_rn(sum, scores[i]);
+                {
+                    const uint32_t n4 = (cnt & ~31u) / 4u;
+                    const float4 *x4 = reinterpret_cast<const float4 *>(scores);
+                    for (uint32_t i = 0; i < n4; i += 8) {
+                        float4 c8[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) c8[j] = x4[i + j];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            sum = __fadd_rn(sum, c8[j].x); sum = __fadd_rn(sum, c8[j].y);
+                            sum = __fadd_rn(sum, c8[j].z); sum = __fadd_rn(sum, c8[j].w);
+                        }
+                    }
+                    for (uint32_t i = n4 * 4u; i < cnt; ++i) sum = __fadd_rn(sum, scores[i]);
+                }
                 s_norm = sum > 0.0f ? 1u : 0u;
                 s_inv = s_norm ? __fdiv_rn(1.0f, sum) : 1.0f;
             }
@@ -341,10 +354,17 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
         __syncthreads();
         if (tid < HD) {
             float o = 0.0f;
-            for (uint32_t i = 0; i < cnt; ++i) {
-                const uint32_t t = t0 + i;
-                const int8_t vv = t == pos ? vq[kvh * HD + tid] : v_cache[(size_t)t * KV + kvh * HD + tid];
-                o = __fadd_rn(o, __fmul_rn(scores[i], __fmul_rn((float)vv, vsc[i])));
+            const int8_t *vcol = v_cache + (size_t)t0 * KV + kvh * HD + tid;
+            const int8_t vcur = vq[kvh * HD + tid];
+            for (uint32_t i0 = 0; i0 < cnt; i0 += 32u) {
+                int8_t vb[32];
+#pragma unroll
+                for (uint32_t u = 0; u < 32u; ++u)
+                    vb[u] = (i0 + u < cnt && t0 + i0 + u != pos) ? vcol[(size_t)(i0 + u) * KV] : vcur;
+#pragma unroll
+                for (uint32_t u = 0; u < 32u; ++u)
+                    if (i0 + u < cnt)
+                        o = __fadd_rn(o, __fmul_rn(scores[i0 + u], __fmul_rn((float)vb[u], vsc[i0 + u])));
             }
             att[h * HD + tid] = o;
         }
