@@ -325,7 +325,7 @@ __device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint3
 // rms_norm: mean = sum(v*v) / K, rsqrt = 1 / sqrt(mean + eps),
 // out = (v * rsqrt) * w, IEEE round-to-nearest (the sum as a tree).
 __device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t K, float *xs,
-                                              float *red) {
+                                              float *red, const float *nw) {
     const uint32_t tid = threadIdx.x, nthr = blockDim.x;
     float ss = 0.0f;
     for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
@@ -365,7 +365,7 @@ __device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t
     const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
     for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
         float4 v = *reinterpret_cast<const float4 *>(xs + i);
-        const float4 w = *reinterpret_cast<const float4 *>(p.norm_w + i);
+        const float4 w = *reinterpret_cast<const float4 *>(nw + i);
         v.x = __fmul_rn(__fmul_rn(v.x, rsqrt), w.x);
         v.y = __fmul_rn(__fmul_rn(v.y, rsqrt), w.y);
         v.z = __fmul_rn(__fmul_rn(v.z, rsqrt), w.z);
@@ -600,6 +600,14 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
                              "l"(p.norm_w + i)
                              : "memory");
             asm volatile("cp.async.commit_group;" ::: "memory");
+        } else if (p.pre != I2S_PRE_NONE) {  // exact mode: after the quantised input
+            float *nw = reinterpret_cast<float *>(smem + nst * stage_bytes + (size_t)K * 5u +
+                                                  I2S_QS_PAD);
+            for (uint32_t i = tid * 4u; i < K; i += I2S_THREADS * 4u)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(nw + i)),
+                             "l"(p.norm_w + i)
+                             : "memory");
+            asm volatile("cp.async.commit_group;" ::: "memory");
         }
     }
     __syncthreads();
@@ -616,8 +624,10 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         float *xs = reinterpret_cast<float *>(smem + nst * stage_bytes);
         int8_t *qs = reinterpret_cast<int8_t *>(xs + K);
         float *us = reinterpret_cast<float *>(qs + K + I2S_QS_PAD);  // K floats (stage_up)
-        float *ysm = us + (p.stage_up ? K : 0u);                      // this CTA's rows (stage_res)
-        if (regs_pre && p.pre != I2S_PRE_NONE) {
+        // exact mode stages the RMSNorm weights where fast mode keeps up
+        const bool nw_exact = !regs_pre;  // (pre != NONE and exact_norm)
+        float *ysm = us + ((p.stage_up || nw_exact) ? K : 0u);        // this CTA's rows (stage_res)
+        if (p.pre != I2S_PRE_NONE) {
             asm volatile("cp.async.wait_all;" ::: "memory");
             __syncthreads();
         }
@@ -643,7 +653,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         if (regs_pre) {
             act_scale = cta_prepare_regs(p, K, xs, qs, red, ared, p.stage_up ? us : nullptr);
         } else {  // exact mode: the reference's sequential sum of squares
-            cta_pre_input(p, K, xs, red);
+            cta_pre_input(p, K, xs, red, us);
             act_scale = cta_quantize(xs, K, xs, qs, red, ared);
         }
         if (blockIdx.x == 0) {
@@ -699,7 +709,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         asm volatile("cp.async.wait_all;" ::: "memory");
         if (p.stage_res)
             ysm = reinterpret_cast<float *>(smem + nst * stage_bytes + (size_t)K * 5u + I2S_QS_PAD +
-                                            (p.stage_up ? (size_t)K * 4u : 0u));
+                                            ((p.stage_up || !regs_pre) ? (size_t)K * 4u : 0u));
     }
     // Every chunk requested up front (no ring reuse): each warp waits for a
     // chunk's weights itself and the loop needs no CTA barrier.  Otherwise

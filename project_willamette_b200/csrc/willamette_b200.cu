@@ -366,6 +366,8 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
         p.stage_up = 1;
         smem += (size_t)K * 4u;
     }
+    if (fuse && L.pre != I2S_PRE_NONE && L.exact_norm)  // staged RMSNorm weights (exact mode)
+        smem += (size_t)K * 4u;
     if (fuse && L.residual && smem + (size_t)p.rows_per_cta * 4u <= (size_t)WL_MAX_DYN_SMEM / 2) {
         p.stage_res = 1;
         smem += ((size_t)p.rows_per_cta * 4u + 15u) & ~(size_t)15u;
