@@ -2,17 +2,17 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload ("bitnet2b_decode_bitlinear_sweep", BASELINE config 2 shapes): one
+Workload ("bitnet2b_decode_bitlinear_sweep", benchmark config 2 shapes): one
 step runs every BitLinear of one decode token -- 30 layers x {Q,K,V fused,
 O, gate/up fused, down}, each an absmax int8 quantisation of a distinct f32
 activation vector followed by the I2_S ternary matvec (210 weight tensors,
 521,011,200 packed bytes, all distinct and resident in HBM).  The working set
 is 4x the 126 MB L2, so no L2 flush is needed between steps.  The metric is
-BASELINE's "I2_S matvec HBM GB/s": algorithmic bytes (packed weights + scale +
+the reference's "I2_S matvec HBM GB/s": algorithmic bytes (packed weights + scale +
 f32 activations in + f32 outputs) per second.
 
-`value` is the sustained streaming rate (SURVEY's "sustains" reading: back to
-back over distinct weight buffers larger than L2): the 210 matvecs, each with
+`value` is the sustained streaming rate (the matvecs run back to back over
+distinct weight buffers larger than L2): the 210 matvecs, each with
 its own input, as one persistent launch per step (wl_dev_i2s_stream_run:
 quantise all inputs, then stream every weight once), CUDA events on the
 launching stream, max over ranks.  `decode_chain` times the same 210 matvecs in
@@ -35,7 +35,7 @@ the weights is under twice L2, several distinct weight copies are cycled step
 to step so that no step reads its weights from L2.
 
 Beside the headline the line carries the decode engines: `decode` is
-BASELINE config 2 (BitNet-2B-shaped greedy decode, 512-token prompt, 128 new
+benchmark config 2 (BitNet-2B-shaped greedy decode, 512-token prompt, 128 new
 tokens; tensor parallel over the N GPUs at N > 1), `smollm_batch_decode` is
 config 5 (SmolLM-135M-shaped Q8_0 model, 32 sequences with contexts
 U[64, 1024], 64 new tokens each; 1 GPU), `lm_head` config 4 and
@@ -410,7 +410,7 @@ def run_gpu(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
-            "dtype": "int8xternary->i32", "data": "synthetic (seeded; BASELINE distributions)",
+            "dtype": "int8xternary->i32", "data": "synthetic (seeded; benchmark configs' distributions)",
             "config": {"workload": WORKLOAD, "layers": LAYERS, "d_model": D_MODEL, "d_ff": D_FF,
                        "kv_dim": D_KV, "matvecs_per_step": LAYERS * 7,
                        "bytes_per_step": bytes_step, "batch": 1,
@@ -535,7 +535,7 @@ def key_fast(exact: bool, persistent: bool) -> bool:
 
 
 def decode_bench(reps: int = 3) -> dict:
-    """BitNet-2B-shaped greedy decode on the device-resident
+    """Benchmark config 2: BitNet-2B-shaped greedy decode on the device-resident
     decode step -- KV cache prefilled to 512 positions (the reference's prompt
     loop, one forward per token), then 128 greedy tokens, device time of the
     128-token loop (CUDA events), median of `reps` runs.  Fast mode (parallel
@@ -582,7 +582,7 @@ def decode_bench(reps: int = 3) -> dict:
 
 
 def decode_tp_bench(world: int, rank: int, max_over_ranks, reps: int = 2) -> dict:
-    """BASELINE config 2 on `world` GPUs: the tensor-parallel engine (every
+    """Benchmark config 2 on `world` GPUs: the tensor-parallel engine (every
     BitLinear row-split and gathered in-kernel over NVLink, attention
     replicated, vocab-sharded greedy head), same prompt / token counts as
     the single-GPU run; device time of the 128-token loop, max over ranks,
@@ -616,7 +616,7 @@ def decode_tp_bench(world: int, rank: int, max_over_ranks, reps: int = 2) -> dic
 
 
 def smollm_bench(reps: int = 2) -> dict:
-    """SmolLM-135M-shaped Q8_0 batched decode -- 32
+    """Benchmark config 5: SmolLM-135M-shaped Q8_0 batched decode -- 32
     independent sequences, KV caches prefilled to seeded contexts U[64, 1024]
     (the reference's prompt loop, all sequences in lock step), then 64 greedy
     tokens each; device time of the 64-step loop (CUDA events), median of
@@ -685,7 +685,7 @@ def int8_peak_tops() -> dict:
 
 
 def gemm_bench(torch, dev, L, stream, rng) -> dict:
-    """prefill GEMM, M in {2048, 512, 128} x the three
+    """Benchmark config 3: prefill GEMM, M in {2048, 512, 128} x the three
     BitNet-2B weight shapes.  Timed per call: the per-token absmax
     quantisation + the warp-specialised tcgen05 GEMM over the int8 ternary
     weights (expanded once per weight, like a load-time layout; the one-off
@@ -874,7 +874,7 @@ def run_reference(args) -> None:
         "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "int8xternary->i32",
-        "data": "synthetic (seeded; BASELINE distributions)",
+        "data": "synthetic (seeded; benchmark configs' distributions)",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "d_model": D_MODEL, "d_ff": D_FF,
                    "kv_dim": D_KV, "batch": 1},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": 1, "kind": "port",

@@ -1,4 +1,4 @@
-"""Seeded synthetic weights and activations with BASELINE's distributions.
+"""Seeded synthetic weights and activations with the benchmark configs' distributions.
 
 The reference builds synthetic GGUFs in src/synth.rs (xorshift codes, scale
 1.0).  The benchmark configurations ask for other distributions, generated
@@ -68,7 +68,7 @@ def q8_0_rows(rng: np.random.Generator, in_dim: int, out_dim: int) -> np.ndarray
     return blocks.reshape(-1)
 
 
-# BitNet-b1.58-2B shapes: (name, in_dim, out_dim) per layer.
+# BitNet-b1.58-2B shapes (benchmark config 2): (name, in_dim, out_dim) per layer.
 BITNET_2B_LAYER = [
     ("attn_q", 2560, 2560), ("attn_k", 2560, 640), ("attn_v", 2560, 640),
     ("attn_output", 2560, 2560), ("ffn_gate", 2560, 6912), ("ffn_up", 2560, 6912),
@@ -83,7 +83,7 @@ def bitnet_model(rng: np.random.Generator, n_layers: int = 30, n_embd: int = 256
                  n_heads: int = 20, n_kv_heads: int = 5, head_dim: int = 128, n_ff: int = 6912,
                  vocab: int = 128256, max_seq: int = 1024, eps: float = 1e-5,
                  freq_base: float = 500000.0) -> dict:
-    """A random BitNet-b1.58-shaped model (BASELINE config 2 distributions):
+    """A random BitNet-b1.58-shaped model (benchmark config 2 distributions):
     every linear I2_S with P(0)=0.5 and a U[0.01, 0.1] scale, norm weights
     U[0.5, 1.5], tied Q6_K embedding / lm-head (config 4 distributions).
     Defaults are the 2B shapes."""
@@ -112,7 +112,7 @@ def llama_q8_model(rng: np.random.Generator, n_layers: int = 30, n_embd: int = 5
                    n_heads: int = 9, n_kv_heads: int = 3, head_dim: int = 64, n_ff: int = 1536,
                    vocab: int = 49152, max_seq: int = 1088, eps: float = 1e-5,
                    freq_base: float = 10000.0) -> dict:
-    """A random SmolLM-135M-shaped Llama model: every
+    """A random SmolLM-135M-shaped Llama model (benchmark config 5): every
     linear and the tied embedding / lm-head Q8_0 (int8 quants U[-127, 127],
     f16 scale |N(0, 0.01)|), norm weights U[0.5, 1.5].  Defaults are the 135M
     shapes.  The norms array keeps the per-layer layout of ``bitnet_model``

@@ -34,7 +34,7 @@ def _profiled(fn):
 
 
 def smollm_decode(steps: int = 2) -> float:
-    """32 sequences prefilled to contexts U[64, 1024],
+    """Benchmark config 5: 32 sequences prefilled to contexts U[64, 1024],
     then `steps` batched greedy steps (fast mode)."""
     from . import synth
     from .llama import LlamaBatch
@@ -50,7 +50,7 @@ def smollm_decode(steps: int = 2) -> float:
 
 
 def bitnet_decode(steps: int = 2) -> float:
-    """BitNet-2B shapes, 512-token prompt, then `steps`
+    """Benchmark config 2: BitNet-2B shapes, 512-token prompt, then `steps`
     greedy steps (fast mode, per-operation engine)."""
     from . import synth
     from .bitnet import BitNet
@@ -64,7 +64,7 @@ def bitnet_decode(steps: int = 2) -> float:
 
 
 def lm_head(calls: int = 2) -> float:
-    """BASELINE config 4: Q6_K tied lm-head + greedy argmax, 128256 x 2560;
+    """Benchmark config 4: Q6_K tied lm-head + greedy argmax, 128256 x 2560;
     `calls` batch-1 calls and one batch-4 call, device entry points on
     device buffers.  Returns the batch-1 ms per call."""
     import torch
@@ -106,7 +106,7 @@ def lm_head(calls: int = 2) -> float:
 
 
 def gemm_small(calls: int = 2) -> float:
-    """BASELINE config 3, M = 128 x (K 6912 -> N 2560): device entry points on
+    """Benchmark config 3, M = 128 x (K 6912 -> N 2560): device entry points on
     device buffers.  Returns ms per call."""
     import torch
     from . import synth

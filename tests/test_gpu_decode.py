@@ -125,7 +125,7 @@ def bitnet2b():
 @pytest.mark.parametrize("exact", [True, False])
 @pytest.mark.parametrize("persistent", [False, True])
 def test_decode_bitnet2b_shapes(bitnet2b, exact, persistent):
-    """BASELINE config 2 shapes (30 layers, 2560, 20/5 heads, 6912, vocab
+    """Benchmark config 2 shapes (30 layers, 2560, 20/5 heads, 6912, vocab
     128256), a short prompt and a few greedy tokens.  Fast mode at 30 layers
     accumulates re-quantisation flips in the hidden state (see the module
     docstring), so only its ids are held to the reference there."""

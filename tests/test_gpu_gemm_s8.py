@@ -64,7 +64,7 @@ def test_gemm_s8_bit_exact(in_dim, out_dim, m):
 
 
 def test_gemm_s8_config3_full_size_sampled():
-    """BASELINE config 3, M = 2048 x (6912 x 2560): sampled tokens against the
+    """Benchmark config 3, M = 2048 x (6912 x 2560): sampled tokens against the
     oracle, every token through y(-X) = -y(X)."""
     import torch
     L = lib()

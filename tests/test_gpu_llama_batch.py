@@ -187,7 +187,7 @@ def smollm():
 
 @pytest.mark.parametrize("exact", [True, False])
 def test_batch_smollm_shapes(smollm, exact):
-    """BASELINE config 5 shapes (30 layers, 576, 9 / 3 heads of 64, 1536,
+    """Benchmark config 5 shapes (30 layers, 576, 9 / 3 heads of 64, 1536,
     vocab 49152, all Q8_0), four sequences of different lengths."""
     from project_willamette_b200.llama import LlamaBatch
     m, prompts, want_ids, want_h = smollm

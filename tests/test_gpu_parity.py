@@ -54,7 +54,7 @@ def _check_i2s(t, packed, scale, x):
 
 
 def test_i2s_config1_bit_exact():
-    """6912 x 2560 ternary, P(0)=0.5, scale U[0.01,0.1], x N(0,1)."""
+    """Benchmark config 1: 6912 x 2560 ternary, P(0)=0.5, scale U[0.01,0.1], x N(0,1)."""
     rng = np.random.default_rng(0x5EED + 1)
     _check_i2s(*_i2s_case(rng, 2560, 6912))
 
@@ -182,7 +182,7 @@ def test_i2s_gemm_with_code3_falls_back_exactly():
 
 
 def test_i2s_gemm_config3_full_size_sampled():
-    """BASELINE config 3 at M = 2048 for the 6912 x 2560 weight: all rows
+    """Benchmark config 3 at M = 2048 for the 6912 x 2560 weight: all rows
     checked against the oracle on a sample of tokens, plus y(-X) = -y(X)."""
     rng = np.random.default_rng(0x5EED + 3)
     in_dim, out_dim, m = 2560, 6912, 2048
@@ -358,7 +358,7 @@ def test_q6k_greedy_batch(batch):
 
 
 def test_q6k_config4_full_vocab():
-    """BASELINE config 4 at full size: 128256 x 2560 Q6_K, batch 1 and a
+    """Benchmark config 4 at full size: 128256 x 2560 Q6_K, batch 1 and a
     sample of a batch-64 call."""
     rng = np.random.default_rng(0x5EED + 4)
     n_embd, vocab = 2560, 128256
