@@ -115,11 +115,18 @@ class TPGroup:
         _check(L.wl_init(rank if device is None else device))
         h = (C.c_uint8 * WL_TP_HANDLE_BYTES)()
         _check(L.wl_tp_create(rank, world, sym_bytes, C.byref(self._g), h))
-        handles = (exchange or _torch_exchange)(bytes(h), world)
-        if len(handles) != world or any(len(x) != WL_TP_HANDLE_BYTES for x in handles):
-            raise WillametteError(8, "handle exchange returned the wrong shape", 0)
-        allh = (C.c_uint8 * (WL_TP_HANDLE_BYTES * world)).from_buffer_copy(b"".join(handles))
-        _check(L.wl_tp_connect(self._g, allh))
+        try:
+            handles = (exchange or _torch_exchange)(bytes(h), world)
+            if len(handles) != world or any(len(x) != WL_TP_HANDLE_BYTES for x in handles):
+                raise WillametteError(8, "handle exchange returned the wrong shape", 0)
+            allh = (C.c_uint8 * (WL_TP_HANDLE_BYTES * world)).from_buffer_copy(b"".join(handles))
+            _check(L.wl_tp_connect(self._g, allh))
+        except BaseException:
+            # A peer that never joined (the exchange timed out or raised) or a
+            # mapping that failed: free this rank's block and any peer mappings
+            # now, not whenever the traceback lets go of this object.
+            self.close()
+            raise
         self.sym_bytes = sym_bytes
 
     def view(self, offset: int, shape, dtype=np.float32) -> SymView:

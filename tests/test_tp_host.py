@@ -130,3 +130,157 @@ def test_tp_split_and_reduce_gloo_world2():
             if p.is_alive():
                 p.kill()
     assert results == {0: "ok", 1: "ok"}, results
+
+
+# ---- group setup when a peer fails: the library's group calls are faked on
+# the host (no GPU); the group must be destroyed before the error propagates.
+class _FakeTpLib:
+    """The TP entry points of the library, answering without a device."""
+    GROUP = 0xB200
+
+    def __init__(self, connect_rc=0):
+        self.connect_rc, self.calls = connect_rc, []
+
+    def wl_init(self, device):
+        self.calls.append(("init", device))
+        return 0
+
+    def wl_tp_create(self, rank, world, sym_bytes, group_ref, handle):
+        group_ref._obj.value = self.GROUP
+        for i in range(len(handle)):
+            handle[i] = rank + 1
+        self.calls.append(("create", rank, world))
+        return 0
+
+    def wl_tp_connect(self, group, handles):
+        self.calls.append(("connect", bytes(handles)))
+        return self.connect_rc
+
+    def wl_tp_destroy(self, group):
+        self.calls.append(("destroy", group.value))
+        return 0
+
+    def wl_last_error(self):
+        return b"opening rank 1's block: fake failure"
+
+    def wl_last_error_tensor_type(self):
+        return 0
+
+
+@pytest.fixture
+def fake_tp(monkeypatch):
+    from project_willamette_b200 import tp
+
+    def make(connect_rc=0):
+        fake = _FakeTpLib(connect_rc)
+        monkeypatch.setattr(tp, "lib", lambda: fake)
+        return fake
+    return make
+
+
+def _destroys(fake):
+    return [c for c in fake.calls if c[0] == "destroy"]
+
+
+def test_group_freed_when_a_peer_never_joins(fake_tp):
+    from project_willamette_b200.tp import TPGroup
+
+    fake = fake_tp()
+
+    def exchange(handle, world):
+        raise TimeoutError("rank 1 never joined the handle exchange")
+    with pytest.raises(TimeoutError):
+        TPGroup(0, 2, 4096, device=0, exchange=exchange)
+    assert _destroys(fake) == [("destroy", _FakeTpLib.GROUP)]
+    assert not any(c[0] == "connect" for c in fake.calls)
+
+
+def test_group_freed_on_a_malformed_exchange(fake_tp):
+    from project_willamette_b200 import WillametteError
+    from project_willamette_b200.tp import TPGroup
+
+    fake = fake_tp()
+    with pytest.raises(WillametteError) as e:
+        TPGroup(0, 2, 4096, device=0, exchange=lambda h, w: [h])  # one handle for two ranks
+    assert e.value.status == 8 and "wrong shape" in e.value.message
+    assert _destroys(fake) == [("destroy", _FakeTpLib.GROUP)]
+
+
+def test_group_freed_when_mapping_a_peer_fails(fake_tp):
+    from project_willamette_b200 import WillametteError
+    from project_willamette_b200.tp import TPGroup
+
+    fake = fake_tp(connect_rc=8)  # WL_ERR_COMM from wl_tp_connect
+    with pytest.raises(WillametteError) as e:
+        TPGroup(1, 2, 4096, device=0, exchange=lambda h, w: [bytes([1]) * len(h), h])
+    assert e.value.status == 8 and "fake failure" in e.value.message
+    assert _destroys(fake) == [("destroy", _FakeTpLib.GROUP)]
+
+
+def test_group_connects_and_closes_once(fake_tp):
+    from project_willamette_b200.tp import TPGroup
+
+    fake = fake_tp()
+    g = TPGroup(1, 2, 4096, device=0, exchange=lambda h, w: [bytes([1]) * len(h), h])
+    connect = [c for c in fake.calls if c[0] == "connect"]
+    assert len(connect) == 1 and connect[0][1] == bytes([1]) * 64 + bytes([2]) * 64
+    assert not _destroys(fake)
+    g.close()
+    g.close()
+    assert _destroys(fake) == [("destroy", _FakeTpLib.GROUP)]
+
+
+def _dead_peer_main(rank, port, q):
+    """Rank 1 joins the process group and exits before the handle exchange;
+    rank 0 must get an error from the exchange, not wait for good, and free
+    its group."""
+    try:
+        import datetime
+
+        import torch.distributed as dist
+        from project_willamette_b200 import tp
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=2,
+                                timeout=datetime.timedelta(seconds=10))
+        if rank == 1:
+            q.put((rank, "left"))
+            q.close()
+            q.join_thread()  # flush the message before the hard exit
+            os._exit(0)  # dies between steps, with nothing in flight
+        fake = _FakeTpLib()
+        tp.lib = lambda: fake
+        try:
+            tp.TPGroup(0, 2, 4096, device=0)
+            q.put((rank, "exchange returned without the peer"))
+        except Exception as e:  # the exchange's own error
+            ok = _destroys(fake) == [("destroy", _FakeTpLib.GROUP)]
+            q.put((rank, "raised+freed" if ok else f"raised, not freed: {e!r}"))
+        q.close()
+        q.join_thread()
+        os._exit(0)  # the group is broken; skip its teardown
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def test_handle_exchange_errors_when_a_rank_leaves_gloo_world2():
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_peer_main, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in procs:
+            try:
+                r, msg = q.get(timeout=90)
+            except Exception:
+                break  # reported below with what did arrive
+            results[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert results == {0: "raised+freed", 1: "left"}, results
