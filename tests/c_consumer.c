@@ -5,7 +5,8 @@
  * points that need no GPU: the version string, the argument validation of
  * the host-buffer entry points with the reference's error classes
  * (src/model/bitlinear.rs:151-155, src/model/bitlinear_sse2.rs:167-175,
- * src/gguf/tensor.rs:286-307, src/model/linear.rs:23), the empty cases
+ * src/gguf/tensor.rs:286-307, src/model/linear.rs:23), the size limits of
+ * the allocation-free matvec (wl_dev_i2s_matvec_f32_noalloc), the empty cases
  * (src/model/lm_head.rs:161 argmax of an empty slice), and the zero-copy GGUF
  * reader (src/gguf/reader.rs:120-415).  With "--no-gpu" it also checks that a
  * valid call on a machine without an sm_100 device is an error, never a CPU
@@ -126,6 +127,22 @@ static void check_linear_dispatch(void) {
     CHECK(wl_linear_matvec_f32(&t, x, 32, y, 2) == WL_ERR_NOT_IMPLEMENTED);
 }
 
+/* The allocation-free matvec checks its sizes before any device work, so the
+ * limit of its static scratch array is visible without a GPU.  The pointers
+ * are never dereferenced on these paths. */
+static void check_noalloc_limits(void) {
+    static _Alignas(16) float xbuf[4];
+    static _Alignas(16) uint8_t pbuf[16];
+    float y = 5.0f;
+    CHECK(wl_dev_i2s_matvec_f32_noalloc(pbuf, 0.05f, WL_NOALLOC_MAX_IN_DIM + 128u, 1, xbuf, &y,
+                                        NULL) == WL_ERR_INVALID_ARGUMENT);
+    CHECK(strstr(wl_last_error(), "WL_NOALLOC_MAX_IN_DIM") != NULL);
+    CHECK(wl_dev_i2s_matvec_f32_noalloc(pbuf, 0.05f, 100u, 1, xbuf, &y, NULL) ==
+          WL_ERR_GGUF_PARSE);
+    CHECK(wl_dev_i2s_matvec_f32_noalloc(pbuf, NAN, 128u, 1, xbuf, &y, NULL) == WL_ERR_GGUF_PARSE);
+    CHECK(y == 5.0f);
+}
+
 static void check_argmax_empty(void) {
     int64_t id = 7;
     CHECK(wl_argmax(NULL, 0, &id) == WL_OK);
@@ -195,6 +212,7 @@ int main(int argc, char **argv) {
     CHECK(strstr(wl_version(), "sm_100a") != NULL);
     check_i2s_validation(no_gpu);
     check_linear_dispatch();
+    check_noalloc_limits();
     check_argmax_empty();
     check_gguf();
     if (failures) fprintf(stderr, "%d check(s) failed\n", failures);
