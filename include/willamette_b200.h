@@ -99,9 +99,27 @@ uint32_t wl_last_error_tensor_type(void);
 int wl_init(int device);
 /* Free every cached device copy of host weights. */
 int wl_release_weights(void);
-/* Device-side error word (bit 0: a bounded wait timed out).  Reading
- * clears it. */
+/* Device-side error word (bit 0: a bounded wait timed out; bit 1: a
+ * tensor-parallel peer never arrived).  Synchronises the device, then reads
+ * and clears it.  Includes the status word of wl_dev_i2s_matvec_f32_noalloc
+ * on the calling thread's current device; when only that entry point has run
+ * in the process, this call allocates nothing either. */
 int wl_device_status(uint32_t *flags);
+/* Limit of every bounded device-side wait (TMA stage waits, peer and flag
+ * waits, grid barriers) on the current device, in ns; default 2 s, accepted
+ * range [1 us, 600 s].  A wait that runs out sets bit 0 (or bit 1 for a peer
+ * wait) of the device status word and its kernel returns; nothing hangs.
+ * Synchronises the device; call it outside stream capture.  No counterpart
+ * in the reference (its CPU path has no device waits). */
+int wl_set_wait_limit_ns(uint64_t ns);
+/* Enqueue on `stream` a bounded device-side wait until the 32-bit word at
+ * `flag` (device or mapped host memory, 4-byte aligned) reaches `target`
+ * (wrap-around compare).  Work queued after it runs once the word is there,
+ * or once the wait limit ran out, which sets bit 0 of the device status word.
+ * The same wait the tensor-parallel kernels use for their peers, exposed for
+ * callers that order GPU work after a word another agent writes.  No
+ * counterpart in the reference. */
+int wl_dev_wait_flag(const uint32_t *flag, uint32_t target, void *stream);
 
 /* ------------------------------------------------- host-buffer entry points */
 
@@ -159,6 +177,16 @@ int wl_lm_head_greedy(const float *hidden, size_t batch, const wl_tensor_view *t
 /* ------------------------------------------------ device-pointer entry points
  * All asynchronous on `stream` (a cudaStream_t; NULL = legacy default
  * stream).  Device buffers must be 16-byte aligned. */
+
+/* rms_norm_f32 (src/model/primitives.rs:227-255) of one f32 vector, bit
+ * for bit: mean = sum(x[i] * x[i]) / n with the sum in the reference's
+ * sequential order, out = (x * (1 / sqrt(mean + eps))) * w.  The norm in
+ * front of every BitLinear of the decode step (exact mode) uses the same
+ * arithmetic.  n a multiple of 4, at most WL_RMS_NORM_MAX_N; n == 0 does
+ * nothing.  out must not overlap x. */
+#define WL_RMS_NORM_MAX_N 16384u
+int wl_dev_rms_norm_f32(const float *x, const float *w, uint32_t n, float eps, float *out,
+                        void *stream);
 
 /* Per-row absmax int8 quantisation (bitlinear_sse2.rs:285-304) of an
  * m x n f32 matrix: q (m x n int8), act_scale (m f32). */
@@ -252,7 +280,13 @@ int wl_dev_i2s_matvec_f32(const uint8_t *packed, float w_scale, uint32_t in_dim,
  * - The first call on each device resolves the array's address and sets
  *   kernel attributes; make that first call before any stream capture.
  * - All calls share the one array: calls that overlap on the GPU (other
- *   streams, other host threads) race and must be serialised by the caller. */
+ *   streams, other host threads) race and must be serialised by the caller.
+ * - A bounded wait that runs out inside the kernel is reported by
+ *   wl_device_status on the same device (its status word sits in the same
+ *   static array).
+ * - The array's address belongs to the CUDA context current at the call;
+ *   after cudaDeviceReset or under another current context it is resolved
+ *   again (again allocating nothing). */
 #define WL_NOALLOC_MAX_IN_DIM 16384u
 int wl_dev_i2s_matvec_f32_noalloc(const uint8_t *packed, float w_scale, uint32_t in_dim,
                                   uint32_t out_dim, const float *x, float *y, void *stream);

@@ -108,6 +108,9 @@ PROTOTYPES = {
     "wl_init": ([_i], _i),
     "wl_release_weights": ([], _i),
     "wl_device_status": ([C.POINTER(_u32)], _i),
+    "wl_set_wait_limit_ns": ([C.c_uint64], _i),
+    "wl_dev_rms_norm_f32": ([_vp, _vp, _u32, C.c_float, _vp, _vp], _i),
+    "wl_dev_wait_flag": ([_vp, _u32, _vp], _i),
     "wl_bitlinear_i2s_matvec_f32": ([_tv, _fp, _sz, _fp, _sz], _i),
     "wl_bitlinear_i2s_matvec_f32_dbg": ([_tv, _fp, _sz, _fp, _sz, C.POINTER(C.c_int32), _fp,
                                          C.POINTER(C.c_int8)], _i),

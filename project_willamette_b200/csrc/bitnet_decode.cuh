@@ -25,6 +25,7 @@
 
 #include <cstdint>
 
+#include "exact_sum.cuh"
 #include "q6k_lmhead.cuh"
 #include "tp.cuh"
 #include "wl_ptx.cuh"
@@ -109,17 +110,49 @@ struct OutNormParams {
     uint32_t exact;  // sequential sum of squares (the reference's order)
 };
 
+// Exact-mode sum of squares of x[0..n) (n a multiple of 4, x 16-byte
+// aligned): the CTA stores the squares into shared memory `buf` (one round of
+// loads, one rounding per square), then adds them with the bits of the
+// reference's sequential loop (block_exact_sum_nonneg).
+__device__ __forceinline__ float block_seq_sum_sq(const float *x, uint32_t n, float *buf,
+                                                  ExactSumSmem &exs) {
+    for (uint32_t i = threadIdx.x * 4u; i < n; i += blockDim.x * 4u) {
+        const float4 v = *reinterpret_cast<const float4 *>(x + i);
+        *reinterpret_cast<float4 *>(buf + i) = make_float4(
+            __fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w));
+    }
+    __syncthreads();
+    return block_exact_sum_nonneg(buf, n, exs);
+}
+
+// rms_norm_f32 (primitives.rs:227-255) of one vector by one CTA:
+// mean = sum(x*x) / n (the reference's sequential sum, bit for bit),
+// rsqrt = 1 / sqrt(mean + eps), out = (x * rsqrt) * w.  Dynamic shared
+// memory: n floats.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ x,
+                                                        const float *__restrict__ w, uint32_t n,
+                                                        float eps, float *__restrict__ out) {
+    extern __shared__ __align__(16) float sq[];
+    __shared__ ExactSumSmem exs;
+    pdl_launch_dependents();
+    pdl_wait();
+    const float sum_sq = block_seq_sum_sq(x, n, sq, exs);
+    const float mean = __fdiv_rn(sum_sq, (float)n);
+    const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], rsqrt), w[i]);
+}
+
+constexpr uint32_t OUT_NORM_MAX = 8192;  // shared-memory copy of the exact-mode input
+
 __global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ OutNormParams p) {
     __shared__ float red[32];
+    __shared__ __align__(16) float hs[OUT_NORM_MAX];
+    __shared__ ExactSumSmem exs;
     pdl_launch_dependents();
     pdl_wait();
     float sum_sq;
     if (p.exact) {
-        if (threadIdx.x == 0) {
-            red[0] = seq_sum_sq(p.hidden, p.n);
-        }
-        __syncthreads();
-        sum_sq = red[0];
+        sum_sq = block_seq_sum_sq(p.hidden, p.n, hs, exs);
     } else {
         float ss = 0.0f;
         for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
@@ -178,6 +211,10 @@ struct AttnParams {
     // Tensor parallel: q / k / v were gathered from every rank's row slice;
     // with tp.wait set, every CTA first waits (bounded) for every rank's stores.
     TpParams tp;
+    // attn_exact_kernel: *pos was written well before the previous kernel
+    // (a previous step), so the cache history may be staged before the
+    // programmatic-dependency wait.
+    uint32_t pos_stable;
 };
 
 __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, int8_t *q,
@@ -478,6 +515,213 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
         reinterpret_cast<float4 *>(att + h * HD)[c] = O;
     }
     if (tid == 0) counters[h] = 0u;  // re-arm for the next launch
+}
+
+// ---------------------------------------------------------------------------
+// Exact-mode attention, one CTA per (query head, sequence): the reference's
+// scaled_dot_product_attention_into (cached_forward.rs:417-449) with
+// softmax_inplace (attention.rs:45-73) in its sequential order, bit for bit
+// except exp (a double exp rounded once).  The head's whole K and V history
+// (int8 rows and scales) is copied into shared memory with cp.async --
+// before the programmatic-dependency wait when the position is not written
+// by the kernels just before this one -- so the three sequential sums
+// (q.k per position, the softmax sum, and per dimension the weighted V sum)
+// read shared memory at the add's latency instead of waiting on global loads.
+constexpr int AX_THREADS = 512;
+
+__host__ __device__ inline uint32_t ax_cap(uint32_t max_seq) { return (max_seq + 3u) & ~3u; }
+
+inline size_t attn_exact_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq) {
+    const size_t cap = ax_cap(max_seq);
+    const size_t half2 = ((hd / 2u + 1u) & ~1u) * 2u;  // float2 RoPE row, in floats
+    return 2 * cap * hd + 3 * cap * 4 + (2 * (size_t)kv + hd + half2) * 4 + 2 * (size_t)kv;
+}
+
+// int8 -> exact float without the conversion unit: (2^23 + (b + 128)) -
+// (2^23 + 128), where b + 128 = (unsigned byte) ^ 0x80.  Byte j (0..3) of a
+// word already XORed with 0x80808080, or one byte.
+__device__ __forceinline__ float i8_byte_to_f32(uint32_t w_xor80, uint32_t j) {
+    return __fsub_rn(__uint_as_float(__byte_perm(w_xor80, 0x4B000000u, 0x7540u + j)), 8388736.0f);
+}
+__device__ __forceinline__ float i8_to_f32(int8_t b) {
+    return __fsub_rn(__uint_as_float(((uint32_t)(uint8_t)b ^ 0x80u) | 0x4B000000u), 8388736.0f);
+}
+
+__global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float red[32];
+    __shared__ float s_ks, s_vs, s_inv;
+    __shared__ uint32_t s_norm;
+    __shared__ ExactSumSmem exs;
+    const uint32_t HD = p.head_dim, KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
+    const uint32_t h = blockIdx.x, kvh = h / p.group, tid = threadIdx.x, z = blockIdx.z;
+    const uint32_t cap = ax_cap(p.max_seq);
+    int8_t *Ksm = reinterpret_cast<int8_t *>(smem);
+    int8_t *Vsm = Ksm + (size_t)cap * HD;
+    float *ksc = reinterpret_cast<float *>(Vsm + (size_t)cap * HD);
+    float *vsc = ksc + cap;
+    float *sc = vsc + cap;
+    float *kf = sc + cap;
+    float *vf = kf + KV;
+    float *qh = vf + KV;
+    float2 *rope = reinterpret_cast<float2 *>(qh + HD);
+    int8_t *kq = reinterpret_cast<int8_t *>(rope + ((half + 1u) & ~1u));
+    int8_t *vq = kq + KV;
+
+    const int8_t *k_cache = p.k_cache + z * p.cache_stride;
+    const int8_t *v_cache = p.v_cache + z * p.cache_stride;
+    const float *k_scale = p.k_scale + (size_t)z * p.scale_stride;
+    const float *v_scale = p.v_scale + (size_t)z * p.scale_stride;
+    // The head's cached rows [0, pos) and their scales, 16 bytes per copy.
+    auto stage_history = [&](uint32_t pos) {
+        const uint32_t pieces = HD / 16u, n = pos * pieces;
+        for (uint32_t i = tid; i < n; i += AX_THREADS) {
+            const uint32_t t = i / pieces, c = i % pieces;
+            const size_t g = (size_t)t * KV + kvh * HD + c * 16u;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Ksm + t * HD + c * 16u)),
+                         "l"(k_cache + g) : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Vsm + t * HD + c * 16u)),
+                         "l"(v_cache + g) : "memory");
+        }
+        for (uint32_t t = tid; t < pos; t += AX_THREADS) {
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ksc + t)),
+                         "l"(k_scale + t) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(vsc + t)),
+                         "l"(v_scale + t) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    uint32_t pos = 0;
+    bool staged = false;
+    if (p.pos_stable && !p.active) {
+        pos = __ldcg(p.pos + z);
+        if (pos < p.max_seq) {
+            stage_history(pos);
+            staged = true;
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    if (p.tp.world && p.tp.wait) {
+        if (tid == 0 && !tp_wait(p.tp)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
+        __syncthreads();
+    }
+    if (p.active && !p.active[z]) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        return;
+    }
+    if (!staged) {
+        pos = p.pos[z];
+        if (pos < p.max_seq) stage_history(pos);
+    }
+    if (pos >= p.max_seq) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        if (tid == 0) atomicOr(p.status, WL_DEV_ERR_POSITION);
+        return;
+    }
+    const float *q_in = p.q + (size_t)z * p.qkv_stride, *k_in = p.k + (size_t)z * p.qkv_stride,
+                *v_in = p.v + (size_t)z * p.qkv_stride;
+    float *att = p.att + (size_t)z * p.att_stride;
+    const float2 *cs = p.rope + (size_t)pos * half;
+    for (uint32_t i = tid; i < KV; i += AX_THREADS) {
+        kf[i] = k_in[i];
+        vf[i] = v_in[i];
+    }
+    for (uint32_t i = tid; i < HD; i += AX_THREADS) qh[i] = q_in[h * HD + i];
+    for (uint32_t j = tid; j < half; j += AX_THREADS) rope[j] = cs[j];
+    __syncthreads();
+    // RoPE on every K head (the K quantisation takes the absmax of all of
+    // them) and on this query head: pair (i0, i1) = NEOX (j, j + half) or
+    // Norm (2j, 2j + 1).
+    const uint32_t pstep = p.rope_pairs ? 2u : 1u, poff = p.rope_pairs ? 1u : half;
+    for (uint32_t i = tid; i < p.n_kv_heads * half; i += AX_THREADS) {
+        const uint32_t hk = i / half, j = i % half;
+        float *x = kf + hk * HD;
+        const uint32_t i0 = j * pstep, i1 = i0 + poff;
+        const float a = x[i0], b = x[i1], c = rope[j].x, sn = rope[j].y;
+        x[i0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+        x[i1] = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+    }
+    for (uint32_t j = tid; j < half; j += AX_THREADS) {
+        const uint32_t i0 = j * pstep, i1 = i0 + poff;
+        const float a = qh[i0], b = qh[i1], c = rope[j].x, sn = rope[j].y;
+        qh[i0] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+        qh[i1] = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+    }
+    __syncthreads();
+    kv_quantise_block(kf, KV, kq, &s_ks, red);
+    kv_quantise_block(vf, KV, vq, &s_vs, red);
+    __syncthreads();
+    if (h == 0) {  // one CTA per sequence appends the position to the cache
+        int8_t *kc = p.k_cache + z * p.cache_stride, *vc = p.v_cache + z * p.cache_stride;
+        for (uint32_t i = tid; i < KV; i += AX_THREADS) {
+            kc[(size_t)pos * KV + i] = kq[i];
+            vc[(size_t)pos * KV + i] = vq[i];
+        }
+        if (tid == 0) {
+            p.k_scale[(size_t)z * p.scale_stride + pos] = s_ks;
+            p.v_scale[(size_t)z * p.scale_stride + pos] = s_vs;
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    // scores[t] = (sum_d q[d] * ((f32)k8[t][d] * s_t)) * scale, d in order
+    const uint32_t n = pos + 1u;
+    for (uint32_t t = tid; t < n; t += AX_THREADS) {
+        const int8_t *kr = t < pos ? Ksm + (size_t)t * HD : kq + kvh * HD;
+        const float sk = t < pos ? ksc[t] : s_ks;
+        float d = 0.0f;
+        for (uint32_t c = 0; c < HD; c += 16u) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(kr + c);
+            const uint32_t wv[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
+                                    w.w ^ 0x80808080u};
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                d = __fadd_rn(d, __fmul_rn(qh[c + e], __fmul_rn(i8_byte_to_f32(wv[e >> 2], e & 3), sk)));
+        }
+        sc[t] = __fmul_rn(d, p.scale);
+    }
+    __syncthreads();
+    // softmax_inplace: the maximum (a block reduction gives the strict-'>'
+    // scan's value: NaN never wins, and +0 / -0 maxima give the same
+    // exponentials), exp, the sequential sum, the scaling by 1 / sum.
+    float mloc = -INFINITY;
+    for (uint32_t t = tid; t < n; t += AX_THREADS) mloc = fmaxf(mloc, sc[t]);
+    const float mx = block_max(mloc, red);
+    if (!isfinite(mx)) {
+        for (uint32_t t = tid; t < n; t += AX_THREADS) sc[t] = 0.0f;
+    } else {
+        for (uint32_t t = tid; t < n; t += AX_THREADS) sc[t] = exp_f32(__fsub_rn(sc[t], mx));
+        __syncthreads();
+        const float sum = block_exact_sum_nonneg(sc, n, exs);  // the sequential sum's bits
+        if (tid == 0) {
+            s_norm = sum > 0.0f ? 1u : 0u;
+            s_inv = s_norm ? __fdiv_rn(1.0f, sum) : 1.0f;
+        }
+        __syncthreads();
+        if (s_norm)
+            for (uint32_t t = tid; t < n; t += AX_THREADS) sc[t] = __fmul_rn(sc[t], s_inv);
+    }
+    __syncthreads();
+    // out[d] = 0 + sum_t w_t * ((f32)v8[t][d] * s_t), t in order (one thread per d);
+    // the loads and products of the next 8 positions run ahead of the adds
+    for (uint32_t d = tid; d < HD; d += AX_THREADS) {
+        float o = 0.0f;
+        const int8_t *vcol = Vsm + d;
+        uint32_t t = 0;
+        for (; t + 8u <= pos; t += 8u) {
+            float vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                vv[u] = __fmul_rn(sc[t + u], __fmul_rn(i8_to_f32(vcol[(size_t)(t + u) * HD]), vsc[t + u]));
+#pragma unroll
+            for (int u = 0; u < 8; ++u) o = __fadd_rn(o, vv[u]);
+        }
+        for (; t < pos; ++t)
+            o = __fadd_rn(o, __fmul_rn(sc[t], __fmul_rn(i8_to_f32(vcol[(size_t)t * HD]), vsc[t])));
+        o = __fadd_rn(o, __fmul_rn(sc[pos], __fmul_rn(i8_to_f32(vq[kvh * HD + d]), s_vs)));
+        att[h * HD + d] = o;
+    }
 }
 
 inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq, uint32_t splits) {

@@ -151,10 +151,10 @@ __device__ __forceinline__ bool mega_barrier(const MegaParams &p, unsigned long 
         uint32_t ok = 1;
         __threadfence();
         atomicAdd(p.arrivals, 1ull);
-        const uint64_t t0 = globaltimer_ns();
+        const uint64_t t0 = globaltimer_ns(), limit = wait_limit_ns();
         while (ld_acquire_gpu_u64(p.arrivals) < target) {
             if (*(volatile uint32_t *)p.abort) { ok = 0; break; }
-            if (globaltimer_ns() - t0 > WL_WAIT_LIMIT_NS) {
+            if (globaltimer_ns() - t0 > limit) {
                 atomicOr(p.status, WL_DEV_ERR_MEGA);
                 atomicExch(p.abort, 1u);
                 ok = 0;

@@ -28,6 +28,7 @@
 
 #include <cstdint>
 
+#include "exact_sum.cuh"
 #include "tp.cuh"
 #include "wl_ptx.cuh"
 
@@ -278,114 +279,24 @@ __device__ __forceinline__ int32_t cta_qsum(const int32_t *ared) {
     return t;
 }
 
-// Absmax quantisation of x[0..K) by the whole CTA into shared memory (same
-// IEEE steps as quantize_absmax_kernel).  Returns the activation scale; the
-// per-warp sums of the quantised values go to `ared`.
-__device__ __forceinline__ float cta_quantize(const float *__restrict__ x, uint32_t K, float *xs,
-                                              int8_t *qs, float *red, int32_t *ared) {
-    const uint32_t tid = threadIdx.x, nthr = blockDim.x;
-    float m = 0.0f;
-    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(x + i);
-        *reinterpret_cast<float4 *>(xs + i) = v;
-        m = fmaxf(fmaxf(fmaxf(m, fabsf(v.x)), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if ((tid & 31) == 0) red[tid >> 5] = m;
-    __syncthreads();
-    float max_abs = red[0];
-    for (uint32_t w = 1; w < nthr / 32; ++w) max_abs = fmaxf(max_abs, red[w]);
-    const float inv = max_abs == 0.0f ? 0.0f : __fdiv_rn(127.0f, max_abs);
-    int32_t qsum = 0;
-    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(xs + i);
-        const float e[4] = {v.x, v.y, v.z, v.w};
-        uint32_t packed = 0;
-        if (max_abs != 0.0f) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int qi = quant_round_i8(__fmul_rn(e[k], inv));
-                packed |= (uint32_t)(qi & 0xFF) << (8 * k);
-            }
-        }
-        *reinterpret_cast<uint32_t *>(qs + qs_index(i, qs_plane(K))) = packed;
-        qsum = __dp4a((int)packed, 0x01010101, qsum);
-    }
-    publish_qsum(qsum, ared);
-    __syncthreads();
-    return max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
-}
-
-// Decode-step input transform, by the whole CTA into xs (every CTA computes
-// the same values in the same order):
-//   I2S_PRE_RMSNORM:       xs = rms_norm(x, w)            (primitives.rs:227-254)
-//   I2S_PRE_RELU2_RMSNORM: xs = rms_norm(relu(x)^2 * x2, w) (ffn.rs:37-65, then
-//                          the ffn_sub_norm of cached_forward.rs:480-494)
-// rms_norm: mean = sum(v*v) / K, rsqrt = 1 / sqrt(mean + eps),
-// out = (v * rsqrt) * w, IEEE round-to-nearest (the sum as a tree).
-__device__ __forceinline__ void cta_pre_input(const I2sMatvecParams &p, uint32_t K, float *xs,
-                                              float *red, const float *nw) {
-    const uint32_t tid = threadIdx.x, nthr = blockDim.x;
-    float ss = 0.0f;
-    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
-        float4 v = *reinterpret_cast<const float4 *>(p.x + i);
-        if (p.pre == I2S_PRE_RELU2_RMSNORM) {
-            const float4 u = *reinterpret_cast<const float4 *>(p.x2 + i);
-            const float r0 = v.x > 0.0f ? v.x : 0.0f, r1 = v.y > 0.0f ? v.y : 0.0f;
-            const float r2 = v.z > 0.0f ? v.z : 0.0f, r3 = v.w > 0.0f ? v.w : 0.0f;
-            v.x = __fmul_rn(__fmul_rn(r0, r0), u.x);
-            v.y = __fmul_rn(__fmul_rn(r1, r1), u.y);
-            v.z = __fmul_rn(__fmul_rn(r2, r2), u.z);
-            v.w = __fmul_rn(__fmul_rn(r3, r3), u.w);
-        }
-        *reinterpret_cast<float4 *>(xs + i) = v;
-        ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
-                                     __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
-    }
-    float sum_sq;
-    if (p.exact_norm) {
-        // the reference's loop: sum_sq += x[i] * x[i], i = 0, 1, ... (one thread)
-        __syncthreads();
-        if (tid == 0) {
-            red[0] = seq_sum_sq(xs, K);
-        }
-        __syncthreads();
-        sum_sq = red[0];
-    } else {
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-            ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-        if ((tid & 31) == 0) red[tid >> 5] = ss;
-        __syncthreads();
-        sum_sq = red[0];
-        for (uint32_t w = 1; w < nthr / 32; ++w) sum_sq = __fadd_rn(sum_sq, red[w]);
-    }
-    const float mean = __fdiv_rn(sum_sq, (float)K);
-    const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-    for (uint32_t i = tid * 4; i < K; i += nthr * 4) {
-        float4 v = *reinterpret_cast<const float4 *>(xs + i);
-        const float4 w = *reinterpret_cast<const float4 *>(nw + i);
-        v.x = __fmul_rn(__fmul_rn(v.x, rsqrt), w.x);
-        v.y = __fmul_rn(__fmul_rn(v.y, rsqrt), w.y);
-        v.z = __fmul_rn(__fmul_rn(v.z, rsqrt), w.z);
-        v.w = __fmul_rn(__fmul_rn(v.w, rsqrt), w.w);
-        *reinterpret_cast<float4 *>(xs + i) = v;
-    }
-    __syncthreads();  // red is reused by the quantiser; xs is complete
-}
-
-// Fast-mode input transform + quantisation with the input held in registers:
+// Decode-step input transform + absmax quantisation (same IEEE steps as
+// quantize_absmax_kernel) by the whole CTA, the input held in registers:
 // every global load of a thread is issued before any is used (one memory
 // round trip per CTA instead of one per 1024-element pass), the RMSNorm
 // weights were copied to `nw` (shared memory) before the dependency wait.
-// Same values, in the same per-thread order, as cta_pre_input (tree sums) +
-// cta_quantize.
+// Every CTA computes the same values in the same order:
+//   I2S_PRE_RMSNORM:       rms_norm(x, w)              (primitives.rs:227-254)
+//   I2S_PRE_RELU2_RMSNORM: rms_norm(relu(x)^2 * x2, w) (ffn.rs:37-65, then the
+//                          ffn_sub_norm of cached_forward.rs:480-494)
+// rms_norm: mean = sum(v*v) / K, rsqrt = 1 / sqrt(mean + eps), out = (v *
+// rsqrt) * w.  The sum of squares is a tree (fast mode), or with `chain`
+// set the reference's sequential loop over the input stored there (exact).
 constexpr int I2S_PRE_V = (int)(I2S_FUSE_Q_MAX_K / (I2S_THREADS * 4u));  // float4 per thread
 
 __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint32_t K,
                                                   const float *nw, int8_t *qs, float *red,
-                                                  int32_t *ared, const float *us) {
+                                                  int32_t *ared, const float *us,
+                                                  float *chain = nullptr) {
     const uint32_t tid = threadIdx.x, nthr = blockDim.x;
     const bool relu2 = p.pre == I2S_PRE_RELU2_RMSNORM;
     // float4 slots this CTA's K needs: the unrolled loops leave at the first
@@ -444,21 +355,40 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
         }
     }
     if (p.pre != I2S_PRE_NONE) {
-        float ss = 0.0f;
+        float sum_sq;
+        if (chain) {
+            // exact mode: the reference's loop sum_sq += x[i] * x[i], i = 0, 1,
+            // ...: the squares (one rounding each) stored in parallel, then
+            // summed with that loop's bits by the whole CTA
 #pragma unroll
-        for (int k = 0; k < I2S_PRE_V; ++k) {
-            if (k >= kmax) break;
-            const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
-            if (i < K)
-                ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v[k].x, v[k].x), __fmul_rn(v[k].y, v[k].y)),
-                                             __fadd_rn(__fmul_rn(v[k].z, v[k].z), __fmul_rn(v[k].w, v[k].w))));
+            for (int k = 0; k < I2S_PRE_V; ++k) {
+                if (k >= kmax) break;
+                const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+                if (i < K)
+                    *reinterpret_cast<float4 *>(chain + i) =
+                        make_float4(__fmul_rn(v[k].x, v[k].x), __fmul_rn(v[k].y, v[k].y),
+                                    __fmul_rn(v[k].z, v[k].z), __fmul_rn(v[k].w, v[k].w));
+            }
+            __syncthreads();
+            __shared__ ExactSumSmem exs;
+            sum_sq = block_exact_sum_nonneg(chain, K, exs);
+        } else {
+            float ss = 0.0f;
+#pragma unroll
+            for (int k = 0; k < I2S_PRE_V; ++k) {
+                if (k >= kmax) break;
+                const uint32_t i = tid * 4u + (uint32_t)k * nthr * 4u;
+                if (i < K)
+                    ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v[k].x, v[k].x), __fmul_rn(v[k].y, v[k].y)),
+                                                 __fadd_rn(__fmul_rn(v[k].z, v[k].z), __fmul_rn(v[k].w, v[k].w))));
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+            if ((tid & 31) == 0) red[tid >> 5] = ss;
+            __syncthreads();
+            sum_sq = red[0];
+            for (uint32_t w = 1; w < nthr / 32; ++w) sum_sq = __fadd_rn(sum_sq, red[w]);
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-        if ((tid & 31) == 0) red[tid >> 5] = ss;
-        __syncthreads();
-        float sum_sq = red[0];
-        for (uint32_t w = 1; w < nthr / 32; ++w) sum_sq = __fadd_rn(sum_sq, red[w]);
         const float mean = __fdiv_rn(sum_sq, (float)K);
         const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
 #pragma unroll
@@ -590,10 +520,12 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
             i2s_issue_chunk(p, c, r0, r1, RPI, row_bytes, smem + c * stage_bytes, &full_bar[c],
                             policy);
     }
-    // fast mode: the RMSNorm weights do not depend on earlier kernels either
-    const bool regs_pre = FUSE_Q && !(p.pre != I2S_PRE_NONE && p.exact_norm);
+    // The RMSNorm weights do not depend on earlier kernels either.  Exact mode
+    // (the reference's sequential sum of squares) keeps them after the
+    // quantised input, so that xs holds the transformed input for that sum.
+    const bool exact_pre = FUSE_Q && p.pre != I2S_PRE_NONE && p.exact_norm;
     if constexpr (FUSE_Q) {
-        if (regs_pre && p.pre != I2S_PRE_NONE) {
+        if (!exact_pre && p.pre != I2S_PRE_NONE) {
             float *nw = reinterpret_cast<float *>(smem + nst * stage_bytes);
             for (uint32_t i = tid * 4u; i < K; i += I2S_THREADS * 4u)
                 asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(nw + i)),
@@ -625,8 +557,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         int8_t *qs = reinterpret_cast<int8_t *>(xs + K);
         float *us = reinterpret_cast<float *>(qs + K + I2S_QS_PAD);  // K floats (stage_up)
         // exact mode stages the RMSNorm weights where fast mode keeps up
-        const bool nw_exact = !regs_pre;  // (pre != NONE and exact_norm)
-        float *ysm = us + ((p.stage_up || nw_exact) ? K : 0u);        // this CTA's rows (stage_res)
+        float *ysm = us + ((p.stage_up || exact_pre) ? K : 0u);       // this CTA's rows (stage_res)
         if (p.pre != I2S_PRE_NONE) {
             asm volatile("cp.async.wait_all;" ::: "memory");
             __syncthreads();
@@ -650,12 +581,10 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
                              : "memory");
             }
         asm volatile("cp.async.commit_group;" ::: "memory");
-        if (regs_pre) {
-            act_scale = cta_prepare_regs(p, K, xs, qs, red, ared, p.stage_up ? us : nullptr);
-        } else {  // exact mode: the reference's sequential sum of squares
-            cta_pre_input(p, K, xs, red, us);
-            act_scale = cta_quantize(xs, K, xs, qs, red, ared);
-        }
+        // exact mode: RMSNorm weights at `us`, the transformed input to xs
+        // for the reference's sequential sum of squares
+        act_scale = exact_pre ? cta_prepare_regs(p, K, us, qs, red, ared, nullptr, xs)
+                              : cta_prepare_regs(p, K, xs, qs, red, ared, p.stage_up ? us : nullptr);
         if (blockIdx.x == 0) {
             if (p.q_out)
                 for (uint32_t i = tid * 16; i < K; i += I2S_THREADS * 16)
@@ -709,7 +638,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         asm volatile("cp.async.wait_all;" ::: "memory");
         if (p.stage_res)
             ysm = reinterpret_cast<float *>(smem + nst * stage_bytes + (size_t)K * 5u + I2S_QS_PAD +
-                                            ((p.stage_up || !regs_pre) ? (size_t)K * 4u : 0u));
+                                            ((p.stage_up || exact_pre) ? (size_t)K * 4u : 0u));
     }
     // Every chunk requested up front (no ring reuse): each warp waits for a
     // chunk's weights itself and the loop needs no CTA barrier.  Otherwise

@@ -25,15 +25,21 @@
 // (nb = n_embd / 256; 2112 bytes per row at n_embd 2560, 0.57 % above the
 // GGUF 2100) so rows and sections are 16-byte aligned for bulk copies.
 //
-// Streaming: 148 persistent CTAs each own a contiguous row range; a producer
-// warp streams 32-row chunks into a 3-stage shared-memory ring with 1-D bulk
-// copies; two consumer groups of 4 warps take alternate chunks.
+// Streaming: one launch for the whole batch.  The batch is cut into groups of
+// BG hidden rows (BG = 1, 2, 4 or 8); the grid is (batch groups) x (vocab
+// ranges), about one CTA per SM, and each CTA stages its group's hidden rows
+// in shared memory once.  A producer warp streams the range's 32-row chunks
+// into a 2-3 stage shared-memory ring with 1-D bulk copies; two consumer
+// groups of 4 warps take alternate chunks, and each decoded weight value is
+// used for all BG hidden rows.  The CTAs of different batch groups stream the
+// same vocab range at the same time, so with more than one group the weight
+// bytes come from DRAM once and from L2 for the other groups.
 //
 // Argmax: key = (orderable(logit) << 32) | (0xFFFFFFFF - row); the maximum
 // key is the reference's answer (ties -> lowest row, -0.0 == +0.0, NaN never
 // wins, except a NaN at row 0, which the strict '>' scan keeps).  CTAs
 // atomicMax into a per-batch-row slot; the last CTA to finish writes the ids
-// and re-zeroes the slots and its counter.
+// of every batch row and re-zeroes the slots and its counter.
 #pragma once
 
 #include <cstdint>
@@ -48,6 +54,7 @@ constexpr int Q6K_THREADS = (Q6K_CONSUMER_WARPS + 1) * 32;
 constexpr int Q6K_GROUP_THREADS = 128;  // 4 warps per consumer group
 constexpr int Q6K_ROWS_PER_CHUNK = Q6K_GROUP_THREADS / 4;  // 4 threads per row
 constexpr int Q6K_STAGES = 3;
+constexpr int Q6K_MAX_BG = 8;
 
 __host__ __device__ constexpr uint32_t q6k_row_stride(uint32_t nb) {
     return (nb * 208u + ((nb * 2u + 15u) & ~15u));
@@ -60,16 +67,18 @@ __device__ __forceinline__ uint32_t q6k_xpad(uint32_t i) { return i + (i >> 5) *
 struct Q6kParams {
     const uint8_t *packed;   // vocab x row_stride bytes, device layout
     uint32_t n_embd, vocab, nb, row_stride;
-    uint32_t rows_per_cta;
+    uint32_t rows_per_cta;   // rows of one vocab range
+    uint32_t n_ranges;       // vocab ranges; CTA c: range c % n_ranges, group c / n_ranges
+    uint32_t batch;          // hidden rows (all groups)
     uint32_t nstages;        // 2 or 3 (<= Q6K_STAGES), whatever fits in shared memory
-    const float *hidden;     // BG x n_embd (this launch's batch rows)
-    float *logits;           // BG x vocab or null
-    uint32_t *ids;           // BG or null
-    unsigned long long *slots;  // BG argmax slots (zero on entry)
+    uint32_t l2_keep;        // several groups read each range: no evict-first hint
+    const float *hidden;     // batch x n_embd
+    float *logits;           // batch x vocab or null
+    uint32_t *ids;           // batch or null
+    unsigned long long *slots;  // batch argmax slots (zero on entry)
     uint32_t *counter;          // CTA completion counter (zero on entry)
     uint32_t *status;
     uint32_t row_offset;        // vocab shard: global id of local row 0
-    uint32_t batch_off;         // first batch row of this launch (key slots)
     TpParams tp;                // world 0: single GPU (ids written here)
 };
 
@@ -175,7 +184,10 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
     float *xs = reinterpret_cast<float *>(smem + nst * chunk_bytes);
     const uint32_t xs_len = p.n_embd + p.n_embd / 8;  // padded floats per batch row
 
-    const uint32_t r0 = blockIdx.x * p.rows_per_cta;
+    const uint32_t range = blockIdx.x % p.n_ranges, bgrp = blockIdx.x / p.n_ranges;
+    const uint32_t b0 = bgrp * BG;                              // first hidden row
+    const uint32_t gcnt = min((uint32_t)BG, p.batch - b0);      // rows of this group
+    const uint32_t r0 = range * p.rows_per_cta;
     const uint32_t r1 = min(r0 + p.rows_per_cta, p.vocab);
     const uint32_t nchunks = r0 < r1 ? (r1 - r0 + Q6K_ROWS_PER_CHUNK - 1) / Q6K_ROWS_PER_CHUNK : 0;
 
@@ -210,18 +222,23 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
                 const uint32_t b = min(a + Q6K_ROWS_PER_CHUNK, r1);
                 const uint32_t bytes = (b - a) * p.row_stride;
                 mbar_arrive_expect_tx(&full_bar[st], bytes);
-                bulk_g2s_evict_first(smem + st * chunk_bytes, p.packed + (size_t)a * p.row_stride,
-                                     bytes, &full_bar[st], policy);
+                if (p.l2_keep)
+                    bulk_g2s(smem + st * chunk_bytes, p.packed + (size_t)a * p.row_stride, bytes,
+                             &full_bar[st]);
+                else
+                    bulk_g2s_evict_first(smem + st * chunk_bytes,
+                                         p.packed + (size_t)a * p.row_stride, bytes, &full_bar[st],
+                                         policy);
             }
         }
     } else {
         // Consumers: wait for the previous kernel (the hidden rows, and the
-        // argmax scratch of a previous call), then stage the hidden rows
-        // (padded) in shared memory.
+        // argmax scratch of a previous call), then stage this group's hidden
+        // rows (padded; rows past the batch as zeros) in shared memory.
         pdl_wait();
         for (uint32_t i = tid; i < BG * p.n_embd; i += Q6K_CONSUMER_WARPS * 32) {
             const uint32_t bg = i / p.n_embd, e = i % p.n_embd;
-            xs[bg * xs_len + q6k_xpad(e)] = p.hidden[(size_t)bg * p.n_embd + e];
+            xs[bg * xs_len + q6k_xpad(e)] = bg < gcnt ? p.hidden[(size_t)(b0 + bg) * p.n_embd + e] : 0.0f;
         }
         asm volatile("bar.sync 1, %0;" ::"n"(Q6K_CONSUMER_WARPS * 32));
 
@@ -280,11 +297,9 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
                                                 (((qhw[m] >> qh_shift) & 0x03030303u) << 4);
                             const float sc_f = m < 4 ? s0 : s1;
                             const float2 sc2 = make_float2(sc_f, sc_f);
-                            // (2^23 + u) - (2^23 + 32) = u - 32, exact; then q * (d * sc).
-                            // Packed pairs here only: no add follows these
-                            // multiplies, so nothing can be fused into an FMA.
-                            // The product with x and the chain add stay scalar
-                            // mul.rn / add.rn, which are never contracted.
+                            // (2^23 + u) - (2^23 + 32) = u - 32, then q * (d * sc):
+                            // both exact, as packed pairs (an add feeding a
+                            // multiply cannot become an FMA).
                             float2 w[2];
 #pragma unroll
                             for (int j = 0; j < 2; ++j) {
@@ -300,10 +315,22 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
                             for (int g = 0; g < BG; ++g) {
                                 const float4 xv = *reinterpret_cast<const float4 *>(
                                     xs + g * xs_len + q6k_xpad(xbase + 4u * m));
-                                acc[g][0] = __fadd_rn(acc[g][0], __fmul_rn(w[0].x, xv.x));
-                                acc[g][1] = __fadd_rn(acc[g][1], __fmul_rn(w[0].y, xv.y));
-                                acc[g][2] = __fadd_rn(acc[g][2], __fmul_rn(w[1].x, xv.z));
-                                acc[g][3] = __fadd_rn(acc[g][3], __fmul_rn(w[1].y, xv.w));
+                                // (q * (d * sc)) * x rounded once, then the
+                                // chain add rounded once: the product as an
+                                // FMA with a +0 addend (never simplified to a
+                                // plain multiply, so never fused with the add;
+                                // equal to the product here because a chain
+                                // that starts at +0 is never -0).
+                                const float2 p0 = f2_fma_rn(w[0], make_float2(xv.x, xv.y),
+                                                            make_float2(0.0f, 0.0f));
+                                const float2 p1 = f2_fma_rn(w[1], make_float2(xv.z, xv.w),
+                                                            make_float2(0.0f, 0.0f));
+                                const float2 a01 = f2_add_rn(make_float2(acc[g][0], acc[g][1]), p0);
+                                const float2 a23 = f2_add_rn(make_float2(acc[g][2], acc[g][3]), p1);
+                                acc[g][0] = a01.x;
+                                acc[g][1] = a01.y;
+                                acc[g][2] = a23.x;
+                                acc[g][3] = a23.y;
                             }
                         }
                     }
@@ -325,8 +352,8 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
                     v[k] = __fadd_rn(pair, hi);                      // lane a=0
                 }
                 const float logit = __fadd_rn(__fadd_rn(v[0], v[3]), __fadd_rn(v[1], v[2]));
-                if (a == 0 && row < r1) {
-                    if (p.logits) p.logits[(size_t)g * p.vocab + row] = logit;
+                if (a == 0 && row < r1 && (uint32_t)g < gcnt) {
+                    if (p.logits) p.logits[(size_t)(b0 + g) * p.vocab + row] = logit;
                     const unsigned long long key =
                         ((unsigned long long)f32_order_key(logit, row + p.row_offset) << 32) |
                         (unsigned long long)(0xFFFFFFFFu - (row + p.row_offset));
@@ -351,7 +378,7 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
     if (tid == 0) {
         if (s_timeout) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
         if (p.ids) {
-            for (int g = 0; g < BG; ++g) atomicMax(&p.slots[g], cta_best[g]);
+            for (uint32_t g = 0; g < gcnt; ++g) atomicMax(&p.slots[b0 + g], cta_best[g]);
             __threadfence();
             s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
         } else {
@@ -359,15 +386,17 @@ __global__ void __launch_bounds__(Q6K_THREADS, 1)
         }
     }
     __syncthreads();
-    if (s_last && tid < BG) {
+    if (s_last) {
         __threadfence();
-        const unsigned long long k = atomicExch(&p.slots[tid], 0ull);
-        if (p.tp.world) {
-            const uint32_t set = tp_key_set(p.tp);
-            for (int r = 0; r < p.tp.world; ++r)
-                *tp_key_slot(p.tp.peer_base[r], set, p.tp.rank, p.batch_off + tid) = k;
-        } else {
-            p.ids[tid] = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+        const uint32_t set = p.tp.world ? tp_key_set(p.tp) : 0u;
+        for (uint32_t b = tid; b < p.batch; b += blockDim.x) {
+            const unsigned long long k = atomicExch(&p.slots[b], 0ull);
+            if (p.tp.world) {
+                for (int r = 0; r < p.tp.world; ++r)
+                    *tp_key_slot(p.tp.peer_base[r], set, p.tp.rank, b) = k;
+            } else {
+                p.ids[b] = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+            }
         }
         if (tid == 0) *p.counter = 0u;
     }

@@ -185,9 +185,8 @@ __global__ void __launch_bounds__(QB_THREADS) q8_batch_kernel(const __grid_const
         for (uint32_t t = warp; t < ntok; t += QB_WARPS) {
             float *xt = xs + (size_t)t * K;
             float ss = 0.0f;
-            if (p.exact_norm) {
-                if (lane == 0)
-                    for (uint32_t i = 0; i < K; ++i) ss = __fadd_rn(ss, __fmul_rn(xt[i], xt[i]));
+            if (p.exact_norm) {  // the reference's sequential loop, loads run ahead
+                if (lane == 0) ss = seq_sum_sq(xt, K);
                 ss = __shfl_sync(0xffffffffu, ss, 0);
             } else {
                 for (uint32_t i = lane; i < K; i += 32u) ss = __fadd_rn(ss, __fmul_rn(xt[i], xt[i]));
@@ -373,6 +372,8 @@ struct OutNormBatchParams {
 
 __global__ void __launch_bounds__(256) out_norm_batch_kernel(const __grid_constant__ OutNormBatchParams p) {
     __shared__ float red[32];
+    __shared__ __align__(16) float hs[OUT_NORM_MAX];
+    __shared__ ExactSumSmem exs;
     pdl_launch_dependents();
     pdl_wait();
     const float *__restrict__ h = p.hidden + (size_t)blockIdx.x * p.n;
@@ -380,11 +381,7 @@ __global__ void __launch_bounds__(256) out_norm_batch_kernel(const __grid_consta
     const float *__restrict__ nw = p.w;
     float sum_sq;
     if (p.exact) {
-        if (threadIdx.x == 0) {
-            red[0] = seq_sum_sq(h, p.n);
-        }
-        __syncthreads();
-        sum_sq = red[0];
+        sum_sq = block_seq_sum_sq(h, p.n, hs, exs);
     } else {
         float ss = 0.0f;
         for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(h[i], h[i]));

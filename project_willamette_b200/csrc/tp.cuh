@@ -95,11 +95,11 @@ __device__ __forceinline__ void tp_arrive(const TpParams &tp) {
 // this rank's own.  Returns false on timeout.
 __device__ __forceinline__ bool tp_wait(const TpParams &tp) {
     const uint32_t target = ld_acquire_sys(tp_counter(tp.local_base, tp.rank));
-    const uint64_t t0 = globaltimer_ns();
+    const uint64_t t0 = globaltimer_ns(), limit = wait_limit_ns();
     for (int s = 0; s < tp.world; ++s) {
         const uint32_t *c = tp_counter(tp.local_base, s);
         while ((int32_t)(ld_acquire_sys(c) - target) < 0) {
-            if (globaltimer_ns() - t0 > WL_WAIT_LIMIT_NS) return false;
+            if (globaltimer_ns() - t0 > limit) return false;
         }
     }
     return true;
@@ -109,6 +109,21 @@ __device__ __forceinline__ bool tp_wait(const TpParams &tp) {
 // that is not itself a library kernel.
 __global__ void tp_wait_kernel(const TpParams tp, uint32_t *status) {
     if (threadIdx.x == 0 && !tp_wait(tp)) atomicOr(status, WL_DEV_ERR_PEER_TIMEOUT);
+}
+
+// Wait (one thread, bounded) until the word another agent writes -- a peer
+// GPU, the host through mapped memory, or an earlier kernel on another
+// stream -- reaches `target` (wrap-around compare); on timeout set
+// WL_DEV_ERR_TIMEOUT and return, so later work on the stream still runs.
+__global__ void wait_flag_kernel(const uint32_t *flag, uint32_t target, uint32_t *status) {
+    if (threadIdx.x != 0) return;
+    const uint64_t t0 = globaltimer_ns(), limit = wait_limit_ns();
+    while ((int32_t)(ld_acquire_sys(flag) - target) < 0) {
+        if (globaltimer_ns() - t0 > limit) {
+            atomicOr(status, WL_DEV_ERR_TIMEOUT);
+            return;
+        }
+    }
 }
 
 }  // namespace wl

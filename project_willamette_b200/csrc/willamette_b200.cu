@@ -141,8 +141,10 @@ int configure_kernels() {
     const void *others[] = {(const void *)i2s_gemm_kernel<64>, (const void *)i2s_gemm_kernel<128>,
                             (const void *)i2s_gemm_kernel<256>,
                             (const void *)kStream[0], (const void *)kStream[1],
-                            (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<4>,
+                            (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<2>,
+                            (const void *)q6k_lmhead_kernel<4>, (const void *)q6k_lmhead_kernel<8>,
                             (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel,
+                            (const void *)attn_exact_kernel, (const void *)rms_norm_kernel,
                             (const void *)bitnet_mega_kernel<false>,
                             (const void *)bitnet_mega_kernel<true>,
                             (const void *)i2s_gemm_ws_kernel<64>,
@@ -406,44 +408,60 @@ int q6k_launch_cfg(uint32_t n_embd, int bg, uint32_t *nst, size_t *smem) {
                 n_embd);
 }
 
-int launch_q6k(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, const float *hidden,
-               uint32_t batch, float *logits, uint32_t *ids, void *scratch, cudaStream_t s,
-               bool pdl) {
-    if (batch == 0 || vocab == 0) return WL_OK;
+// One launch for all `batch` hidden rows: groups of BG rows (the largest of
+// 8, 4, 2, 1 that the batch fills and whose hidden rows plus two weight
+// stages fit in shared memory) x vocab ranges, about one CTA per SM.
+int launch_q6k_all(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, uint32_t row_offset,
+                   const float *hidden, uint32_t batch, float *logits, uint32_t *ids,
+                   void *scratch, cudaStream_t s, bool pdl, const TpParams *tp) {
     uint32_t *status = status_ptr();
     if (!status) return WL_ERR_NO_DEVICE;
-    unsigned long long *slots = reinterpret_cast<unsigned long long *>(scratch);
-    uint32_t *counter = reinterpret_cast<uint32_t *>(slots + batch);
-    const uint32_t G = std::min<uint32_t>((uint32_t)sm_count_for_launch(), vocab);
+    int bg = batch >= 8 ? 8 : batch >= 4 ? 4 : batch >= 2 ? 2 : 1;
+    uint32_t nst = 0;
+    size_t smem = 0;
+    while (q6k_launch_cfg(n_embd, bg, &nst, &smem) != WL_OK) {
+        if (bg == 1) return WL_ERR_INVALID_ARGUMENT;  // message set by q6k_launch_cfg
+        bg /= 2;
+    }
+    const uint32_t groups = (batch + (uint32_t)bg - 1) / (uint32_t)bg;
+    const uint32_t v = std::max(vocab, 1u);
+    const uint32_t sms = (uint32_t)sm_count_for_launch();
+    const uint32_t ranges = std::min<uint32_t>(v, std::max<uint32_t>(1u, sms / groups));
     Q6kParams p = {};
     p.packed = packed;
     p.n_embd = n_embd;
     p.vocab = vocab;
     p.nb = n_embd / 256u;
     p.row_stride = q6k_row_stride(p.nb);
-    p.rows_per_cta = (vocab + G - 1) / G;
-    p.counter = counter;
+    p.rows_per_cta = (v + ranges - 1) / ranges;
+    p.n_ranges = (v + p.rows_per_cta - 1) / p.rows_per_cta;
+    p.batch = batch;
+    p.nstages = nst;
+    p.l2_keep = groups > 1 ? 1u : 0u;
+    p.hidden = hidden;
+    p.logits = logits;
+    p.ids = ids;
+    p.slots = reinterpret_cast<unsigned long long *>(scratch);
+    p.counter = reinterpret_cast<uint32_t *>(p.slots + batch);
     p.status = status;
-    const uint32_t grid = (vocab + p.rows_per_cta - 1) / p.rows_per_cta;
-    for (uint32_t b0 = 0; b0 < batch;) {
-        const int bg = (batch - b0 >= 4) ? 4 : 1;
-        uint32_t nst;
-        size_t smem;
-        int rc = q6k_launch_cfg(n_embd, bg, &nst, &smem);
-        if (rc) return rc;
-        p.nstages = nst;
-        p.hidden = hidden + (size_t)b0 * n_embd;
-        p.logits = logits ? logits + (size_t)b0 * vocab : nullptr;
-        p.ids = ids ? ids + b0 : nullptr;
-        p.slots = slots + b0;
-        if (bg == 4) {
-            WL_CUDA(launch(q6k_lmhead_kernel<4>, dim3(grid), dim3(Q6K_THREADS), smem, s, pdl, p));
-        } else {
-            WL_CUDA(launch(q6k_lmhead_kernel<1>, dim3(grid), dim3(Q6K_THREADS), smem, s, pdl, p));
-        }
-        b0 += (uint32_t)bg;
+    p.row_offset = row_offset;
+    if (tp) p.tp = *tp;
+    const dim3 grid(p.n_ranges * groups);
+    switch (bg) {
+        case 8: WL_CUDA(launch(q6k_lmhead_kernel<8>, grid, dim3(Q6K_THREADS), smem, s, pdl, p)); break;
+        case 4: WL_CUDA(launch(q6k_lmhead_kernel<4>, grid, dim3(Q6K_THREADS), smem, s, pdl, p)); break;
+        case 2: WL_CUDA(launch(q6k_lmhead_kernel<2>, grid, dim3(Q6K_THREADS), smem, s, pdl, p)); break;
+        default: WL_CUDA(launch(q6k_lmhead_kernel<1>, grid, dim3(Q6K_THREADS), smem, s, pdl, p)); break;
     }
     return WL_OK;
+}
+
+int launch_q6k(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, const float *hidden,
+               uint32_t batch, float *logits, uint32_t *ids, void *scratch, cudaStream_t s,
+               bool pdl) {
+    if (batch == 0 || vocab == 0) return WL_OK;
+    return launch_q6k_all(packed, n_embd, vocab, 0, hidden, batch, logits, ids, scratch, s, pdl,
+                          nullptr);
 }
 
 int launch_q8(const uint8_t *packed, uint32_t K, uint32_t N, const float *x, float *y,
@@ -830,31 +848,78 @@ namespace {
 
 struct NoAllocDevice {
     bool ready = false;
+    void *ctx = nullptr;         // CUDA context the address was resolved in
     uint8_t *scratch = nullptr;  // device address of g_noalloc_scratch
 };
 std::mutex g_noalloc_mu;
 NoAllocDevice g_noalloc_dev[64];
 
-// Once per device, with that device current: resolve the array's device
-// address and raise the kernels' shared-memory limit.  Allocates nothing.
-int noalloc_setup(uint8_t **scratch) {
+// The calling thread's current CUDA context (driver API through the runtime's
+// entry-point table, so the library needs no -lcuda).  A module is loaded
+// per context: after cudaDeviceReset, or in a caller that made another
+// context current, g_noalloc_scratch has a new address.
+int current_context(void **out) {
+    using GetCtx = int (*)(void **);
+    static GetCtx fn = nullptr;
+    if (!fn) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f)
+            return fail(WL_ERR_CUDA, "cuCtxGetCurrent entry point unavailable");
+        fn = reinterpret_cast<GetCtx>(f);
+    }
+    *out = nullptr;
+    if (fn(out) != 0) return fail(WL_ERR_CUDA, "cuCtxGetCurrent failed");
+    return WL_OK;
+}
+
+// Once per (device, context), with that device current: resolve the array's
+// device address and raise the kernels' shared-memory limit.  Allocates
+// nothing.  With create = false, only reports an address resolved earlier
+// in the current context (nullptr if none).
+int noalloc_setup(uint8_t **scratch, bool create = true) {
+    *scratch = nullptr;
     int dev = 0;
     WL_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(WL_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+    void *cur = nullptr;
+    int rc = current_context(&cur);
+    if (rc) return rc;
     std::lock_guard<std::mutex> g(g_noalloc_mu);
     NoAllocDevice &d = g_noalloc_dev[dev];
-    if (!d.ready) {
-        void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess)
-            return fail(WL_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) on device %d: %s",
-                        dev, cudaGetErrorString(e));
-        int rc = configure_kernels();
-        if (rc) return rc;
-        d.scratch = static_cast<uint8_t *>(p);
-        d.ready = true;
+    if (d.ready && cur && d.ctx == cur) {
+        *scratch = d.scratch;
+        return WL_OK;
     }
+    if (!create) return WL_OK;
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+        return fail(WL_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) on device %d: %s", dev,
+                    cudaGetErrorString(e));
+    if ((rc = configure_kernels())) return rc;
+    if (!cur && (rc = current_context(&cur))) return rc;  // the runtime made its context now
+    d.scratch = static_cast<uint8_t *>(p);
+    d.ctx = cur;
+    d.ready = true;
     *scratch = d.scratch;
+    return WL_OK;
+}
+
+// Read and clear the allocation-free entry point's status word on the
+// current device, if that entry point has run there in this context.
+int noalloc_take_status(uint32_t *flags) {
+    *flags = 0;
+    uint8_t *scratch = nullptr;
+    int rc = noalloc_setup(&scratch, false);
+    if (rc || !scratch) return rc;
+    WL_CUDA(cudaDeviceSynchronize());
+    WL_CUDA(cudaMemcpyFromSymbol(flags, g_noalloc_scratch, 4, 4));
+    if (*flags) {
+        const uint32_t zero = 0;
+        WL_CUDA(cudaMemcpyToSymbol(g_noalloc_scratch, &zero, 4, 4));
+    }
     return WL_OK;
 }
 
@@ -1204,43 +1269,9 @@ int check_sym_range(wl_tp_group *g, const float *y, size_t n_floats) {
 int launch_q6k_tp(const uint8_t *packed, uint32_t n_embd, uint32_t vocab, uint32_t row_offset,
                   const float *hidden, uint32_t batch, uint32_t *ids, void *scratch,
                   cudaStream_t s, const TpParams *tp) {
-    uint32_t *status = status_ptr();
-    if (!status) return WL_ERR_NO_DEVICE;
-    unsigned long long *slots = reinterpret_cast<unsigned long long *>(scratch);
-    uint32_t *counter = reinterpret_cast<uint32_t *>(slots + batch);
-    const uint32_t v = std::max(vocab, 1u);
-    const uint32_t G = std::min<uint32_t>((uint32_t)sm_count_for_launch(), v);
-    Q6kParams p = {};
-    p.packed = packed;
-    p.n_embd = n_embd;
-    p.vocab = vocab;
-    p.nb = n_embd / 256u;
-    p.row_stride = q6k_row_stride(p.nb);
-    p.rows_per_cta = (v + G - 1) / G;
-    p.counter = counter;
-    p.status = status;
-    p.row_offset = row_offset;
-    p.tp = *tp;
-    const uint32_t grid = (v + p.rows_per_cta - 1) / p.rows_per_cta;
-    for (uint32_t b0 = 0; b0 < batch;) {
-        const int bg = (batch - b0 >= 4) ? 4 : 1;
-        uint32_t nst;
-        size_t smem;
-        int rc = q6k_launch_cfg(n_embd, bg, &nst, &smem);
-        if (rc) return rc;
-        p.nstages = nst;
-        p.hidden = hidden + (size_t)b0 * n_embd;
-        p.logits = nullptr;
-        p.ids = ids + b0;
-        p.slots = slots + b0;
-        p.batch_off = b0;
-        if (bg == 4)
-            WL_CUDA(launch(q6k_lmhead_kernel<4>, dim3(grid), dim3(Q6K_THREADS), smem, s, true, p));
-        else
-            WL_CUDA(launch(q6k_lmhead_kernel<1>, dim3(grid), dim3(Q6K_THREADS), smem, s, true, p));
-        b0 += (uint32_t)bg;
-    }
-    return WL_OK;
+    // (an empty shard still launches, so that its rank's keys and arrival exist)
+    return launch_q6k_all(packed, n_embd, vocab, row_offset, hidden, batch, nullptr, ids, scratch,
+                          s, true, tp);
 }
 
 }  // namespace
@@ -1265,6 +1296,7 @@ struct wl_bitnet {
     uint32_t ids_cap = 0;
     uint32_t splits = 1;                   // attention CTAs per head (per-op path)
     bool gqa_attn = false;                 // fast mode: attn_gqa_batch_kernel (KV head x split CTAs)
+    bool exact_attn = false;               // exact mode: attn_exact_kernel (history in shared memory)
     uint32_t attn_chunk = 0;               // its positions per CTA
     float *attn_partial = nullptr;
     uint32_t *attn_counters = nullptr;
@@ -1512,8 +1544,9 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
     ep.step = m->d_step;
     WL_CUDA(launch(embed_q6k_kernel, dim3(nb), dim3(256), 0, s, true, ep));
     const uint32_t group = c.n_heads / c.n_kv_heads;
-    const size_t attn_smem = m->gqa_attn ? attn_gqa_smem_bytes(KV, c.head_dim, group, m->attn_chunk)
-                                         : attn_smem_bytes(KV, c.head_dim, c.max_seq, m->splits);
+    const size_t attn_smem = m->gqa_attn     ? attn_gqa_smem_bytes(KV, c.head_dim, group, m->attn_chunk)
+                             : m->exact_attn ? attn_exact_smem_bytes(KV, c.head_dim, c.max_seq)
+                                             : attn_smem_bytes(KV, c.head_dim, c.max_seq, m->splits);
     const float scale = 1.0f / sqrtf((float)c.head_dim);  // attention_scale, primitives.rs:354
     int rc;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
@@ -1552,6 +1585,10 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
             ap.chunk = m->attn_chunk;
             WL_CUDA(launch(gqa_attn_kernel(c.head_dim, group), dim3(c.n_kv_heads, 1, m->splits),
                            dim3(AB_THREADS), attn_smem, s, true, ap));
+        } else if (m->exact_attn) {
+            ap.pos_stable = 1u;  // the position advances only at the end of a step
+            WL_CUDA(launch(attn_exact_kernel, dim3(c.n_heads, 1, 1), dim3(AX_THREADS), attn_smem, s,
+                           true, ap));
         } else {
             WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits), dim3(ATTN_THREADS),
                            attn_smem, s, true, ap));
@@ -1705,9 +1742,24 @@ int wl_release_weights(void) {
 }
 
 int wl_device_status(uint32_t *flags) {
+    // The allocation-free entry point keeps its status word in its static
+    // array, on the caller's current device: read it first (no allocation),
+    // and without initialising the library if only that entry point has run.
+    uint32_t na = 0;
+    int rc = noalloc_take_status(&na);
+    if (rc) return rc;
     Ctx &c = ctx();
     std::lock_guard<std::mutex> g(c.mu);
-    int rc = ensure_init(c);
+    bool noalloc_used = false;
+    {
+        uint8_t *scratch = nullptr;
+        noalloc_used = noalloc_setup(&scratch, false) == WL_OK && scratch != nullptr;
+    }
+    if (!c.inited && noalloc_used) {
+        if (flags) *flags = na;
+        return WL_OK;
+    }
+    rc = ensure_init(c);
     if (rc) return rc;
     uint32_t f = 0;
     // Kernels of every stream (library and caller streams) must have finished.
@@ -1715,7 +1767,30 @@ int wl_device_status(uint32_t *flags) {
     WL_CUDA(cudaMemcpy(&f, c.d_status, 4, cudaMemcpyDeviceToHost));
     WL_CUDA(cudaMemset(c.d_status, 0, 4));
     WL_CUDA(cudaDeviceSynchronize());
-    if (flags) *flags = f;
+    if (flags) *flags = f | na;
+    return WL_OK;
+}
+
+int wl_set_wait_limit_ns(uint64_t ns) {
+    if (ns < 1000ull || ns > 600000000000ull)
+        return fail(WL_ERR_INVALID_ARGUMENT, "wait limit %llu ns outside [1 us, 600 s]",
+                    (unsigned long long)ns);
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+        return fail(WL_ERR_NO_DEVICE, "no CUDA device visible");
+    WL_CUDA(cudaDeviceSynchronize());  // no kernel reads the old value mid-wait
+    WL_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)));
+    return WL_OK;
+}
+
+int wl_dev_wait_flag(const uint32_t *flag, uint32_t target, void *stream) {
+    if (!flag) return fail(WL_ERR_INVALID_ARGUMENT, "NULL flag");
+    if (reinterpret_cast<uintptr_t>(flag) & 3u)
+        return fail(WL_ERR_INVALID_ARGUMENT, "flag not 4-byte aligned");
+    uint32_t *status = status_ptr();
+    if (!status) return WL_ERR_NO_DEVICE;
+    wait_flag_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flag, target, status);
+    WL_CUDA(cudaGetLastError());
     return WL_OK;
 }
 
@@ -1842,6 +1917,21 @@ int wl_lm_head_greedy(const float *hidden, size_t batch, const wl_tensor_view *t
     }
     return rows_host_call(token_embd, embedding_length, vocab_size, row_bytes, hidden, batch,
                           logits, token_ids);
+}
+
+int wl_dev_rms_norm_f32(const float *x, const float *w, uint32_t n, float eps, float *out,
+                        void *stream) {
+    if (n == 0) return WL_OK;
+    if (n % 4 != 0 || n > WL_RMS_NORM_MAX_N)
+        return fail(WL_ERR_INVALID_ARGUMENT, "rms_norm: n %u must be a multiple of 4 <= %u", n,
+                    WL_RMS_NORM_MAX_N);
+    if (!x || !w || !out) return fail(WL_ERR_INVALID_ARGUMENT, "NULL pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(out))
+        return fail(WL_ERR_INVALID_ARGUMENT, "x / w / out not 16-byte aligned");
+    if (!status_ptr()) return WL_ERR_NO_DEVICE;
+    WL_CUDA(launch(rms_norm_kernel, dim3(1), dim3(256), (size_t)n * 4u, (cudaStream_t)stream, true,
+                   x, w, n, eps, out));
+    return WL_OK;
 }
 
 int wl_dev_quantize_absmax_i8(const float *x, uint32_t n, uint32_t m, int8_t *q, float *act_scale,
@@ -2444,6 +2534,9 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
             }
         }
     }
+    // exact mode: the whole history of a head in shared memory, when it fits
+    m->exact_attn = c.exact && attn_exact_smem_bytes(KV, c.head_dim, c.max_seq) <=
+                                   (size_t)WL_MAX_DYN_SMEM;
     m->mega_grid = (uint32_t)cx.sm_count;
     m->mega_splits = c.exact ? 1u : std::max<uint32_t>(1u, m->mega_grid / c.n_heads);
     BN_ALLOC(m->attn_partial, (size_t)c.n_heads * std::max(m->splits, m->mega_splits) *
@@ -2690,6 +2783,7 @@ struct wl_llama_batch {
     float *attn_partial = nullptr;
     uint32_t splits = 1, ids_cap_steps = 0;
     bool gqa_attn = false;                    // attn_gqa_batch_kernel (fast mode) or attn_decode_kernel
+    bool exact_attn = false;                  // exact mode: attn_exact_kernel
     uint32_t attn_chunk = 0;                  // positions per attention CTA (gqa kernel)
     uint32_t fixed_tg = 0;                    // tokens per CTA of the linears, 0: chosen per launch
     std::vector<uint32_t> pos;                // host mirror of every position
@@ -2811,7 +2905,8 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
     WL_CUDA(launch(embed_q8_batch_kernel, dim3(S), dim3(256), 0, s, true, ep));
     const size_t attn_smem = m->gqa_attn ? attn_gqa_smem_bytes(KV, HD, c.n_heads / c.n_kv_heads,
                                                                m->attn_chunk)
-                                         : attn_smem_bytes(KV, HD, c.max_seq, m->splits);
+                             : m->exact_attn ? attn_exact_smem_bytes(KV, HD, c.max_seq)
+                                             : attn_smem_bytes(KV, HD, c.max_seq, m->splits);
     const float scale = 1.0f / sqrtf((float)HD);  // attention_scale (primitives.rs:354-357)
     int rc;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
@@ -2855,6 +2950,11 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
         if (m->gqa_attn) {
             WL_CUDA(launch(gqa_attn_kernel(HD, c.n_heads / c.n_kv_heads), dim3(c.n_kv_heads, S, m->splits),
                            dim3(AB_THREADS), attn_smem, s, true, ap));
+        } else if (m->exact_attn) {
+            // the positions were latched by this step's embedding kernel:
+            // the history is staged after the dependency wait (pos_stable 0)
+            WL_CUDA(launch(attn_exact_kernel, dim3(c.n_heads, 1, S), dim3(AX_THREADS), attn_smem, s,
+                           true, ap));
         } else {
             WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits, S), dim3(ATTN_THREADS),
                            attn_smem, s, true, ap));
@@ -2999,6 +3099,8 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
             m->splits = (c.max_seq + chunk - 1) / chunk;
         }
     }
+    m->exact_attn = c.exact && attn_exact_smem_bytes(KV, c.head_dim, c.max_seq) <=
+                                   (size_t)WL_MAX_DYN_SMEM;
     if (!c.exact && !m->gqa_attn)
         m->splits = std::max<uint32_t>(1u, std::min<uint32_t>(
                                                (c.max_seq + 63) / 64,

@@ -2,17 +2,25 @@
 // copies (TMA engine, global -> this CTA's shared memory), programmatic
 // dependent launch, and bounded waits.
 //
-// Every wait in this library is bounded by WL_WAIT_LIMIT_NS of %globaltimer;
-// a wait that runs out returns false and the caller records
-// WL_DEV_ERR_TIMEOUT in the library's device status word instead of hanging.
+// Every wait in this library is bounded by g_wait_limit_ns of %globaltimer
+// (2 s unless wl_set_wait_limit_ns changed it on this device); a wait that
+// runs out returns false and the caller records WL_DEV_ERR_TIMEOUT in the
+// library's device status word instead of hanging.
 #pragma once
 
 #include <cstdint>
 
 namespace wl {
 
-constexpr uint64_t WL_WAIT_LIMIT_NS = 2000000000ull;  // 2 s
+constexpr uint64_t WL_WAIT_LIMIT_DEFAULT_NS = 2000000000ull;  // 2 s
 constexpr uint32_t WL_DEV_ERR_TIMEOUT = 1u;
+
+// The limit of every bounded wait, one copy per device (set from the host by
+// wl_set_wait_limit_ns).  Read once when a wait starts to spin.
+__device__ uint64_t g_wait_limit_ns = WL_WAIT_LIMIT_DEFAULT_NS;
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+    return *reinterpret_cast<volatile const uint64_t *>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -59,9 +67,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Wait for the phase with the given parity to complete; false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const uint64_t t0 = globaltimer_ns(), limit = wait_limit_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > WL_WAIT_LIMIT_NS) return false;
+        if (globaltimer_ns() - t0 > limit) return false;
     }
     return true;
 }
@@ -110,10 +118,44 @@ __device__ __forceinline__ uint4 lds128(const void *p) {
     return v;
 }
 
+// t[0] + t[1] + ... + t[n-1] added in that order from +0, one rounding per
+// add (the reference's sequential loops, bit for bit), with the loads of the
+// next 32 elements issued ahead of the dependent adds so that the loop runs
+// at the add's latency (about 4 cycles per element).  t 16-byte aligned.
+__device__ __forceinline__ float seq_sum(const float *t, uint32_t n) {
+    float s = 0.0f;
+    const uint32_t n4 = (n & ~31u) / 4u;
+    const float4 *t4 = reinterpret_cast<const float4 *>(t);
+    if (n4) {
+        float4 nxt[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) nxt[j] = t4[j];
+        for (uint32_t i = 0; i < n4; i += 8) {
+            float4 cur[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            if (i + 8 < n4) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) nxt[j] = t4[i + 8 + j];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                s = __fadd_rn(s, cur[j].x);
+                s = __fadd_rn(s, cur[j].y);
+                s = __fadd_rn(s, cur[j].z);
+                s = __fadd_rn(s, cur[j].w);
+            }
+        }
+    }
+    for (uint32_t i = n4 * 4u; i < n; ++i) s = __fadd_rn(s, t[i]);
+    return s;
+}
+
 // Sum of x[i] * x[i] for i = 0, 1, ..., n - 1 in that order, one rounding per
 // product and per add (the reference's sequential RMSNorm loop, bit for bit),
-// with the loads and products of the next 32 elements issued ahead of the
-// dependent adds, so the loop runs at the add's latency.  x 16-byte aligned.
+// by one thread.  A CTA that can spare the threads squares the elements in
+// parallel first and calls seq_sum (a multiply in the dependent loop costs
+// about twice the add's latency per element).  x 16-byte aligned.
 __device__ __forceinline__ float seq_sum_sq(const float *x, uint32_t n) {
     float t = 0.0f;
     const uint32_t n4 = (n & ~31u) / 4u;  // float4s in whole groups of 32 elements
@@ -178,6 +220,18 @@ __device__ __forceinline__ float2 f2_mul_rn(float2 a, float2 b) {
         "mov.b64 {%0, %1}, d;}"
         : "=f"(d.x), "=f"(d.y)
         : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 f2_fma_rn(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{.reg .b64 a, b, c, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 d, a, b, c;\n\t"
+        "mov.b64 {%0, %1}, d;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
     return d;
 }
 __device__ __forceinline__ float2 f2_add_rn(float2 a, float2 b) {

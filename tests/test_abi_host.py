@@ -187,3 +187,14 @@ def test_tensor_view_struct_cached_and_invalidated():
     assert v4 is not v3 and v4.data_len == 512
     t2 = pickle.loads(pickle.dumps(t))
     assert "_cview" not in t2.__dict__ and list(t2.shape) == [256, 8]
+
+
+def test_wait_limit_and_flag_wait_validation():
+    """wl_set_wait_limit_ns rejects limits outside [1 us, 600 s] and
+    wl_dev_wait_flag a NULL or misaligned flag, before touching a device."""
+    L = lib()
+    for bad in (0, 999, 600_000_000_001):
+        assert L.wl_set_wait_limit_ns(bad) == WLStatus.INVALID_ARGUMENT
+        assert b"wait limit" in L.wl_last_error()
+    assert L.wl_dev_wait_flag(None, 1, None) == WLStatus.INVALID_ARGUMENT
+    assert L.wl_dev_wait_flag(2, 1, None) == WLStatus.INVALID_ARGUMENT

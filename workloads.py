@@ -1,10 +1,11 @@
 """Named single workloads at the benchmark's shapes, for profiling one
 kernel family without the rest of ``bench.py``:
 
-    python -m project_willamette_b200.workloads smollm_decode
-    python -m project_willamette_b200.workloads bitnet_decode
-    python -m project_willamette_b200.workloads lm_head
-    python -m project_willamette_b200.workloads gemm_small
+    python workloads.py smollm_decode
+    python workloads.py bitnet_decode
+    python workloads.py bitnet_decode_exact
+    python workloads.py lm_head
+    python workloads.py gemm_small
 
 Each sets its model up (seeded as in ``bench.py``), prefills, and then runs
 two decode steps inside a CUDA profiler range (``cudaProfilerStart`` /
@@ -17,9 +18,12 @@ expanded int8 weights) twice inside the range.
 """
 from __future__ import annotations
 
+import os
 import sys
 
 import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 SEED = 0x5EED + 2  # bench.py's seed base
 
@@ -36,8 +40,8 @@ def _profiled(fn):
 def smollm_decode(steps: int = 2) -> float:
     """Benchmark config 5: 32 sequences prefilled to contexts U[64, 1024],
     then `steps` batched greedy steps (fast mode)."""
-    from . import synth
-    from .llama import LlamaBatch
+    from project_willamette_b200 import synth
+    from project_willamette_b200.llama import LlamaBatch
     m = synth.llama_q8_model(np.random.default_rng(SEED + 11))
     rng = np.random.default_rng(SEED + 12)
     ctx = rng.integers(64, 1025, 32)
@@ -49,14 +53,15 @@ def smollm_decode(steps: int = 2) -> float:
     return ms
 
 
-def bitnet_decode(steps: int = 2) -> float:
+def bitnet_decode(steps: int = 2, exact: bool = False) -> float:
     """Benchmark config 2: BitNet-2B shapes, 512-token prompt, then `steps`
-    greedy steps (fast mode, per-operation engine)."""
-    from . import synth
-    from .bitnet import BitNet
+    greedy steps (per-operation engine; fast mode, or exact mode with the
+    reference's sequential sums)."""
+    from project_willamette_b200 import synth
+    from project_willamette_b200.bitnet import BitNet
     m = synth.bitnet_model(np.random.default_rng(SEED + 7), max_seq=512 + 128)
     prompt = np.random.default_rng(SEED + 8).integers(0, m["config"]["vocab"], 512)
-    g = BitNet(m)
+    g = BitNet(m, exact=exact)
     g.prefill(prompt)
     _, ms = _profiled(lambda: g.decode(steps, timed=True))
     g.close()
@@ -68,8 +73,8 @@ def lm_head(calls: int = 2) -> float:
     `calls` batch-1 calls and one batch-4 call, device entry points on
     device buffers.  Returns the batch-1 ms per call."""
     import torch
-    from . import synth
-    from ._abi import lib
+    from project_willamette_b200 import synth
+    from project_willamette_b200._abi import lib
     L = lib()
     d_model, vocab = 2560, 128256
     dev = torch.device("cuda:0")
@@ -109,8 +114,8 @@ def gemm_small(calls: int = 2) -> float:
     """Benchmark config 3, M = 128 x (K 6912 -> N 2560): device entry points on
     device buffers.  Returns ms per call."""
     import torch
-    from . import synth
-    from ._abi import lib
+    from project_willamette_b200 import synth
+    from project_willamette_b200._abi import lib
     L = lib()
     M, K, N = 128, 6912, 2560
     dev = torch.device("cuda:0")
@@ -144,11 +149,17 @@ def gemm_small(calls: int = 2) -> float:
     return _profiled(run)
 
 
+def bitnet_decode_exact(steps: int = 2) -> float:
+    """`bitnet_decode` in exact mode."""
+    return bitnet_decode(steps, exact=True)
+
+
 WORKLOADS = {"smollm_decode": smollm_decode, "bitnet_decode": bitnet_decode,
+             "bitnet_decode_exact": bitnet_decode_exact,
              "lm_head": lm_head, "gemm_small": gemm_small}
 
 if __name__ == "__main__":
     name = sys.argv[1] if len(sys.argv) > 1 else ""
     if name not in WORKLOADS:
-        sys.exit(f"usage: python -m project_willamette_b200.workloads {{{','.join(WORKLOADS)}}}")
+        sys.exit(f"usage: python workloads.py {{{','.join(WORKLOADS)}}}")
     print(f"{name}: {WORKLOADS[name]():.3f} ms")
