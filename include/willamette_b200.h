@@ -139,6 +139,31 @@ int wl_bitlinear_i2s_matvec_f32_dbg(const wl_tensor_view *weight, const float *i
                                     size_t input_len, float *output, size_t output_len,
                                     int32_t *acc_out, float *act_scale_out, int8_t *act_q_out);
 
+/* The reference's dispatch choice (src/model/dispatch.rs:47-71 Kernel) for
+ * bitlinear_i2s_matvec_f32 (bitlinear.rs:67-142), for a caller whose host or
+ * build does not take the x86 default:
+ *   WL_I2S_KERNEL_SCALAR      Kernel::Scalar -> bitlinear_i2s_matvec_f32_scalar
+ *                             (bitlinear.rs:146-242)
+ *   WL_I2S_KERNEL_NEON        Kernel::AArch64Neon: no GPU arm, returns
+ *                             WL_ERR_NOT_IMPLEMENTED (keep the CPU kernel)
+ *   WL_I2S_KERNEL_SSE2_I8     Kernel::X86Sse2, the default build: same as
+ *                             wl_bitlinear_i2s_matvec_f32
+ *   WL_I2S_KERNEL_SCALAR_LUT  Kernel::X86Sse2ScalarLut -> bitlinear_i2s_matvec_f32_lut_scalar
+ *                             (bitlinear_lut.rs:59-131)
+ *   WL_I2S_KERNEL_SSE2_F32    Kernel::X86Sse2 in a --cfg willamette_sse2_f32 build ->
+ *                             bitlinear_i2s_matvec_f32_sse2 (bitlinear_sse2.rs:89-124)
+ * The f32-activation kernels reproduce that kernel's f32 summation order bit
+ * for bit (results differ from the int8 default's); validation as that
+ * kernel (scalar and LUT want data_len == in_dim/4 * out_dim). */
+#define WL_I2S_KERNEL_SCALAR 0u
+#define WL_I2S_KERNEL_NEON 1u
+#define WL_I2S_KERNEL_SSE2_I8 2u
+#define WL_I2S_KERNEL_SCALAR_LUT 3u
+#define WL_I2S_KERNEL_SSE2_F32 4u
+int wl_bitlinear_i2s_matvec_f32_kernel(const wl_tensor_view *weight, const float *input,
+                                       size_t input_len, float *output, size_t output_len,
+                                       uint32_t kernel);
+
 /* Prefill over m tokens: the reference runs bitlinear_i2s_matvec_f32 once
  * per token (src/model/generate.rs:241-250, src/model/multi_forward.rs:106-110),
  * i.e. per-token absmax quantisation; here one int8 tensor-core GEMM.
@@ -178,6 +203,13 @@ int wl_lm_head_greedy(const float *hidden, size_t batch, const wl_tensor_view *t
  * All asynchronous on `stream` (a cudaStream_t; NULL = legacy default
  * stream).  Device buffers must be 16-byte aligned. */
 
+/* One of the f32-activation kernels of wl_bitlinear_i2s_matvec_f32_kernel
+ * (WL_I2S_KERNEL_SCALAR, _SSE2_F32 or _SCALAR_LUT) on device buffers:
+ * y[out_dim] from x[in_dim] and the packed weight. */
+int wl_dev_i2s_matvec_f32act(const uint8_t *packed, float w_scale, uint32_t in_dim,
+                             uint32_t out_dim, const float *x, float *y, uint32_t kernel,
+                             void *stream);
+
 /* rms_norm_f32 (src/model/primitives.rs:227-255) of one f32 vector, bit
  * for bit: mean = sum(x[i] * x[i]) / n with the sum in the reference's
  * sequential order, out = (x * (1 / sqrt(mean + eps))) * w.  The norm in
@@ -187,6 +219,14 @@ int wl_lm_head_greedy(const float *hidden, size_t batch, const wl_tensor_view *t
 #define WL_RMS_NORM_MAX_N 16384u
 int wl_dev_rms_norm_f32(const float *x, const float *w, uint32_t n, float eps, float *out,
                         void *stream);
+
+/* softmax_inplace (src/model/attention.rs:45-73) of one f32 vector, in
+ * place, bit for bit: exp is the reference's f32::exp (the C library's expf:
+ * glibc's algorithm, restated), the sum in the reference's sequential order.
+ * The attention of the decode step (exact mode) uses the same arithmetic.
+ * n at most WL_SOFTMAX_MAX_N; n == 0 does nothing. */
+#define WL_SOFTMAX_MAX_N 16384u
+int wl_dev_softmax_f32(float *x, uint32_t n, void *stream);
 
 /* Per-row absmax int8 quantisation (bitlinear_sse2.rs:285-304) of an
  * m x n f32 matrix: q (m x n int8), act_scale (m f32). */

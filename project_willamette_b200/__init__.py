@@ -193,13 +193,24 @@ def _matvec_entry():
     return _matvec_fn
 
 
-def bitlinear_i2s_matvec_f32(weight: TensorView, input, output: np.ndarray) -> None:
+def bitlinear_i2s_matvec_f32(weight: TensorView, input, output: np.ndarray,
+                             kernel: Optional[int] = None) -> None:
     """output = i2_scale * (W_ternary . input) via int8 activations
-    (bitlinear.rs:67 -> bitlinear_sse2.rs:313).  Writes ``output`` in place."""
+    (bitlinear.rs:67 -> bitlinear_sse2.rs:313).  Writes ``output`` in place.
+
+    ``kernel`` (an ``_abi.I2sKernel``) picks the kernel the reference's
+    dispatch would run instead of the x86 default: SCALAR, SCALAR_LUT and
+    SSE2_F32 are its f32-activation kernels, reproduced bit for bit; NEON
+    raises WillametteError(NOT_IMPLEMENTED)."""
     x = _f32(input)
     y = _out(output, "output")
     v, keep = _view(weight)
-    _check(_matvec_entry()(C.byref(v), x.ctypes.data, x.size, y.ctypes.data, y.size))
+    if kernel is None:
+        _check(_matvec_entry()(C.byref(v), x.ctypes.data, x.size, y.ctypes.data, y.size))
+    else:
+        _check(lib().wl_bitlinear_i2s_matvec_f32_kernel(
+            C.byref(v), x.ctypes.data_as(C.POINTER(C.c_float)), x.size,
+            y.ctypes.data_as(C.POINTER(C.c_float)), y.size, int(kernel)))
 
 
 def bitlinear_i2s_matvec_f32_dbg(weight: TensorView, input):

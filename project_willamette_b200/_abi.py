@@ -59,6 +59,15 @@ class WlI2sDevWeight(C.Structure):
 WL_I2S_NO_CODE3 = 1
 
 
+class I2sKernel(enum.IntEnum):
+    """The reference's dispatch choice (src/model/dispatch.rs:47-71 Kernel)."""
+    SCALAR = 0       # bitlinear_i2s_matvec_f32_scalar
+    NEON = 1         # aarch64: no GPU arm (WL_ERR_NOT_IMPLEMENTED)
+    SSE2_I8 = 2      # the x86 default (int8 activations)
+    SCALAR_LUT = 3   # SSE2 hosts without SSSE3
+    SSE2_F32 = 4     # x86 under --cfg willamette_sse2_f32
+
+
 class WlI2sStreamOp(C.Structure):
     _fields_ = [
         ("packed", C.c_void_p),
@@ -110,6 +119,9 @@ PROTOTYPES = {
     "wl_device_status": ([C.POINTER(_u32)], _i),
     "wl_set_wait_limit_ns": ([C.c_uint64], _i),
     "wl_dev_rms_norm_f32": ([_vp, _vp, _u32, C.c_float, _vp, _vp], _i),
+    "wl_dev_softmax_f32": ([_vp, _u32, _vp], _i),
+    "wl_bitlinear_i2s_matvec_f32_kernel": ([_tv, _fp, _sz, _fp, _sz, _u32], _i),
+    "wl_dev_i2s_matvec_f32act": ([_vp, C.c_float, _u32, _u32, _vp, _vp, _u32, _vp], _i),
     "wl_dev_wait_flag": ([_vp, _u32, _vp], _i),
     "wl_bitlinear_i2s_matvec_f32": ([_tv, _fp, _sz, _fp, _sz], _i),
     "wl_bitlinear_i2s_matvec_f32_dbg": ([_tv, _fp, _sz, _fp, _sz, C.POINTER(C.c_int32), _fp,

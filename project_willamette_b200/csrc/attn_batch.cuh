@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) attn_gqa_batch_kernel(const __g
 #pragma unroll
             for (uint32_t g = 0; g < G; ++g)
                 {
-                    const float e = isfinite(mx[g]) ? expf(scores[g * chunk_max + i] - mx[g]) : 0.0f;
+                    const float e = isfinite(mx[g]) ? exp_f32(__fsub_rn(scores[g * chunk_max + i], mx[g])) : 0.0f;
                     scores[g * chunk_max + i] = __fmul_rn(e, vsc[i]);  // the V scale folded in
                     l[g] += e;
                 }

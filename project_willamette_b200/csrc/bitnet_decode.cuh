@@ -19,13 +19,14 @@
 // host fills with the C library's powf/sinf/cosf exactly as the reference
 // computes them.  Sums (RMSNorm, attention dot products, softmax, the V
 // weighted sum) run as parallel trees instead of the reference's sequential
-// loops, and exp is evaluated in double and rounded to f32, so hidden states
+// loops (exp is glibc's expf restated, glibc_expf.cuh), so hidden states
 // agree to rounding level, not bit for bit.
 #pragma once
 
 #include <cstdint>
 
 #include "exact_sum.cuh"
+#include "glibc_expf.cuh"
 #include "q6k_lmhead.cuh"
 #include "tp.cuh"
 #include "wl_ptx.cuh"
@@ -96,6 +97,35 @@ __global__ void __launch_bounds__(256) embed_q6k_kernel(const __grid_constant__ 
         p.ids[*p.step] = tok;
         *p.step += 1u;
     }
+}
+
+// softmax_inplace (attention.rs:45-73) of one vector by one CTA: the maximum
+// (any order gives the strict-'>' scan's value), exp(v - max) with glibc's
+// expf, the sequential sum's bits, then v * (1 / sum); a non-finite maximum
+// gives zeros, a sum that is not positive leaves the exponentials.  Dynamic
+// shared memory: n floats.
+__global__ void __launch_bounds__(512) softmax_kernel(float *__restrict__ x, uint32_t n) {
+    extern __shared__ __align__(16) float e[];
+    __shared__ float red[32];
+    __shared__ ExactSumSmem exs;
+    pdl_launch_dependents();
+    pdl_wait();
+    float m = -INFINITY;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        e[i] = x[i];
+        m = fmaxf(m, e[i]);
+    }
+    const float mx = block_max(m, red);
+    if (!isfinite(mx)) {
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = 0.0f;
+        return;
+    }
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) e[i] = glibc_expf(__fsub_rn(e[i], mx));
+    __syncthreads();
+    const float sum = block_exact_sum_nonneg(e, n, exs);
+    const bool norm = sum > 0.0f;
+    const float inv = norm ? __fdiv_rn(1.0f, sum) : 1.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = norm ? __fmul_rn(e[i], inv) : e[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -234,9 +264,8 @@ __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, in
     if (threadIdx.x == 0) *scale_out = zero ? 0.0f : __fdiv_rn(absmax, 127.0f);
 }
 
-__device__ __forceinline__ float exp_f32(float x) {
-    return (float)exp((double)x);  // exp rounded once to f32
-}
+// f32::exp of the reference: glibc's expf, restated bit for bit.
+__device__ __forceinline__ float exp_f32(float x) { return glibc_expf(x); }
 
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_constant__ AttnParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -521,7 +550,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
 // Exact-mode attention, one CTA per (query head, sequence): the reference's
 // scaled_dot_product_attention_into (cached_forward.rs:417-449) with
 // softmax_inplace (attention.rs:45-73) in its sequential order, bit for bit
-// except exp (a double exp rounded once).  The head's whole K and V history
+// (exp is glibc's expf, restated in glibc_expf.cuh).  The head's whole K and V history
 // (int8 rows and scales) is copied into shared memory with cp.async --
 // before the programmatic-dependency wait when the position is not written
 // by the kernels just before this one -- so the three sequential sums

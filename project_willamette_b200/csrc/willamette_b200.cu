@@ -20,6 +20,7 @@
 #include "argmax.cuh"
 #include "bitnet_decode.cuh"
 #include "bitnet_mega.cuh"
+#include "i2s_f32act.cuh"
 #include "i2s_matvec.cuh"
 #include "i2s_stream.cuh"
 #include "i2s_gemm.cuh"
@@ -129,6 +130,16 @@ const I2sKernel kI2s[3][2][2] = {
 };
 const I2sStreamKernel kStream[2] = {i2s_stream_kernel<false>, i2s_stream_kernel<true>};
 
+// Dynamic shared memory a kernel can get: the per-block limit (227 KB on
+// sm_100) minus its static shared memory, at most `want`.
+size_t kernel_dyn_cap(const void *k, size_t want = (size_t)WL_MAX_DYN_SMEM) {
+    cudaFuncAttributes a;
+    if (cudaFuncGetAttributes(&a, k) != cudaSuccess) return 0;
+    const size_t limit = (size_t)227 * 1024;
+    const size_t cap = a.sharedSizeBytes < limit ? limit - a.sharedSizeBytes : 0;
+    return std::min(want, cap);
+}
+
 // Raise the dynamic shared-memory limit of every kernel once, at init, so
 // launches never call cudaFuncSetAttribute (they can be captured in graphs).
 int configure_kernels() {
@@ -145,6 +156,7 @@ int configure_kernels() {
                             (const void *)q6k_lmhead_kernel<4>, (const void *)q6k_lmhead_kernel<8>,
                             (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel,
                             (const void *)attn_exact_kernel, (const void *)rms_norm_kernel,
+                            (const void *)softmax_kernel,
                             (const void *)bitnet_mega_kernel<false>,
                             (const void *)bitnet_mega_kernel<true>,
                             (const void *)i2s_gemm_ws_kernel<64>,
@@ -168,7 +180,7 @@ int configure_kernels() {
                             (const void *)attn_gqa_batch_kernel<128, 4>};
     for (const void *k : others)
         WL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     WL_MAX_DYN_SMEM));
+                                     (int)kernel_dyn_cap(k)));
     return WL_OK;
 }
 
@@ -748,6 +760,71 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
     if (acc_out) memcpy(acc_out, pacc, yout);
     if (act_q_out) memcpy(act_q_out, pq, m * (size_t)K);
     if (act_scale_out) memcpy(act_scale_out, ps, m * 4);
+    return WL_OK;
+}
+
+// The reference's f32-activation kernels (scalar, SSE2 f32, scalar LUT).
+int launch_i2s_f32act(const uint8_t *packed, float w_scale, uint32_t K, uint32_t N,
+                      const float *x, float *y, uint32_t kernel, cudaStream_t s, bool pdl) {
+    if (N == 0) return WL_OK;
+    const dim3 grid((N + I2S_F32ACT_THREADS - 1) / I2S_F32ACT_THREADS), block(I2S_F32ACT_THREADS);
+    switch (kernel) {
+        case I2S_KERNEL_SCALAR:
+            WL_CUDA(launch(i2s_f32act_kernel<I2S_KERNEL_SCALAR>, grid, block, 0, s, pdl, packed,
+                           w_scale, K, N, x, y));
+            break;
+        case I2S_KERNEL_SSE2_F32:
+            WL_CUDA(launch(i2s_f32act_kernel<I2S_KERNEL_SSE2_F32>, grid, block, 0, s, pdl, packed,
+                           w_scale, K, N, x, y));
+            break;
+        case I2S_KERNEL_SCALAR_LUT:
+            WL_CUDA(launch(i2s_f32act_kernel<I2S_KERNEL_SCALAR_LUT>, grid, block, 0, s, pdl,
+                           packed, w_scale, K, N, x, y));
+            break;
+        default:
+            return fail(WL_ERR_INVALID_ARGUMENT, "unknown I2_S kernel %u", kernel);
+    }
+    return WL_OK;
+}
+
+// Host-buffer call of an f32-activation kernel: validation as that kernel
+// (the scalar and LUT kernels want the packed length exactly, bitlinear.rs:192,
+// bitlinear_lut.rs:174; the SSE2 kernels accept longer data), cached upload,
+// one kernel, y and the status word back in one copy.
+int i2s_f32act_host_call(const wl_tensor_view *weight, const float *input, size_t input_len,
+                         float *output, size_t output_len, uint32_t kernel) {
+    uint32_t K = 0, N = 0;
+    float w_scale = 0.f;
+    int rc = validate_i2s(weight, input_len, output_len, true, &K, &N, &w_scale);
+    if (rc) return rc;
+    const uint64_t expected = (uint64_t)K / 4 * N;
+    if (kernel != I2S_KERNEL_SSE2_F32 && weight->data_len != expected)
+        return fail(WL_ERR_GGUF_PARSE,
+                    "bitlinear_i2s_matvec_f32: weight \"%s\" data.len()=%zu != expected packed "
+                    "%llu (= in_dim/4 x out_dim)",
+                    tname(weight), weight->data_len, (unsigned long long)expected);
+    if (N == 0) return WL_OK;
+    if (!input || !output) return fail(WL_ERR_INVALID_ARGUMENT, "input/output is NULL");
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> g(c.mu);
+    if ((rc = ensure_init(c))) return rc;
+    CachedWeight *cw = nullptr;
+    if ((rc = get_weight(c, weight, K, N, (size_t)K / 4 * N, &cw))) return rc;
+    const size_t xin = (size_t)K * 4, yout = (size_t)N * 4;
+    if ((rc = grow(c.x, xin)) || (rc = grow(c.ys, yout + 16)) ||
+        (rc = grow_pinned(c, xin + yout + 64)))
+        return rc;
+    uint8_t *pin = (uint8_t *)c.pinned;
+    memcpy(pin, input, xin);
+    WL_CUDA(cudaMemcpyAsync(c.x.p, pin, xin, cudaMemcpyHostToDevice, c.stream));
+    if ((rc = launch_i2s_f32act((const uint8_t *)cw->dptr, w_scale, K, N, (const float *)c.x.p,
+                                (float *)((uint8_t *)c.ys.p + 16), kernel, c.stream, false)))
+        return rc;
+    uint8_t *pys = pin + xin;  // [status][y]
+    WL_CUDA(cudaMemcpyAsync(pys, c.ys.p, yout + 16, cudaMemcpyDeviceToHost, c.stream));
+    cudaError_t e = cudaStreamSynchronize(c.stream);
+    if (e != cudaSuccess) return fail(WL_ERR_CUDA, "kernel execution: %s", cudaGetErrorString(e));
+    memcpy(output, pys + 16, yout);
     return WL_OK;
 }
 
@@ -1807,6 +1884,45 @@ int wl_bitlinear_i2s_matvec_f32_dbg(const wl_tensor_view *weight, const float *i
                          act_q_out);
 }
 
+int wl_bitlinear_i2s_matvec_f32_kernel(const wl_tensor_view *weight, const float *input,
+                                       size_t input_len, float *output, size_t output_len,
+                                       uint32_t kernel) {
+    switch (kernel) {
+        case WL_I2S_KERNEL_SSE2_I8:
+            return i2s_host_call(weight, input, input_len, output, output_len, 1, nullptr,
+                                 nullptr, nullptr);
+        case WL_I2S_KERNEL_SCALAR:
+        case WL_I2S_KERNEL_SSE2_F32:
+        case WL_I2S_KERNEL_SCALAR_LUT:
+            return i2s_f32act_host_call(weight, input, input_len, output, output_len, kernel);
+        case WL_I2S_KERNEL_NEON:
+            return fail(WL_ERR_NOT_IMPLEMENTED,
+                        "bitlinear_i2s_matvec_f32: the aarch64 NEON kernel has no GPU arm; keep "
+                        "the CPU kernel");
+        default:
+            return fail(WL_ERR_INVALID_ARGUMENT, "unknown I2_S kernel %u", kernel);
+    }
+}
+
+int wl_dev_i2s_matvec_f32act(const uint8_t *packed, float w_scale, uint32_t in_dim,
+                             uint32_t out_dim, const float *x, float *y, uint32_t kernel,
+                             void *stream) {
+    if (in_dim == 0 || in_dim % 128)
+        return fail(WL_ERR_GGUF_PARSE, "in_dim %u is not a positive multiple of 128", in_dim);
+    if (!std::isfinite(w_scale))
+        return fail(WL_ERR_GGUF_PARSE, "i2s_scale: non-finite scale (%g)", w_scale);
+    if (kernel != WL_I2S_KERNEL_SCALAR && kernel != WL_I2S_KERNEL_SSE2_F32 &&
+        kernel != WL_I2S_KERNEL_SCALAR_LUT)
+        return fail(WL_ERR_INVALID_ARGUMENT, "kernel %u is not an f32-activation kernel", kernel);
+    if (out_dim == 0) return WL_OK;
+    if (!packed || !x || !y) return fail(WL_ERR_INVALID_ARGUMENT, "NULL pointer");
+    if (!aligned16(packed) || !aligned16(x))
+        return fail(WL_ERR_INVALID_ARGUMENT, "packed / x not 16-byte aligned");
+    if (!status_ptr()) return WL_ERR_NO_DEVICE;
+    return launch_i2s_f32act(packed, w_scale, in_dim, out_dim, x, y, kernel, (cudaStream_t)stream,
+                             true);
+}
+
 int wl_bitlinear_i2s_gemm_f32(const wl_tensor_view *weight, const float *input, size_t m,
                               float *output, int32_t *acc_out) {
     return i2s_host_call(weight, input, 0, output, 0, m, acc_out, nullptr, nullptr);
@@ -1931,6 +2047,18 @@ int wl_dev_rms_norm_f32(const float *x, const float *w, uint32_t n, float eps, f
     if (!status_ptr()) return WL_ERR_NO_DEVICE;
     WL_CUDA(launch(rms_norm_kernel, dim3(1), dim3(256), (size_t)n * 4u, (cudaStream_t)stream, true,
                    x, w, n, eps, out));
+    return WL_OK;
+}
+
+int wl_dev_softmax_f32(float *x, uint32_t n, void *stream) {
+    if (n == 0) return WL_OK;
+    if (n > WL_SOFTMAX_MAX_N)
+        return fail(WL_ERR_INVALID_ARGUMENT, "softmax: n %u exceeds %u", n, WL_SOFTMAX_MAX_N);
+    if (!x) return fail(WL_ERR_INVALID_ARGUMENT, "NULL pointer");
+    if (!aligned16(x)) return fail(WL_ERR_INVALID_ARGUMENT, "x not 16-byte aligned");
+    if (!status_ptr()) return WL_ERR_NO_DEVICE;
+    WL_CUDA(launch(softmax_kernel, dim3(1), dim3(512), (size_t)((n + 3u) & ~3u) * 4u,
+                   (cudaStream_t)stream, true, x, n));
     return WL_OK;
 }
 
@@ -2536,7 +2664,7 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
     }
     // exact mode: the whole history of a head in shared memory, when it fits
     m->exact_attn = c.exact && attn_exact_smem_bytes(KV, c.head_dim, c.max_seq) <=
-                                   (size_t)WL_MAX_DYN_SMEM;
+                                   kernel_dyn_cap((const void *)attn_exact_kernel);
     m->mega_grid = (uint32_t)cx.sm_count;
     m->mega_splits = c.exact ? 1u : std::max<uint32_t>(1u, m->mega_grid / c.n_heads);
     BN_ALLOC(m->attn_partial, (size_t)c.n_heads * std::max(m->splits, m->mega_splits) *
@@ -3100,7 +3228,7 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
         }
     }
     m->exact_attn = c.exact && attn_exact_smem_bytes(KV, c.head_dim, c.max_seq) <=
-                                   (size_t)WL_MAX_DYN_SMEM;
+                                   kernel_dyn_cap((const void *)attn_exact_kernel);
     if (!c.exact && !m->gqa_attn)
         m->splits = std::max<uint32_t>(1u, std::min<uint32_t>(
                                                (c.max_seq + 63) / 64,

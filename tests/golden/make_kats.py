@@ -5,7 +5,8 @@ these machines (no Rust toolchain), so its unit tests are transcribed here
 as data: each case rebuilds the exact input bytes the Rust test constructs
 and records the value or tolerance the Rust test asserts, with the
 file:line it comes from.  Both the CPU oracle (tests/test_oracle_kats.py)
-and the CUDA library (tests/test_gpu_kats.py) are checked against this file.
+and the CUDA library (the KAT cases of tests/test_gpu_parity.py) are checked
+against this file.
 
 Cases whose expected value the Rust test computes at run time from its own
 inputs (e.g. "expected = sum of the inputs") are evaluated here with the same

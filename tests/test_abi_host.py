@@ -198,3 +198,19 @@ def test_wait_limit_and_flag_wait_validation():
         assert b"wait limit" in L.wl_last_error()
     assert L.wl_dev_wait_flag(None, 1, None) == WLStatus.INVALID_ARGUMENT
     assert L.wl_dev_wait_flag(2, 1, None) == WLStatus.INVALID_ARGUMENT
+
+
+def test_f32_activation_dispatch_validation():
+    """Before any device work: the NEON choice has no GPU arm (the caller keeps
+    its CPU kernel), an unknown kernel is rejected, and the scalar and LUT
+    kernels want the packed length exactly (bitlinear.rs:192,
+    bitlinear_lut.rs:174) while the SSE2 kernels accept longer data."""
+    from project_willamette_b200._abi import I2sKernel
+    x = np.ones(128, np.float32)
+    y = np.full(1, 7.0, np.float32)
+    _expect(WLStatus.NOT_IMPLEMENTED, wl.bitlinear_i2s_matvec_f32, _i2s(), x, y, I2sKernel.NEON)
+    _expect(WLStatus.INVALID_ARGUMENT, wl.bitlinear_i2s_matvec_f32, _i2s(), x, y, 9)
+    for k in (I2sKernel.SCALAR, I2sKernel.SCALAR_LUT):
+        e = _expect(WLStatus.GGUF_PARSE, wl.bitlinear_i2s_matvec_f32, _i2s(data_len=40), x, y, k)
+        assert "expected packed" in str(e)
+    assert y[0] == 7.0

@@ -1,12 +1,12 @@
 """Device-resident BitNet decode step against the oracle of the reference's
 cached forward and greedy generation (oracle/bitnet_forward.c).
 
-Two modes.  Exact mode runs every sum in the reference's sequential order:
-hidden states must agree within EXACT_RTOL (1e-5, the north-star f32 bound;
-the only arithmetic not reproduced bit for bit is exp, rounded here from a
-double-precision exp) and greedy ids must be identical.  Fast mode (the
-benchmarked one) sums RMSNorm, softmax and the weighted V as parallel
-trees: rounding-level differences, which the int8 re-quantisation at every
+Two modes.  Exact mode is the reference's arithmetic -- its sequential sums
+(bit for bit, csrc/exact_sum.cuh) and its exp (glibc's expf, restated in
+csrc/glibc_expf.cuh): hidden states must agree within EXACT_RTOL (1e-5, the
+north-star f32 bound, stated here although the arithmetic is the
+reference's own) and greedy ids must be identical.  Fast mode sums RMSNorm,
+softmax and the weighted V as parallel trees: rounding-level differences, which the int8 re-quantisation at every
 BitLinear occasionally turns into a one-step flip of one activation (about
 1 % of a hidden vector), so it is held to greedy-id identity plus a
 rounding-level median and a flip-level maximum on small models.

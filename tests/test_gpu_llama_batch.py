@@ -2,9 +2,9 @@
 against the oracle of the reference's per-sequence greedy generation with the
 VanillaLlama forward (oracle/bitnet_forward.c, variant 1, Q8_0).
 
-Exact mode runs the reference's summation order everywhere: the Q8_0 linears
-are bit-exact, and the only arithmetic not reproduced bit for bit is exp
-(softmax and SiLU, rounded here from a double-precision exp), so hidden
+Exact mode runs the reference's arithmetic everywhere: the Q8_0 linears are
+bit-exact, the norms and softmax sum in the reference's order, and exp
+(softmax and SiLU) is glibc's expf restated (csrc/glibc_expf.cuh), so hidden
 states are held to EXACT_RTOL (the north-star f32 bound) and greedy ids must
 be identical.  Fast mode contracts the Q8_0 products into FMAs and sums norms
 and softmax as trees: rounding-level differences, which the per-token int8

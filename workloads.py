@@ -11,7 +11,7 @@ Each sets its model up (seeded as in ``bench.py``), prefills, and then runs
 two decode steps inside a CUDA profiler range (``cudaProfilerStart`` /
 ``Stop``), so ``ncu --profile-from-start off`` captures only the steady
 decode kernels.  ``lm_head`` repacks a 128256 x 2560 Q6_K matrix (config 4)
-and runs the greedy head at batch 1 (twice) and batch 4 (once) inside the
+and runs the greedy head at batch 1 (twice) and batch 64 (once) inside the
 range.  ``gemm_small`` runs the prefill GEMM of config 3's smallest case
 (M 128, K 6912, N 2560: quantisation + warp-specialised tcgen05 GEMM over
 expanded int8 weights) twice inside the range.
@@ -70,7 +70,7 @@ def bitnet_decode(steps: int = 2, exact: bool = False) -> float:
 
 def lm_head(calls: int = 2) -> float:
     """Benchmark config 4: Q6_K tied lm-head + greedy argmax, 128256 x 2560;
-    `calls` batch-1 calls and one batch-4 call, device entry points on
+    `calls` batch-1 calls and one batch-64 call, device entry points on
     device buffers.  Returns the batch-1 ms per call."""
     import torch
     from project_willamette_b200 import synth
@@ -85,9 +85,9 @@ def lm_head(calls: int = 2) -> float:
     if L.wl_dev_q6k_repack(raw.data_ptr(), d_model, vocab, packed.data_ptr(), s):
         raise RuntimeError(L.wl_last_error().decode())
     del raw
-    H = torch.randn(4, d_model, device=dev, generator=torch.Generator(dev).manual_seed(SEED))
-    ids = torch.zeros(4, dtype=torch.int32, device=dev)
-    scratch = torch.zeros(L.wl_q6k_scratch_bytes(4), dtype=torch.uint8, device=dev)
+    H = torch.randn(64, d_model, device=dev, generator=torch.Generator(dev).manual_seed(SEED))
+    ids = torch.zeros(64, dtype=torch.int32, device=dev)
+    scratch = torch.zeros(L.wl_q6k_scratch_bytes(64), dtype=torch.uint8, device=dev)
 
     def head(batch):
         if L.wl_dev_q6k_lm_head(packed.data_ptr(), d_model, vocab, H.data_ptr(), batch, None,
@@ -103,7 +103,7 @@ def lm_head(calls: int = 2) -> float:
         for _ in range(calls):
             head(1)
         b.record()
-        head(4)
+        head(64)
         torch.cuda.synchronize()
         return a.elapsed_time(b) / calls
 
