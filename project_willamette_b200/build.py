@@ -2,11 +2,16 @@
 
     python -m project_willamette_b200.build [--ptxas-verbose]
 
-Produces project_willamette_b200/_lib/libwillamette_b200.so: one nvcc
-translation unit (csrc/willamette_b200.cu includes the kernel headers),
--gencode arch=compute_100a,code=sm_100a, cudart linked statically so the
-library needs nothing beyond the driver at run time.  Cross-compiles on a
-machine without a GPU.
+Produces, from one nvcc translation unit (csrc/willamette_b200.cu includes
+the kernel headers), -gencode arch=compute_100a,code=sm_100a:
+  project_willamette_b200/_lib/libwillamette_b200.so -- cudart linked
+      statically, so it needs nothing beyond the driver at run time (the
+      Python package and the C client load it);
+  project_willamette_b200/_lib/libwillamette_b200.a -- the same object as a
+      static library, for a host program that links the C ABI into itself
+      (a Rust build.rs: link it with cudart_static, rt, pthread, dl and
+      stdc++).
+Cross-compiles on a machine without a GPU.
 """
 from __future__ import annotations
 
@@ -19,14 +24,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIBDIR, "libwillamette_b200.so")
+STATIC_LIB = os.path.join(LIBDIR, "libwillamette_b200.a")
 MAIN = os.path.join(CSRC, "willamette_b200.cu")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "willamette_b200.h")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
-    "-Xcompiler", "-fPIC", "-shared",
-    "-cudart", "static",
+    "-Xcompiler", "-fPIC",
     # IEEE division/sqrt and no FMA contraction across the explicit
     # __fmul_rn/__fadd_rn sequences the parity contract relies on.
     "-prec-div=true", "-prec-sqrt=true", "-fmad=false",
@@ -49,9 +54,9 @@ def _sources() -> list[str]:
 
 
 def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(STATIC_LIB):
         return False
-    t = os.path.getmtime(LIB)
+    t = min(os.path.getmtime(LIB), os.path.getmtime(STATIC_LIB))
     return all(os.path.getmtime(s) <= t for s in _sources())
 
 
@@ -59,12 +64,21 @@ def build(force: bool = False, ptxas_verbose: bool = False) -> str:
     if not force and not ptxas_verbose and up_to_date():
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)
-    tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, MAIN]
+    obj = os.path.join(LIBDIR, "willamette_b200.o")
+    cmd = [nvcc(), *NVCC_FLAGS, "-c", "-o", obj, MAIN]
     if ptxas_verbose:
         cmd[1:1] = ["-Xptxas", "-v"]
     subprocess.run(cmd, check=True)
+    tmp = LIB + ".tmp"
+    subprocess.run([nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart",
+                    "static", "-o", tmp, obj], check=True)
     os.replace(tmp, LIB)
+    tmp_a = STATIC_LIB + ".tmp"
+    if os.path.exists(tmp_a):
+        os.remove(tmp_a)
+    subprocess.run(["ar", "rcs", tmp_a, obj], check=True)
+    os.replace(tmp_a, STATIC_LIB)
+    os.remove(obj)
     return LIB
 
 

@@ -25,7 +25,6 @@
 
 #include <cstdint>
 
-#include "exact_sum.cuh"
 #include "glibc_expf.cuh"
 #include "q6k_lmhead.cuh"
 #include "tp.cuh"
@@ -101,13 +100,12 @@ __global__ void __launch_bounds__(256) embed_q6k_kernel(const __grid_constant__ 
 
 // softmax_inplace (attention.rs:45-73) of one vector by one CTA: the maximum
 // (any order gives the strict-'>' scan's value), exp(v - max) with glibc's
-// expf, the sequential sum's bits, then v * (1 / sum); a non-finite maximum
+// expf, the sequential sum, then v * (1 / sum); a non-finite maximum
 // gives zeros, a sum that is not positive leaves the exponentials.  Dynamic
 // shared memory: n floats.
 __global__ void __launch_bounds__(512) softmax_kernel(float *__restrict__ x, uint32_t n) {
     extern __shared__ __align__(16) float e[];
     __shared__ float red[32];
-    __shared__ ExactSumSmem exs;
     pdl_launch_dependents();
     pdl_wait();
     float m = -INFINITY;
@@ -122,7 +120,9 @@ __global__ void __launch_bounds__(512) softmax_kernel(float *__restrict__ x, uin
     }
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) e[i] = glibc_expf(__fsub_rn(e[i], mx));
     __syncthreads();
-    const float sum = block_exact_sum_nonneg(e, n, exs);
+    if (threadIdx.x == 0) red[0] = seq_sum(e, n);
+    __syncthreads();
+    const float sum = red[0];
     const bool norm = sum > 0.0f;
     const float inv = norm ? __fdiv_rn(1.0f, sum) : 1.0f;
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = norm ? __fmul_rn(e[i], inv) : e[i];
@@ -142,17 +142,19 @@ struct OutNormParams {
 
 // Exact-mode sum of squares of x[0..n) (n a multiple of 4, x 16-byte
 // aligned): the CTA stores the squares into shared memory `buf` (one round of
-// loads, one rounding per square), then adds them with the bits of the
-// reference's sequential loop (block_exact_sum_nonneg).
+// loads, one rounding per square), then one thread adds them in the
+// reference's order.
 __device__ __forceinline__ float block_seq_sum_sq(const float *x, uint32_t n, float *buf,
-                                                  ExactSumSmem &exs) {
+                                                  float *red) {
     for (uint32_t i = threadIdx.x * 4u; i < n; i += blockDim.x * 4u) {
         const float4 v = *reinterpret_cast<const float4 *>(x + i);
         *reinterpret_cast<float4 *>(buf + i) = make_float4(
             __fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w));
     }
     __syncthreads();
-    return block_exact_sum_nonneg(buf, n, exs);
+    if (threadIdx.x == 0) red[0] = seq_sum(buf, n);
+    __syncthreads();
+    return red[0];
 }
 
 // rms_norm_f32 (primitives.rs:227-255) of one vector by one CTA:
@@ -163,10 +165,10 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__
                                                         const float *__restrict__ w, uint32_t n,
                                                         float eps, float *__restrict__ out) {
     extern __shared__ __align__(16) float sq[];
-    __shared__ ExactSumSmem exs;
+    __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
-    const float sum_sq = block_seq_sum_sq(x, n, sq, exs);
+    const float sum_sq = block_seq_sum_sq(x, n, sq, red);
     const float mean = __fdiv_rn(sum_sq, (float)n);
     const float rsqrt = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], rsqrt), w[i]);
@@ -177,12 +179,11 @@ constexpr uint32_t OUT_NORM_MAX = 8192;  // shared-memory copy of the exact-mode
 __global__ void __launch_bounds__(256) out_norm_kernel(const __grid_constant__ OutNormParams p) {
     __shared__ float red[32];
     __shared__ __align__(16) float hs[OUT_NORM_MAX];
-    __shared__ ExactSumSmem exs;
     pdl_launch_dependents();
     pdl_wait();
     float sum_sq;
     if (p.exact) {
-        sum_sq = block_seq_sum_sq(p.hidden, p.n, hs, exs);
+        sum_sq = block_seq_sum_sq(p.hidden, p.n, hs, red);
     } else {
         float ss = 0.0f;
         for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x)
@@ -581,7 +582,6 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
     __shared__ float red[32];
     __shared__ float s_ks, s_vs, s_inv;
     __shared__ uint32_t s_norm;
-    __shared__ ExactSumSmem exs;
     const uint32_t HD = p.head_dim, KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
     const uint32_t h = blockIdx.x, kvh = h / p.group, tid = threadIdx.x, z = blockIdx.z;
     const uint32_t cap = ax_cap(p.max_seq);
@@ -722,8 +722,8 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
     } else {
         for (uint32_t t = tid; t < n; t += AX_THREADS) sc[t] = exp_f32(__fsub_rn(sc[t], mx));
         __syncthreads();
-        const float sum = block_exact_sum_nonneg(sc, n, exs);  // the sequential sum's bits
         if (tid == 0) {
+            const float sum = seq_sum(sc, n);  // the reference's order
             s_norm = sum > 0.0f ? 1u : 0u;
             s_inv = s_norm ? __fdiv_rn(1.0f, sum) : 1.0f;
         }

@@ -28,7 +28,6 @@
 
 #include <cstdint>
 
-#include "exact_sum.cuh"
 #include "tp.cuh"
 #include "wl_ptx.cuh"
 
@@ -289,10 +288,11 @@ __device__ __forceinline__ int32_t cta_qsum(const int32_t *ared) {
 //   I2S_PRE_RELU2_RMSNORM: rms_norm(relu(x)^2 * x2, w) (ffn.rs:37-65, then the
 //                          ffn_sub_norm of cached_forward.rs:480-494)
 // rms_norm: mean = sum(v*v) / K, rsqrt = 1 / sqrt(mean + eps), out = (v *
-// rsqrt) * w.  The sum of squares is a tree (fast mode), or with `chain`
-// set the reference's sequential loop over the input stored there (exact).
+// rsqrt) * w.  The sum of squares is a tree (fast mode), or with EXACT the
+// reference's sequential loop over the squares stored in `chain`.
 constexpr int I2S_PRE_V = (int)(I2S_FUSE_Q_MAX_K / (I2S_THREADS * 4u));  // float4 per thread
 
+template <bool EXACT>
 __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint32_t K,
                                                   const float *nw, int8_t *qs, float *red,
                                                   int32_t *ared, const float *us,
@@ -356,10 +356,10 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
     }
     if (p.pre != I2S_PRE_NONE) {
         float sum_sq;
-        if (chain) {
+        if constexpr (EXACT) {
             // exact mode: the reference's loop sum_sq += x[i] * x[i], i = 0, 1,
             // ...: the squares (one rounding each) stored in parallel, then
-            // summed with that loop's bits by the whole CTA
+            // added in order by one thread
 #pragma unroll
             for (int k = 0; k < I2S_PRE_V; ++k) {
                 if (k >= kmax) break;
@@ -370,8 +370,9 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
                                     __fmul_rn(v[k].z, v[k].z), __fmul_rn(v[k].w, v[k].w));
             }
             __syncthreads();
-            __shared__ ExactSumSmem exs;
-            sum_sq = block_exact_sum_nonneg(chain, K, exs);
+            if (tid == 0) red[0] = seq_sum(chain, K);
+            __syncthreads();
+            sum_sq = red[0];
         } else {
             float ss = 0.0f;
 #pragma unroll
@@ -479,7 +480,7 @@ __device__ __forceinline__ void i2s_issue_chunk(const I2sMatvecParams &p, uint32
 // copies there.  (Triggering at entry let them run their prologue beside this
 // op's whole pre-phase and row loop on the same SMs, which slowed this op's
 // slowest CTAs by 2-4 us: a BitNet decode token took 1631 instead of 1427 us.)
-template <int LPR, int NP, bool FUSE_Q, bool C3>
+template <int LPR, int NP, bool FUSE_Q, bool C3, bool EXACT = false>
 __global__ void __launch_bounds__(I2S_THREADS, 2)
     i2s_matvec_kernel(const __grid_constant__ I2sMatvecParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     // The RMSNorm weights do not depend on earlier kernels either.  Exact mode
     // (the reference's sequential sum of squares) keeps them after the
     // quantised input, so that xs holds the transformed input for that sum.
-    const bool exact_pre = FUSE_Q && p.pre != I2S_PRE_NONE && p.exact_norm;
+    const bool exact_pre = EXACT && FUSE_Q && p.pre != I2S_PRE_NONE;
     if constexpr (FUSE_Q) {
         if (!exact_pre && p.pre != I2S_PRE_NONE) {
             float *nw = reinterpret_cast<float *>(smem + nst * stage_bytes);
@@ -583,8 +584,11 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         asm volatile("cp.async.commit_group;" ::: "memory");
         // exact mode: RMSNorm weights at `us`, the transformed input to xs
         // for the reference's sequential sum of squares
-        act_scale = exact_pre ? cta_prepare_regs(p, K, us, qs, red, ared, nullptr, xs)
-                              : cta_prepare_regs(p, K, xs, qs, red, ared, p.stage_up ? us : nullptr);
+        if constexpr (EXACT)
+            act_scale = exact_pre ? cta_prepare_regs<true>(p, K, us, qs, red, ared, nullptr, xs)
+                                  : cta_prepare_regs<false>(p, K, xs, qs, red, ared, nullptr);
+        else
+            act_scale = cta_prepare_regs<false>(p, K, xs, qs, red, ared, p.stage_up ? us : nullptr);
         if (blockIdx.x == 0) {
             if (p.q_out)
                 for (uint32_t i = tid * 16; i < K; i += I2S_THREADS * 16)

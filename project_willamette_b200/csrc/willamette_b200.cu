@@ -117,6 +117,13 @@ int launch_i2s_expand(const uint8_t *packed, uint32_t K, uint32_t N, int8_t *out
 using I2sKernel = void (*)(I2sMatvecParams);
 using I2sStreamKernel = void (*)(I2sStreamParams);
 
+// The exact-mode decode kernels: the input transform's sum of squares with
+// the reference's sequential bits, indexed [shape][c3] (fused input only).
+const I2sKernel kI2sExact[2][2] = {
+    {i2s_matvec_kernel<8, 5, true, false, true>, i2s_matvec_kernel<8, 5, true, true, true>},
+    {i2s_matvec_kernel<32, 4, true, false, true>, i2s_matvec_kernel<32, 4, true, true, true>},
+};
+
 // Every I2_S per-op kernel variant, indexed [shape][fuse_q][c3]:
 // shape 0 = 8 lanes/row x 5 slots (in_dim <= 2560), 1 = 32 x 4 (<= 8192),
 // 2 = 32 lanes, activations re-read from L1 (larger; never fused).
@@ -149,6 +156,11 @@ int configure_kernels() {
                 WL_CUDA(cudaFuncSetAttribute((const void *)k,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              WL_MAX_DYN_SMEM / 2));
+    for (auto &a : kI2sExact)
+        for (I2sKernel k : a)
+            WL_CUDA(cudaFuncSetAttribute((const void *)k,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         WL_MAX_DYN_SMEM / 2));
     const void *others[] = {(const void *)i2s_gemm_kernel<64>, (const void *)i2s_gemm_kernel<128>,
                             (const void *)i2s_gemm_kernel<256>,
                             (const void *)kStream[0], (const void *)kStream[1],
@@ -362,7 +374,9 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     if (fuse && (shape == 2 || K > I2S_FUSE_Q_MAX_K))
         return fail(WL_ERR_INVALID_ARGUMENT, "fused quantisation needs in_dim <= %u",
                     I2S_FUSE_Q_MAX_K);
-    I2sKernel k = kI2s[shape][fuse ? 1 : 0][weights_may_have_code3(L.w, L.nw) ? 1 : 0];
+    const int c3 = weights_may_have_code3(L.w, L.nw) ? 1 : 0;
+    I2sKernel k = (fuse && L.pre != I2S_PRE_NONE && L.exact_norm) ? kI2sExact[shape][c3]
+                                                                  : kI2s[shape][fuse ? 1 : 0][c3];
     const uint32_t rpi = (uint32_t)I2S_WARPS * (32u / (uint32_t)lpr);
     // (a tensor-parallel rank with an empty slice still launches one CTA,
     // which only signals its arrival)

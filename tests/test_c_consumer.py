@@ -35,3 +35,24 @@ def test_c_client_links_and_runs(tmp_path):
     args = [] if torch.cuda.is_available() else ["--no-gpu"]
     r = subprocess.run([str(exe), *args], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stderr
+
+
+def test_c_client_links_the_static_library(tmp_path):
+    """The static library (what a Rust build.rs links into its binary) gives
+    the same C client everything it needs: cudart linked statically, no
+    shared library of ours at run time."""
+    from project_willamette_b200 import build
+    _abi.lib()
+    assert os.path.exists(build.STATIC_LIB)
+    cuda_lib = os.path.join(os.path.dirname(os.path.dirname(build.nvcc())), "lib64")
+    exe = tmp_path / "c_consumer_static"
+    r = subprocess.run(["gcc", "-std=c11", *STRICT, "-I", INCLUDE,
+                        os.path.join(HERE, "c_consumer.c"), "-o", str(exe), build.STATIC_LIB,
+                        "-L", cuda_lib, "-lcudart_static", "-lrt", "-lpthread", "-ldl", "-lstdc++",
+                        "-lm"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run(["ldd", str(exe)], capture_output=True, text=True)
+    assert "willamette" not in r.stdout and "cudart" not in r.stdout, r.stdout
+    args = [] if torch.cuda.is_available() else ["--no-gpu"]
+    r = subprocess.run([str(exe), *args], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr

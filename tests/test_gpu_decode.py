@@ -2,8 +2,7 @@
 cached forward and greedy generation (oracle/bitnet_forward.c).
 
 Two modes.  Exact mode is the reference's arithmetic -- its sequential sums
-(bit for bit, csrc/exact_sum.cuh) and its exp (glibc's expf, restated in
-csrc/glibc_expf.cuh): hidden states must agree within EXACT_RTOL (1e-5, the
+in its order and its exp (glibc's expf, restated in csrc/glibc_expf.cuh): hidden states must agree within EXACT_RTOL (1e-5, the
 north-star f32 bound, stated here although the arithmetic is the
 reference's own) and greedy ids must be identical.  Fast mode sums RMSNorm,
 softmax and the weighted V as parallel trees: rounding-level differences, which the int8 re-quantisation at every

@@ -1,23 +1,19 @@
 """The reference's sequential f32 sums and its exp, bit for bit, on the GPU.
 
-Exact mode reproduces rms_norm_f32's sum of squares (primitives.rs:245-248)
-and softmax_inplace's denominator (attention.rs:61-65) with the bits of the
-reference's one-term-at-a-time loop, but computes them in parallel
-(csrc/exact_sum.cuh): runs of additions that stay inside one binade are
-exact integer steps and are summed with a block scan, and only binade
-crossings and rounding ties are added one by one.  These cases drive that
-algorithm through wl_dev_rms_norm_f32 with inputs chosen to break it --
-exact ties (dyadic and integer squares), many binade crossings, subnormal
-partial sums, zeros, a dynamic range of 10^30, and the fallbacks (NaN, inf,
-totals near the f32 limit) -- and compare every output bit with the oracle's
-rms_norm_f32.
+rms_norm_f32's sum of squares (primitives.rs:245-248) and softmax_inplace's
+denominator (attention.rs:61-65) are one-term-at-a-time f32 loops; exact mode
+runs them in that order (wl_ptx.cuh seq_sum, the squares formed in
+parallel first).  wl_dev_rms_norm_f32 is checked with inputs that stress f32
+rounding -- exact ties (dyadic and integer squares), many binade crossings,
+subnormal partial sums, zeros, a dynamic range of 10^30, NaN, inf and totals
+beyond the f32 range -- against the oracle's rms_norm_f32, every output bit.
 
 wl_dev_softmax_f32 adds the reference's exp: f32::exp is the C library's
 expf (glibc 2.39 here), restated in csrc/glibc_expf.cuh.  Its cases put one
 element at 0 (the maximum) so that every other element's exponential is
 expf of that element itself, over a sweep of arguments from -104 to 0, the
-two arguments where glibc corrects its polynomial, and random vectors,
-compared bit for bit with the oracle's softmax_inplace.
+argument where glibc corrects its polynomial, and random vectors, compared
+bit for bit with the oracle's softmax_inplace.
 """
 import numpy as np
 import pytest
