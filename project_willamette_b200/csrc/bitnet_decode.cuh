@@ -601,7 +601,9 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
     const int8_t *v_cache = p.v_cache + z * p.cache_stride;
     const float *k_scale = p.k_scale + (size_t)z * p.scale_stride;
     const float *v_scale = p.v_scale + (size_t)z * p.scale_stride;
-    // The head's cached rows [0, pos) and their scales, 16 bytes per copy.
+    // The head's cached rows [0, pos) and their scales, 16 bytes per copy:
+    // K first (the scores need it), then V in a second copy group (the
+    // weighted sum needs it only after the softmax).
     auto stage_history = [&](uint32_t pos) {
         const uint32_t pieces = HD / 16u, n = pos * pieces;
         for (uint32_t i = tid; i < n; i += AX_THREADS) {
@@ -609,15 +611,20 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
             const size_t g = (size_t)t * KV + kvh * HD + c * 16u;
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Ksm + t * HD + c * 16u)),
                          "l"(k_cache + g) : "memory");
+        }
+        for (uint32_t t = tid; t < pos; t += AX_THREADS)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ksc + t)),
+                         "l"(k_scale + t) : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        for (uint32_t i = tid; i < n; i += AX_THREADS) {
+            const uint32_t t = i / pieces, c = i % pieces;
+            const size_t g = (size_t)t * KV + kvh * HD + c * 16u;
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Vsm + t * HD + c * 16u)),
                          "l"(v_cache + g) : "memory");
         }
-        for (uint32_t t = tid; t < pos; t += AX_THREADS) {
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ksc + t)),
-                         "l"(k_scale + t) : "memory");
+        for (uint32_t t = tid; t < pos; t += AX_THREADS)
             asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(vsc + t)),
                          "l"(v_scale + t) : "memory");
-        }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     uint32_t pos = 0;
@@ -652,11 +659,12 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
                 *v_in = p.v + (size_t)z * p.qkv_stride;
     float *att = p.att + (size_t)z * p.att_stride;
     const float2 *cs = p.rope + (size_t)pos * half;
-    for (uint32_t i = tid; i < KV; i += AX_THREADS) {
-        kf[i] = k_in[i];
-        vf[i] = v_in[i];
+    for (uint32_t i = tid; i < KV / 4u; i += AX_THREADS) {  // KV, HD multiples of 32
+        reinterpret_cast<float4 *>(kf)[i] = reinterpret_cast<const float4 *>(k_in)[i];
+        reinterpret_cast<float4 *>(vf)[i] = reinterpret_cast<const float4 *>(v_in)[i];
     }
-    for (uint32_t i = tid; i < HD; i += AX_THREADS) qh[i] = q_in[h * HD + i];
+    for (uint32_t i = tid; i < HD / 4u; i += AX_THREADS)
+        reinterpret_cast<float4 *>(qh)[i] = reinterpret_cast<const float4 *>(q_in + h * HD)[i];
     for (uint32_t j = tid; j < half; j += AX_THREADS) rope[j] = cs[j];
     __syncthreads();
     // RoPE on every K head (the K quantisation takes the absmax of all of
@@ -692,21 +700,36 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
             p.v_scale[(size_t)z * p.scale_stride + pos] = s_vs;
         }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // the K history is in
     __syncthreads();
-    // scores[t] = (sum_d q[d] * ((f32)k8[t][d] * s_t)) * scale, d in order
+    // scores[t] = (sum_d q[d] * ((f32)k8[t][d] * s_t)) * scale, d in order.
+    // The int8 -> f32 conversion and the two products run as packed pairs
+    // (each lane rounded as the scalar operation); the dependent adds stay
+    // scalar, in order (a packed product feeding a packed add could be
+    // contracted into one FMA).
     const uint32_t n = pos + 1u;
+    const float2 cbias = make_float2(-8388736.0f, -8388736.0f);
     for (uint32_t t = tid; t < n; t += AX_THREADS) {
         const int8_t *kr = t < pos ? Ksm + (size_t)t * HD : kq + kvh * HD;
         const float sk = t < pos ? ksc[t] : s_ks;
+        const float2 sk2 = make_float2(sk, sk);
         float d = 0.0f;
         for (uint32_t c = 0; c < HD; c += 16u) {
             const uint4 w = *reinterpret_cast<const uint4 *>(kr + c);
             const uint32_t wv[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
                                     w.w ^ 0x80808080u};
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-                d = __fadd_rn(d, __fmul_rn(qh[c + e], __fmul_rn(i8_byte_to_f32(wv[e >> 2], e & 3), sk)));
+            for (int e = 0; e < 16; e += 2) {
+                const uint32_t wd = wv[e >> 2];
+                const float2 kv8 = f2_add_rn(
+                    make_float2(__uint_as_float(__byte_perm(wd, 0x4B000000u, 0x7540u + (e & 3))),
+                                __uint_as_float(__byte_perm(wd, 0x4B000000u, 0x7541u + (e & 3)))),
+                    cbias);
+                const float2 qk = f2_mul_rn(*reinterpret_cast<const float2 *>(qh + c + e),
+                                            f2_mul_rn(kv8, sk2));
+                d = __fadd_rn(d, qk.x);
+                d = __fadd_rn(d, qk.y);
+            }
         }
         sc[t] = __fmul_rn(d, p.scale);
     }
@@ -732,19 +755,31 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
             for (uint32_t t = tid; t < n; t += AX_THREADS) sc[t] = __fmul_rn(sc[t], s_inv);
     }
     __syncthreads();
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // the V history is in
+    __syncthreads();
     // out[d] = 0 + sum_t w_t * ((f32)v8[t][d] * s_t), t in order (one thread per d);
-    // the loads and products of the next 8 positions run ahead of the adds
+    // the loads and products of the next 8 positions run ahead of the adds,
+    // the products as packed pairs of positions, the adds scalar and in order
     for (uint32_t d = tid; d < HD; d += AX_THREADS) {
         float o = 0.0f;
         const int8_t *vcol = Vsm + d;
         uint32_t t = 0;
         for (; t + 8u <= pos; t += 8u) {
-            float vv[8];
+            float2 vv[4];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                vv[u] = __fmul_rn(sc[t + u], __fmul_rn(i8_to_f32(vcol[(size_t)(t + u) * HD]), vsc[t + u]));
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t b0 = (uint32_t)(uint8_t)vcol[(size_t)(t + 2 * u) * HD] ^ 0x80u;
+                const uint32_t b1 = (uint32_t)(uint8_t)vcol[(size_t)(t + 2 * u + 1) * HD] ^ 0x80u;
+                const float2 v8 = f2_add_rn(make_float2(__uint_as_float(b0 | 0x4B000000u),
+                                                        __uint_as_float(b1 | 0x4B000000u)), cbias);
+                vv[u] = f2_mul_rn(*reinterpret_cast<const float2 *>(sc + t + 2 * u),
+                                  f2_mul_rn(v8, *reinterpret_cast<const float2 *>(vsc + t + 2 * u)));
+            }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) o = __fadd_rn(o, vv[u]);
+            for (int u = 0; u < 4; ++u) {
+                o = __fadd_rn(o, vv[u].x);
+                o = __fadd_rn(o, vv[u].y);
+            }
         }
         for (; t < pos; ++t)
             o = __fadd_rn(o, __fmul_rn(sc[t], __fmul_rn(i8_to_f32(vcol[(size_t)t * HD]), vsc[t])));
