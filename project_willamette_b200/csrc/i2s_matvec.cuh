@@ -28,6 +28,7 @@
 
 #include <cstdint>
 
+#include "exact_sum.cuh"
 #include "tp.cuh"
 #include "wl_ptx.cuh"
 
@@ -359,7 +360,7 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
         if constexpr (EXACT) {
             // exact mode: the reference's loop sum_sq += x[i] * x[i], i = 0, 1,
             // ...: the squares (one rounding each) stored in parallel, then
-            // added in order by one thread
+            // their sequential sum (exact_sum.cuh)
 #pragma unroll
             for (int k = 0; k < I2S_PRE_V; ++k) {
                 if (k >= kmax) break;
@@ -370,9 +371,14 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
                                     __fmul_rn(v[k].z, v[k].z), __fmul_rn(v[k].w, v[k].w));
             }
             __syncthreads();
-            if (tid == 0) red[0] = seq_sum(chain, K);
-            __syncthreads();
-            sum_sq = red[0];
+            if (K + I2S_QS_PAD >= exact_sum_scratch_bytes(I2S_THREADS)) {
+                // the quantised-input buffer is free until the quantisation
+                sum_sq = cta_exact_sum_nonneg_call(chain, K, reinterpret_cast<uint8_t *>(qs));
+            } else {
+                if (tid == 0) red[0] = seq_sum(chain, K);
+                __syncthreads();
+                sum_sq = red[0];
+            }
         } else {
             float ss = 0.0f;
 #pragma unroll

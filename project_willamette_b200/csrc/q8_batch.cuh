@@ -373,6 +373,7 @@ struct OutNormBatchParams {
 __global__ void __launch_bounds__(256) out_norm_batch_kernel(const __grid_constant__ OutNormBatchParams p) {
     __shared__ float red[32];
     __shared__ __align__(16) float hs[OUT_NORM_MAX];
+    __shared__ __align__(16) uint8_t xscr[exact_sum_scratch_bytes(256)];
     pdl_launch_dependents();
     pdl_wait();
     const float *__restrict__ h = p.hidden + (size_t)blockIdx.x * p.n;
@@ -380,7 +381,7 @@ __global__ void __launch_bounds__(256) out_norm_batch_kernel(const __grid_consta
     const float *__restrict__ nw = p.w;
     float sum_sq;
     if (p.exact) {
-        sum_sq = block_seq_sum_sq(h, p.n, hs, red);
+        sum_sq = block_seq_sum_sq(h, p.n, hs, xscr);
     } else {
         float ss = 0.0f;
         for (uint32_t i = threadIdx.x; i < p.n; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(h[i], h[i]));

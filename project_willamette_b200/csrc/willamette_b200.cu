@@ -2059,8 +2059,9 @@ int wl_dev_rms_norm_f32(const float *x, const float *w, uint32_t n, float eps, f
     if (!aligned16(x) || !aligned16(w) || !aligned16(out))
         return fail(WL_ERR_INVALID_ARGUMENT, "x / w / out not 16-byte aligned");
     if (!status_ptr()) return WL_ERR_NO_DEVICE;
-    WL_CUDA(launch(rms_norm_kernel, dim3(1), dim3(256), (size_t)n * 4u, (cudaStream_t)stream, true,
-                   x, w, n, eps, out));
+    WL_CUDA(launch(rms_norm_kernel, dim3(1), dim3(256),
+                   (size_t)n * 4u + exact_sum_scratch_bytes(256), (cudaStream_t)stream, true, x, w,
+                   n, eps, out));
     return WL_OK;
 }
 
@@ -2071,7 +2072,8 @@ int wl_dev_softmax_f32(float *x, uint32_t n, void *stream) {
     if (!x) return fail(WL_ERR_INVALID_ARGUMENT, "NULL pointer");
     if (!aligned16(x)) return fail(WL_ERR_INVALID_ARGUMENT, "x not 16-byte aligned");
     if (!status_ptr()) return WL_ERR_NO_DEVICE;
-    WL_CUDA(launch(softmax_kernel, dim3(1), dim3(512), (size_t)((n + 3u) & ~3u) * 4u,
+    WL_CUDA(launch(softmax_kernel, dim3(1), dim3(512),
+                   (size_t)((n + 3u) & ~3u) * 4u + exact_sum_scratch_bytes(512),
                    (cudaStream_t)stream, true, x, n));
     return WL_OK;
 }
