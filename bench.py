@@ -640,16 +640,24 @@ def decode_bench(reps: int = 3) -> dict:
                      "(Q6_K tied), KV i8 per-token absmax (the reference's layout)",
            "prompt": n_prompt, "new_tokens": n_new, "headline_mode": "exact",
            "bytes_per_token": int(step_bytes)}
+    kv_bytes16 = LAYERS * 2 * avg_ctx * kv * 2
     notes = {"exact": "the reference's arithmetic: ids and hidden states held to the oracle "
                       "(1e-5) at this configuration",
              "fast": "sums as trees (not the reference's order): hidden states not held to "
                      "1e-5; ids compared with the oracle at this configuration",
-             "fast_persistent": "fast mode as one persistent whole-forward kernel"}
-    for key, exact, persistent in (("exact", True, False), ("fast", False, False),
-                                   ("fast_persistent", False, True)):
-        g = BitNet(m, exact=exact, persistent=persistent)
+             "fast_persistent": "fast mode as one persistent whole-forward kernel",
+             "exact_f16kv": "exact mode with BASELINE config 2's f16 KV cache (binary16 rows, "
+                            "not the reference's int8 layout): held to the oracle's f16 variant",
+             "fast_f16kv": "fast mode with the f16 KV cache"}
+    for key, exact, persistent, f16 in (("exact", True, False, False),
+                                        ("fast", False, False, False),
+                                        ("fast_persistent", False, True, False),
+                                        ("exact_f16kv", True, False, True),
+                                        ("fast_f16kv", False, False, True)):
+        g = BitNet(m, exact=exact, persistent=persistent, kv_f16=f16)
         times, walls = [], []
-        for r in range(reps if not persistent else 1):
+        sb = step_bytes - kv_bytes + kv_bytes16 if f16 else step_bytes
+        for r in range(reps if not (persistent or f16) else 1):
             g.reset()
             g.prefill(prompts[r])
             t0 = time.perf_counter()
@@ -658,7 +666,7 @@ def decode_bench(reps: int = 3) -> dict:
             times.append(ms)
         g.close()
         ms = statistics.median(times)
-        gbs = step_bytes / (ms / n_new * 1e-3) / 1e9
+        gbs = sb / (ms / n_new * 1e-3) / 1e9
         out[key] = {"tok_s": round(n_new / (ms * 1e-3), 1), "ms_per_token": round(ms / n_new, 4),
                     "e2e_tok_s": round(n_new / statistics.median(walls), 1),
                     "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks()["hbm_gbs"], 4),

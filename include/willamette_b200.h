@@ -394,6 +394,15 @@ typedef struct {
      * barriers between phases, weights prefetched into shared memory).
      * Same arithmetic. */
     uint32_t persistent;
+    /* KV cache layout.  0: the reference's per-token absmax int8 rows with
+     * one f32 scale each (kv_cache.rs:245-259), the layout every parity
+     * claim is made on.  1: IEEE binary16 rows (round to nearest even from
+     * the f32 K after RoPE and V; read back exactly), the f16 cache of
+     * benchmark config 2 -- not a reference layout, so its results are
+     * compared with the oracle's f16 variant only.  The BitNet engine only
+     * (the Llama batch engine requires 0); runs per operation (`persistent`
+     * is ignored). */
+    uint32_t kv_f16;
 } wl_bitnet_config;
 
 typedef struct {

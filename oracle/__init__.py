@@ -248,7 +248,7 @@ class OrBitnetConfig(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("n_layers", "n_embd", "n_heads", "n_kv_heads",
                                           "head_dim", "n_ff", "vocab", "n_rot", "max_seq")] + \
                [("eps", C.c_float), ("freq_base", C.c_float), ("variant", _u32),
-                ("linear_type", _u32), ("embd_type", _u32)]
+                ("linear_type", _u32), ("embd_type", _u32), ("kv_f16", _u32)]
 
 
 class OrBitnetWeights(C.Structure):
@@ -328,13 +328,16 @@ class BitnetOracle:
     """The reference's cached forward + greedy generation on a model dict
     (see project_willamette_b200.synth.bitnet_model)."""
 
-    def __init__(self, model: dict):
+    def __init__(self, model: dict, kv_f16: bool = False):
+        """kv_f16: binary16 KV rows instead of the reference's int8 ones (the
+        checker of the library's kv_f16 option; not a reference layout)."""
         self.m = model
         c = model["config"]
         self.cfg = OrBitnetConfig(**{k: c[k] for k in (
             "n_layers", "n_embd", "n_heads", "n_kv_heads", "head_dim", "n_ff", "vocab", "n_rot",
             "max_seq", "eps", "freq_base")}, variant=c.get("variant", 0),
-            linear_type=c.get("linear_type", 0), embd_type=c.get("embd_type", 14))
+            linear_type=c.get("linear_type", 0), embd_type=c.get("embd_type", 14),
+            kv_f16=int(kv_f16))
         ws = model["w"]
         self._wp = (_u8p * len(ws))(*[_p(a, _u8p) for a in ws])
         self.weights = OrBitnetWeights(self._wp, _p(model["w_scale"], _f32p),
@@ -342,8 +345,9 @@ class BitnetOracle:
                                        _p(model["token_embd"], _u8p))
         kv = c["n_kv_heads"] * c["head_dim"]
         n = c["n_layers"] * c["max_seq"]
-        self.kq = np.zeros(n * kv, np.int8)
-        self.vq = np.zeros(n * kv, np.int8)
+        esz = 2 if kv_f16 else 1
+        self.kq = np.zeros(n * kv * esz, np.int8)
+        self.vq = np.zeros(n * kv * esz, np.int8)
         self.ks = np.zeros(n, np.float32)
         self.vs = np.zeros(n, np.float32)
         self.kv = OrKvCache(_p(self.kq, _i8p), _p(self.vq, _i8p), _p(self.ks, _f32p),

@@ -193,29 +193,48 @@ int or_bitnet_forward(const or_bitnet_config *c, const or_bitnet_weights *w, or_
         for (uint32_t h = 0; h < c->n_kv_heads; ++h)
             (llama ? or_rope_norm : or_rope_neox)(k + h * HD, c->n_rot, position, c->freq_base);
         /* KVCache::append then read_into (dequantised f32 of every position) */
-        int8_t *kq = kv->k_q + ((size_t)l * c->max_seq + position) * KV;
-        int8_t *vq = kv->v_q + ((size_t)l * c->max_seq + position) * KV;
-        or_kv_quantise(k, KV, kq, kv->k_s + (size_t)l * c->max_seq + position);
-        or_kv_quantise(v, KV, vq, kv->v_s + (size_t)l * c->max_seq + position);
+        const size_t row = (size_t)l * c->max_seq + position;
+        if (c->kv_f16) {
+            uint16_t *kh = (uint16_t *)kv->k_q + row * KV, *vh = (uint16_t *)kv->v_q + row * KV;
+            for (uint32_t i = 0; i < KV; ++i) {
+                kh[i] = or_f32_to_f16(k[i]);
+                vh[i] = or_f32_to_f16(v[i]);
+            }
+        } else {
+            or_kv_quantise(k, KV, kv->k_q + row * KV, kv->k_s + row);
+            or_kv_quantise(v, KV, kv->v_q + row * KV, kv->v_s + row);
+        }
         const uint32_t n_past = position + 1;
         memset(att, 0, (size_t)E * 4);
         for (uint32_t h = 0; h < c->n_heads; ++h) {
             const uint32_t kvh = h / group;
             const float *qh = q + h * HD;
             for (uint32_t p = 0; p < n_past; ++p) {
-                const int8_t *kp = kv->k_q + ((size_t)l * c->max_seq + p) * KV + kvh * HD;
-                const float sk = kv->k_s[(size_t)l * c->max_seq + p];
+                const size_t r = ((size_t)l * c->max_seq + p) * KV + kvh * HD;
                 float d = 0.0f;
-                for (uint32_t i = 0; i < HD; ++i) d += qh[i] * ((float)kp[i] * sk);
+                if (c->kv_f16) {
+                    const uint16_t *kp = (const uint16_t *)kv->k_q + r;
+                    for (uint32_t i = 0; i < HD; ++i) d += qh[i] * or_f16_to_f32(kp[i]);
+                } else {
+                    const int8_t *kp = kv->k_q + r;
+                    const float sk = kv->k_s[(size_t)l * c->max_seq + p];
+                    for (uint32_t i = 0; i < HD; ++i) d += qh[i] * ((float)kp[i] * sk);
+                }
                 scores[p] = d * scale;
             }
             or_softmax_inplace(scores, n_past);
             float *oh = att + h * HD;
             for (uint32_t p = 0; p < n_past; ++p) {
-                const int8_t *vp = kv->v_q + ((size_t)l * c->max_seq + p) * KV + kvh * HD;
-                const float sv = kv->v_s[(size_t)l * c->max_seq + p];
+                const size_t r = ((size_t)l * c->max_seq + p) * KV + kvh * HD;
                 const float wgt = scores[p];
-                for (uint32_t i = 0; i < HD; ++i) oh[i] += wgt * ((float)vp[i] * sv);
+                if (c->kv_f16) {
+                    const uint16_t *vp = (const uint16_t *)kv->v_q + r;
+                    for (uint32_t i = 0; i < HD; ++i) oh[i] += wgt * or_f16_to_f32(vp[i]);
+                } else {
+                    const int8_t *vp = kv->v_q + r;
+                    const float sv = kv->v_s[(size_t)l * c->max_seq + p];
+                    for (uint32_t i = 0; i < HD; ++i) oh[i] += wgt * ((float)vp[i] * sv);
+                }
             }
         }
         if (!llama) or_rms_norm(att, attn_sub_norm, c->eps, sub, E);

@@ -132,6 +132,10 @@ typedef struct {
     uint32_t variant;
     uint32_t linear_type;  /* 0 = I2_S (w_scale used), 8 = Q8_0 */
     uint32_t embd_type;    /* tied embedding / lm-head: 14 = Q6_K, 8 = Q8_0 */
+    /* 0: the reference's i8 KV cache; 1: binary16 K / V rows (round to nearest
+     * even, read back exactly) -- not a reference layout: the checker of the
+     * library's kv_f16 engine option.  k_q / v_q then hold uint16 values. */
+    uint32_t kv_f16;
 } or_bitnet_config;
 
 typedef struct {
@@ -144,7 +148,7 @@ typedef struct {
 } or_bitnet_weights;
 
 typedef struct { /* src/model/kv_cache.rs layout, one slab per layer */
-    int8_t *k_q, *v_q; /* n_layers * max_seq * kv_dim */
+    int8_t *k_q, *v_q; /* n_layers * max_seq * kv_dim (uint16 each with kv_f16) */
     float *k_s, *v_s;  /* n_layers * max_seq */
     uint32_t pos;
 } or_kv_cache;

@@ -89,7 +89,7 @@ class WlBitnetConfig(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in ("n_layers", "n_embd", "n_heads", "n_kv_heads",
                                           "head_dim", "n_ff", "vocab", "n_rot", "max_seq")] + \
                [("eps", C.c_float), ("freq_base", C.c_float), ("exact", C.c_uint32),
-                ("persistent", C.c_uint32)]
+                ("persistent", C.c_uint32), ("kv_f16", C.c_uint32)]
 
 
 class WlBitnetWeights(C.Structure):

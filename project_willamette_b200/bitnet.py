@@ -35,15 +35,17 @@ def _fp(a: Optional[np.ndarray]):
 
 class BitNet:
     def __init__(self, model: dict, device: int = 0, exact: bool = False,
-                 persistent: bool = False, tp=None):
+                 persistent: bool = False, tp=None, kv_f16: bool = False):
         """tp: a connected ``tp.TPGroup`` (one per rank) for the tensor-parallel
-        engine; its symmetric region must hold ``BitNet.tp_sym_bytes(model)``."""
+        engine; its symmetric region must hold ``BitNet.tp_sym_bytes(model)``.
+        kv_f16: binary16 KV cache rows (benchmark config 2's layout) instead
+        of the reference's per-token absmax int8 rows."""
         L = lib()
         if tp is None:
             _check(L.wl_init(device))
         c = model["config"]
         self.cfg = WlBitnetConfig(**{k: c[k] for k in _CFG_KEYS}, exact=int(exact),
-                                  persistent=int(persistent))
+                                  persistent=int(persistent), kv_f16=int(kv_f16))
         self.n_embd = c["n_embd"]
         ws = [np.ascontiguousarray(a, np.uint8) for a in model["w"]]
         self._keep = [ws, np.ascontiguousarray(model["w_scale"], np.float32),

@@ -23,7 +23,10 @@
 // agree to rounding level, not bit for bit.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include <cstdint>
+#include <type_traits>
 
 #include "exact_sum.cuh"
 #include "glibc_expf.cuh"
@@ -266,7 +269,23 @@ __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, in
 // f32::exp of the reference: glibc's expf, restated bit for bit.
 __device__ __forceinline__ float exp_f32(float x) { return glibc_expf(x); }
 
+// A cached K / V element as f32: (f32)q * s for the int8 layout, the exact
+// value of the half for the f16 layout (s unused).
+template <bool F16>
+__device__ __forceinline__ float kv_value(typename std::conditional<F16, uint16_t, int8_t>::type raw,
+                                          float s) {
+    if constexpr (F16) return __half2float(__ushort_as_half(raw));
+    else return __fmul_rn((float)raw, s);
+}
+
+// F16: the cache holds K and V as IEEE binary16 (round to nearest even from
+// the f32 values; no scales) instead of the reference's per-token absmax
+// int8 -- the KV layout of benchmark config 2.  Every read converts back to
+// f32 exactly; the arithmetic around it is the int8 path's with the
+// dequantised value (f32)k8 * s replaced by the f16 value.
+template <bool F16>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+    using KvT = typename std::conditional<F16, uint16_t, int8_t>::type;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float red[32];
     __shared__ float s_ks, s_vs;
@@ -283,8 +302,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     float *vsc = scores + chunk_max;              // chunk_max: V scales of the split
     float2 *rope = reinterpret_cast<float2 *>(vsc + chunk_max);  // half (rounded to 2)
     float *comb = reinterpret_cast<float *>(rope + ((half + 1u) & ~1u));  // splits*(2+HD)
-    int8_t *kq = reinterpret_cast<int8_t *>(comb + ((p.splits * (2u + HD) + 3u) & ~3u));  // KV
-    int8_t *vq = kq + KV;                                                                 // KV
+    KvT *kq = reinterpret_cast<KvT *>(comb + ((p.splits * (2u + HD) + 3u) & ~3u));  // KV
+    KvT *vq = kq + KV;                                                              // KV
 
     pdl_launch_dependents();
     pdl_wait();
@@ -302,7 +321,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     const float *q_in = p.q + (size_t)z * p.qkv_stride, *k_in = p.k + (size_t)z * p.qkv_stride,
                 *v_in = p.v + (size_t)z * p.qkv_stride;
     float *att = p.att + (size_t)z * p.att_stride;
-    int8_t *k_cache = p.k_cache + z * p.cache_stride, *v_cache = p.v_cache + z * p.cache_stride;
+    KvT *k_cache = reinterpret_cast<KvT *>(p.k_cache) + z * p.cache_stride;
+    KvT *v_cache = reinterpret_cast<KvT *>(p.v_cache) + z * p.cache_stride;
     float *k_scale = p.k_scale + (size_t)z * p.scale_stride,
           *v_scale = p.v_scale + (size_t)z * p.scale_stride;
     float *partial = p.partial + (size_t)z * gridDim.x * p.splits * (HD + 4u);
@@ -333,15 +353,23 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
         qh[i1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
     }
     __syncthreads();
-    kv_quantise_block(ks, KV, kq, &s_ks, red);
-    kv_quantise_block(vs, KV, vq, &s_vs, red);
+    if constexpr (F16) {
+        for (uint32_t i = tid; i < KV; i += blockDim.x) {
+            kq[i] = __half_as_ushort(__float2half_rn(ks[i]));
+            vq[i] = __half_as_ushort(__float2half_rn(vs[i]));
+        }
+        if (tid == 0) s_ks = s_vs = 1.0f;  // no scales: the dequantised value is the f16's
+    } else {
+        kv_quantise_block(ks, KV, kq, &s_ks, red);
+        kv_quantise_block(vs, KV, vq, &s_vs, red);
+    }
     __syncthreads();
     if (h == 0 && sp == 0) {
         for (uint32_t i = tid; i < KV; i += blockDim.x) {
             k_cache[(size_t)pos * KV + i] = kq[i];
             v_cache[(size_t)pos * KV + i] = vq[i];
         }
-        if (tid == 0) {
+        if (!F16 && tid == 0) {
             k_scale[pos] = s_ks;
             v_scale[pos] = s_vs;
         }
@@ -351,9 +379,33 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     const uint32_t t0 = min(n, sp * chunk), t1 = min(n, t0 + chunk), cnt = t1 - t0;
     // scores: one thread per position, the head's row loaded whole first
     // (one memory round trip), then summed in the reference's order
-    for (uint32_t i = tid; i < cnt; i += blockDim.x) {
+    for (uint32_t i = tid; i < cnt && F16; i += blockDim.x) {
+        // f16 rows: q . k with k the exact f32 of each half, in order
         const uint32_t t = t0 + i;
-        const int8_t *kr = t == pos ? kq + kvh * HD : k_cache + (size_t)t * KV + kvh * HD;
+        const uint16_t *kr = reinterpret_cast<const uint16_t *>(
+            t == pos ? kq + kvh * HD : k_cache + (size_t)t * KV + kvh * HD);
+        float d = 0.0f;
+        for (uint32_t c = 0; c < HD; c += 32u) {
+            uint4 w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint4 *>(kr + c + 8u * j);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t wv[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float kf = __half2float(__ushort_as_half((uint16_t)(wv[e >> 1] >> (16 * (e & 1)))));
+                    d = __fadd_rn(d, __fmul_rn(qh[c + 8u * j + e], kf));
+                }
+            }
+        }
+        scores[i] = __fmul_rn(d, p.scale);
+        vsc[i] = 1.0f;
+    }
+    for (uint32_t i = tid; i < cnt && !F16; i += blockDim.x) {
+        const uint32_t t = t0 + i;
+        const int8_t *kr = reinterpret_cast<const int8_t *>(
+            t == pos ? kq + kvh * HD : k_cache + (size_t)t * KV + kvh * HD);
         const float sk = t == pos ? s_ks : k_scale[t];
         vsc[i] = t == pos ? s_vs : v_scale[t];
         uint4 w[16];
@@ -419,17 +471,17 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
         __syncthreads();
         if (tid < HD) {
             float o = 0.0f;
-            const int8_t *vcol = v_cache + (size_t)t0 * KV + kvh * HD + tid;
-            const int8_t vcur = vq[kvh * HD + tid];
+            const KvT *vcol = v_cache + (size_t)t0 * KV + kvh * HD + tid;
+            const KvT vcur = vq[kvh * HD + tid];
             for (uint32_t i0 = 0; i0 < cnt; i0 += 32u) {
-                int8_t vb[32];
+                KvT vb[32];
 #pragma unroll
                 for (uint32_t u = 0; u < 32u; ++u)
                     vb[u] = (i0 + u < cnt && t0 + i0 + u != pos) ? vcol[(size_t)(i0 + u) * KV] : vcur;
 #pragma unroll
                 for (uint32_t u = 0; u < 32u; ++u)
                     if (i0 + u < cnt)
-                        o = __fadd_rn(o, __fmul_rn(scores[i0 + u], __fmul_rn((float)vb[u], vsc[i0 + u])));
+                        o = __fadd_rn(o, __fmul_rn(scores[i0 + u], kv_value<F16>(vb[u], vsc[i0 + u])));
             }
             att[h * HD + tid] = o;
         }
@@ -454,19 +506,19 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const __grid_
     const uint32_t groups = blockDim.x / HD, d = tid % HD, g = tid / HD;
     float acc = 0.0f;
     if (finite && g < groups) {
-        const int8_t *vbase = v_cache + (size_t)kvh * HD + d;
+        const KvT *vbase = v_cache + (size_t)kvh * HD + d;
         for (uint32_t i0 = g; i0 < cnt; i0 += 8u * groups) {
-            int8_t vv[8];
+            KvT vv[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const uint32_t i = i0 + (uint32_t)u * groups;
                 const uint32_t t = t0 + i;
-                vv[u] = i >= cnt ? (int8_t)0 : (t == pos ? vq[kvh * HD + d] : vbase[(size_t)t * KV]);
+                vv[u] = i >= cnt ? (KvT)0 : (t == pos ? vq[kvh * HD + d] : vbase[(size_t)t * KV]);
             }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const uint32_t i = i0 + (uint32_t)u * groups;
-                if (i < cnt) acc = __fadd_rn(acc, __fmul_rn(scores[i], __fmul_rn((float)vv[u], vsc[i])));
+                if (i < cnt) acc = __fadd_rn(acc, __fmul_rn(scores[i], kv_value<F16>(vv[u], vsc[i])));
             }
         }
     }
@@ -841,11 +893,13 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
     }
 }
 
-inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq, uint32_t splits) {
+inline size_t attn_smem_bytes(uint32_t kv, uint32_t hd, uint32_t max_seq, uint32_t splits,
+                              bool f16 = false) {
     const uint32_t chunk = ((max_seq + splits - 1) / splits + 3u) & ~3u;
     const uint32_t half2 = ((hd / 2u + 1u) & ~1u) * 2u;  // float2 RoPE row, in floats
     const uint32_t comb = (splits * (2u + hd) + 3u) & ~3u;
-    return (size_t)(2 * kv + hd + ATTN_THREADS + 2 * chunk + half2 + comb) * 4u + 2u * kv + 16u;
+    return (size_t)(2 * kv + hd + ATTN_THREADS + 2 * chunk + half2 + comb) * 4u +
+           2u * kv * (f16 ? 2u : 1u) + 16u;
 }
 
 }  // namespace wl

@@ -166,7 +166,8 @@ int configure_kernels() {
                             (const void *)kStream[0], (const void *)kStream[1],
                             (const void *)q6k_lmhead_kernel<1>, (const void *)q6k_lmhead_kernel<2>,
                             (const void *)q6k_lmhead_kernel<4>, (const void *)q6k_lmhead_kernel<8>,
-                            (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel,
+                            (const void *)q8_0_matvec_kernel, (const void *)attn_decode_kernel<false>,
+                            (const void *)attn_decode_kernel<true>,
                             (const void *)attn_exact_kernel, (const void *)rms_norm_kernel,
                             (const void *)softmax_kernel,
                             (const void *)bitnet_mega_kernel<false>,
@@ -1453,7 +1454,8 @@ int bn_validate(const wl_bitnet_config *c) {
                     "multiple of 128", HD);
     if (!c->n_rot || c->n_rot % 2 || c->n_rot > HD)
         return fail(WL_ERR_GGUF_PARSE, "rope_dimension_count %u", c->n_rot);
-    if (attn_smem_bytes(bn_kv(*c), HD, c->max_seq, 1) > (size_t)WL_MAX_DYN_SMEM)
+    if (c->kv_f16 > 1) return fail(WL_ERR_INVALID_ARGUMENT, "kv_f16 must be 0 or 1");
+    if (attn_smem_bytes(bn_kv(*c), HD, c->max_seq, 1, c->kv_f16 != 0) > (size_t)WL_MAX_DYN_SMEM)
         return fail(WL_ERR_INVALID_ARGUMENT, "max_seq %u too long for the attention kernel",
                     c->max_seq);
     if (!std::isfinite(c->eps) || !std::isfinite(c->freq_base))
@@ -1637,7 +1639,8 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
     const uint32_t group = c.n_heads / c.n_kv_heads;
     const size_t attn_smem = m->gqa_attn     ? attn_gqa_smem_bytes(KV, c.head_dim, group, m->attn_chunk)
                              : m->exact_attn ? attn_exact_smem_bytes(KV, c.head_dim, c.max_seq)
-                                             : attn_smem_bytes(KV, c.head_dim, c.max_seq, m->splits);
+                                             : attn_smem_bytes(KV, c.head_dim, c.max_seq, m->splits,
+                                                               c.kv_f16 != 0);
     const float scale = 1.0f / sqrtf((float)c.head_dim);  // attention_scale, primitives.rs:354
     int rc;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
@@ -1651,8 +1654,9 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
         ap.k = m->k;
         ap.v = m->v;
         ap.att = m->att;
-        ap.k_cache = m->kq + (size_t)l * c.max_seq * KV;
-        ap.v_cache = m->vq + (size_t)l * c.max_seq * KV;
+        const size_t kv_esz = c.kv_f16 ? 2u : 1u;  // bytes per cached element
+        ap.k_cache = m->kq + (size_t)l * c.max_seq * KV * kv_esz;
+        ap.v_cache = m->vq + (size_t)l * c.max_seq * KV * kv_esz;
         ap.k_scale = m->ks + (size_t)l * c.max_seq;
         ap.v_scale = m->vs + (size_t)l * c.max_seq;
         ap.rope = m->rope;
@@ -1681,7 +1685,8 @@ int bn_enqueue_forward(wl_bitnet *m, cudaStream_t s, bool commit) {
             WL_CUDA(launch(attn_exact_kernel, dim3(c.n_heads, 1, 1), dim3(AX_THREADS), attn_smem, s,
                            true, ap));
         } else {
-            WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits), dim3(ATTN_THREADS),
+            WL_CUDA(launch(c.kv_f16 ? attn_decode_kernel<true> : attn_decode_kernel<false>,
+                           dim3(c.n_heads, m->splits), dim3(ATTN_THREADS),
                            attn_smem, s, true, ap));
         }
         float *o[1] = {m->hidden};
@@ -2608,7 +2613,7 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
     const size_t nrm = (size_t)c.n_layers * (3 * E + F);
     const size_t q6_raw = (size_t)c.vocab * (E / 256) * 210;
     const size_t q6_packed = (size_t)c.vocab * q6k_row_stride(E / 256);
-    const size_t kv_bytes = (size_t)c.n_layers * c.max_seq * KV;
+    const size_t kv_bytes = (size_t)c.n_layers * c.max_seq * KV * (c.kv_f16 ? 2u : 1u);
     const size_t kvs = (size_t)c.n_layers * c.max_seq;
     m->ids_cap = 1u << 16;
     void *p = nullptr;
@@ -2664,7 +2669,7 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
     {   // fast mode: one CTA per (KV head, split of `chunk` positions) for the
         // whole query group, when the group and head size have a kernel
         const uint32_t group = c.n_heads / c.n_kv_heads;
-        if (!c.exact && gqa_attn_kernel(c.head_dim, group) && c.n_rot % 4 == 0) {
+        if (!c.exact && !c.kv_f16 && gqa_attn_kernel(c.head_dim, group) && c.n_rot % 4 == 0) {
             // 64 positions per CTA measured fastest at BitNet-2B shapes with a
             // 640-position cache (1309 us per token; 1359 at 32, 1334 at 128)
             uint32_t chunk = 64;
@@ -2679,8 +2684,9 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
         }
     }
     // exact mode: the whole history of a head in shared memory, when it fits
-    m->exact_attn = c.exact && attn_exact_smem_bytes(KV, c.head_dim, c.max_seq) <=
-                                   kernel_dyn_cap((const void *)attn_exact_kernel);
+    m->exact_attn = c.exact && !c.kv_f16 &&
+                    attn_exact_smem_bytes(KV, c.head_dim, c.max_seq) <=
+                        kernel_dyn_cap((const void *)attn_exact_kernel);
     m->mega_grid = (uint32_t)cx.sm_count;
     m->mega_splits = c.exact ? 1u : std::max<uint32_t>(1u, m->mega_grid / c.n_heads);
     BN_ALLOC(m->attn_partial, (size_t)c.n_heads * std::max(m->splits, m->mega_splits) *
@@ -2741,7 +2747,7 @@ int bn_create(const wl_bitnet_config *cfg, const wl_bitnet_weights *w, wl_tp_gro
     if (e == cudaSuccess) e = cudaMemsetAsync(m->d_step, 0, 16, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cleanup(fail(WL_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e)));
-    if (c.persistent && (rc = bn_setup_mega(m))) return cleanup(rc);
+    if (c.persistent && !c.kv_f16 && (rc = bn_setup_mega(m))) return cleanup(rc);
     *out = m;
     return WL_OK;
 }
@@ -2953,6 +2959,7 @@ int lb_validate(const wl_bitnet_config *c, uint32_t n_seqs) {
     if (!c) return fail(WL_ERR_INVALID_ARGUMENT, "config is NULL");
     const uint32_t E = c->n_embd, F = c->n_ff, HD = c->head_dim;
     if (!n_seqs || n_seqs > 1024) return fail(WL_ERR_INVALID_ARGUMENT, "n_seqs %u (1..1024)", n_seqs);
+    if (c->kv_f16) return fail(WL_ERR_INVALID_ARGUMENT, "kv_f16: the Llama batch engine keeps the int8 cache");
     if (!c->n_layers || !E || !F || !HD || !c->n_heads || !c->n_kv_heads || !c->vocab ||
         !c->max_seq)
         return fail(WL_ERR_GGUF_PARSE, "llama config: zero dimension");
@@ -3100,7 +3107,7 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
             WL_CUDA(launch(attn_exact_kernel, dim3(c.n_heads, 1, S), dim3(AX_THREADS), attn_smem, s,
                            true, ap));
         } else {
-            WL_CUDA(launch(attn_decode_kernel, dim3(c.n_heads, m->splits, S), dim3(ATTN_THREADS),
+            WL_CUDA(launch(attn_decode_kernel<false>, dim3(c.n_heads, m->splits, S), dim3(ATTN_THREADS),
                            attn_smem, s, true, ap));
         }
         Q8BatchJob o[1] = {{w[3], E, 0, 0}};
@@ -3760,6 +3767,7 @@ int wl_bitnet_create_from_gguf(const wl_gguf *g, uint32_t max_seq, uint32_t exac
     if (max_seq) c.max_seq = max_seq;
     c.exact = exact;
     c.persistent = persistent;
+    c.kv_f16 = 0;
     const uint64_t E = c.n_embd, F = c.n_ff, KV = (uint64_t)c.head_dim * c.n_kv_heads, V = c.vocab;
     const std::vector<uint64_t> shapes[7] = {{E, E}, {E, KV}, {E, KV}, {E, E}, {E, F}, {E, F}, {F, E}};
     const Tensor *t;
@@ -3818,6 +3826,7 @@ int wl_llama_batch_create_from_gguf(const wl_gguf *g, uint32_t n_seqs, uint32_t 
     if (max_seq) c.max_seq = max_seq;
     c.exact = exact;
     c.persistent = 0;
+    c.kv_f16 = 0;
     const uint64_t E = c.n_embd, F = c.n_ff, KV = (uint64_t)c.head_dim * c.n_kv_heads, V = c.vocab;
     const std::vector<uint64_t> shapes[7] = {{E, E}, {E, KV}, {E, KV}, {E, E}, {E, F}, {E, F}, {F, E}};
     if (g->by_name.count("output.weight"))

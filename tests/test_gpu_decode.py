@@ -139,3 +139,54 @@ def test_decode_bitnet2b_shapes(bitnet2b, exact, persistent):
             _check_exact([_rel(a, b) for a, b in zip(got_h, want_h)], "decode")
     finally:
         g.close()
+
+
+@pytest.mark.parametrize("exact", [False, True])
+@pytest.mark.parametrize("name", list(CASES))
+def test_decode_f16_kv_matches_oracle_f16_variant(name, exact):
+    """kv_f16: binary16 KV rows (benchmark config 2's cache layout).  The
+    reference has no such cache, so the checker is the oracle's f16 variant
+    (the same forward with the rows rounded to binary16 and read back):
+    exact mode to EXACT_RTOL with identical ids.  Fast mode: identical ids
+    and every step within FLIP_RTOL -- not the rounding-level median, since
+    one re-quantisation flip during the prefill changes the cached rows of
+    every later position (with the int8 cache too; at these seeds the int8
+    runs happen to have none).  The persistent flag is ignored with this
+    layout (per-operation engine)."""
+    from project_willamette_b200.bitnet import BitNet
+    m = _model(200 + list(CASES).index(name), **CASES[name])
+    rng = np.random.default_rng(2)
+    n_prompt = m["config"]["max_seq"] // 2
+    prompt = rng.integers(0, m["config"]["vocab"], n_prompt)
+    n_new = m["config"]["max_seq"] - n_prompt
+    o = oracle.BitnetOracle(m, kv_f16=True)
+    want_ids, want_h = o.generate(prompt, n_new, hiddens=True)
+    g = BitNet(m, exact=exact, persistent=True, kv_f16=True)
+    assert not g.persistent
+    try:
+        got_ids, got_h = g.generate(prompt, n_new, hiddens=True)
+        assert got_ids.tolist() == want_ids.tolist()
+        errs = [_rel(a, b) for a, b in zip(got_h, want_h)]
+        if exact:
+            _check_exact(errs, "decode")
+        else:
+            assert max(errs) <= FLIP_RTOL, f"decode: per-step rel err {np.round(errs, 4)}"
+    finally:
+        g.close()
+
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_decode_f16_kv_bitnet2b_shapes(bitnet2b, exact):
+    """kv_f16 at benchmark config 2 shapes against the oracle's f16 variant
+    (ids; exact mode also the hidden states)."""
+    from project_willamette_b200.bitnet import BitNet
+    m, prompt, _, _ = bitnet2b
+    want_ids, want_h = oracle.BitnetOracle(m, kv_f16=True).generate(prompt, 6, hiddens=True)
+    g = BitNet(m, exact=exact, kv_f16=True)
+    try:
+        got_ids, got_h = g.generate(prompt, 6, hiddens=True)
+        assert got_ids.tolist() == want_ids.tolist()
+        if exact:
+            _check_exact([_rel(a, b) for a, b in zip(got_h, want_h)], "decode")
+    finally:
+        g.close()

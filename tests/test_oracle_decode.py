@@ -159,3 +159,27 @@ def test_llama_q8_forward_follows_its_primitives():
     want = oracle.rms_norm(h, m["output_norm"], c["eps"])  # cached_forward.rs:248-257
     got = oracle.BitnetOracle(m).forward(tok, 0)
     assert np.array_equal(got, want)
+
+
+def test_f16_kv_variant_stores_rounded_rows():
+    """The oracle's binary16-KV variant (the checker of the library's kv_f16
+    option): each cached row is the f32 row rounded to nearest even, the
+    first forward (one position: softmax weight 1) equals the i8 variant's
+    except through the cached values, and generation stays finite."""
+    m = _small(seed=5)
+    o16 = oracle.BitnetOracle(m, kv_f16=True)
+    o8 = oracle.BitnetOracle(m)
+    h16 = o16.forward(7, 0)
+    h8 = o8.forward(7, 0)
+    c = m["config"]
+    kv = c["n_kv_heads"] * c["head_dim"]
+    row = o16.kq.view(np.uint16)[:kv]
+    # every stored value is a finite half, and re-rounding it is the identity
+    vals = row.view(np.float16).astype(np.float32)
+    assert np.all(np.isfinite(vals))
+    assert np.array_equal(vals.astype(np.float16).view(np.uint16), row)
+    # the i8 variant's cache for the same forward quantises differently
+    assert not np.array_equal(h16, h8)
+    assert np.max(np.abs(h16 - h8)) / np.max(np.abs(h8)) < 0.5
+    ids = o16.generate([3, 141, 59], 4)
+    assert len(ids) == 4
