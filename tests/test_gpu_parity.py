@@ -358,8 +358,9 @@ def test_q6k_greedy_batch(batch):
 
 
 def test_q6k_config4_full_vocab():
-    """Benchmark config 4 at full size: 128256 x 2560 Q6_K, batch 1 and a
-    sample of a batch-64 call."""
+    """Benchmark config 4 at full size: 128256 x 2560 Q6_K, batch 1, and a
+    batch-64 call (one launch: every hidden row against each weight chunk)
+    with all 64 logit rows bit for bit and every id."""
     rng = np.random.default_rng(0x5EED + 4)
     n_embd, vocab = 2560, 128256
     t, raw = _q6k(rng, n_embd, vocab)
@@ -369,9 +370,10 @@ def test_q6k_config4_full_vocab():
     assert_bitexact(got, want, "full-vocab logits")
     assert int(wl.lm_head_greedy(h, t, n_embd, vocab)[0]) == oracle.argmax(want)
     H = synth.activations(rng, 64, n_embd)
-    ids = wl.lm_head_greedy(H, t, n_embd, vocab)
-    for b in (0, 17, 63):
+    ids, logits = wl.lm_head_greedy(H, t, n_embd, vocab, return_logits=True)
+    for b in range(64):
         ref = oracle.compute_logits(H[b], raw, 14, n_embd, vocab)
+        assert_bitexact(logits[b], ref, f"batch-64 row {b}")
         assert ids[b] == oracle.argmax(ref), b
 
 
