@@ -7,8 +7,9 @@
 //  * every rank maps every peer's symmetric block (CUDA IPC), so a kernel can
 //    store straight into a peer's memory over NVLink;
 //  * a matvec CTA writes each output row it computes to the same offset of
-//    every rank's block (its own included), then, after a system-scope fence,
-//    adds 1 to its rank's arrival counter in every rank's block;
+//    every rank's block (its own included) and releases them at system
+//    scope; the grid's last CTA then adds 1 to its rank's arrival counter in
+//    every rank's block (a system-scope release);
 //  * a kernel that consumes a gathered vector first waits (bounded, on its
 //    own memory) until every rank's counter has caught up with this rank's
 //    own -- every rank has then finished every exchange op this rank has
@@ -70,23 +71,35 @@ __device__ __forceinline__ void tp_store_all(const TpParams &tp, float *local, f
     for (int r = 0; r < tp.world; ++r) *tp_peer_ptr(tp, local, r) = v;
 }
 
-// One arrival of this rank in every rank's block (release, system scope).
+// Release / acquire fences (no sequentially consistent fence is needed for
+// these message-passing patterns; `fence.sc.sys` measured about 3.7 us per
+// CTA after its peer stores and again in the last CTA).
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// One arrival of this rank in every rank's block: a release at system scope
+// by a thread that follows (CTA barrier) the stores it publishes, so the
+// fence is cumulative over the CTA's stores.
 __device__ __forceinline__ void tp_signal(const TpParams &tp) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     for (int r = 0; r < tp.world; ++r) red_release_sys_add(tp_counter(tp.peer_base[r], tp.rank), 1u);
 }
 
 // Called by thread 0 of every CTA after a CTA barrier that follows all of the
-// CTA's peer stores.  Each CTA fences its stores system-wide and counts
-// itself; the last CTA of the grid re-arms the counter and signals one
-// arrival to every rank -- one arrival per kernel, whatever its grid size.
+// CTA's peer stores.  Each CTA releases its stores at system scope and counts
+// itself; the last CTA of the grid acquires the other CTAs' counts (and with
+// them everything they released), re-arms the counter and signals one
+// arrival to every rank with a system-scope release -- one arrival per
+// kernel, whatever its grid size.
 __device__ __forceinline__ void tp_arrive(const TpParams &tp) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     uint32_t *done = reinterpret_cast<uint32_t *>(tp.local_base + TP_DONE_OFF);
     const uint32_t ctas = gridDim.x * gridDim.y * gridDim.z;
     if (atomicAdd(done, 1u) == ctas - 1u) {
+        fence_acq_rel_gpu();
         atomicExch(done, 0u);
-        tp_signal(tp);
+        for (int r = 0; r < tp.world; ++r)
+            red_release_sys_add(tp_counter(tp.peer_base[r], tp.rank), 1u);
     }
 }
 
