@@ -861,29 +861,36 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
     asm volatile("cp.async.wait_group 0;" ::: "memory");  // the V history is in
     __syncthreads();
     // out[d] = 0 + sum_t w_t * ((f32)v8[t][d] * s_t), t in order (one thread per d);
-    // the loads and products of the next 8 positions run ahead of the adds,
-    // the products as packed pairs of positions, the adds scalar and in order.
-    // (Producer warps filling product buffers for HD consumer threads through
-    // named barriers measured slower: 7.3 against 6.1 us at 516 positions.)
+    // software-pipelined: the loads and products of positions t + 8 .. t + 15
+    // are issued before the in-order adds of t .. t + 7 (weights and scales
+    // as float4 loads; sc and vsc are 16-byte aligned, t a multiple of 8).  (Producer warps filling
+    // product buffers for HD consumer threads through named barriers measured
+    // slower: 7.3 against 6.1 us at 516 positions.)
     for (uint32_t d = tid; d < HD; d += AX_THREADS) {
         float o = 0.0f;
         const int8_t *vcol = Vsm + d;
+        auto prods = [&](uint32_t t, float (&vv)[8]) {
+            const float4 w0 = *reinterpret_cast<const float4 *>(sc + t);
+            const float4 w1 = *reinterpret_cast<const float4 *>(sc + t + 4);
+            const float4 s0 = *reinterpret_cast<const float4 *>(vsc + t);
+            const float4 s1 = *reinterpret_cast<const float4 *>(vsc + t + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                vv[u] = __fmul_rn(wv[u], __fmul_rn(i8_to_f32(vcol[(size_t)(t + u) * HD]), sv[u]));
+        };
         uint32_t t = 0;
+        float cur[8], nxt[8];
+        if (pos >= 8u) prods(0u, cur);
         for (; t + 8u <= pos; t += 8u) {
-            float2 vv[4];
+            const bool more = t + 16u <= pos;
+            if (more) prods(t + 8u, nxt);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t b0 = (uint32_t)(uint8_t)vcol[(size_t)(t + 2 * u) * HD] ^ 0x80u;
-                const uint32_t b1 = (uint32_t)(uint8_t)vcol[(size_t)(t + 2 * u + 1) * HD] ^ 0x80u;
-                const float2 v8 = f2_add_rn(make_float2(__uint_as_float(b0 | 0x4B000000u),
-                                                        __uint_as_float(b1 | 0x4B000000u)), cbias);
-                vv[u] = f2_mul_rn(*reinterpret_cast<const float2 *>(sc + t + 2 * u),
-                                  f2_mul_rn(v8, *reinterpret_cast<const float2 *>(vsc + t + 2 * u)));
-            }
+            for (int u = 0; u < 8; ++u) o = __fadd_rn(o, cur[u]);
+            if (more) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                o = __fadd_rn(o, vv[u].x);
-                o = __fadd_rn(o, vv[u].y);
+                for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
             }
         }
         for (; t < pos; ++t)
