@@ -634,6 +634,24 @@ __device__ __forceinline__ float i8_to_f32(int8_t b) {
     return __fsub_rn(__uint_as_float(((uint32_t)(uint8_t)b ^ 0x80u) | 0x4B000000u), 8388736.0f);
 }
 
+// Shared-memory accesses by 32-bit shared address (ld/st.shared): the V
+// phase below indexes its buffers through computed offsets, and generic
+// 64-bit addressing there cost about twice the time.
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds_u32x2(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts_f32x4(uint32_t a, float x, float y, float z, float w) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w)
+                 : "memory");
+}
+
 // Shared-memory layout (cap = max_seq rounded up to 4, kcap >= cap):
 //   Ksm [kcap][HD] int8   K history; row t's 16-byte piece c sits at piece
 //                         c ^ (t & smask), so the 8 rows a quarter-warp reads
@@ -860,41 +878,89 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");  // the V history is in
     __syncthreads();
-    // out[d] = 0 + sum_t w_t * ((f32)v8[t][d] * s_t), t in order (one thread per d);
-    // software-pipelined: the loads and products of positions t + 8 .. t + 15
-    // are issued before the in-order adds of t .. t + 7 (weights and scales
-    // as float4 loads; sc and vsc are 16-byte aligned, t a multiple of 8).  (Producer warps filling
-    // product buffers for HD consumer threads through named barriers measured
-    // slower: 7.3 against 6.1 us at 516 positions.)
+    // out[d] = 0 + sum_t w_t * ((f32)v8[t][d] * s_t), t in order.  HD threads
+    // add (one per d, a shared-memory load and an add per position) while the
+    // other warps form the next block of B positions' products into the K
+    // region (free after the softmax), double-buffered, one barrier per
+    // block.  (One thread per d forming its own products ran at about 29
+    // cycles per position with 4 of the 16 warps busy.)
+    if (HD <= AX_THREADS / 2u) {
+        const uint32_t B = kcap >= 512u ? 64u : kcap >= 256u ? 32u : 16u;  // 8 * B <= kcap
+        float *pbuf = reinterpret_cast<float *>(Ksm);
+        const uint32_t nb = (pos + B - 1u) / B, q = HD / 8u;
+        // producer pr = tid - HD: row pr / q of each pass, dimensions 8 * (pr % q) ..
+        // + 7; conversions and products as packed pairs (each lane rounded as
+        // the scalar operation; an add feeding a multiply is not contracted)
+        const uint32_t pr = tid - HD, rows_pass = (AX_THREADS - HD) / q;
+        const uint32_t prow = pr / q, d8 = 8u * (pr % q);
+        const float2 cbias = make_float2(-8388736.0f, -8388736.0f);
+        const uint32_t pb = smem_u32(pbuf), vb = smem_u32(Vsm), scb = smem_u32(sc), vsb = smem_u32(vsc);
+        auto produce = [&](uint32_t b) {
+            const uint32_t dst = pb + (b & 1u) * B * HD * 4u + d8 * 4u;
+            const uint32_t t0 = b * B, cnt = min(B, pos - t0);
+            for (uint32_t tt = prow; tt < cnt; tt += rows_pass) {
+                const uint32_t t = t0 + tt;
+                const uint2 w = lds_u32x2(vb + t * HD + d8);
+                const float st = lds_f32(vsb + 4u * t), wt = lds_f32(scb + 4u * t);
+                const uint32_t wx = w.x ^ 0x80808080u, wy = w.y ^ 0x80808080u;
+                const float2 s2 = make_float2(st, st), w2 = make_float2(wt, wt);
+                float2 r[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t wd = j < 2 ? wx : wy, e = 2u * (j & 1);
+                    const float2 v = f2_add_rn(
+                        make_float2(__uint_as_float(__byte_perm(wd, 0x4B000000u, 0x7540u + e)),
+                                    __uint_as_float(__byte_perm(wd, 0x4B000000u, 0x7541u + e))),
+                        cbias);
+                    r[j] = f2_mul_rn(w2, f2_mul_rn(v, s2));
+                }
+                const uint32_t o = dst + tt * HD * 4u;
+                sts_f32x4(o, r[0].x, r[0].y, r[1].x, r[1].y);
+                sts_f32x4(o + 16u, r[2].x, r[2].y, r[3].x, r[3].y);
+            }
+        };
+        const bool producer = tid >= HD && prow < rows_pass;
+        if (producer && nb > 0u) produce(0u);
+        __syncthreads();
+        float o = 0.0f;
+        const uint32_t stride = HD * 4u;
+        for (uint32_t b = 0; b < nb; ++b) {
+            if (tid < HD) {
+                const uint32_t src = pb + (b & 1u) * B * HD * 4u + tid * 4u;
+                const uint32_t cnt = min(B, pos - b * B);
+                if (cnt == B) {  // 16 loads in flight ahead of the 16 adds that use the previous ones
+                    float x[16];
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) x[u] = lds_f32(src + u * stride);
+                    for (uint32_t tt = 16; tt < B; tt += 16) {
+                        float y[16];
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) y[u] = lds_f32(src + (tt + u) * stride);
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) o = __fadd_rn(o, x[u]);
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) x[u] = y[u];
+                    }
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) o = __fadd_rn(o, x[u]);
+                } else {
+                    for (uint32_t tt = 0; tt < cnt; ++tt) o = __fadd_rn(o, lds_f32(src + tt * stride));
+                }
+            } else if (producer && b + 1u < nb) {
+                produce(b + 1u);
+            }
+            __syncthreads();
+        }
+        if (tid < HD) {
+            o = __fadd_rn(o, __fmul_rn(sc[pos], __fmul_rn(i8_to_f32(vq[kvh * HD + tid]), s_vs)));
+            att[h * HD + tid] = o;
+        }
+        return;
+    }
     for (uint32_t d = tid; d < HD; d += AX_THREADS) {
         float o = 0.0f;
-        const int8_t *vcol = Vsm + d;
-        auto prods = [&](uint32_t t, float (&vv)[8]) {
-            const float4 w0 = *reinterpret_cast<const float4 *>(sc + t);
-            const float4 w1 = *reinterpret_cast<const float4 *>(sc + t + 4);
-            const float4 s0 = *reinterpret_cast<const float4 *>(vsc + t);
-            const float4 s1 = *reinterpret_cast<const float4 *>(vsc + t + 4);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                vv[u] = __fmul_rn(wv[u], __fmul_rn(i8_to_f32(vcol[(size_t)(t + u) * HD]), sv[u]));
-        };
-        uint32_t t = 0;
-        float cur[8], nxt[8];
-        if (pos >= 8u) prods(0u, cur);
-        for (; t + 8u <= pos; t += 8u) {
-            const bool more = t + 16u <= pos;
-            if (more) prods(t + 8u, nxt);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) o = __fadd_rn(o, cur[u]);
-            if (more) {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
-            }
-        }
-        for (; t < pos; ++t)
-            o = __fadd_rn(o, __fmul_rn(sc[t], __fmul_rn(i8_to_f32(vcol[(size_t)t * HD]), vsc[t])));
+        for (uint32_t t = 0; t < pos; ++t)
+            o = __fadd_rn(o, __fmul_rn(sc[t], __fmul_rn(i8_to_f32(Vsm[(size_t)t * HD + d]), vsc[t])));
         o = __fadd_rn(o, __fmul_rn(sc[pos], __fmul_rn(i8_to_f32(vq[kvh * HD + d]), s_vs)));
         att[h * HD + d] = o;
     }
