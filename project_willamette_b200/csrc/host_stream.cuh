@@ -278,12 +278,20 @@ int build_stream_plan(const wl_i2s_stream_op *ops, uint32_t n_ops, wl_i2s_stream
         for (uint32_t j = 0; j < n_ops; ++j)
             total_bytes += (uint64_t)(ops[j].out_dim + STREAM_BOX_ROWS - 1) / STREAM_BOX_ROWS *
                            STREAM_BOX_ROWS * (ops[j].in_dim / 4);
+        // each boundary at the block edge nearest its share (a boundary
+        // always placed after the crossing block gave the first CTAs up to a
+        // whole block more than the last ones)
         uint32_t j = 0, b = 1;
         uint64_t cum = 0;
         for (uint32_t blk = 0; blk < (uint32_t)total_blocks && b < G; ++blk) {
             while (j + 1 < n_ops && blk >= block_begin[j + 1]) ++j;
+            const uint64_t before = cum;
             cum += (uint64_t)STREAM_BOX_ROWS * (ops[j].in_dim / 4);
-            while (b < G && cum >= total_bytes * b / G) cb[b++] = blk + 1;
+            while (b < G && cum >= total_bytes * b / G) {
+                const uint64_t target = total_bytes * b / G;
+                cb[b] = (cum - target > target - before && blk > cb[b - 1]) ? blk : blk + 1;
+                ++b;
+            }
         }
         for (; b < G; ++b) cb[b] = (uint32_t)total_blocks;
         cb[G] = (uint32_t)total_blocks;

@@ -71,16 +71,46 @@ struct QuantJob {
 };
 
 // One CTA per distinct input vector; same steps as quantize_absmax_kernel.
+// An input of up to QJ_REGS float4 per thread is loaded once, all loads in
+// flight together, and quantised from registers (a loop waiting for each
+// load in turn, twice, took about 5 us for a 6912-element input).
+constexpr int QJ_REGS = 4;
+__device__ __forceinline__ uint32_t quant_pack4(float4 v, float inv, bool nz) {
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    uint32_t packed = 0;
+    if (nz) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int qi = quant_round_i8(__fmul_rn(e[k], inv));
+            packed |= (uint32_t)(qi & 0xFF) << (8 * k);
+        }
+    }
+    return packed;
+}
+__device__ __forceinline__ float absmax4(float m, float4 v) {
+    return fmaxf(fmaxf(fmaxf(m, fabsf(v.x)), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
 __global__ void __launch_bounds__(QUANT_THREADS)
     quantize_jobs_kernel(const QuantJob *__restrict__ jobs) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float red[QUANT_THREADS / 32];
     const QuantJob j = jobs[blockIdx.x];
+    const float4 *x4 = reinterpret_cast<const float4 *>(j.x);
+    const uint32_t n4 = j.n / 4u;  // n is a multiple of 512
+    const bool in_regs = n4 <= (uint32_t)(QUANT_THREADS * QJ_REGS);
+    float4 v[QJ_REGS];
     float m = 0.0f;
-    for (uint32_t i = threadIdx.x * 4; i < j.n; i += QUANT_THREADS * 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(j.x + i);
-        m = fmaxf(fmaxf(fmaxf(m, fabsf(v.x)), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    if (in_regs) {
+#pragma unroll
+        for (int k = 0; k < QJ_REGS; ++k) {
+            const uint32_t i = threadIdx.x + (uint32_t)k * QUANT_THREADS;
+            v[k] = i < n4 ? x4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < QJ_REGS; ++k) m = absmax4(m, v[k]);
+    } else {
+        for (uint32_t i = threadIdx.x; i < n4; i += QUANT_THREADS) m = absmax4(m, x4[i]);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
@@ -90,18 +120,16 @@ __global__ void __launch_bounds__(QUANT_THREADS)
 #pragma unroll
     for (int w = 1; w < QUANT_THREADS / 32; ++w) max_abs = fmaxf(max_abs, red[w]);
     const float inv = max_abs == 0.0f ? 0.0f : __fdiv_rn(127.0f, max_abs);
-    for (uint32_t i = threadIdx.x * 4; i < j.n; i += QUANT_THREADS * 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(j.x + i);
-        const float e[4] = {v.x, v.y, v.z, v.w};
-        uint32_t packed = 0;
-        if (max_abs != 0.0f) {
+    const bool nz = max_abs != 0.0f;
+    uint32_t *q4 = reinterpret_cast<uint32_t *>(j.q);
+    if (in_regs) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int qi = quant_round_i8(__fmul_rn(e[k], inv));
-                packed |= (uint32_t)(qi & 0xFF) << (8 * k);
-            }
+        for (int k = 0; k < QJ_REGS; ++k) {
+            const uint32_t i = threadIdx.x + (uint32_t)k * QUANT_THREADS;
+            if (i < n4) q4[i] = quant_pack4(v[k], inv, nz);
         }
-        *reinterpret_cast<uint32_t *>(j.q + i) = packed;
+    } else {
+        for (uint32_t i = threadIdx.x; i < n4; i += QUANT_THREADS) q4[i] = quant_pack4(x4[i], inv, nz);
     }
     if (threadIdx.x == 0) *j.scale = max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
 }
@@ -116,25 +144,59 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
-// A warp's walk over (block, slice) boxes: blocks bi = first, first+8, ...
-// below `end`; slices 0 .. ceil(K/512)-1 of each block.
+// A warp's walk over (block, slice) boxes.  Block mode: blocks bi = first,
+// first + STREAM_WARPS, ... below `end`, every slice 0 .. ceil(K/512)-1 of
+// each.  Box mode (a CTA with few blocks): the CTA's boxes in order, `left`
+// of them from (first, si).
+// Each op's first block and box count per row, copied into shared memory at
+// kernel start when there are at most STREAM_OPS_SMEM ops (the walk looks
+// them up at every block; read from global memory they were a chain of
+// dependent loads, 2-6 us before a CTA's first box).
+constexpr uint32_t STREAM_OPS_SMEM = 512;
+struct OpTab {
+    const uint32_t *beg, *S;  // shared memory, or null
+    const I2sStreamOp *ops;
+    uint32_t n;
+    __device__ __forceinline__ uint32_t begin(uint32_t j) const { return beg ? beg[j] : ops[j].block_begin; }
+    __device__ __forceinline__ uint32_t boxes(uint32_t j) const { return S ? S[j] : (ops[j].K + 511u) / 512u; }
+};
+
 struct BoxWalk {
-    uint32_t bi, end, j, si, S;
+    uint32_t bi, end, j, si, S, step, left;
 
-    __device__ __forceinline__ bool valid() const { return bi < end; }
+    __device__ __forceinline__ bool valid() const { return bi < end && left != 0u; }
 
-    __device__ __forceinline__ void seek_op(const I2sStreamOp *ops, uint32_t n_ops) {
-        while (j + 1 < n_ops && bi >= ops[j + 1].block_begin) ++j;
-        S = (ops[j].K + 511u) / 512u;
+    __device__ __forceinline__ void seek_op(const OpTab &t) {
+        while (j + 1 < t.n && bi >= t.begin(j + 1)) ++j;
+        S = t.boxes(j);
     }
 
-    __device__ __forceinline__ void next(const I2sStreamOp *ops, uint32_t n_ops) {
+    __device__ __forceinline__ void next(const OpTab &t) {
+        --left;
         if (++si < S) return;
         si = 0;
-        bi += STREAM_WARPS;
-        if (bi < end) seek_op(ops, n_ops);
+        bi += step;
+        if (bi < end) seek_op(t);
     }
 };
+
+// Op of block bi (binary search over the ops' first blocks).
+__device__ __forceinline__ uint32_t stream_op_of(const OpTab &t, uint32_t bi) {
+    uint32_t lo = 0, hi = t.n;
+    while (lo + 1 < hi) {
+        const uint32_t mid = (lo + hi) / 2;
+        if (t.begin(mid) <= bi) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+// A CTA with fewer blocks than this splits its boxes evenly over its warps
+// (a block's rows then combine partial dots in shared memory); with more, each
+// warp takes every STREAM_WARPS-th block, so that the warps stream
+// neighbouring rows.  (A small row slice, e.g. one rank's share of a model
+// split 8 ways, is about 11 blocks of 5 or 14 boxes per CTA: dealt whole
+// blocks, one warp streamed 14 boxes while others had none.)
+constexpr uint32_t STREAM_SPLIT_MAX_BLOCKS = 3 * STREAM_WARPS;
 
 template <bool C3>
 __global__ void __launch_bounds__(STREAM_THREADS, 1)
@@ -147,18 +209,57 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     uint8_t *ring = smem + (size_t)warp * STREAM_WSTAGES * STREAM_BOX;
     uint64_t *bar = bars + warp * STREAM_WSTAGES;
     const uint32_t b0 = p.cta_blocks[blockIdx.x], b1 = p.cta_blocks[blockIdx.x + 1];
-
-    // first op of this warp's first block
-    BoxWalk walk = {b0 + warp, b1, 0, 0, 1};
-    if (walk.valid()) {
-        uint32_t lo = 0, hi = p.n_ops;
-        while (lo + 1 < hi) {
-            const uint32_t mid = (lo + hi) / 2;
-            if (p.ops[mid].block_begin <= walk.bi) lo = mid; else hi = mid;
+    // Box mode: a block shared by several warps adds its rows' partial dots
+    // into part[slot] (slot = the first warp whose range reaches into the
+    // block) and counts its boxes in cnt[slot]; the warp completing the count
+    // finishes the rows.
+    __shared__ int32_t part[STREAM_WARPS][STREAM_BOX_ROWS];
+    __shared__ uint32_t cnt[STREAM_WARPS];
+    __shared__ uint32_t s_beg[STREAM_OPS_SMEM], s_S[STREAM_OPS_SMEM];
+    const bool tab_smem = p.n_ops <= STREAM_OPS_SMEM;
+    if (tab_smem)
+        for (uint32_t i = threadIdx.x; i < p.n_ops; i += STREAM_THREADS) {
+            s_beg[i] = p.ops[i].block_begin;
+            s_S[i] = (p.ops[i].K + 511u) / 512u;
         }
-        walk.j = lo;
-        walk.seek_op(p.ops, p.n_ops);
+    const OpTab tab = {tab_smem ? s_beg : nullptr, tab_smem ? s_S : nullptr, p.ops, p.n_ops};
+    __syncthreads();  // the op table
+    const bool split = b1 - b0 < STREAM_SPLIT_MAX_BLOCKS;
+    uint32_t T = 0;  // box mode: the CTA's boxes; warp w streams [rw(w), rw(w + 1))
+    auto rw = [&](uint32_t w) { return (uint32_t)(((uint64_t)T * w) / STREAM_WARPS); };
+    BoxWalk walk = {b0 + warp, b1, 0, 0, 1, STREAM_WARPS, 0xFFFFFFFFu};
+    if (split) {
+        for (uint32_t i = threadIdx.x; i < STREAM_WARPS * STREAM_BOX_ROWS; i += STREAM_THREADS)
+            (&part[0][0])[i] = 0;
+        if (threadIdx.x < STREAM_WARPS) cnt[threadIdx.x] = 0u;
+        if (b1 > b0) {
+            uint32_t j = stream_op_of(tab, b0);
+            for (uint32_t bi = b0; bi < b1; ++bi) {
+                while (j + 1 < tab.n && bi >= tab.begin(j + 1)) ++j;
+                T += tab.boxes(j);
+            }
+        }
+        // this warp's first box: block and slice of box rw(warp)
+        walk = {b0, b1, 0, 0, 1, 1u, rw(warp + 1u) - rw(warp)};
+        if (walk.valid()) {
+            walk.j = stream_op_of(tab, b0);
+            walk.seek_op(tab);
+            uint32_t g = 0;
+            while (g + walk.S <= rw(warp)) {
+                g += walk.S;
+                ++walk.bi;
+                walk.seek_op(tab);
+            }
+            walk.si = rw(warp) - g;
+        }
+        __syncthreads();  // part and cnt cleared
+    } else if (walk.valid()) {
+        walk.j = stream_op_of(tab, walk.bi);
+        walk.seek_op(tab);
     }
+    // box index (within the CTA) of the current block's first box, box mode
+    uint32_t gblk = split && walk.valid() ? rw(warp) - walk.si : 0u;
+    uint32_t bstart = walk.si;  // first slice of the current block this warp streams
     BoxWalk ahead = walk;  // the issue cursor runs STREAM_WSTAGES boxes ahead
     const uint64_t policy = l2_policy_evict_first();
     if (lane == 0) {
@@ -172,7 +273,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         mbar_arrive_expect_tx(&bar[stage], STREAM_BOX);
         tma_load_2d(ring + stage * STREAM_BOX, p.maps + ahead.j, ahead.si * STREAM_BOX_BYTES,
                     (ahead.bi - op.block_begin) * STREAM_BOX_ROWS, &bar[stage], policy);
-        ahead.next(p.ops, p.n_ops);
+        ahead.next(tab);
         ++issued;
     };
     if (lane == 0)
@@ -207,9 +308,19 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         if (walk.j != cur) {  // op switch: sum of this op's activations
             cur = walk.j;
             P = op.K >> 6;
+            // 8 loads in flight per lane (a plain loop waited for each in turn:
+            // 14 round trips, about 6 us, for a 6912-element input)
             int32_t s = 0;
-            for (uint32_t i = lane * 16; i < op.K; i += 32 * 16)
-                s += sum_bytes(__ldg(reinterpret_cast<const uint4 *>(op.q + i)));
+            for (uint32_t i0 = lane * 16; i0 < op.K; i0 += 8 * 32 * 16) {
+                uint4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const uint32_t i = i0 + (uint32_t)u * 32u * 16u;
+                    v[u] = i < op.K ? __ldg(reinterpret_cast<const uint4 *>(op.q + i)) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) s += sum_bytes(v[u]);
+            }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
             asum = s;
@@ -261,22 +372,58 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         }
         __syncwarp();  // every lane is done with this stage
         if (lane == 0 && ahead.valid()) issue(st);
-        if (walk.si + 1 == walk.S) {  // last box of the block: finish the rows
+        const bool block_end = walk.si + 1 == walk.S;
+        if (block_end || walk.left == 1u) {  // this warp's last box of the block
+            bool finish = true;
+            int32_t part_dot[STREAM_RPL];
+#pragma unroll
+            for (int r = 0; r < STREAM_RPL; ++r) part_dot[r] = i2s_acc_total(acc[r]) - 2 * corr[r];
+            if (split && !(bstart == 0u && block_end)) {
+                // shared block: add the partial dots, count this warp's boxes
+                uint32_t slot = 0;
+#pragma unroll
+                for (uint32_t w = 1; w < (uint32_t)STREAM_WARPS; ++w)
+                    if (rw(w) <= gblk) slot = w;
+#pragma unroll
+                for (int r = 0; r < STREAM_RPL; ++r) atomicAdd(&part[slot][lane + 32u * r], part_dot[r]);
+                __syncwarp();
+                uint32_t done = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    const uint32_t mine = walk.si + 1u - bstart;
+                    done = atomicAdd(&cnt[slot], mine) + mine == walk.S ? 1u : 0u;
+                    __threadfence_block();
+                }
+                finish = __shfl_sync(0xffffffffu, done, 0) != 0u;
+                if (finish) {
+#pragma unroll
+                    for (int r = 0; r < STREAM_RPL; ++r) part_dot[r] = atomicAdd(&part[slot][lane + 32u * r], 0);
+                }
+            }
+            if (finish) {
+#pragma unroll
+                for (int r = 0; r < STREAM_RPL; ++r) {
+                    const uint32_t row = (walk.bi - op.block_begin) * STREAM_BOX_ROWS + lane + 32u * r;
+                    if (row < op.N) {
+                        const int32_t dot = part_dot[r] - asum;
+                        const float yv = __fmul_rn(combined, __int2float_rn(dot));
+                        if (p.tp.world) tp_store_all(p.tp, op.y + op.row_off + row, yv);
+                        else op.y[op.row_off + row] = yv;
+                        if (op.acc) op.acc[op.row_off + row] = dot;
+                    }
+                }
+            }
 #pragma unroll
             for (int r = 0; r < STREAM_RPL; ++r) {
-                const uint32_t row = (walk.bi - op.block_begin) * STREAM_BOX_ROWS + lane + 32u * r;
-                if (row < op.N) {
-                    const int32_t dot = i2s_acc_total(acc[r]) - asum - 2 * corr[r];
-                    const float yv = __fmul_rn(combined, __int2float_rn(dot));
-                    if (p.tp.world) tp_store_all(p.tp, op.y + op.row_off + row, yv);
-                    else op.y[op.row_off + row] = yv;
-                    if (op.acc) op.acc[op.row_off + row] = dot;
-                }
                 acc[r] = {0, 0, 0, 0};
                 corr[r] = 0;
             }
         }
-        walk.next(p.ops, p.n_ops);
+        if (block_end) {
+            gblk += walk.S;
+            bstart = 0;
+        }
+        walk.next(tab);
     }
     if (timeout && lane == 0) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
     if (p.tp.world) {  // count this CTA in every rank once all its stores are out
