@@ -5,7 +5,9 @@
 //  * every op's weight is cut into 32-row blocks; the blocks of all ops form
 //    one list, and each CTA (one per SM) owns a contiguous, byte-balanced
 //    range of it;
-//  * each of the 12 warps of a CTA takes every 12th block of that range and
+//  * each of the 12 warps of a CTA takes every 12th block of that range (or,
+//    in a CTA with few blocks, an equal contiguous run of its boxes, partial
+//    row dots combined in shared memory) and
 //    streams it as 64-row x 128-byte boxes with 2-D TMA tensor copies
 //    (cp.async.bulk.tensor, 128-byte swizzle) through its own 2-stage
 //    shared-memory ring (12 x 2 beat 8 x 3 and 6-7 x 4 with the same bytes
@@ -190,13 +192,18 @@ __device__ __forceinline__ uint32_t stream_op_of(const OpTab &t, uint32_t bi) {
     return lo;
 }
 
-// A CTA with fewer blocks than this splits its boxes evenly over its warps
-// (a block's rows then combine partial dots in shared memory); with more, each
-// warp takes every STREAM_WARPS-th block, so that the warps stream
-// neighbouring rows.  (A small row slice, e.g. one rank's share of a model
-// split 8 ways, is about 11 blocks of 5 or 14 boxes per CTA: dealt whole
-// blocks, one warp streamed 14 boxes while others had none.)
-constexpr uint32_t STREAM_SPLIT_MAX_BLOCKS = 3 * STREAM_WARPS;
+// A CTA with fewer blocks than this splits its boxes evenly over its warps,
+// each warp a contiguous range (a block's rows then combine partial dots in
+// shared memory); with more, each warp takes every STREAM_WARPS-th block, so
+// that the warps stream neighbouring rows.  (A small row slice, e.g. one
+// rank's share of a model split 8 ways, is about 11 blocks of 5 or 14 boxes
+// per CTA: dealt whole blocks, one warp streamed 14 boxes while others had
+// none.  Measured on the BitNet-2B sweep: the whole model, 72 blocks per CTA,
+// 108 us in block mode and 123 us with contiguous ranges; a half, 36 per CTA,
+// 67.5 and 65.8 us.  Dealing the boxes round robin instead of in contiguous
+// ranges measured 114 / 64 / 41 / 29 us at 1 / 1/2 / 1/4 / 1/8 of the model,
+// against 108 / 66 / 37 / 27: more op switches per warp.)
+constexpr uint32_t STREAM_SPLIT_MAX_BLOCKS = 64;
 
 template <bool C3>
 __global__ void __launch_bounds__(STREAM_THREADS, 1)
@@ -309,7 +316,11 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
             cur = walk.j;
             P = op.K >> 6;
             // 8 loads in flight per lane (a plain loop waited for each in turn:
-            // 14 round trips, about 6 us, for a 6912-element input)
+            // 14 round trips, about 6 us, for a 6912-element input).  The loop
+            // also brings the activations into L1 for this op's boxes: the
+            // sum formed by the quantiser instead, with the lines prefetched
+            // (prefetch.global.L1) and not waited for, measured slower (113
+            // against 108 us for the whole model, 28.7 against 26.7 for 1/8).
             int32_t s = 0;
             for (uint32_t i0 = lane * 16; i0 < op.K; i0 += 8 * 32 * 16) {
                 uint4 v[8];
