@@ -230,7 +230,17 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
             s_S[i] = (p.ops[i].K + 511u) / 512u;
         }
     const OpTab tab = {tab_smem ? s_beg : nullptr, tab_smem ? s_S : nullptr, p.ops, p.n_ops};
-    __syncthreads();  // the op table
+    // Block mode deals blocks dynamically: warp w starts with block b0 + w and
+    // then claims the next unclaimed block of the CTA (next_blk) whenever its
+    // issue cursor reaches the end of a block, so warps that drew short
+    // blocks take more of them.  The claims go through a per-warp ring that
+    // the warp's consumer side reads in the same order.  (Claiming the CTA's
+    // longest blocks first, to end on short ones, measured slower: 108.7
+    // against 105.3 us for the whole BitNet-2B sweep.)
+    __shared__ uint32_t next_blk;
+    __shared__ uint32_t claim[STREAM_WARPS][4];
+    if (threadIdx.x == 0) next_blk = b0 + STREAM_WARPS;
+    __syncthreads();  // the op table, next_blk
     const bool split = b1 - b0 < STREAM_SPLIT_MAX_BLOCKS;
     uint32_t T = 0;  // box mode: the CTA's boxes; warp w streams [rw(w), rw(w + 1))
     auto rw = [&](uint32_t w) { return (uint32_t)(((uint64_t)T * w) / STREAM_WARPS); };
@@ -274,13 +284,22 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         fence_mbar_init();
     }
     __syncwarp();
-    uint32_t issued = 0;
+    uint32_t issued = 0, claims = 0, taken = 0;
     auto issue = [&](uint32_t stage) {
         const I2sStreamOp &op = p.ops[ahead.j];
         mbar_arrive_expect_tx(&bar[stage], STREAM_BOX);
         tma_load_2d(ring + stage * STREAM_BOX, p.maps + ahead.j, ahead.si * STREAM_BOX_BYTES,
                     (ahead.bi - op.block_begin) * STREAM_BOX_ROWS, &bar[stage], policy);
-        ahead.next(tab);
+        if (!split && ahead.si + 1 == ahead.S) {  // claim the next block
+            uint32_t nb = atomicAdd(&next_blk, 1u);
+            nb = nb < b1 ? nb : b1;
+            claim[warp][claims++ & 3u] = nb;
+            ahead.si = 0;
+            ahead.bi = nb;
+            if (nb < b1) ahead.seek_op(tab);
+        } else {
+            ahead.next(tab);
+        }
         ++issued;
     };
     if (lane == 0)
@@ -434,7 +453,13 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
             gblk += walk.S;
             bstart = 0;
         }
-        walk.next(tab);
+        if (!split && walk.si + 1 == walk.S) {  // the block the issue cursor claimed
+            walk.si = 0;
+            walk.bi = reinterpret_cast<volatile uint32_t *>(claim[warp])[taken++ & 3u];
+            if (walk.bi < walk.end) walk.seek_op(tab);
+        } else {
+            walk.next(tab);
+        }
     }
     if (timeout && lane == 0) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
     if (p.tp.world) {  // count this CTA in every rank once all its stores are out
