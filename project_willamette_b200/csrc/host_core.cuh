@@ -67,6 +67,7 @@ struct Ctx {
     uint32_t *d_status = nullptr;
     uint32_t *h_status = nullptr;  // pinned
     void *pinned = nullptr;
+    uint8_t *pinned_dev = nullptr;  // the same buffer as the device reaches it
     size_t pinned_cap = 0;
     DevBuf x, y, q, scale, acc, ids, scratch, rowsum;
     // plain host-buffer matvec calls: [device status word, 16 B][y], so one
@@ -229,7 +230,16 @@ int grow_pinned(Ctx &c, size_t bytes) {
     c.pinned = nullptr;
     c.pinned_cap = 0;
     size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
-    WL_CUDA(cudaMallocHost(&c.pinned, cap));
+    // mapped: the host-buffer matvec's kernel writes its output here directly
+    WL_CUDA(cudaHostAlloc(&c.pinned, cap, cudaHostAllocMapped | cudaHostAllocPortable));
+    void *dev = nullptr;
+    cudaError_t e = cudaHostGetDevicePointer(&dev, c.pinned, 0);
+    if (e != cudaSuccess) {
+        cudaFreeHost(c.pinned);
+        c.pinned = nullptr;
+        return fail(WL_ERR_CUDA, "cudaHostGetDevicePointer: %s", cudaGetErrorString(e));
+    }
+    c.pinned_dev = (uint8_t *)dev;
     c.pinned_cap = cap;
     return WL_OK;
 }
@@ -302,6 +312,7 @@ struct I2sLaunch {
     int8_t *q_out = nullptr;
     float *scale_out = nullptr;
     const TpParams *tp = nullptr;      // tensor-parallel exchange, or null
+    uint32_t *status_host = nullptr;   // host-mapped error word, or null
     const uint32_t *row_offs = nullptr;  // per weight (tensor parallel)
     // decode-step fusions (fused-input kernels only)
     uint32_t pre = I2S_PRE_NONE;
@@ -340,6 +351,7 @@ int launch_i2s_with_status(const I2sLaunch &L, cudaStream_t s, bool pdl, uint32_
     p.q_out = L.q_out;
     p.scale_out = L.scale_out;
     p.status = status;
+    p.status_host = L.status_host;
     if (L.tp) p.tp = *L.tp;
     p.pre = L.pre;
     p.norm_w = L.norm_w;
@@ -682,10 +694,15 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
     // bytes -- the memory-for-speed trade a 180 GB device affords).
     const bool gemm = m >= I2S_GEMM_MIN_TOKENS && m <= 0x7FFFFFFFu;
     const bool fuse = !gemm && K <= I2S_FUSE_Q_MAX_K;
-    // no debug outputs: y and the status word come back in one copy
+    // No debug outputs: the kernel writes y straight into the mapped pinned
+    // buffer (no device-to-host copy to wait for: about 2 us of a call) and
+    // sets a host-mapped word beside it if any status bit is raised; the
+    // status bits themselves stay in device memory (c.ys).
     const bool plain = !gemm && !acc_out && !act_q_out && !act_scale_out;
-    if (plain && (rc = grow(c.ys, yout + 16))) return rc;
-    float *ydev = plain ? (float *)((uint8_t *)c.ys.p + 16) : (float *)c.y.p;
+    if (plain && (rc = grow(c.ys, 16))) return rc;
+    volatile uint32_t *hflag = reinterpret_cast<volatile uint32_t *>(pin + xin);  // [flag][pad][y]
+    if (plain) *hflag = 0u;
+    float *ydev = plain ? (float *)(c.pinned_dev + xin + 16) : (float *)c.y.p;
     uint32_t *dstat = plain ? (uint32_t *)c.ys.p : c.d_status;
     if (gemm) {
         if (!cw->ternary) {
@@ -717,6 +734,7 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
         L.w = &dw;
         L.nw = 1;
         L.K = K;
+        if (plain) L.status_host = (uint32_t *)(c.pinned_dev + xin);
         if (fuse) {
             L.x = (const float *)c.x.p + t * K;
             L.q_out = act_q_out ? (int8_t *)c.q.p + t * K : nullptr;
@@ -729,18 +747,17 @@ int i2s_host_call(const wl_tensor_view *weight, const float *input, size_t input
     }
     m = m_rows;
     if (plain) {
-        uint8_t *pys = pin + xin;  // [status][y]
-        WL_CUDA(cudaMemcpyAsync(pys, c.ys.p, yout + 16, cudaMemcpyDeviceToHost, c.stream));
         cudaError_t e = cudaStreamSynchronize(c.stream);
         if (e != cudaSuccess) return fail(WL_ERR_CUDA, "kernel execution: %s", cudaGetErrorString(e));
-        uint32_t f;
-        memcpy(&f, pys, 4);
-        if (f) {
+        if (*hflag) {
+            uint32_t f = 0;
+            WL_CUDA(cudaMemcpyAsync(c.h_status + 9, c.ys.p, 4, cudaMemcpyDeviceToHost, c.stream));
             WL_CUDA(cudaMemsetAsync(c.ys.p, 0, 4, c.stream));
             WL_CUDA(cudaStreamSynchronize(c.stream));
+            f = c.h_status[9];
             return fail(WL_ERR_DEVICE_TIMEOUT, "a device-side wait timed out (flags 0x%x)", f);
         }
-        memcpy(output, pys + 16, yout);
+        memcpy(output, pin + xin + 16, yout);
         return WL_OK;
     }
     uint8_t *py = pin + xin, *pacc = py + yout, *pq = pacc + yout, *ps = pq + m * (size_t)K;

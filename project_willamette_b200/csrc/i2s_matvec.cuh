@@ -65,6 +65,7 @@ struct I2sMatvecParams {
     int8_t *q_out;          // FUSE_Q: optional copy of the quantised input (CTA 0)
     float *scale_out;       // FUSE_Q: optional activation scale (CTA 0)
     uint32_t *status;
+    uint32_t *status_host;  // optional: host-mapped word set to 1 (plain store) with any status bit
     TpParams tp;            // world 0: single GPU
     // Decode-step fusions (FUSE_Q only): the CTA transforms its input before
     // quantising it, and the epilogue can add the output into y in place.
@@ -449,6 +450,14 @@ __device__ __forceinline__ float cta_prepare_regs(const I2sMatvecParams &p, uint
     return max_abs == 0.0f ? 1.0f : __fdiv_rn(max_abs, 127.0f);
 }
 
+// A host-mapped copy of "some status bit is set", for the host-buffer call that
+// reads its output straight from pinned host memory and so has no device
+// copy to bring the status word back with (a plain store: device atomics on
+// host memory are not available over every host link).
+__device__ __forceinline__ void i2s_flag_host(const I2sMatvecParams &p) {
+    if (p.status_host) *reinterpret_cast<volatile uint32_t *>(p.status_host) = 1u;
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 2: per-op matvec (one BitLinear, or several sharing one input).
 
@@ -553,7 +562,10 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
     pdl_wait();  // the input comes from the previous kernel
     if (p.tp.world && p.tp.wait) {
         // the input is a vector all ranks gathered into this rank's block
-        if (tid == 0 && !tp_wait(p.tp)) atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
+        if (tid == 0 && !tp_wait(p.tp)) {
+            atomicOr(p.status, WL_DEV_ERR_PEER_TIMEOUT);
+            i2s_flag_host(p);
+        }
         __syncthreads();
     }
 
@@ -663,7 +675,10 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
                 break;
             }
         } else if (!__syncthreads_and(mbar_wait(&full_bar[st], (c / nst) & 1u))) {
-            if (tid == 0) atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
+            if (tid == 0) {
+                atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
+                i2s_flag_host(p);
+            }
             // Give the copies already in flight a bounded chance to land
             // before this CTA's shared memory is released.
             for (uint32_t k = c; k < min(nchunks, c + nst); ++k)
@@ -724,14 +739,20 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
                 float v = yv;
                 if (p.residual) {
                     v = __fadd_rn(ysm ? ysm[row - r0] : job.y[job.row_off + local], yv);
-                    if (p.finite_flag && !isfinite(v)) atomicOr(p.status, p.finite_flag);
+                    if (p.finite_flag && !isfinite(v)) {
+                        atomicOr(p.status, p.finite_flag);
+                        i2s_flag_host(p);
+                    }
                 }
                 tp_store_all(p.tp, job.y + job.row_off + local, v);
             } else if (p.residual) {
                 float *dst = job.y + job.row_off + local;
                 const float nv = __fadd_rn(ysm ? ysm[row - r0] : *dst, yv);
                 *dst = nv;
-                if (p.finite_flag && !isfinite(nv)) atomicOr(p.status, p.finite_flag);
+                if (p.finite_flag && !isfinite(nv)) {
+                    atomicOr(p.status, p.finite_flag);
+                    i2s_flag_host(p);
+                }
             } else {
                 job.y[job.row_off + local] = yv;
             }
@@ -749,6 +770,7 @@ __global__ void __launch_bounds__(I2S_THREADS, 2)
         __syncthreads();
         if (s_bad && tid == 0) {
             atomicOr(p.status, WL_DEV_ERR_TIMEOUT);
+            i2s_flag_host(p);
             // bounded waits for the copies still in flight before the CTA's
             // shared memory is released
             for (uint32_t k = 0; k < nchunks; ++k) (void)mbar_wait(&full_bar[k], 0u);
