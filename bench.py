@@ -481,9 +481,9 @@ class _Null:
 
 
 # DRAM traffic of one i2s_stream_kernel launch of the 1-GPU sweep (one ncu
-# capture: dram__bytes_read.sum + dram__bytes_write.sum = 542,717,440 +
-# 4,833,536 bytes).
-TRAFFIC_PER_STEP_BYTES = 547550976
+# capture: dram__bytes_read.sum + dram__bytes_write.sum = 545,170,944 +
+# 4,862,208 bytes).
+TRAFFIC_PER_STEP_BYTES = 550033152
 
 
 def config1_bench(torch, dev, L, stream, reps: int = 400) -> dict:
