@@ -177,7 +177,7 @@ int wl_tp_i2s_stream_run(wl_tp_group *g, wl_i2s_stream_plan *plan, void *stream)
     cudaStream_t s = (cudaStream_t)stream;
     WL_CUDA(launch(quantize_jobs_kernel, dim3(plan->n_quant), dim3(QUANT_THREADS), 0, s, true,
                    (const QuantJob *)plan->d_qjobs));
-    I2sStreamParams p = {};  // single GPU: tp.world = 0
+    I2sStreamParams p = {};
     p.ops = plan->d_ops;
     p.maps = plan->d_maps;
     p.n_ops = plan->n_ops;

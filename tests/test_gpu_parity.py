@@ -269,6 +269,44 @@ def test_i2s_fused_input_and_code3_scan():
             assert_bitexact(yd.cpu().numpy(), ry, f"fused {K}x{n}")
 
 
+def test_i2s_stream_plan_block_mode_bit_exact():
+    """A plan large enough that each CTA owns more than 64 row blocks, so the
+    streaming kernel deals whole blocks to its warps dynamically (5, 2 and 1
+    boxes per block mixed), bit-exact against the oracle, run twice."""
+    import ctypes
+    import torch
+    L = wl.lib()
+    rng = np.random.default_rng(4242)
+    specs = [(512, 300000), (2560, 150000), (1024, 200003)]
+    ops, keep, ref = [], [], []
+    for K, N in specs:
+        x = synth.activations(rng, K)
+        p = synth.i2s_packed(rng, K, N)
+        s = synth.i2s_scale(rng)
+        pd, xd = _dev(torch, p), _dev(torch, x)
+        yd = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+        keep += [pd, xd, yd]
+        op = wl._abi.WlI2sStreamOp()
+        op.packed, op.w_scale, op.in_dim, op.out_dim = pd.data_ptr(), s, K, N
+        op.x, op.y, op.acc, op.flags = xd.data_ptr(), yd.data_ptr(), None, 0
+        ops.append(op)
+        ref.append((yd, oracle.i2s_matvec_sse2_i8(p, s, K, N, x)[0]))
+    blocks = sum((N + 63) // 64 for _, N in specs)
+    assert blocks > 64 * 148  # block mode on a 148-SM B200
+    arr = (wl._abi.WlI2sStreamOp * len(ops))(*ops)
+    plan = ctypes.c_void_p()
+    assert L.wl_i2s_stream_plan_create(arr, len(ops), ctypes.byref(plan)) == 0, L.wl_last_error()
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        for yd, _r in ref:
+            yd.fill_(float("nan"))
+        assert L.wl_dev_i2s_stream_run(plan, stream) == 0
+        torch.cuda.synchronize()
+        for yd, ry in ref:
+            assert_bitexact(yd.cpu().numpy(), ry, "stream block mode")
+    assert L.wl_i2s_stream_plan_destroy(plan) == 0
+
+
 @pytest.mark.parametrize("with_code3", [False, True])
 def test_i2s_stream_plan_bit_exact(with_code3):
     """Many independent matvecs (mixed in_dim, shared and distinct inputs,
