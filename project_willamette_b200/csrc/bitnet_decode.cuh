@@ -247,6 +247,10 @@ struct AttnParams {
     // (a previous step), so the cache history may be staged before the
     // programmatic-dependency wait.
     uint32_t pos_stable;
+    // attn_exact_kernel, batched: grid z index -> sequence (null: identity).
+    // The engine lists the longest contexts first, so that their CTAs, the
+    // longest-running, are dispatched first and the short ones fill in.
+    const uint32_t *seq_order;
 };
 
 __device__ __forceinline__ void kv_quantise_block(const float *x, uint32_t n, int8_t *q,
@@ -666,7 +670,8 @@ __global__ void __launch_bounds__(AX_THREADS) attn_exact_kernel(const __grid_con
     __shared__ float s_ks, s_vs, s_inv;
     __shared__ uint32_t s_norm;
     const uint32_t HD = p.head_dim, KV = p.n_kv_heads * HD, half = p.n_rot / 2u;
-    const uint32_t h = blockIdx.x, kvh = h / p.group, tid = threadIdx.x, z = blockIdx.z;
+    const uint32_t h = blockIdx.x, kvh = h / p.group, tid = threadIdx.x;
+    const uint32_t z = p.seq_order ? p.seq_order[blockIdx.z] : blockIdx.z;
     const uint32_t cap = ax_cap(p.max_seq), kcap = ax_kcap(p.max_seq);
     const uint32_t pieces = HD / 16u, smask = (pieces < 8u ? pieces : 8u) - 1u;
     int8_t *Ksm = reinterpret_cast<int8_t *>(smem);

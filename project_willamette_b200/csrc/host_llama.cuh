@@ -7,6 +7,8 @@
 // standalone header).
 #pragma once
 
+#include <algorithm>
+
 // ============================================ batched Q8_0 Llama decode engine
 // Independent sequences decoded in lock step (one token per sequence per
 // step), each with its own i8 KV cache and position; every step is one CUDA
@@ -32,7 +34,8 @@ struct wl_llama_batch {
           *final_h = nullptr;
     uint32_t *d_tokens = nullptr, *d_active = nullptr, *d_ones = nullptr, *d_pos = nullptr,
              *d_cur_pos = nullptr, *d_step = nullptr, *d_ids = nullptr, *d_status = nullptr,
-             *d_counter = nullptr, *attn_counters = nullptr;
+             *d_counter = nullptr, *attn_counters = nullptr,
+             *d_seq_order = nullptr;  // exact attention: sequences, longest context first
     unsigned long long *d_slots = nullptr;
     float *attn_partial = nullptr;
     uint32_t splits = 1, ids_cap_steps = 0;
@@ -202,6 +205,7 @@ int lb_enqueue_forward(wl_llama_batch *m, cudaStream_t s) {
         ap.active = m->d_active;
         ap.rope_pairs = 1;  // RopeType::Norm for VanillaLlama (cached_forward.rs:505-509)
         ap.chunk = m->attn_chunk;
+        ap.seq_order = m->d_seq_order;
         if (m->gqa_attn) {
             WL_CUDA(launch(gqa_attn_kernel(HD, c.n_heads / c.n_kv_heads), dim3(c.n_kv_heads, S, m->splits),
                            dim3(AB_THREADS), attn_smem, s, true, ap));
@@ -386,6 +390,7 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
     LB_ALLOC(m->d_tokens, (size_t)S * 4);
     LB_ALLOC(m->d_active, (size_t)S * 4);
     LB_ALLOC(m->d_ones, (size_t)S * 4);
+    LB_ALLOC(m->d_seq_order, (size_t)S * 4);
     LB_ALLOC(m->d_pos, (size_t)S * 4);
     LB_ALLOC(m->d_cur_pos, (size_t)S * 4);
     LB_ALLOC(m->d_step, 16);
@@ -430,8 +435,12 @@ int wl_llama_batch_create(const wl_bitnet_config *cfg, const wl_llama_weights *w
     std::vector<uint32_t> ones(S, 1u);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(m->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice, s);
+    std::vector<uint32_t> ident(S);
+    for (uint32_t b = 0; b < S; ++b) ident[b] = b;
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(m->d_ones, ones.data(), (size_t)S * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->d_seq_order, ident.data(), (size_t)S * 4, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(m->d_pos, 0, (size_t)S * 4, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(m->d_step, 0, 16, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(m->d_status, 0, 16, s);
@@ -454,7 +463,7 @@ int wl_llama_batch_destroy(wl_llama_batch *m) {
                     m->vq, m->ks, m->vs, m->hidden, m->qkv, m->att, m->fused, m->final_h,
                     m->d_tokens, m->d_active, m->d_ones, m->d_pos, m->d_cur_pos, m->d_step,
                     m->d_status, m->d_counter, m->d_slots, m->d_ids, m->attn_partial,
-                    m->attn_counters};
+                    m->attn_counters, m->d_seq_order};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -563,6 +572,16 @@ int wl_llama_batch_decode(wl_llama_batch *m, uint32_t n_new, uint32_t *out_ids, 
     if (!m->g_last && (rc = lb_capture(m, 2, &m->g_last))) return rc;
     WL_CUDA(cudaMemsetAsync(m->d_step, 0, 4, m->stream));
     WL_CUDA(cudaMemcpyAsync(m->d_active, m->d_ones, (size_t)S * 4, cudaMemcpyDeviceToDevice, m->stream));
+    {
+        // every step adds one position to every sequence: the order by
+        // context length holds for the whole call
+        std::vector<uint32_t> order(S);
+        for (uint32_t b = 0; b < S; ++b) order[b] = b;
+        std::stable_sort(order.begin(), order.end(),
+                         [&](uint32_t x, uint32_t y) { return m->pos[x] > m->pos[y]; });
+        WL_CUDA(cudaMemcpyAsync(m->d_seq_order, order.data(), (size_t)S * 4, cudaMemcpyHostToDevice,
+                                m->stream));  // pageable source: staged before the call returns
+    }
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (device_ms) {
         WL_CUDA(cudaEventCreate(&e0));
